@@ -1,0 +1,172 @@
+/*
+ * textsift_cuda.h — C ABI of libtextsift_cuda.so, a B200 (sm_100a) backend for
+ * textsift's privacy-filter forward pass.
+ *
+ * The library replaces, for this one path, what textsift's Node backend binds
+ * through N-API (packages/textsift/src/native/backend.ts:34-60 `NativeApi`,
+ * exported by packages/textsift/src/native/napi.zig:42-47) and what the WASM
+ * backend computes in packages/textsift/src/browser/backends/wasm.ts:728-805
+ * (`WasmBackend.forward`).  Weight upload and every device buffer live inside
+ * the library; the host passes named tensors once and token ids per forward.
+ *
+ * Conventions (after packages/textsift/src/native/vulkan/bridge.h:5-8):
+ *   - every function returning int returns TS_OK (0) or a negative TS_ERR_*;
+ *     ts_cuda_last_error() gives a message for the calling thread;
+ *   - constructors return NULL on failure and write a message to err (if any);
+ *   - pointers documented "host" are plain host memory, "device" are CUDA
+ *     device pointers of the handle's device; `stream` is a cudaStream_t
+ *     (NULL = the handle's own stream).
+ * Handles are not thread-safe: one caller at a time per handle, as the
+ * reference serializes forwards (browser/privacy-filter.ts:522-526).
+ */
+#ifndef TEXTSIFT_CUDA_H
+#define TEXTSIFT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TS_CUDA_ABI_VERSION 1
+
+enum {
+  TS_OK = 0,
+  TS_ERR_ARG = -1,          /* bad argument (null pointer, size, unknown name) */
+  TS_ERR_STATE = -2,        /* handle not ready (weights missing / not finalized) */
+  TS_ERR_CUDA = -3,         /* CUDA runtime error */
+  TS_ERR_UNSUPPORTED = -4,  /* shape or value the kernels do not handle */
+  TS_ERR_DEVICE = -5        /* a kernel reported an error through its device flag */
+};
+
+enum { TS_DTYPE_U8 = 0, TS_DTYPE_F16 = 1, TS_DTYPE_F32 = 2, TS_DTYPE_I32 = 3 };
+
+/* TS_MODE_FAST: tensor-core GEMMs (fp16 operands, f32 accumulation) and
+ * tensor-core attention.  TS_MODE_EXACT: every GEMM and the attention in the
+ * reference's own f32 summation order on CUDA cores. */
+enum { TS_MODE_FAST = 0, TS_MODE_EXACT = 1 };
+
+typedef struct ts_cuda ts_cuda_t;
+typedef struct ts_cuda_w4 ts_cuda_w4_t;
+
+/* Architecture constants; defaults are packages/textsift/src/browser/
+ * backends/wasm.ts:464-483 (PF_CONFIG) with vocab 200064. */
+typedef struct ts_cuda_cfg {
+  int32_t device;
+  uint32_t vocab, d_model, n_layers, n_heads, n_kv_heads, head_dim, window;
+  uint32_t d_ff, n_experts, top_k, n_classes;
+  float eps;
+  double rope_theta, rope_factor, rope_original_max_pos, rope_beta_fast, rope_beta_slow;
+  uint32_t max_tokens;  /* largest packed forward (sum of sequence lengths) */
+  uint32_t max_seq_len; /* longest single sequence (RoPE table rows) */
+  int32_t mode;         /* TS_MODE_FAST or TS_MODE_EXACT */
+} ts_cuda_cfg;
+
+int ts_cuda_abi_version(void);
+void ts_cuda_default_cfg(ts_cuda_cfg* cfg);
+
+/* Create a backend on cfg->device.  Replaces NativeApi.createBackend
+ * (native/backend.ts:36; napi.zig:547 vulkanCreateBackend). */
+ts_cuda_t* ts_cuda_create(const ts_cuda_cfg* cfg, char* err, size_t err_cap);
+
+/* Upload one tensor under the name loadOnnxWeights gives it
+ * (browser/backends/wasm.ts:358-446), e.g. "embed.int4",
+ * "layers.0.attn.q_proj.scales", "layers.3.experts.gate_up.zp", "score.bias".
+ * Bytes are copied; shape is checked against cfg.  Replaces
+ * NativeApi.createBuffer per weight (native/backend.ts:140-236). */
+int ts_cuda_load_tensor(ts_cuda_t* h, const char* name, int32_t dtype, const int64_t* shape, int32_t ndim,
+                        const void* host_data, size_t nbytes);
+
+/* Check that every tensor is present, repack the int4 GEMM weights into
+ * tensor-core tiles and build the YaRN RoPE tables.  Idempotent, like
+ * InferenceBackend.warmup (browser/backends/abstract.ts:44). */
+int ts_cuda_finalize(ts_cuda_t* h);
+
+int ts_cuda_set_mode(ts_cuda_t* h, int32_t mode);
+
+/* One sequence: ids (host) [T], mask (host, 1 = token, 0 = padding, may be
+ * NULL) [T] -> logits (host) f32 [T, n_classes].  Replaces
+ * InferenceBackend.forward (browser/backends/abstract.ts:46-55). */
+int ts_cuda_forward(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, uint32_t T, float* logits);
+
+/* Many independent sequences packed back to back: sequence s covers tokens
+ * [seq_offsets[s], seq_offsets[s+1]) (host, n_seqs+1 entries, offsets[0] = 0).
+ * Each sequence is computed exactly as its own forward would be. */
+int ts_cuda_forward_packed(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
+                           uint32_t n_seqs, float* logits);
+
+/* As ts_cuda_forward_packed with ids/mask/logits in device memory, enqueued on
+ * `stream` without synchronizing (seq_offsets stays a host array). */
+int ts_cuda_forward_packed_device(ts_cuda_t* h, const int32_t* d_ids, const uint8_t* d_mask,
+                                  const uint32_t* seq_offsets, uint32_t n_seqs, float* d_logits, void* stream);
+
+/* Synchronize the handle's work on `stream` and report a device-side error
+ * flag (bounded waits that timed out, bad indices) as TS_ERR_DEVICE. */
+int ts_cuda_check(ts_cuda_t* h, void* stream);
+
+const char* ts_cuda_device_name(ts_cuda_t* h);  /* NativeApi.deviceName (native/backend.ts:38) */
+const char* ts_cuda_last_error(void);
+void ts_cuda_destroy(ts_cuda_t* h);             /* NativeApi.destroyBackend (native/backend.ts:37) */
+
+/* ---- per-op entry points: the analogue of the reference's
+ * vulkanDispatchOneShot conformance path (native/vulkan_backend.zig:342-364,
+ * tests/native/vulkan/conformance-all.js).  All device pointers. ---- */
+
+/* GatherBlockQuantized embedding (zig/wasm_exports.zig:1523-1573). */
+int ts_cuda_op_gather_bq(const uint8_t* d_int4, const uint16_t* d_scales, const uint8_t* d_zp,
+                         const int32_t* d_ids, uint16_t* d_out, uint32_t T, uint32_t V, uint32_t D, void* stream);
+
+/* RMSNorm fp16 -> f32 (zig/wasm_exports.zig:229-277); d_b non-NULL selects
+ * the fused add+RMSNorm (288-350), which also writes d_sum (fp16). */
+int ts_cuda_op_rmsnorm(const uint16_t* d_a, const uint16_t* d_b, const uint16_t* d_gamma, uint16_t* d_sum,
+                       float* d_out, uint32_t T, uint32_t D, float eps, void* stream);
+
+/* A MatMulNBits weight (uint4 [E][N][K/2], fp16 scales [E][N][K/32], uint4
+ * zero points [E][N][ceil(K/64)] or NULL, fp16 bias [E][N] or NULL; host
+ * memory), uploaded and repacked for the tensor-core kernel. */
+ts_cuda_w4_t* ts_cuda_w4_create(int32_t device, const uint8_t* int4, const uint16_t* scales, const uint8_t* zp,
+                                const uint16_t* bias, uint32_t E, uint32_t N, uint32_t K, char* err,
+                                size_t err_cap);
+void ts_cuda_w4_destroy(ts_cuda_w4_t* w);
+
+/* The dequantised fp16 operand fp16((q - zp) * scale) of expert e, exactly as
+ * the tensor-core GEMM places it in shared memory, row-major [N, K]. */
+int ts_cuda_op_dequant(const ts_cuda_w4_t* w, uint32_t expert, uint16_t* d_out, void* stream);
+
+/* MatMulNBits y = x . dequant(W)^T + b for expert e (zig/wasm_exports.zig:
+ * 560-766).  x: [M, K], x_dtype TS_DTYPE_F16 (fast/exact) or TS_DTYPE_F32
+ * (exact only); out: [M, N], out_dtype TS_DTYPE_F16 or TS_DTYPE_F32. */
+int ts_cuda_op_matmul_nbits(const ts_cuda_w4_t* w, uint32_t expert, const void* d_x, int32_t x_dtype, void* d_out,
+                            int32_t out_dtype, uint32_t M, int32_t mode, void* stream);
+
+/* Router of layer `layer`: f32 logits in the reference order, top-k with the
+ * reference tie rule, softmax over k, x 1/k (browser/inference/block.ts:
+ * 154-207).  d_x: f32 [T, d_model]; d_idx: i32 [T, k]; d_w: f32 [T, k]. */
+int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32_t* d_idx, float* d_w, uint32_t T,
+                           void* stream);
+
+/* MoE half of block `layer` (router + experts, browser/inference/block.ts:
+ * 286-299 + expert.ts:104-212): d_x f32 [T, d_model] -> d_out fp16
+ * [T, d_model] = fp16(K * sum_k w_k expert_k(x)); routing written to
+ * d_idx/d_w when non-NULL.  Uses the handle's mode. */
+int ts_cuda_op_moe(ts_cuda_t* h, uint32_t layer, const float* d_x, uint16_t* d_out, int32_t* d_idx, float* d_w,
+                   uint32_t T, void* stream);
+
+/* Banded GQA attention with sinks (zig/wasm_exports.zig:1286-1432) over
+ * packed sequences (seq_offsets host, NULL = one sequence of T tokens).
+ * q fp16 [T, Hq*hd], k/v fp16 [T, Hkv*hd], sinks f32 [Hq], mask u8 [T] or
+ * NULL, out fp16 [T, Hq*hd]. */
+int ts_cuda_op_banded_attention(const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v, const float* d_sinks,
+                                const uint8_t* d_mask, uint16_t* d_out, uint32_t T, uint32_t Hq, uint32_t Hkv,
+                                uint32_t head_dim, uint32_t window, const uint32_t* seq_offsets, uint32_t n_seqs,
+                                int32_t mode, void* stream);
+
+/* YaRN RoPE tables of the handle (browser/inference/rope.ts:348-356), fp16
+ * [rows, head_dim/2] each, copied to host. */
+int ts_cuda_rope_tables(ts_cuda_t* h, uint32_t rows, uint16_t* cos_out, uint16_t* sin_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TEXTSIFT_CUDA_H */

@@ -1,0 +1,154 @@
+"""Model-level parity on the GPU through the C ABI (CudaBackend): router
+top-k, the MoE half of a block, and the whole forward, against the oracle's
+restatement of textsift's WASM forward on the same seeded weights and ids.
+
+Gates: top-k expert indices bit-exact for identical
+router inputs; logits within 2e-2 max-abs of the reference; argmax labels
+identical except where the reference's own top-2 logit margin is inside that
+tolerance.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import dev, empty, f16, host, ptr, stream, ulp_diff
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+
+
+def rng(seed):
+    return np.random.Generator(np.random.PCG64(seed))
+
+
+@pytest.fixture(scope="module")
+def small():
+    """2-layer model, real hidden sizes, nonzero biases and sinks."""
+    from textsift_b200 import make_weights, small_config
+    cfg = small_config(n_layers=2, vocab=4096)
+    w = make_weights(cfg, seed=11, bias_std=0.02, sink_range=1.0)
+    return cfg, w
+
+
+@pytest.fixture(scope="module")
+def small_backend(small, cuda_lib):
+    from textsift_b200 import CudaBackend
+    cfg, w = small
+    b = CudaBackend(w, cfg, max_tokens=8192, max_seq_len=4096)
+    b.warmup()
+    yield b
+    b.dispose()
+
+
+@pytest.fixture(scope="module")
+def small_oracle(small, oracle):
+    cfg, w = small
+    return oracle.OracleModel(cfg, w)
+
+
+def test_router_topk_bit_exact(small_backend, small_oracle, cuda_lib):
+    T = 1000
+    x = rng(1).normal(0, 1, size=(T, 640)).astype(np.float32)
+    idx = empty((T, 4), np.int32)
+    w = empty((T, 4), np.float32)
+    for layer in (0, 1):
+        assert cuda_lib.ts_cuda_op_router_topk(small_backend.handle, layer, ptr(dev(x)), ptr(idx), ptr(w), T,
+                                               stream()) == 0
+        _, ridx, rw = small_oracle.moe(layer, x)
+        assert np.array_equal(host(idx, np.int32), ridx)
+        np.testing.assert_allclose(host(w, np.float32), rw, rtol=2e-7, atol=0)
+
+
+@pytest.mark.parametrize("mode", [1, 0])
+def test_moe_layer(small_backend, small_oracle, cuda_lib, mode):
+    from textsift_b200 import abi
+    T = 777
+    x = rng(2).normal(0, 1, size=(T, 640)).astype(np.float32)
+    small_backend.set_mode(mode)
+    try:
+        out = empty((T, 640), np.uint16)
+        idx = empty((T, 4), np.int32)
+        assert cuda_lib.ts_cuda_op_moe(small_backend.handle, 1, ptr(dev(x)), ptr(out), ptr(idx), None, T,
+                                       stream()) == 0, abi.last_error()
+        ref, ridx, _ = small_oracle.moe(1, x)
+        got = host(out, np.uint16)
+        assert np.array_equal(host(idx, np.int32), ridx)
+        if mode == abi.TS_MODE_EXACT:
+            assert ulp_diff(got, ref).max() <= 1 and (got == ref).mean() > 0.99
+        else:
+            e = np.abs(f16(got) - f16(ref))
+            assert e.max() <= 1e-2 * np.abs(f16(ref)).max(), e.max()
+            assert np.sqrt((e ** 2).mean() / (f16(ref) ** 2).mean()) < 3e-3
+    finally:
+        small_backend.set_mode(0)
+
+
+def test_forward_exact_mode_matches_reference(small_backend, small_oracle):
+    """Every GEMM and the attention in the reference order on CUDA cores:
+    logits equal the reference's except for ulp-level expf effects."""
+    ids = rng(3).integers(0, 4096, size=203).astype(np.int32)
+    small_backend.set_mode(1)
+    try:
+        got = small_backend.forward(ids, np.ones_like(ids, dtype=np.uint8)).as_2d()
+    finally:
+        small_backend.set_mode(0)
+    ref = small_oracle.forward(ids)
+    assert np.abs(got - ref).max() <= 4e-3
+    assert (got == ref).mean() > 0.98
+
+
+def test_forward_fast_small(small_backend, small_oracle):
+    ids = rng(4).integers(0, 4096, size=300).astype(np.int32)
+    got = small_backend.forward(ids, np.ones_like(ids, dtype=np.uint8)).as_2d()
+    ref = small_oracle.forward(ids)
+    assert np.abs(got - ref).max() <= LOGIT_TOL
+
+
+def test_forward_mask_and_oob_ids(small_backend, small_oracle):
+    ids = rng(5).integers(0, 4096, size=150).astype(np.int32)
+    ids[[3, 77]] = [-5, 4096]  # out-of-vocab ids embed as zero rows
+    mask = np.ones(150, np.uint8)
+    mask[135:] = 0
+    got = small_backend.forward(ids, mask).as_2d()
+    ref = small_oracle.forward(ids, mask)
+    assert np.abs(got - ref).max() <= LOGIT_TOL
+
+
+def test_forward_packed_equals_separate(small_backend):
+    r = rng(6)
+    chunks = [r.integers(0, 4096, size=n).astype(np.int32) for n in (1, 17, 129, 300, 8, 256)]
+    packed = small_backend.forward_packed(chunks)
+    for c, p in zip(chunks, packed):
+        single = small_backend.forward(c, np.ones_like(c, dtype=np.uint8))
+        assert np.array_equal(single.data, p.data)
+
+
+def test_forward_rejects_bad_input(small_backend):
+    from textsift_b200 import TextsiftCudaError
+    with pytest.raises(ValueError):
+        small_backend.forward([1, 2, 3], [1, 1])
+    with pytest.raises(TextsiftCudaError):
+        small_backend.forward(np.zeros(5000, np.int32), np.ones(5000, np.uint8))  # > max_seq_len
+    assert small_backend.forward([], []).sequence_length == 0
+
+
+def test_full_model_config0_logits(oracle, cuda_lib):
+    """the full 8-layer, 128-expert, vocab-200064 model at
+    1 x 512 tokens, seeded q4f16 weights (uint4 U{0..15}, scales U[1e-3,1e-2],
+    zero point 8, norms 1, biases and sinks 0)."""
+    from textsift_b200 import PF_CONFIG, CudaBackend, make_weights
+    w = make_weights(PF_CONFIG, seed=0)
+    ids = rng(7).integers(0, PF_CONFIG["vocab"], size=512).astype(np.int32)
+    b = CudaBackend(w, PF_CONFIG, max_tokens=4096, max_seq_len=2048)
+    b.warmup()
+    try:
+        got = b.forward(ids, np.ones(512, np.uint8)).as_2d()
+    finally:
+        b.dispose()
+    ref = oracle.OracleModel(PF_CONFIG, w).forward(ids, n_threads=1)
+    err = np.abs(got - ref).max()
+    assert err <= LOGIT_TOL, err
+    top2 = np.sort(ref, axis=1)[:, -2:]
+    margin = top2[:, 1] - top2[:, 0]
+    flips = np.argmax(got, 1) != np.argmax(ref, 1)
+    assert not np.any(flips & (margin > 2 * LOGIT_TOL)), (flips.sum(), margin[flips])

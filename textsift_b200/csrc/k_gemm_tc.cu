@@ -1,0 +1,459 @@
+// k_gemm_tc.cu — MatMulNBits (uint4, block 32, fp16 scale, uint4 zero point)
+// as a tcgen05 tensor-core GEMM for sm_100a.
+//
+// Reference semantics: packages/textsift/src/zig/wasm_exports.zig:560-766
+// (matmulInt4BlockImpl) computes y = x . dequant(W)^T + bias with
+// dequant(W)[n,k] = (q - zp) * scale.  Here the dequantised value is formed
+// exactly as fp16((q - zp) * s) (bit-identical to the reference helper
+// fp16(float(q - zp) * float(s)) for every normal scale) inside shared
+// memory, and the product runs on the 5th-generation tensor core with f32
+// accumulation in TMEM.  Activations enter as fp16.
+//
+// CTA = 128 output rows x BN output columns, 8 warps:
+//   warp 0      producer: TMA tile of A (128 x 64 fp16, 128B swizzle) and one
+//               bulk copy of the packed weight blob per 64-wide K chunk
+//   warp 1      MMA issuer: 4 x tcgen05.mma (K=16) per chunk, commit frees the
+//               stage; a final commit publishes the accumulator
+//   warp 2      TMEM allocator
+//   warps 4..7  dequantise each stage's int4 blob into the swizzled fp16 B
+//               tile, then run the epilogue (tcgen05.ld -> bias -> fused op ->
+//               global stores); warp 4+i owns TMEM lanes 32i..32i+31
+// All waits are bounded (ts_common.cuh) and set the device error flag.
+#include "ts_common.cuh"
+#include "ts_kernels.h"
+
+#include <cstring>
+#include <mutex>
+
+namespace ts {
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN == 256 ? 3 : 4;
+  static constexpr uint32_t A_BYTES = 128 * 128;            // 128 rows x 64 fp16
+  static constexpr uint32_t B_BYTES = BN * 128;             // BN rows x 64 fp16
+  static constexpr uint32_t RAW_BYTES = BN * 37;            // packed blob
+  static constexpr uint32_t RAW_STRIDE = (RAW_BYTES + 1023) & ~1023u;
+  static constexpr uint32_t OFF_B = STAGES * A_BYTES;
+  static constexpr uint32_t OFF_RAW = OFF_B + STAGES * B_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_RAW + STAGES * RAW_STRIDE;
+  static constexpr uint32_t NUM_BARS = 3 * STAGES + 1;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+  static constexpr uint32_t TMEM_COLS = 256;
+};
+
+// Bounded wait that also gives up as soon as another role aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_dev_err(err, kDevErrWaitTimeout);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
+
+// The reference's RoPE on one (a, b) fp16 pair: three fp16 roundings per
+// output (wasm_exports.zig:1488-1498).
+__device__ __forceinline__ void rope_pair_ref(uint16_t& a16, uint16_t& b16, uint16_t c16, uint16_t s16) {
+  float c = f16_ref_to_f32(c16), s = f16_ref_to_f32(s16);
+  float a = f16_ref_to_f32(a16), b = f16_ref_to_f32(b16);
+  float ac = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(a, c)));
+  float bs = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(b, s)));
+  float bc = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(b, c)));
+  float as = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(a, s)));
+  a16 = f32_to_f16_ref(__fsub_rn(ac, bs));
+  b16 = f32_to_f16_ref(__fadd_rn(bc, as));
+}
+
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t grow, uint32_t ncol0,
+                                                    const uint16_t* bias, const uint32_t (&v)[32]) {
+  float acc[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    uint32_t n = ncol0 + j;
+    float b = n < a.N ? f16_ref_to_f32(bias[n]) : 0.0f;
+    acc[j] = __fadd_rn(__uint_as_float(v[j]), b);
+  }
+  const bool full = ncol0 + 32 <= a.N;
+  if constexpr (EPI == kEpiF16) {
+    uint16_t* o = reinterpret_cast<uint16_t*>(a.out0) + (size_t)grow * a.ld0 + ncol0;
+    if (full) {
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) w[j] = pack_h2(f32_to_f16_ref(acc[2 * j]), f32_to_f16_ref(acc[2 * j + 1]));
+      uint4* o4 = reinterpret_cast<uint4*>(o);
+#pragma unroll
+      for (int q = 0; q < 4; q++) o4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    } else {
+      for (int j = 0; j < 32; j++)
+        if (ncol0 + j < a.N) o[j] = f32_to_f16_ref(acc[j]);
+    }
+  } else if constexpr (EPI == kEpiF32) {
+    float* o = reinterpret_cast<float*>(a.out0) + (size_t)grow * a.ld0 + ncol0;
+    if (full) {
+      float4* o4 = reinterpret_cast<float4*>(o);
+#pragma unroll
+      for (int q = 0; q < 8; q++) o4[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+    } else {
+      for (int j = 0; j < 32; j++)
+        if (ncol0 + j < a.N) o[j] = acc[j];
+    }
+  } else if constexpr (EPI == kEpiQkvRope) {
+    // Columns [0,q_cols) are Q, [q_cols, q_cols+k_cols) K, the rest V.  Every
+    // 32-column chunk lies inside one 64-wide head of one region.
+    uint16_t h[32];
+#pragma unroll
+    for (int j = 0; j < 32; j++) h[j] = f32_to_f16_ref(acc[j]);
+    uint16_t* o;
+    if (ncol0 < a.q_cols + a.k_cols) {
+      const int p0 = (int)(ncol0 & 63u) >> 1;
+      const size_t trow = (size_t)a.pos[grow] * 32;
+      const uint16_t* cr = a.rope_cos + trow + p0;
+      const uint16_t* sr = a.rope_sin + trow + p0;
+#pragma unroll
+      for (int p = 0; p < 16; p++) rope_pair_ref(h[2 * p], h[2 * p + 1], cr[p], sr[p]);
+      if (ncol0 < a.q_cols)
+        o = reinterpret_cast<uint16_t*>(a.out0) + (size_t)grow * a.ld0 + ncol0;
+      else
+        o = reinterpret_cast<uint16_t*>(a.out1) + (size_t)grow * a.ld1 + (ncol0 - a.q_cols);
+    } else {
+      o = reinterpret_cast<uint16_t*>(a.out2) + (size_t)grow * a.ld2 + (ncol0 - a.q_cols - a.k_cols);
+    }
+    uint4* o4 = reinterpret_cast<uint4*>(o);
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      o4[q] = make_uint4(pack_h2(h[8 * q], h[8 * q + 1]), pack_h2(h[8 * q + 2], h[8 * q + 3]),
+                         pack_h2(h[8 * q + 4], h[8 * q + 5]), pack_h2(h[8 * q + 6], h[8 * q + 7]));
+  } else if constexpr (EPI == kEpiSwiglu) {
+    // gate = even column, up = odd column (wasm_exports.zig:855-903).
+    uint16_t* o = reinterpret_cast<uint16_t*>(a.out0) + (size_t)grow * a.ld0 + (ncol0 >> 1);
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      float g0 = swiglu_ref(acc[4 * j], acc[4 * j + 1]);
+      float g1 = swiglu_ref(acc[4 * j + 2], acc[4 * j + 3]);
+      w[j] = pack_h2(__half_as_ushort(__float2half_rn(g0)), __half_as_ushort(__float2half_rn(g1)));
+    }
+    if (full) {
+      uint4* o4 = reinterpret_cast<uint4*>(o);
+      o4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      o4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      for (int j = 0; j < 8; j++) {
+        if (ncol0 + 4 * j + 1 < a.N) o[2 * j] = (uint16_t)(w[j] & 0xffff);
+        if (ncol0 + 4 * j + 3 < a.N) o[2 * j + 1] = (uint16_t)(w[j] >> 16);
+      }
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(256, 1)
+    gemm_w4_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs args) {
+  using C = GemmCfg<BN>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::OFF_B;
+  uint8_t* sR = smem + C::OFF_RAW;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* bready = bars + 2 * S;
+  uint64_t* accum = bars + 3 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  // ---- tile selection (dense or grouped) ----
+  uint32_t expert = args.dense_expert, row0, row_end;
+  if (args.tiles) {
+    if ((int)blockIdx.y >= *args.n_tiles) return;
+    const int4 t = args.tiles[blockIdx.y];
+    expert = (uint32_t)t.x;
+    row0 = (uint32_t)t.y;
+    row_end = (uint32_t)t.z;
+  } else {
+    row0 = blockIdx.y * 128u;
+    row_end = min(args.M, row0 + 128u);
+  }
+  const uint32_t n_tile = blockIdx.x;
+  const uint32_t n0 = n_tile * BN;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&bready[s], 128);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t n_kc = args.n_kc;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint8_t* wb = args.wblob + (size_t)expert * args.expert_stride + (size_t)n_tile * n_kc * C::RAW_BYTES;
+      for (uint32_t kc = 0; kc < n_kc; kc++) {
+        const int s = kc % S;
+        const uint32_t ph = (kc / S) & 1u;
+        if (!wait_or_abort(&empty[s], ph ^ 1u, args.err, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::RAW_BYTES);
+        tma_load_2d(sA + s * C::A_BYTES, &tmap_a, (int32_t)(kc * kChunkK), (int32_t)row0, &full[s]);
+        bulk_g2s(sR + s * C::RAW_STRIDE, wb + (size_t)kc * C::RAW_BYTES, C::RAW_BYTES, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16_f32(128, BN);
+      bool ok = true;
+      for (uint32_t kc = 0; kc < n_kc && ok; kc++) {
+        const int s = kc % S;
+        const uint32_t ph = (kc / S) & 1u;
+        ok = wait_or_abort(&full[s], ph, args.err, abort_flag) && wait_or_abort(&bready[s], ph, args.err, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
+        const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+          tc_mma_f16(tmem_base, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
+                     (kc | (uint32_t)k) != 0u);
+        tc_commit(&empty[s]);
+      }
+      if (ok) tc_commit(accum);
+    }
+  } else if (warp >= 4) {
+    const int t = threadIdx.x - 128;  // 0..127
+    // ---- dequantise: one (or two) B rows per thread per stage ----
+    bool ok = true;
+    for (uint32_t kc = 0; kc < n_kc; kc++) {
+      const int s = kc % S;
+      const uint32_t ph = (kc / S) & 1u;
+      if (!wait_or_abort(&full[s], ph, args.err, abort_flag)) { ok = false; break; }
+      const uint8_t* raw = sR + s * C::RAW_STRIDE;
+      uint8_t* bdst = sB + s * C::B_BYTES;
+#pragma unroll
+      for (int rr = 0; rr < BN / 128; rr++) {
+        const int r = t + rr * 128;
+        const uint4 h0 = *reinterpret_cast<const uint4*>(raw + r * 16);
+        const uint4 h1 = *reinterpret_cast<const uint4*>(raw + BN * 16 + r * 16);
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + BN * 32 + r * 4);
+        const uint32_t z = raw[BN * 36 + r];
+        const uint32_t s0 = (sc & 0xffffu) * 0x00010001u, s1 = (sc >> 16) * 0x00010001u;
+        const uint32_t z0 = (0x6400u | (z & 15u)) * 0x00010001u, z1 = (0x6400u | (z >> 4)) * 0x00010001u;
+        const uint32_t wds[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          const uint32_t w = wds[c];
+          const uint32_t sz = c < 4 ? s0 : s1, zz = c < 4 ? z0 : z1;
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const uint32_t bits = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+            __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&bits), *reinterpret_cast<const __half2*>(&zz));
+            __half2 d = __hmul2(q, *reinterpret_cast<const __half2*>(&sz));
+            o[j] = *reinterpret_cast<uint32_t*>(&d);
+          }
+          *reinterpret_cast<uint4*>(bdst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bready[s]);
+    }
+    // ---- epilogue ----
+    if (ok && wait_or_abort(accum, 0, args.err, abort_flag)) {
+      tc_fence_after();
+      const uint32_t grow = row0 + (uint32_t)t;
+      const bool row_ok = grow < row_end;
+      const uint32_t lane_base = (uint32_t)(warp - 4) * 32u;
+      const uint16_t* bias = args.bias + (size_t)expert * args.N;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + (uint32_t)c0, v);
+        tmem_ld_wait();
+        if (row_ok && n0 + c0 < args.N) gemm_epilogue_chunk<EPI>(args, grow, n0 + c0, bias, v);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+// One thread per tile row: gathers the row's 64 K elements of one chunk from
+// the reference layout and writes them in blob layout (see ts_kernels.h).
+__global__ void w4_repack_kernel(const uint8_t* __restrict__ int4, const uint16_t* __restrict__ scales,
+                                 const uint8_t* __restrict__ zp, uint32_t N, uint32_t K, uint32_t BN,
+                                 uint32_t n_tiles, uint32_t n_kc, uint8_t* __restrict__ dst) {
+  const uint32_t r = threadIdx.x + blockIdx.x * blockDim.x;
+  const uint32_t kc = blockIdx.y, nt = blockIdx.z % n_tiles, e = blockIdx.z / n_tiles;
+  if (r >= BN) return;
+  const uint32_t nb = K / 32, zs = (nb + 1) / 2;
+  const uint32_t n = nt * BN + r;
+  const size_t erow = (size_t)e * N;  // first row of this expert
+  uint8_t* b = dst + (((size_t)e * n_tiles + nt) * n_kc + kc) * w4_blob_bytes(BN);
+  uint32_t words[8];
+  for (int w = 0; w < 8; w++) {
+    uint32_t word = 0;
+    for (int j = 0; j < 8; j++) {
+      const uint32_t k = kc * kChunkK + 8 * w + j;
+      uint32_t q = 8;  // padding: (8 - 8) * 0 = 0
+      if (n < N && k < K) {
+        const uint8_t byte = int4[(erow + n) * (K / 2) + k / 2];
+        q = (k & 1) ? (byte >> 4) & 15u : byte & 15u;
+      }
+      word |= q << ((j & 1) ? 16 + 4 * (j >> 1) : 4 * (j >> 1));
+    }
+    words[w] = word;
+  }
+  uint16_t sc[2] = {0, 0};
+  uint32_t zb = 0x88;
+  for (int hh = 0; hh < 2; hh++) {
+    const uint32_t blk = 2 * kc + hh;
+    if (n < N && blk < nb) {
+      sc[hh] = scales[(erow + n) * nb + blk];
+      uint32_t zv = 0;  // a missing zero-point tensor means zp = 0 (wasm_exports.zig:580)
+      if (zp) {
+        const uint8_t byte = zp[(erow + n) * zs + (blk >> 1)];
+        zv = (blk & 1) ? (byte >> 4) & 15u : byte & 15u;
+      }
+      zb = hh ? ((zb & 0x0Fu) | (zv << 4)) : ((zb & 0xF0u) | zv);
+    }
+  }
+  uint32_t* w0 = reinterpret_cast<uint32_t*>(b + r * 16);
+  uint32_t* w1 = reinterpret_cast<uint32_t*>(b + BN * 16 + r * 16);
+  for (int i = 0; i < 4; i++) { w0[i] = words[i]; w1[i] = words[4 + i]; }
+  *reinterpret_cast<uint32_t*>(b + BN * 32 + r * 4) = (uint32_t)sc[0] | ((uint32_t)sc[1] << 16);
+  b[BN * 36 + r] = (uint8_t)zb;
+}
+
+// Counts fp16 scales that are neither zero nor a finite normal number.  The
+// tensor-core dequantisation is bit-exact with the reference for all others.
+__global__ void count_bad_scales_kernel(const uint16_t* __restrict__ s, size_t n, int* __restrict__ bad) {
+  int c = 0;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t e = (s[i] >> 10) & 31u, m = s[i] & 0x3ffu;
+    c += (e == 31u) || (e == 0u && m != 0u);
+  }
+  if (c) atomicAdd(bad, c);
+}
+
+cudaError_t launch_w4_repack(const uint8_t* int4, const uint16_t* scales, const uint8_t* zp, uint32_t E, uint32_t N,
+                             uint32_t K, uint32_t BN, uint8_t* dst, cudaStream_t st) {
+  const uint32_t n_tiles = (N + BN - 1) / BN, n_kc = (K + kChunkK - 1) / kChunkK;
+  dim3 grid((BN + 127) / 128, n_kc, E * n_tiles);
+  w4_repack_kernel<<<grid, 128, 0, st>>>(int4, scales, zp, N, K, BN, n_tiles, n_kc, dst);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_count_bad_scales(const uint16_t* s, size_t n, int* bad, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  size_t g = (n + 255) / 256;
+  count_bad_scales_kernel<<<(unsigned)(g > 2048 ? 2048 : g), 256, 0, st>>>(s, n, bad);
+  return cudaGetLastError();
+}
+
+typedef CUresult (*PFN_tmapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                        const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                        CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                        CUtensorMapFloatOOBfill);
+
+static PFN_tmapEncodeTiled get_encode_fn() {
+  static PFN_tmapEncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_tmapEncodeTiled>(p);
+  });
+  return fn;
+}
+
+bool make_act_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K) {
+  PFN_tmapEncodeTiled enc = get_encode_fn();
+  if (!enc || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15u) || ((K * 2) & 15u)) return false;
+  cuuint64_t gdim[2] = {K, rows};
+  cuuint64_t gstride[1] = {K * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+static cudaError_t launch_one(const CUtensorMap& tmap, const GemmArgs& args, uint32_t n_tiles, uint32_t grid_m,
+                              cudaStream_t st) {
+  using C = GemmCfg<BN>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_w4_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  dim3 grid(n_tiles, grid_m);
+  gemm_w4_tc_kernel<BN, EPI><<<grid, 256, C::SMEM_BYTES, st>>>(tmap, args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_w4_tc(const W4Tiles& w, const CUtensorMap& tmap_a, GemmArgs args, int epi, uint32_t grid_m,
+                              cudaStream_t st) {
+  if (grid_m == 0) return cudaSuccess;
+  args.wblob = w.blobs;
+  args.expert_stride = w.expert_stride;
+  args.bias = w.bias;
+  args.N = w.N;
+  args.n_kc = w.n_kc;
+  if (w.BN == 128) {
+    switch (epi) {
+      case kEpiF16: return launch_one<128, kEpiF16>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiF32: return launch_one<128, kEpiF32>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiQkvRope: return launch_one<128, kEpiQkvRope>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiSwiglu: return launch_one<128, kEpiSwiglu>(tmap_a, args, w.n_tiles, grid_m, st);
+    }
+  } else if (w.BN == 256) {
+    switch (epi) {
+      case kEpiF16: return launch_one<256, kEpiF16>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiF32: return launch_one<256, kEpiF32>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiSwiglu: return launch_one<256, kEpiSwiglu>(tmap_a, args, w.n_tiles, grid_m, st);
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ts

@@ -1,0 +1,947 @@
+// runtime.cu — libtextsift_cuda: model handle, weight upload, forward pass and
+// the extern "C" ABI declared in include/textsift_cuda.h.
+//
+// Forward composition follows packages/textsift/src/browser/inference/
+// model.ts:50-105, block.ts:213-302, attention.ts:347-517 and
+// expert.ts:104-212; tensor names follow loadOnnxWeights
+// (browser/backends/wasm.ts:358-446).  All weights and activations stay in
+// HBM; a forward over many packed sequences is one pass of ~15 launches per
+// layer with no host round trip.
+#include "textsift_cuda.h"
+#include "ts_common.cuh"
+#include "ts_kernels.h"
+#include "ts_simt.h"
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define TS_CUDA_TRY(expr)                                                                    \
+  do {                                                                                       \
+    cudaError_t e_ = (expr);                                                                 \
+    if (e_ != cudaSuccess) return fail(TS_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+// math.zig:54-82 on the host (RoPE tables are built once per handle).
+uint16_t host_f32_to_f16_ref(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  uint32_t sign = (u >> 16) & 0x8000u, exp32 = (u >> 23) & 0xffu, mant = u & 0x7fffffu;
+  if (exp32 == 0xffu) return (uint16_t)(sign | 0x7c00u | (mant ? 0x200u : 0u));
+  int e16 = (int)exp32 - 112;
+  if (e16 >= 0x1f) return (uint16_t)(sign | 0x7c00u);
+  if (e16 <= 0) {
+    if (e16 < -10) return (uint16_t)sign;
+    uint32_t shift = (uint32_t)(14 - e16);
+    return (uint16_t)(sign | (((mant | 0x800000u) + (1u << (shift - 1))) >> shift));
+  }
+  uint32_t m10 = (mant + 0xfffu + ((mant >> 13) & 1u)) >> 13;
+  uint32_t ue = (uint32_t)e16;
+  if (m10 >= 0x400u) {
+    m10 = 0;
+    if (++ue >= 0x1fu) return (uint16_t)(sign | 0x7c00u);
+  }
+  return (uint16_t)(sign | (ue << 10) | m10);
+}
+
+// YaRN cos/sin tables (browser/inference/rope.ts:27-144): the reference's
+// published method in double precision, stored through f32 into fp16 with
+// +0 for zero (rope.ts:78-104).
+void build_rope_tables(const ts_cuda_cfg& c, uint32_t rows, std::vector<uint16_t>& cs, std::vector<uint16_t>& sn) {
+  const uint32_t hd = c.head_dim, half = hd / 2;
+  std::vector<float> extrap(half), interp(half), inv(half);
+  for (uint32_t i = 0; i < half; i++) {
+    double pf = std::pow(c.rope_theta, (double)(2 * i) / (double)hd);
+    extrap[i] = (float)(1.0 / pf);
+    interp[i] = (float)(1.0 / (c.rope_factor * pf));
+  }
+  const double two_pi = 2.0 * 3.141592653589793;
+  auto corr = [&](double rot) {
+    return ((double)hd * std::log(c.rope_original_max_pos / (rot * two_pi))) / (2.0 * std::log(c.rope_theta));
+  };
+  double lo = corr(c.rope_beta_fast), hi = corr(c.rope_beta_slow);
+  if (lo < 0) lo = 0;
+  if (hi > (double)(hd - 1)) hi = (double)(hd - 1);
+  const double rmax = hi == lo ? lo + 0.001 : hi;
+  for (uint32_t i = 0; i < half; i++) {
+    double lin = ((double)i - lo) / (rmax - lo);
+    double ramp = lin < 0 ? 0 : (lin > 1 ? 1 : lin);
+    double ef = 1.0 - ramp;
+    double a = (double)interp[i] * (1.0 - ef);
+    double b = (double)extrap[i] * ef;
+    inv[i] = (float)(a + b);
+  }
+  const double att = c.rope_factor <= 1.0 ? 1.0 : 0.1 * std::log(c.rope_factor) + 1.0;
+  cs.resize((size_t)rows * half);
+  sn.resize((size_t)rows * half);
+  for (uint32_t t = 0; t < rows; t++)
+    for (uint32_t i = 0; i < half; i++) {
+      double ang = (double)t * (double)inv[i];
+      double cv = std::cos(ang) * att, sv = std::sin(ang) * att;
+      cs[(size_t)t * half + i] = cv == 0.0 ? 0 : host_f32_to_f16_ref((float)cv);
+      sn[(size_t)t * half + i] = sv == 0.0 ? 0 : host_f32_to_f16_ref((float)sv);
+    }
+}
+
+template <typename T>
+struct DevArr {
+  T* p = nullptr;
+  size_t n = 0;
+  DevArr() = default;
+  DevArr(const DevArr&) = delete;
+  DevArr& operator=(const DevArr&) = delete;
+  ~DevArr() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  cudaError_t alloc(size_t count) {
+    if (count <= n && p) return cudaSuccess;
+    release();
+    n = count;
+    return cudaMalloc(&p, count * sizeof(T) + 16);
+  }
+};
+
+// One MatMulNBits weight (E experts of [N, K]) in reference layout plus its
+// tensor-core tiles.
+struct W4Dev {
+  uint32_t E = 1, N = 0, K = 0, BN = 128;
+  DevArr<uint8_t> int4, zp, blobs;
+  DevArr<uint16_t> scales, bias;
+  bool has_zp = true;
+  ts::W4Tiles tiles() const {
+    ts::W4Tiles t;
+    t.blobs = blobs.p;
+    t.N = N;
+    t.K = K;
+    t.BN = BN;
+    t.n_tiles = (N + BN - 1) / BN;
+    t.n_kc = (K + ts::kChunkK - 1) / ts::kChunkK;
+    t.expert_stride = (uint64_t)t.n_tiles * t.n_kc * ts::w4_blob_bytes(BN);
+    t.bias = bias.p;
+    return t;
+  }
+  ts::ExactArgs exact() const {
+    ts::ExactArgs a;
+    a.w_int4 = int4.p;
+    a.w_scales = scales.p;
+    a.w_zp = has_zp ? zp.p : nullptr;
+    a.bias = bias.p;
+    a.w_int4_estride = (uint64_t)N * (K / 2);
+    a.w_scales_estride = (uint64_t)N * (K / 32);
+    a.w_zp_estride = (uint64_t)N * ((K / 32 + 1) / 2);
+    a.bias_estride = N;
+    a.N = N;
+    a.K = K;
+    return a;
+  }
+};
+
+// Upload host arrays (reference layout) into a W4Dev and build its tiles.
+int w4_upload(W4Dev& w, const uint8_t* int4, const uint16_t* scales, const uint8_t* zp, const uint16_t* bias,
+              uint32_t E, uint32_t N, uint32_t K, uint32_t BN, bool tc, int* d_bad, cudaStream_t st) {
+  if (K % 32 != 0 || N == 0 || K == 0 || E == 0) return fail(TS_ERR_UNSUPPORTED, "int4 weight: K=%u must be a multiple of 32", K);
+  w.E = E; w.N = N; w.K = K; w.BN = BN;
+  const size_t n4 = (size_t)E * N * (K / 2), ns = (size_t)E * N * (K / 32), nz = (size_t)E * N * ((K / 32 + 1) / 2);
+  TS_CUDA_TRY(w.int4.alloc(n4));
+  TS_CUDA_TRY(w.scales.alloc(ns));
+  TS_CUDA_TRY(w.bias.alloc((size_t)E * N));
+  TS_CUDA_TRY(cudaMemcpyAsync(w.int4.p, int4, n4, cudaMemcpyHostToDevice, st));
+  TS_CUDA_TRY(cudaMemcpyAsync(w.scales.p, scales, ns * 2, cudaMemcpyHostToDevice, st));
+  if (bias) TS_CUDA_TRY(cudaMemcpyAsync(w.bias.p, bias, (size_t)E * N * 2, cudaMemcpyHostToDevice, st));
+  else TS_CUDA_TRY(cudaMemsetAsync(w.bias.p, 0, (size_t)E * N * 2, st));
+  w.has_zp = zp != nullptr;
+  if (zp) {
+    TS_CUDA_TRY(w.zp.alloc(nz));
+    TS_CUDA_TRY(cudaMemcpyAsync(w.zp.p, zp, nz, cudaMemcpyHostToDevice, st));
+  }
+  if (tc) {
+    ts::W4Tiles t = w.tiles();
+    TS_CUDA_TRY(w.blobs.alloc((size_t)E * t.expert_stride));
+    TS_CUDA_TRY(ts::launch_w4_repack(w.int4.p, w.scales.p, w.has_zp ? w.zp.p : nullptr, E, N, K, BN, w.blobs.p, st));
+    if (d_bad) TS_CUDA_TRY(ts::launch_count_bad_scales(w.scales.p, ns, d_bad, st));
+  }
+  return TS_OK;
+}
+
+struct HostTensor {
+  std::vector<uint8_t> bytes;
+  int32_t dtype = 0;
+};
+
+struct LayerDev {
+  DevArr<uint16_t> ln1, ln2;
+  DevArr<float> sinks;
+  W4Dev qkv, o, router, gate_up, down;
+};
+
+struct Workspace {
+  uint32_t cap = 0;  // tokens
+  DevArr<int32_t> ids;
+  DevArr<uint8_t> mask;
+  DevArr<uint32_t> offs;
+  DevArr<int> pos, sstart, slen;
+  DevArr<uint16_t> x0, x1, xn16, q, k, v, attn, o16, res2, qkv16;
+  DevArr<float> n32, hf32, rlogits, rw;
+  DevArr<int32_t> ridx;
+  DevArr<int> counts, seg_end, perm_tok, route_pos, n_tiles;
+  DevArr<int4> tiles;
+  DevArr<uint16_t> aperm16, glu16;
+  DevArr<float> aperm32, gu32, glu32, down32;
+  DevArr<float> logits;
+  bool exact_ready = false;
+};
+
+}  // namespace
+
+struct ts_cuda {
+  ts_cuda_cfg cfg{};
+  cudaStream_t stream = nullptr;
+  std::string name;
+  std::map<std::string, HostTensor> staged;
+  bool finalized = false;
+  // device weights
+  DevArr<uint8_t> embed_int4, embed_zp;
+  DevArr<uint16_t> embed_scales, final_norm;
+  W4Dev score;
+  std::vector<std::unique_ptr<LayerDev>> layers;
+  DevArr<uint16_t> rope_cos, rope_sin;
+  DevArr<int> err;
+  Workspace ws;
+  // pinned staging for the host-pointer forward
+  uint8_t* pin = nullptr;
+  size_t pin_bytes = 0;
+};
+
+struct ts_cuda_w4 {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  W4Dev w;
+  DevArr<int> err;
+};
+
+namespace {
+
+struct DevGuard {
+  int prev = -1;
+  explicit DevGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DevGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// Expected byte size and dtype of each named tensor (loader layout).
+bool expected_tensor(const ts_cuda_cfg& c, const std::string& name, size_t& bytes, int32_t& dtype) {
+  const size_t D = c.d_model, V = c.vocab, C = c.n_classes, E = c.n_experts, F = c.d_ff;
+  const size_t Hq = c.n_heads, Hkv = c.n_kv_heads, hd = c.head_dim;
+  auto i4 = [&](const std::string& f, size_t Ex, size_t N, size_t K) {
+    if (f == "int4") { bytes = Ex * N * K / 2; dtype = TS_DTYPE_U8; return true; }
+    if (f == "scales") { bytes = Ex * N * (K / 32) * 2; dtype = TS_DTYPE_F16; return true; }
+    if (f == "zp") { bytes = Ex * N * ((K / 32 + 1) / 2); dtype = TS_DTYPE_U8; return true; }
+    if (f == "bias") { bytes = Ex * N * 2; dtype = TS_DTYPE_F16; return true; }
+    return false;
+  };
+  if (name == "embed.int4") { bytes = V * D / 2; dtype = TS_DTYPE_U8; return true; }
+  if (name == "embed.scales") { bytes = V * (D / 32) * 2; dtype = TS_DTYPE_F16; return true; }
+  if (name == "embed.zp") { bytes = V * ((D / 32 + 1) / 2); dtype = TS_DTYPE_U8; return true; }
+  if (name == "final_norm") { bytes = D * 2; dtype = TS_DTYPE_F16; return true; }
+  if (name.rfind("score.", 0) == 0) return i4(name.substr(6), 1, C, D);
+  unsigned L = 0;
+  int n = 0;
+  if (sscanf(name.c_str(), "layers.%u.%n", &L, &n) == 1 && n > 0 && L < c.n_layers) {
+    std::string r = name.substr((size_t)n);
+    if (r == "input_layernorm" || r == "post_attention_layernorm") { bytes = D * 2; dtype = TS_DTYPE_F16; return true; }
+    if (r == "attn.sinks") { bytes = Hq * 4; dtype = TS_DTYPE_F32; return true; }
+    if (r.rfind("attn.q_proj.", 0) == 0) return i4(r.substr(12), 1, Hq * hd, D);
+    if (r.rfind("attn.k_proj.", 0) == 0) return i4(r.substr(12), 1, Hkv * hd, D);
+    if (r.rfind("attn.v_proj.", 0) == 0) return i4(r.substr(12), 1, Hkv * hd, D);
+    if (r.rfind("attn.o_proj.", 0) == 0) return i4(r.substr(12), 1, D, Hq * hd);
+    if (r.rfind("router.", 0) == 0) return i4(r.substr(7), 1, E, D);
+    if (r.rfind("experts.gate_up.", 0) == 0) return i4(r.substr(16), E, 2 * F, D);
+    if (r.rfind("experts.down.", 0) == 0) return i4(r.substr(13), E, D, F);
+  }
+  return false;
+}
+
+std::vector<std::string> required_names(const ts_cuda_cfg& c) {
+  std::vector<std::string> v = {"embed.int4", "embed.scales", "embed.zp", "final_norm",
+                                "score.int4", "score.scales", "score.zp"};
+  const char* i4f[] = {"int4", "scales", "zp", "bias"};
+  for (uint32_t L = 0; L < c.n_layers; L++) {
+    std::string p = "layers." + std::to_string(L) + ".";
+    v.push_back(p + "input_layernorm");
+    v.push_back(p + "post_attention_layernorm");
+    v.push_back(p + "attn.sinks");
+    for (const char* pr : {"attn.q_proj.", "attn.k_proj.", "attn.v_proj.", "attn.o_proj.", "router.",
+                           "experts.gate_up.", "experts.down."})
+      for (const char* f : i4f) v.push_back(p + pr + f);
+  }
+  return v;
+}
+
+const uint8_t* staged_ptr(ts_cuda* h, const std::string& n) {
+  auto it = h->staged.find(n);
+  return it == h->staged.end() ? nullptr : it->second.bytes.data();
+}
+
+int ensure_workspace(ts_cuda* h, bool exact) {
+  Workspace& w = h->ws;
+  const ts_cuda_cfg& c = h->cfg;
+  const size_t T = c.max_tokens, D = c.d_model, K = c.top_k, E = c.n_experts, F = c.d_ff;
+  const size_t Q = (size_t)c.n_heads * c.head_dim, KV = (size_t)c.n_kv_heads * c.head_dim;
+  const size_t R = T * K;
+  if (w.cap == 0) {
+    TS_CUDA_TRY(w.ids.alloc(T));
+    TS_CUDA_TRY(w.mask.alloc(T));
+    TS_CUDA_TRY(w.offs.alloc(T + 1));
+    TS_CUDA_TRY(w.pos.alloc(T));
+    TS_CUDA_TRY(w.sstart.alloc(T));
+    TS_CUDA_TRY(w.slen.alloc(T));
+    TS_CUDA_TRY(w.x0.alloc(T * D));
+    TS_CUDA_TRY(w.x1.alloc(T * D));
+    TS_CUDA_TRY(w.xn16.alloc(T * D));
+    TS_CUDA_TRY(w.q.alloc(T * Q));
+    TS_CUDA_TRY(w.k.alloc(T * KV));
+    TS_CUDA_TRY(w.v.alloc(T * KV));
+    TS_CUDA_TRY(w.attn.alloc(T * Q));
+    TS_CUDA_TRY(w.o16.alloc(T * D));
+    TS_CUDA_TRY(w.res2.alloc(T * D));
+    TS_CUDA_TRY(w.n32.alloc(T * D));
+    TS_CUDA_TRY(w.rlogits.alloc(T * E));
+    TS_CUDA_TRY(w.ridx.alloc(R));
+    TS_CUDA_TRY(w.rw.alloc(R));
+    TS_CUDA_TRY(w.counts.alloc(E));
+    TS_CUDA_TRY(w.seg_end.alloc(E));
+    TS_CUDA_TRY(w.perm_tok.alloc(R));
+    TS_CUDA_TRY(w.route_pos.alloc(R));
+    TS_CUDA_TRY(w.n_tiles.alloc(1));
+    TS_CUDA_TRY(w.tiles.alloc(R / 128 + E + 1));
+    TS_CUDA_TRY(w.aperm16.alloc(R * D));
+    TS_CUDA_TRY(w.glu16.alloc(R * F));
+    TS_CUDA_TRY(w.down32.alloc(R * D));
+    TS_CUDA_TRY(w.logits.alloc(T * c.n_classes));
+    w.cap = (uint32_t)T;
+  }
+  if (exact && !w.exact_ready) {
+    TS_CUDA_TRY(w.hf32.alloc(T * D));
+    TS_CUDA_TRY(w.qkv16.alloc(T * (Q + 2 * KV)));
+    TS_CUDA_TRY(w.aperm32.alloc(R * D));
+    TS_CUDA_TRY(w.gu32.alloc(R * 2 * F));
+    TS_CUDA_TRY(w.glu32.alloc(R * F));
+    w.exact_ready = true;
+  }
+  return TS_OK;
+}
+
+#define TS_K(expr)                                                                                   \
+  do {                                                                                               \
+    cudaError_t e_ = (expr);                                                                         \
+    if (e_ != cudaSuccess) return fail(TS_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_));        \
+  } while (0)
+
+// The MoE half of a block: routing from n32 (f32), experts, deterministic
+// combine.  res == nullptr writes the bare MoE output fp16(K * sum w e(x)).
+int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, const uint16_t* res, uint16_t* out,
+             uint32_t T, const int* rloc, const int* rlen, bool exact, cudaStream_t st) {
+  Workspace& w = h->ws;
+  const ts_cuda_cfg& c = h->cfg;
+  const uint32_t D = c.d_model, K = c.top_k, E = c.n_experts, F = c.d_ff;
+  const uint32_t R = T * K;
+  const uint32_t grid_tiles = R / 128 + E + 1;
+  // router logits in the reference order, then top-k
+  ts::ExactArgs ra = L.router.exact();
+  ra.x = n32; ra.ldx = D; ra.M = T; ra.rloc = rloc; ra.rlen = rlen; ra.out = w.rlogits.p; ra.ldo = E;
+  TS_K(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
+  TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, T, E, K, st));
+  TS_K(ts::launch_moe_permute(w.ridx.p, T, K, E, w.counts.p, w.perm_tok.p, w.route_pos.p, w.tiles.p, w.n_tiles.p,
+                              w.seg_end.p, st));
+  if (!exact) {
+    TS_K(ts::launch_gather_rows(xn16, w.aperm16.p, w.perm_tok.p, nullptr, R, D * 2, st));
+    CUtensorMap ta, tg;
+    if (!ts::make_act_tmap(&ta, w.aperm16.p, R, D) || !ts::make_act_tmap(&tg, w.glu16.p, R, F))
+      return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the expert operands");
+    ts::GemmArgs g;
+    g.tiles = w.tiles.p; g.n_tiles = w.n_tiles.p; g.err = h->err.p;
+    g.out0 = w.glu16.p; g.ld0 = F;
+    TS_K(ts::launch_gemm_w4_tc(L.gate_up.tiles(), ta, g, ts::kEpiSwiglu, grid_tiles, st));
+    ts::GemmArgs g2;
+    g2.tiles = w.tiles.p; g2.n_tiles = w.n_tiles.p; g2.err = h->err.p;
+    g2.out0 = w.down32.p; g2.ld0 = D;
+    TS_K(ts::launch_gemm_w4_tc(L.down.tiles(), tg, g2, ts::kEpiF32, grid_tiles, st));
+  } else {
+    TS_K(ts::launch_gather_rows(n32, w.aperm32.p, w.perm_tok.p, nullptr, R, D * 4, st));
+    ts::ExactArgs ga = L.gate_up.exact();
+    ga.x = w.aperm32.p; ga.ldx = D; ga.tiles = w.tiles.p; ga.n_tiles = w.n_tiles.p; ga.seg_end = w.seg_end.p;
+    ga.out = w.gu32.p; ga.ldo = 2 * F;
+    TS_K(ts::launch_matmul_exact(ga, true, ts::kOutF32, grid_tiles, st));
+    TS_K(ts::launch_swiglu_exact(w.gu32.p, w.glu32.p, nullptr, R, F, st));
+    ts::ExactArgs da = L.down.exact();
+    da.x = w.glu32.p; da.ldx = F; da.tiles = w.tiles.p; da.n_tiles = w.n_tiles.p; da.seg_end = w.seg_end.p;
+    da.out = w.down32.p; da.ldo = D;
+    TS_K(ts::launch_matmul_exact(da, true, ts::kOutF32, grid_tiles, st));
+  }
+  TS_K(ts::launch_moe_combine(w.down32.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E, st));
+  return TS_OK;
+}
+
+int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, const uint32_t* offs, uint32_t n_seqs,
+                   float* d_logits, cudaStream_t st) {
+  if (!h->finalized) return fail(TS_ERR_STATE, "ts_cuda_finalize has not succeeded");
+  const ts_cuda_cfg& c = h->cfg;
+  if (!offs || n_seqs == 0) return fail(TS_ERR_ARG, "seq_offsets must hold n_seqs + 1 >= 2 entries");
+  if (offs[0] != 0) return fail(TS_ERR_ARG, "seq_offsets[0] must be 0");
+  for (uint32_t s = 0; s < n_seqs; s++) {
+    if (offs[s + 1] <= offs[s]) return fail(TS_ERR_ARG, "sequence %u is empty or offsets decrease", s);
+    if (offs[s + 1] - offs[s] > c.max_seq_len)
+      return fail(TS_ERR_UNSUPPORTED, "sequence %u has %u tokens > max_seq_len %u", s, offs[s + 1] - offs[s], c.max_seq_len);
+  }
+  const uint32_t T = offs[n_seqs];
+  if (T > c.max_tokens) return fail(TS_ERR_UNSUPPORTED, "%u tokens > max_tokens %u", T, c.max_tokens);
+  const bool exact = c.mode == TS_MODE_EXACT;
+  int rc = ensure_workspace(h, exact);
+  if (rc) return rc;
+  Workspace& w = h->ws;
+  const uint32_t D = c.d_model, Q = c.n_heads * c.head_dim, KV = c.n_kv_heads * c.head_dim;
+
+  TS_K(cudaMemcpyAsync(w.offs.p, offs, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st));
+  TS_K(ts::launch_seq_info(w.offs.p, n_seqs, T, w.pos.p, w.sstart.p, w.slen.p, st));
+  TS_K(ts::launch_embed(h->embed_int4.p, h->embed_scales.p, h->embed_zp.p, d_ids, w.x0.p, T, c.vocab, D, st));
+
+  CUtensorMap t_xn, t_attn;
+  if (!exact) {
+    if (!ts::make_act_tmap(&t_xn, w.xn16.p, T, D) || !ts::make_act_tmap(&t_attn, w.attn.p, T, Q))
+      return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation operands");
+  }
+  ts::AttnArgs aa;
+  aa.q = w.q.p; aa.k = w.k.p; aa.v = w.v.p; aa.mask = d_mask; aa.out = w.attn.p;
+  aa.sstart = w.sstart.p; aa.slen = w.slen.p; aa.T = T; aa.Hq = c.n_heads; aa.Hkv = c.n_kv_heads;
+  aa.hd = c.head_dim; aa.window = c.window; aa.err = h->err.p;
+
+  uint16_t* src = w.x0.p;
+  uint16_t* dst = w.x1.p;
+  const uint32_t mt = (T + 127) / 128;
+  for (uint32_t li = 0; li < c.n_layers; li++) {
+    LayerDev& L = *h->layers[li];
+    aa.sinks = L.sinks.p;
+    if (!exact) {
+      TS_K(ts::launch_rmsnorm(src, L.ln1.p, nullptr, w.xn16.p, T, D, c.eps, st));
+      ts::GemmArgs g;
+      g.M = T; g.err = h->err.p;
+      g.out0 = w.q.p; g.ld0 = Q; g.out1 = w.k.p; g.ld1 = KV; g.out2 = w.v.p; g.ld2 = KV;
+      g.q_cols = Q; g.k_cols = KV; g.pos = w.pos.p; g.rope_cos = h->rope_cos.p; g.rope_sin = h->rope_sin.p;
+      TS_K(ts::launch_gemm_w4_tc(L.qkv.tiles(), t_xn, g, ts::kEpiQkvRope, mt, st));
+      TS_K(ts::launch_attention_tc(aa, st));
+      ts::GemmArgs go;
+      go.M = T; go.err = h->err.p; go.out0 = w.o16.p; go.ld0 = D;
+      TS_K(ts::launch_gemm_w4_tc(L.o.tiles(), t_attn, go, ts::kEpiF16, mt, st));
+      TS_K(ts::launch_add_rmsnorm(src, w.o16.p, L.ln2.p, w.res2.p, w.n32.p, w.xn16.p, T, D, c.eps, st));
+    } else {
+      TS_K(ts::launch_rmsnorm(src, L.ln1.p, w.hf32.p, nullptr, T, D, c.eps, st));
+      ts::ExactArgs qa = L.qkv.exact();
+      qa.x = w.hf32.p; qa.ldx = D; qa.M = T; qa.rloc = w.pos.p; qa.rlen = w.slen.p; qa.out = w.qkv16.p;
+      qa.ldo = Q + 2 * KV;
+      TS_K(ts::launch_matmul_exact(qa, true, ts::kOutF16, mt, st));
+      TS_K(ts::launch_split_rope(w.qkv16.p, w.q.p, w.k.p, w.v.p, w.pos.p, h->rope_cos.p, h->rope_sin.p, T, Q, KV, KV,
+                                 c.head_dim, st));
+      TS_K(ts::launch_attention_exact(aa, st));
+      ts::ExactArgs oa = L.o.exact();
+      oa.x = w.attn.p; oa.ldx = Q; oa.M = T; oa.rloc = w.pos.p; oa.rlen = w.slen.p; oa.out = w.o16.p; oa.ldo = D;
+      TS_K(ts::launch_matmul_exact(oa, false, ts::kOutF16, mt, st));
+      TS_K(ts::launch_add_rmsnorm(src, w.o16.p, L.ln2.p, w.res2.p, w.n32.p, nullptr, T, D, c.eps, st));
+    }
+    rc = moe_half(h, L, w.n32.p, w.xn16.p, w.res2.p, dst, T, w.pos.p, w.slen.p, exact, st);
+    if (rc) return rc;
+    std::swap(src, dst);
+  }
+  TS_K(ts::launch_rmsnorm(src, h->final_norm.p, w.n32.p, nullptr, T, D, c.eps, st));
+  ts::ExactArgs sa = h->score.exact();
+  sa.x = w.n32.p; sa.ldx = D; sa.M = T; sa.rloc = w.pos.p; sa.rlen = w.slen.p; sa.out = d_logits; sa.ldo = c.n_classes;
+  TS_K(ts::launch_matmul_exact(sa, true, ts::kOutF16Widen, mt, st));
+  return TS_OK;
+}
+
+int check_dev_err(int* d_err, cudaStream_t st) {
+  int herr = 0;
+  TS_CUDA_TRY(cudaMemcpyAsync(&herr, d_err, 4, cudaMemcpyDeviceToHost, st));
+  TS_CUDA_TRY(cudaStreamSynchronize(st));
+  if (herr != 0) {
+    cudaMemsetAsync(d_err, 0, 4, st);
+    cudaStreamSynchronize(st);
+    return fail(TS_ERR_DEVICE, "device error flag %d (%s)", herr,
+                herr == ts::kDevErrWaitTimeout ? "bounded wait timed out" : "bad index");
+  }
+  return TS_OK;
+}
+
+}  // namespace
+
+// =============================================================================
+// extern "C" ABI
+// =============================================================================
+extern "C" {
+
+int ts_cuda_abi_version(void) { return TS_CUDA_ABI_VERSION; }
+
+const char* ts_cuda_last_error(void) { return g_err.c_str(); }
+
+void ts_cuda_default_cfg(ts_cuda_cfg* c) {
+  if (!c) return;
+  memset(c, 0, sizeof *c);
+  c->device = 0;
+  c->vocab = 200064;
+  c->d_model = 640;
+  c->n_layers = 8;
+  c->n_heads = 14;
+  c->n_kv_heads = 2;
+  c->head_dim = 64;
+  c->window = 128;
+  c->d_ff = 640;
+  c->n_experts = 128;
+  c->top_k = 4;
+  c->n_classes = 33;
+  c->eps = 1e-5f;
+  c->rope_theta = 150000.0;
+  c->rope_factor = 32.0;
+  c->rope_original_max_pos = 4096.0;
+  c->rope_beta_fast = 32.0;
+  c->rope_beta_slow = 1.0;
+  c->max_tokens = 65536;
+  c->max_seq_len = 8192;
+  c->mode = TS_MODE_FAST;
+}
+
+ts_cuda_t* ts_cuda_create(const ts_cuda_cfg* cfg, char* err, size_t err_cap) {
+  auto bad = [&](const char* msg) -> ts_cuda_t* {
+    g_err = msg;
+    if (err && err_cap) snprintf(err, err_cap, "%s", msg);
+    return nullptr;
+  };
+  if (!cfg) return bad("ts_cuda_create: cfg is NULL");
+  const ts_cuda_cfg& c = *cfg;
+  if (c.d_model % 64 || c.d_ff % 64 || (c.n_heads * c.head_dim) % 64 || c.head_dim != 64 || c.n_kv_heads == 0 ||
+      c.n_heads % c.n_kv_heads || c.n_heads / c.n_kv_heads > 7 || c.top_k == 0 || c.top_k > 8 ||
+      c.top_k > c.n_experts || c.n_classes == 0 || c.max_tokens == 0 || c.max_seq_len == 0 || c.n_layers == 0)
+    return bad("ts_cuda_create: unsupported configuration (head_dim must be 64, d_model/d_ff multiples of 64, "
+               "GQA group <= 7, top_k <= 8)");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || c.device < 0 || c.device >= ndev)
+    return bad("ts_cuda_create: no such CUDA device");
+  DevGuard g(c.device);
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, c.device) != cudaSuccess) return bad("ts_cuda_create: cudaGetDeviceProperties failed");
+  if (prop.major != 10) return bad("ts_cuda_create: this library is built for sm_100a (B200); device is not compute capability 10.x");
+  auto* h = new ts_cuda();
+  h->cfg = c;
+  h->name = prop.name;
+  if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess || h->err.alloc(1) != cudaSuccess ||
+      cudaMemset(h->err.p, 0, 4) != cudaSuccess) {
+    delete h;
+    return bad("ts_cuda_create: CUDA initialisation failed");
+  }
+  return h;
+}
+
+int ts_cuda_load_tensor(ts_cuda_t* h, const char* name, int32_t dtype, const int64_t* shape, int32_t ndim,
+                        const void* data, size_t nbytes) {
+  if (!h || !name || !data) return fail(TS_ERR_ARG, "ts_cuda_load_tensor: null argument");
+  size_t want = 0;
+  int32_t wdt = 0;
+  if (!expected_tensor(h->cfg, name, want, wdt)) return fail(TS_ERR_ARG, "unknown tensor name \"%s\"", name);
+  if (dtype != wdt) return fail(TS_ERR_ARG, "tensor \"%s\": dtype %d, expected %d", name, dtype, wdt);
+  if (nbytes != want) return fail(TS_ERR_ARG, "tensor \"%s\": %zu bytes, expected %zu", name, nbytes, want);
+  if (shape && ndim > 0) {
+    int64_t prod = 1;
+    for (int i = 0; i < ndim; i++) prod *= shape[i];
+    const int64_t esz = dtype == TS_DTYPE_U8 ? 1 : (dtype == TS_DTYPE_F16 ? 2 : 4);
+    if (prod * esz != (int64_t)nbytes && !(dtype == TS_DTYPE_U8 && prod / 2 == (int64_t)nbytes))
+      return fail(TS_ERR_ARG, "tensor \"%s\": shape does not match %zu bytes", name, nbytes);
+  }
+  HostTensor& t = h->staged[name];
+  t.bytes.assign((const uint8_t*)data, (const uint8_t*)data + nbytes);
+  t.dtype = dtype;
+  h->finalized = false;
+  return TS_OK;
+}
+
+int ts_cuda_finalize(ts_cuda_t* h) {
+  if (!h) return fail(TS_ERR_ARG, "ts_cuda_finalize: null handle");
+  if (h->finalized) return TS_OK;
+  const ts_cuda_cfg& c = h->cfg;
+  for (const std::string& n : required_names(c))
+    if (!h->staged.count(n)) return fail(TS_ERR_STATE, "tensor \"%s\" has not been loaded", n.c_str());
+  DevGuard g(c.device);
+  cudaStream_t st = h->stream;
+  const uint32_t D = c.d_model, E = c.n_experts, F = c.d_ff, Q = c.n_heads * c.head_dim, KV = c.n_kv_heads * c.head_dim;
+  auto up = [&](auto& arr, const std::string& n) -> int {
+    const HostTensor& t = h->staged[n];
+    using Tp = typename std::remove_reference<decltype(*arr.p)>::type;
+    TS_CUDA_TRY(arr.alloc(t.bytes.size() / sizeof(Tp)));
+    TS_CUDA_TRY(cudaMemcpyAsync(arr.p, t.bytes.data(), t.bytes.size(), cudaMemcpyHostToDevice, st));
+    return TS_OK;
+  };
+  int rc;
+  if ((rc = up(h->embed_int4, "embed.int4")) || (rc = up(h->embed_scales, "embed.scales")) ||
+      (rc = up(h->embed_zp, "embed.zp")) || (rc = up(h->final_norm, "final_norm")))
+    return rc;
+  auto p8 = [&](const std::string& n) { return staged_ptr(h, n); };
+  auto p16 = [&](const std::string& n) { return reinterpret_cast<const uint16_t*>(staged_ptr(h, n)); };
+  rc = w4_upload(h->score, p8("score.int4"), p16("score.scales"), p8("score.zp"),
+                 h->staged.count("score.bias") ? p16("score.bias") : nullptr, 1, c.n_classes, D, 128, false, nullptr, st);
+  if (rc) return rc;
+  DevArr<int> bad;
+  TS_CUDA_TRY(bad.alloc(1));
+  TS_CUDA_TRY(cudaMemsetAsync(bad.p, 0, 4, st));
+  h->layers.clear();
+  for (uint32_t li = 0; li < c.n_layers; li++) {
+    auto L = std::make_unique<LayerDev>();
+    const std::string p = "layers." + std::to_string(li) + ".";
+    if ((rc = up(L->ln1, p + "input_layernorm")) || (rc = up(L->ln2, p + "post_attention_layernorm")) ||
+        (rc = up(L->sinks, p + "attn.sinks")))
+      return rc;
+    // Q, K and V fused along N into one [Q + 2 KV, D] weight.
+    std::vector<uint8_t> i4, zp;
+    std::vector<uint16_t> sc, bs;
+    for (const char* pr : {"attn.q_proj.", "attn.k_proj.", "attn.v_proj."}) {
+      const HostTensor& a = h->staged[p + pr + "int4"];
+      const HostTensor& s = h->staged[p + pr + "scales"];
+      const HostTensor& z = h->staged[p + pr + "zp"];
+      const HostTensor& b = h->staged[p + pr + "bias"];
+      i4.insert(i4.end(), a.bytes.begin(), a.bytes.end());
+      zp.insert(zp.end(), z.bytes.begin(), z.bytes.end());
+      const uint16_t* sp = reinterpret_cast<const uint16_t*>(s.bytes.data());
+      sc.insert(sc.end(), sp, sp + s.bytes.size() / 2);
+      const uint16_t* bp = reinterpret_cast<const uint16_t*>(b.bytes.data());
+      bs.insert(bs.end(), bp, bp + b.bytes.size() / 2);
+    }
+    if ((rc = w4_upload(L->qkv, i4.data(), sc.data(), zp.data(), bs.data(), 1, Q + 2 * KV, D, 128, true, bad.p, st)))
+      return rc;
+    TS_CUDA_TRY(cudaStreamSynchronize(st));  // host vectors above are released at scope end
+    if ((rc = w4_upload(L->o, p8(p + "attn.o_proj.int4"), p16(p + "attn.o_proj.scales"), p8(p + "attn.o_proj.zp"),
+                        p16(p + "attn.o_proj.bias"), 1, D, Q, 128, true, bad.p, st)) ||
+        (rc = w4_upload(L->router, p8(p + "router.int4"), p16(p + "router.scales"), p8(p + "router.zp"),
+                        p16(p + "router.bias"), 1, E, D, 128, false, nullptr, st)) ||
+        (rc = w4_upload(L->gate_up, p8(p + "experts.gate_up.int4"), p16(p + "experts.gate_up.scales"),
+                        p8(p + "experts.gate_up.zp"), p16(p + "experts.gate_up.bias"), E, 2 * F, D, 256, true, bad.p,
+                        st)) ||
+        (rc = w4_upload(L->down, p8(p + "experts.down.int4"), p16(p + "experts.down.scales"),
+                        p8(p + "experts.down.zp"), p16(p + "experts.down.bias"), E, D, F, 128, true, bad.p, st)))
+      return rc;
+    h->layers.push_back(std::move(L));
+  }
+  std::vector<uint16_t> cs, sn;
+  build_rope_tables(c, c.max_seq_len, cs, sn);
+  TS_CUDA_TRY(h->rope_cos.alloc(cs.size()));
+  TS_CUDA_TRY(h->rope_sin.alloc(sn.size()));
+  TS_CUDA_TRY(cudaMemcpyAsync(h->rope_cos.p, cs.data(), cs.size() * 2, cudaMemcpyHostToDevice, st));
+  TS_CUDA_TRY(cudaMemcpyAsync(h->rope_sin.p, sn.data(), sn.size() * 2, cudaMemcpyHostToDevice, st));
+  int nbad = 0;
+  TS_CUDA_TRY(cudaMemcpyAsync(&nbad, bad.p, 4, cudaMemcpyDeviceToHost, st));
+  TS_CUDA_TRY(cudaStreamSynchronize(st));
+  if (nbad)
+    return fail(TS_ERR_UNSUPPORTED,
+                "%d fp16 weight scales are subnormal, inf or NaN; the tensor-core path reproduces the reference "
+                "dequantisation only for zero or normal scales",
+                nbad);
+  if ((rc = ensure_workspace(h, c.mode == TS_MODE_EXACT))) return rc;
+  const size_t pin_need = (size_t)c.max_tokens * (4 + 1 + 4 * c.n_classes) + 64;
+  if (!h->pin) {
+    TS_CUDA_TRY(cudaMallocHost(&h->pin, pin_need));
+    h->pin_bytes = pin_need;
+  }
+  h->staged.clear();
+  h->finalized = true;
+  return TS_OK;
+}
+
+int ts_cuda_set_mode(ts_cuda_t* h, int32_t mode) {
+  if (!h || (mode != TS_MODE_FAST && mode != TS_MODE_EXACT)) return fail(TS_ERR_ARG, "ts_cuda_set_mode: bad mode");
+  h->cfg.mode = mode;
+  return TS_OK;
+}
+
+int ts_cuda_forward_packed_device(ts_cuda_t* h, const int32_t* d_ids, const uint8_t* d_mask,
+                                  const uint32_t* seq_offsets, uint32_t n_seqs, float* d_logits, void* stream) {
+  if (!h || !d_ids || !d_logits) return fail(TS_ERR_ARG, "ts_cuda_forward_packed_device: null argument");
+  DevGuard g(h->cfg.device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+  return forward_device(h, d_ids, d_mask, seq_offsets, n_seqs, d_logits, st);
+}
+
+int ts_cuda_forward_packed(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
+                           uint32_t n_seqs, float* logits) {
+  if (!h || !ids || !logits || !seq_offsets || n_seqs == 0) return fail(TS_ERR_ARG, "ts_cuda_forward_packed: null argument");
+  if (!h->finalized) return fail(TS_ERR_STATE, "ts_cuda_finalize has not succeeded");
+  const uint32_t T = seq_offsets[n_seqs];
+  if (T > h->cfg.max_tokens) return fail(TS_ERR_UNSUPPORTED, "%u tokens > max_tokens %u", T, h->cfg.max_tokens);
+  DevGuard g(h->cfg.device);
+  cudaStream_t st = h->stream;
+  Workspace& w = h->ws;
+  const size_t C = h->cfg.n_classes;
+  // host -> pinned -> device (the pinned block is only reused after the sync below)
+  uint8_t* pin_ids = h->pin;
+  uint8_t* pin_mask = h->pin + (size_t)h->cfg.max_tokens * 4;
+  uint8_t* pin_log = pin_mask + h->cfg.max_tokens + 16 - ((uintptr_t)(pin_mask + h->cfg.max_tokens) & 15u);
+  memcpy(pin_ids, ids, (size_t)T * 4);
+  TS_CUDA_TRY(cudaMemcpyAsync(w.ids.p, pin_ids, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+  const uint8_t* dmask = nullptr;
+  if (mask) {
+    memcpy(pin_mask, mask, T);
+    TS_CUDA_TRY(cudaMemcpyAsync(w.mask.p, pin_mask, T, cudaMemcpyHostToDevice, st));
+    dmask = w.mask.p;
+  }
+  int rc = forward_device(h, w.ids.p, dmask, seq_offsets, n_seqs, w.logits.p, st);
+  if (rc) {
+    cudaStreamSynchronize(st);
+    return rc;
+  }
+  TS_CUDA_TRY(cudaMemcpyAsync(pin_log, w.logits.p, (size_t)T * C * 4, cudaMemcpyDeviceToHost, st));
+  rc = check_dev_err(h->err.p, st);
+  if (rc) return rc;
+  memcpy(logits, pin_log, (size_t)T * C * 4);
+  return TS_OK;
+}
+
+int ts_cuda_forward(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, uint32_t T, float* logits) {
+  if (T == 0) return TS_OK;
+  const uint32_t offs[2] = {0, T};
+  return ts_cuda_forward_packed(h, ids, mask, offs, 1, logits);
+}
+
+int ts_cuda_check(ts_cuda_t* h, void* stream) {
+  if (!h) return fail(TS_ERR_ARG, "ts_cuda_check: null handle");
+  DevGuard g(h->cfg.device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(TS_ERR_CUDA, "stream: %s", cudaGetErrorString(e));
+  return check_dev_err(h->err.p, st);
+}
+
+const char* ts_cuda_device_name(ts_cuda_t* h) { return h ? h->name.c_str() : ""; }
+
+void ts_cuda_destroy(ts_cuda_t* h) {
+  if (!h) return;
+  {
+    DevGuard g(h->cfg.device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    if (h->pin) cudaFreeHost(h->pin);
+    h->layers.clear();
+    if (h->stream) cudaStreamDestroy(h->stream);
+    h->stream = nullptr;
+  }
+  DevGuard g(h->cfg.device);
+  delete h;
+}
+
+// ---------------------------------------------------------------------------
+// per-op entry points
+// ---------------------------------------------------------------------------
+int ts_cuda_op_gather_bq(const uint8_t* d_int4, const uint16_t* d_scales, const uint8_t* d_zp, const int32_t* d_ids,
+                         uint16_t* d_out, uint32_t T, uint32_t V, uint32_t D, void* stream) {
+  if (!d_int4 || !d_scales || !d_zp || !d_ids || !d_out) return fail(TS_ERR_ARG, "ts_cuda_op_gather_bq: null pointer");
+  if (D % 32) return fail(TS_ERR_UNSUPPORTED, "D=%u must be a multiple of 32", D);
+  TS_CUDA_TRY(ts::launch_embed(d_int4, d_scales, d_zp, d_ids, d_out, T, V, D, (cudaStream_t)stream));
+  return TS_OK;
+}
+
+int ts_cuda_op_rmsnorm(const uint16_t* d_a, const uint16_t* d_b, const uint16_t* d_gamma, uint16_t* d_sum, float* d_out,
+                       uint32_t T, uint32_t D, float eps, void* stream) {
+  if (!d_a || !d_gamma || !d_out || (d_b && !d_sum)) return fail(TS_ERR_ARG, "ts_cuda_op_rmsnorm: null pointer");
+  if (D > 8192) return fail(TS_ERR_UNSUPPORTED, "D=%u too large", D);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (d_b) TS_CUDA_TRY(ts::launch_add_rmsnorm(d_a, d_b, d_gamma, d_sum, d_out, nullptr, T, D, eps, st));
+  else TS_CUDA_TRY(ts::launch_rmsnorm(d_a, d_gamma, d_out, nullptr, T, D, eps, st));
+  return TS_OK;
+}
+
+ts_cuda_w4_t* ts_cuda_w4_create(int32_t device, const uint8_t* int4, const uint16_t* scales, const uint8_t* zp,
+                                const uint16_t* bias, uint32_t E, uint32_t N, uint32_t K, char* err, size_t err_cap) {
+  auto bad = [&](const char* msg) -> ts_cuda_w4_t* {
+    g_err = msg;
+    if (err && err_cap) snprintf(err, err_cap, "%s", msg);
+    return nullptr;
+  };
+  if (!int4 || !scales || E == 0 || N == 0 || K == 0) return bad("ts_cuda_w4_create: bad argument");
+  DevGuard g(device);
+  auto* w = new ts_cuda_w4_t();
+  w->device = device;
+  if (cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess || w->err.alloc(1) != cudaSuccess ||
+      cudaMemset(w->err.p, 0, 4) != cudaSuccess) {
+    delete w;
+    return bad("ts_cuda_w4_create: CUDA initialisation failed");
+  }
+  DevArr<int> nb;
+  const uint32_t BN = N >= 256 && N % 256 == 0 ? 256 : 128;
+  int rc = nb.alloc(1) == cudaSuccess && cudaMemsetAsync(nb.p, 0, 4, w->stream) == cudaSuccess
+               ? w4_upload(w->w, int4, scales, zp, bias, E, N, K, BN, true, nb.p, w->stream)
+               : TS_ERR_CUDA;
+  int nbad = 0;
+  if (rc == TS_OK && (cudaMemcpyAsync(&nbad, nb.p, 4, cudaMemcpyDeviceToHost, w->stream) != cudaSuccess ||
+                      cudaStreamSynchronize(w->stream) != cudaSuccess))
+    rc = TS_ERR_CUDA;
+  if (rc != TS_OK || nbad) {
+    std::string m = rc != TS_OK ? g_err : "weight scales must be zero or normal fp16 numbers";
+    if (w->stream) cudaStreamDestroy(w->stream);
+    delete w;
+    return bad(m.c_str());
+  }
+  return w;
+}
+
+void ts_cuda_w4_destroy(ts_cuda_w4_t* w) {
+  if (!w) return;
+  DevGuard g(w->device);
+  if (w->stream) {
+    cudaStreamSynchronize(w->stream);
+    cudaStreamDestroy(w->stream);
+  }
+  delete w;
+}
+
+int ts_cuda_op_dequant(const ts_cuda_w4_t* w, uint32_t expert, uint16_t* d_out, void* stream) {
+  if (!w || !d_out || expert >= w->w.E) return fail(TS_ERR_ARG, "ts_cuda_op_dequant: bad argument");
+  ts::W4Tiles t = w->w.tiles();
+  TS_CUDA_TRY(ts::launch_dequant_tiles(t.blobs + (size_t)expert * t.expert_stride, w->w.N, w->w.K, w->w.BN, t.n_kc,
+                                       d_out, (cudaStream_t)stream));
+  return TS_OK;
+}
+
+int ts_cuda_op_matmul_nbits(const ts_cuda_w4_t* w, uint32_t expert, const void* d_x, int32_t x_dtype, void* d_out,
+                            int32_t out_dtype, uint32_t M, int32_t mode, void* stream) {
+  if (!w || !d_x || !d_out || expert >= w->w.E) return fail(TS_ERR_ARG, "ts_cuda_op_matmul_nbits: bad argument");
+  if (M == 0) return TS_OK;
+  if (out_dtype != TS_DTYPE_F16 && out_dtype != TS_DTYPE_F32) return fail(TS_ERR_ARG, "out_dtype must be F16 or F32");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (mode == TS_MODE_FAST) {
+    if (x_dtype != TS_DTYPE_F16) return fail(TS_ERR_UNSUPPORTED, "the tensor-core path takes fp16 activations");
+    CUtensorMap tm;
+    if (!ts::make_act_tmap(&tm, d_x, M, w->w.K)) return fail(TS_ERR_UNSUPPORTED, "activation tensor map (16-byte alignment)");
+    ts::GemmArgs g;
+    g.M = M; g.dense_expert = expert; g.err = w->err.p; g.out0 = d_out; g.ld0 = w->w.N;
+    TS_CUDA_TRY(ts::launch_gemm_w4_tc(w->w.tiles(), tm, g, out_dtype == TS_DTYPE_F16 ? ts::kEpiF16 : ts::kEpiF32,
+                                      (M + 127) / 128, st));
+    return TS_OK;
+  }
+  if (x_dtype != TS_DTYPE_F16 && x_dtype != TS_DTYPE_F32) return fail(TS_ERR_ARG, "x_dtype must be F16 or F32");
+  ts::ExactArgs a = w->w.exact();
+  a.w_int4 += (size_t)expert * a.w_int4_estride;
+  a.w_scales += (size_t)expert * a.w_scales_estride;
+  if (a.w_zp) a.w_zp += (size_t)expert * a.w_zp_estride;
+  a.bias += (size_t)expert * a.bias_estride;
+  a.x = d_x; a.ldx = w->w.K; a.M = M; a.out = d_out; a.ldo = w->w.N;
+  TS_CUDA_TRY(ts::launch_matmul_exact(a, x_dtype == TS_DTYPE_F32, out_dtype == TS_DTYPE_F16 ? ts::kOutF16 : ts::kOutF32,
+                                      (M + 127) / 128, st));
+  return TS_OK;
+}
+
+int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32_t* d_idx, float* d_w, uint32_t T,
+                           void* stream) {
+  if (!h || !d_x || !d_idx || !d_w) return fail(TS_ERR_ARG, "ts_cuda_op_router_topk: null argument");
+  if (!h->finalized || layer >= h->cfg.n_layers) return fail(TS_ERR_STATE, "handle not finalized or bad layer");
+  if (T > h->cfg.max_tokens) return fail(TS_ERR_UNSUPPORTED, "T > max_tokens");
+  DevGuard g(h->cfg.device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+  int rc = ensure_workspace(h, false);
+  if (rc) return rc;
+  const ts_cuda_cfg& c = h->cfg;
+  ts::ExactArgs ra = h->layers[layer]->router.exact();
+  ra.x = d_x; ra.ldx = c.d_model; ra.M = T; ra.out = h->ws.rlogits.p; ra.ldo = c.n_experts;
+  TS_CUDA_TRY(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
+  TS_CUDA_TRY(ts::launch_router_topk(h->ws.rlogits.p, d_idx, d_w, T, c.n_experts, c.top_k, st));
+  return TS_OK;
+}
+
+int ts_cuda_op_moe(ts_cuda_t* h, uint32_t layer, const float* d_x, uint16_t* d_out, int32_t* d_idx, float* d_w,
+                   uint32_t T, void* stream) {
+  if (!h || !d_x || !d_out) return fail(TS_ERR_ARG, "ts_cuda_op_moe: null argument");
+  if (!h->finalized || layer >= h->cfg.n_layers) return fail(TS_ERR_STATE, "handle not finalized or bad layer");
+  if (T > h->cfg.max_tokens) return fail(TS_ERR_UNSUPPORTED, "T > max_tokens");
+  if (T == 0) return TS_OK;
+  DevGuard g(h->cfg.device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+  const bool exact = h->cfg.mode == TS_MODE_EXACT;
+  int rc = ensure_workspace(h, exact);
+  if (rc) return rc;
+  const ts_cuda_cfg& c = h->cfg;
+  if (!exact) TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, h->ws.xn16.p, (size_t)T * c.d_model, st));
+  rc = moe_half(h, *h->layers[layer], d_x, h->ws.xn16.p, nullptr, d_out, T, nullptr, nullptr, exact, st);
+  if (rc) return rc;
+  if (d_idx) TS_CUDA_TRY(cudaMemcpyAsync(d_idx, h->ws.ridx.p, (size_t)T * c.top_k * 4, cudaMemcpyDeviceToDevice, st));
+  if (d_w) TS_CUDA_TRY(cudaMemcpyAsync(d_w, h->ws.rw.p, (size_t)T * c.top_k * 4, cudaMemcpyDeviceToDevice, st));
+  return TS_OK;
+}
+
+int ts_cuda_op_banded_attention(const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v, const float* d_sinks,
+                                const uint8_t* d_mask, uint16_t* d_out, uint32_t T, uint32_t Hq, uint32_t Hkv,
+                                uint32_t head_dim, uint32_t window, const uint32_t* seq_offsets, uint32_t n_seqs,
+                                int32_t mode, void* stream) {
+  if (!d_q || !d_k || !d_v || !d_sinks || !d_out) return fail(TS_ERR_ARG, "ts_cuda_op_banded_attention: null pointer");
+  if (T == 0) return TS_OK;
+  if (Hkv == 0 || Hq % Hkv) return fail(TS_ERR_ARG, "Hq must be a multiple of Hkv");
+  if (window > 1024) return fail(TS_ERR_UNSUPPORTED, "window %u > 1024", window);
+  cudaStream_t st = (cudaStream_t)stream;
+  // per-token sequence info (a scratch allocation per call: this is a test/benchmark entry point)
+  DevArr<uint32_t> offs;
+  DevArr<int> pos, ss, sl;
+  std::vector<uint32_t> one = {0, T};
+  const uint32_t* ho = seq_offsets ? seq_offsets : one.data();
+  const uint32_t ns = seq_offsets ? n_seqs : 1;
+  if (ns == 0 || ho[0] != 0 || ho[ns] != T) return fail(TS_ERR_ARG, "seq_offsets must run from 0 to T");
+  for (uint32_t s = 0; s < ns; s++)
+    if (ho[s + 1] <= ho[s]) return fail(TS_ERR_ARG, "empty sequence %u", s);
+  TS_CUDA_TRY(offs.alloc(ns + 1));
+  TS_CUDA_TRY(pos.alloc(T));
+  TS_CUDA_TRY(ss.alloc(T));
+  TS_CUDA_TRY(sl.alloc(T));
+  TS_CUDA_TRY(cudaMemcpyAsync(offs.p, ho, (size_t)(ns + 1) * 4, cudaMemcpyHostToDevice, st));
+  TS_CUDA_TRY(ts::launch_seq_info(offs.p, ns, T, pos.p, ss.p, sl.p, st));
+  ts::AttnArgs a;
+  a.q = d_q; a.k = d_k; a.v = d_v; a.sinks = d_sinks; a.mask = d_mask; a.out = d_out;
+  a.sstart = ss.p; a.slen = sl.p; a.T = T; a.Hq = Hq; a.Hkv = Hkv; a.hd = head_dim; a.window = window;
+  if (mode == TS_MODE_FAST) {
+    if (head_dim != 64 || Hq / Hkv > 7) return fail(TS_ERR_UNSUPPORTED, "tensor-core attention needs head_dim 64, group <= 7");
+    TS_CUDA_TRY(ts::launch_attention_tc(a, st));
+  } else {
+    TS_CUDA_TRY(ts::launch_attention_exact(a, st));
+  }
+  TS_CUDA_TRY(cudaStreamSynchronize(st));  // scratch above is freed on return
+  return TS_OK;
+}
+
+int ts_cuda_rope_tables(ts_cuda_t* h, uint32_t rows, uint16_t* cos_out, uint16_t* sin_out) {
+  if (!h || !cos_out || !sin_out) return fail(TS_ERR_ARG, "ts_cuda_rope_tables: null argument");
+  if (!h->finalized) return fail(TS_ERR_STATE, "handle not finalized");
+  if (rows > h->cfg.max_seq_len) return fail(TS_ERR_ARG, "rows > max_seq_len");
+  DevGuard g(h->cfg.device);
+  const size_t n = (size_t)rows * (h->cfg.head_dim / 2) * 2;
+  TS_CUDA_TRY(cudaMemcpy(cos_out, h->rope_cos.p, n, cudaMemcpyDeviceToHost));
+  TS_CUDA_TRY(cudaMemcpy(sin_out, h->rope_sin.p, n, cudaMemcpyDeviceToHost));
+  return TS_OK;
+}
+
+}  // extern "C"

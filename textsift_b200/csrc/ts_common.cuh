@@ -1,0 +1,290 @@
+// ts_common.cuh — shared device helpers for libtextsift_cuda.
+//
+// * fp16 <-> f32 conversions that follow textsift's WASM numerics bit for bit
+//   (packages/textsift/src/zig/math.zig:45-82).  They are used wherever the
+//   reference reads or writes an fp16 activation, bias, scale or table, so
+//   that the CUDA kernels round at exactly the same points.
+// * PTX wrappers for mbarriers, bulk/tensor copies and tcgen05 (sm_100a).
+//   Every wait is bounded: after kWaitLimitNs of %globaltimer the waiting
+//   thread records an error code in a device flag and gives up, so a
+//   programming error can never hang the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace ts {
+
+// ---------------------------------------------------------------------------
+// Reference fp16 conversions (math.zig)
+// ---------------------------------------------------------------------------
+
+// math.zig:45-52: sign<<16 | (rest ? (rest<<13) + (112<<23) : 0).  Subnormal
+// and inf/NaN fp16 inputs decode to the same (non-IEEE) values as the WASM.
+__device__ __forceinline__ float f16_ref_to_f32(uint16_t bits) {
+  uint32_t u = bits;
+  uint32_t sign = (u & 0x8000u) << 16;
+  uint32_t rest = u & 0x7fffu;
+  uint32_t biased = rest == 0 ? 0u : (rest << 13) + (112u << 23);
+  return __uint_as_float(sign | biased);
+}
+
+// math.zig:54-82: RNE for normals, half-up for subnormals, NaN -> 0x7e00|s.
+__device__ __forceinline__ uint16_t f32_to_f16_ref(float f) {
+  uint32_t u = __float_as_uint(f);
+  uint32_t sign = (u >> 16) & 0x8000u;
+  uint32_t exp32 = (u >> 23) & 0xffu;
+  uint32_t mant = u & 0x7fffffu;
+  if (exp32 == 0xffu) return (uint16_t)(sign | 0x7c00u | (mant ? 0x200u : 0u));
+  int e16 = (int)exp32 - 112;
+  if (e16 >= 0x1f) return (uint16_t)(sign | 0x7c00u);
+  if (e16 <= 0) {
+    if (e16 < -10) return (uint16_t)sign;
+    uint32_t shift = (uint32_t)(14 - e16);
+    uint32_t mant24 = mant | 0x800000u;
+    return (uint16_t)(sign | ((mant24 + (1u << (shift - 1))) >> shift));
+  }
+  uint32_t lsb = (mant >> 13) & 1u;
+  uint32_t m10 = (mant + 0xfffu + lsb) >> 13;
+  uint32_t ue = (uint32_t)e16;
+  if (m10 >= 0x400u) {
+    m10 = 0;
+    ue += 1;
+    if (ue >= 0x1fu) return (uint16_t)(sign | 0x7c00u);
+  }
+  return (uint16_t)(sign | (ue << 10) | m10);
+}
+
+// Exact fp16 -> f32 (IEEE, subnormals included): packages/textsift/src/
+// browser/backends/wasm.ts:776-797 widens the final logits this way.
+__device__ __forceinline__ float f16_ieee_to_f32(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+// wasm_exports.zig:812-838, one lane: exp(x) for x <= 0 via 2^(x*log2 e),
+// floor split, 5th-degree Horner polynomial (fused steps), exponent twiddle.
+// This is the reference's own published approximation, restated.
+__device__ __forceinline__ float exp_approx_ref(float x) {
+  const float LOG2_E = 1.44269504088896340736f;
+  float cl = x > -88.0f ? x : -88.0f;
+  float y = __fmul_rn(cl, LOG2_E);
+  float fl = floorf(y);
+  int iv = (int)fl;
+  float frac = __fsub_rn(y, (float)iv);
+  float p = __fmaf_rn(0.001333355f, frac, 0.009679494f);
+  p = __fmaf_rn(p, frac, 0.055053319f);
+  p = __fmaf_rn(p, frac, 0.240226522f);
+  p = __fmaf_rn(p, frac, 0.693154774f);
+  p = __fmaf_rn(p, frac, 1.000000012f);
+  float scale = __uint_as_float((uint32_t)(iv + 127) << 23);
+  return __fmul_rn(p, scale);
+}
+
+// wasm_exports.zig:844-853
+__device__ __forceinline__ float sigmoid_approx_ref(float x) {
+  float mn = x < 0.0f ? x : 0.0f;
+  float mx = x > 0.0f ? x : 0.0f;
+  float e = exp_approx_ref(__fsub_rn(mn, mx));
+  float sig_neg = __fdiv_rn(e, __fadd_rn(1.0f, e));
+  return x >= 0.0f ? __fsub_rn(1.0f, sig_neg) : sig_neg;
+}
+
+// wasm_exports.zig:878-888 (one lane of the 4-lane body): gate<=7, up in
+// [-7,7], (up+1) * gate * sigmoid(1.702*gate), every op rounded separately.
+__device__ __forceinline__ float swiglu_ref(float g, float u) {
+  float gate = g < 7.0f ? g : 7.0f;
+  float up = u < 7.0f ? u : 7.0f;
+  up = up > -7.0f ? up : -7.0f;
+  float sig = sigmoid_approx_ref(__fmul_rn(gate, 1.702f));
+  float glu = __fmul_rn(gate, sig);
+  return __fmul_rn(__fadd_rn(up, 1.0f), glu);
+}
+
+// ---------------------------------------------------------------------------
+// Error flag shared by every kernel (bounded waits, bad indices)
+// ---------------------------------------------------------------------------
+enum DevErr : int {
+  kDevErrNone = 0,
+  kDevErrWaitTimeout = 1,
+  kDevErrBadIndex = 2,
+};
+
+constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // 4 s
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void set_dev_err(int* flag, int code) {
+  if (flag) atomicCAS(flag, 0, code);
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory address / mbarrier helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false (and records kDevErrWaitTimeout) if the phase
+// did not complete within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_dev_err(err, kDevErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 1-D bulk copy global -> shared, completing on an mbarrier (tx bytes).
+// Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 2-D tiled tensor copy global -> shared (no multicast).
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int32_t c0, int32_t c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (5th-gen tensor core, TMEM accumulators)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (fp16 x fp16 -> f32), 1 CTA.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on an mbarrier once all previously issued tcgen05.mma of this
+// thread have completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives
+// row (lane base + i), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand stored with the
+// 128-byte swizzle: rows of 128 B (64 fp16), 8-row atoms 1024 B apart.
+// Fields (sm_100 UMMA descriptor): start>>4 [0,14), LBO>>4 [16,30),
+// SBO>>4 [32,46), version=1 [46,48), base offset [49,52), layout [61,64)
+// with 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(16u >> 4) << 16;    // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;  // SBO: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;             // version
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D f32, A/B fp16, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_f32(uint32_t M, uint32_t N) {
+  return (1u << 4)            // D format: f32
+         | (0u << 7)          // A format: f16
+         | (0u << 10)         // B format: f16
+         | ((N >> 3) << 17)   // N >> 3
+         | ((M >> 4) << 24);  // M >> 4
+}
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+}  // namespace ts

@@ -1,0 +1,78 @@
+// ts_simt.h — launchers of the CUDA-core kernels (internal to the library).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ts {
+
+enum ExactOut : int { kOutF16 = 0, kOutF32 = 1, kOutF16Widen = 2 };
+
+// Arguments of the exact-order int4 matmul.  Weight pointers are the
+// reference layout ([E][N][K/2] nibbles, [E][N][K/32] scales, [E][N][ceil(K/64)]
+// zero points, [E][N] bias), with per-expert strides in elements.
+struct ExactArgs {
+  const void* x = nullptr;
+  uint32_t ldx = 0;
+  const uint8_t* w_int4 = nullptr;
+  const uint16_t* w_scales = nullptr;
+  const uint8_t* w_zp = nullptr;
+  const uint16_t* bias = nullptr;
+  uint64_t w_int4_estride = 0, w_scales_estride = 0, w_zp_estride = 0, bias_estride = 0;
+  uint32_t N = 0, K = 0, M = 0;
+  const int* rloc = nullptr;  // dense: index of each row inside its sequence (null: one sequence of M rows)
+  const int* rlen = nullptr;  // dense: length of each row's sequence
+  const int4* tiles = nullptr;    // grouped: {expert, row0, row_end, seg_start}
+  const int* n_tiles = nullptr;   // grouped: device tile count
+  const int* seg_end = nullptr;   // grouped: end row of each expert segment
+  void* out = nullptr;
+  uint32_t ldo = 0;
+};
+
+cudaError_t launch_seq_info(const uint32_t* offs, uint32_t n_seqs, uint32_t T, int* pos, int* sstart, int* slen,
+                            cudaStream_t st);
+cudaError_t launch_embed(const uint8_t* w, const uint16_t* sc, const uint8_t* zp, const int32_t* ids, uint16_t* out,
+                         uint32_t T, uint32_t V, uint32_t D, cudaStream_t st);
+cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gamma, float* out32, uint16_t* out16, uint32_t T,
+                           uint32_t D, float eps, cudaStream_t st);
+cudaError_t launch_add_rmsnorm(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
+                               float* out32, uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st);
+cudaError_t launch_matmul_exact(const ExactArgs& a, bool x_f32, int out_mode, uint32_t grid_m, cudaStream_t st);
+cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, uint32_t T, uint32_t E, uint32_t K,
+                               cudaStream_t st);
+cudaError_t launch_moe_permute(const int32_t* idx, uint32_t T, uint32_t K, uint32_t E, int* counts, int* perm_tok,
+                               int* route_pos, int4* tiles, int* n_tiles, int* seg_end, cudaStream_t st);
+cudaError_t launch_gather_rows(const void* src, void* dst, const int* perm_tok, const int* n_rows_dev,
+                               uint32_t max_rows, uint32_t row_bytes, cudaStream_t st);
+cudaError_t launch_moe_combine(const float* down, const int32_t* idx, const float* w, const int* route_pos,
+                               const uint16_t* res, uint16_t* out, uint32_t T, uint32_t D, uint32_t K, uint32_t E,
+                               cudaStream_t st);
+cudaError_t launch_swiglu_exact(const float* gu, float* out, const int* n_rows_dev, uint32_t max_rows, uint32_t D,
+                                cudaStream_t st);
+cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uint16_t* v, const int* pos,
+                              const uint16_t* cos_t, const uint16_t* sin_t, uint32_t T, uint32_t qc, uint32_t kc,
+                              uint32_t vc, uint32_t hd, cudaStream_t st);
+cudaError_t launch_f16_to_f32_ref(const uint16_t* src, float* dst, size_t n, cudaStream_t st);
+cudaError_t launch_f32_to_f16(const float* src, uint16_t* dst, size_t n, cudaStream_t st);
+cudaError_t launch_dequant_tiles(const uint8_t* blobs, uint32_t N, uint32_t K, uint32_t BN, uint32_t n_kc,
+                                 uint16_t* out, cudaStream_t st);
+
+// Banded GQA attention with sinks (k_attn.cu).  Sequences are packed along
+// T; sstart/slen give each token's sequence (null: one sequence of T tokens).
+struct AttnArgs {
+  const uint16_t* q = nullptr;   // [T, Hq*hd]
+  const uint16_t* k = nullptr;   // [T, Hkv*hd]
+  const uint16_t* v = nullptr;   // [T, Hkv*hd]
+  const float* sinks = nullptr;  // [Hq]
+  const uint8_t* mask = nullptr; // [T] or null
+  uint16_t* out = nullptr;       // [T, Hq*hd]
+  const int* sstart = nullptr;
+  const int* slen = nullptr;
+  uint32_t T = 0, Hq = 0, Hkv = 0, hd = 0, window = 0;
+  int* err = nullptr;
+};
+cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st);     // mma.sync tensor-core path
+cudaError_t launch_attention_exact(const AttnArgs& a, cudaStream_t st);  // reference-order CUDA-core path
+
+}  // namespace ts
