@@ -101,11 +101,43 @@ int ts_cuda_forward_packed(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask
 int ts_cuda_forward_packed_device(ts_cuda_t* h, const int32_t* d_ids, const uint8_t* d_mask,
                                   const uint32_t* seq_offsets, uint32_t n_seqs, float* d_logits, void* stream);
 
+/* As ts_cuda_forward_packed, also copying each layer's top-k expert indices
+ * to topk_trace (host, i32 [n_layers][T][top_k], descending router logit).
+ * Parity tooling (no counterpart in the reference): it lets a caller
+ * compare routing decisions layer by layer. */
+int ts_cuda_forward_trace(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
+                          uint32_t n_seqs, float* logits, int32_t* topk_trace);
+
 /* Synchronize the handle's work on `stream` and report a device-side error
  * flag (bounded waits that timed out, bad indices) as TS_ERR_DEVICE. */
 int ts_cuda_check(ts_cuda_t* h, void* stream);
 
 const char* ts_cuda_device_name(ts_cuda_t* h);  /* NativeApi.deviceName (native/backend.ts:38) */
+
+/* Phases timed by ts_cuda_profile.  The reference only measures whole
+ * forwards with performance.now() (tests/native/forward-vulkan.js:499-555);
+ * these per-phase CUDA-event timings have no counterpart there. */
+enum {
+  TS_PHASE_EXPERT_GATE_UP = 0, /* grouped gate_up GEMM + SwiGLU epilogue (all experts in exact mode) */
+  TS_PHASE_EXPERT_DOWN = 1,    /* grouped down GEMM */
+  TS_PHASE_QKV = 2,            /* fused Q/K/V GEMM + RoPE epilogue */
+  TS_PHASE_ATTENTION = 3,      /* banded attention */
+  TS_PHASE_O = 4,              /* O projection */
+  TS_PHASE_ROUTER = 5,         /* router logits + top-k + expert permutation */
+  TS_PHASE_OTHER = 6,          /* norms, embedding, gathers, combine, classifier */
+  TS_PHASE_COUNT = 7
+};
+
+/* enable != 0: bracket every phase of later forwards / MoE ops with CUDA
+ * events on the stream they run on; always resets the accumulators and the
+ * kernel-launch counter. */
+int ts_cuda_profile(ts_cuda_t* h, int32_t enable);
+
+/* Accumulated per-phase device milliseconds, phase executions and algorithmic
+ * flops since the last ts_cuda_profile (arrays of TS_PHASE_COUNT, any may be
+ * NULL), plus the number of kernels launched (counted with or without
+ * profiling).  Waits for the recorded events. */
+int ts_cuda_profile_read(ts_cuda_t* h, double* ms, uint64_t* launches, uint64_t* flops, uint64_t* total_launches);
 const char* ts_cuda_last_error(void);
 void ts_cuda_destroy(ts_cuda_t* h);             /* NativeApi.destroyBackend (native/backend.ts:37) */
 

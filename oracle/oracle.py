@@ -68,6 +68,7 @@ def lib():
         L.tso_add_rmsnorm_fp16_to_f32.argtypes = [P, P, P, P, P, U32, U32, F32]
         L.tso_topk_partial_f32.argtypes = [P, P, P, U32, U32, U32]
         L.tso_matmul_int4.argtypes = [I32, I32, P, P, P, P, P, P, U32, U32, U32]
+        L.tso_matmul_int4_scalar.argtypes = [I32, I32, P, P, P, P, P, P, U32, U32, U32]
         L.tso_swiglu_clamp_f32.argtypes = [P, P, U32, U32]
         L.tso_softmax_f32.argtypes = [P, P, U32, U32]
         L.tso_add_fp16.argtypes = [P, P, P, U32]
@@ -87,6 +88,8 @@ def lib():
         L.tso_model_set.restype = I32
         L.tso_model_forward.argtypes = [P, P, P, U32, P, I32, P, P, P]
         L.tso_model_forward.restype = I32
+        L.tso_model_forward_forced.argtypes = [P, P, P, U32, P, I32, P, P, P, P]
+        L.tso_model_forward_forced.restype = I32
         L.tso_moe_forward.argtypes = [P, U32, P, U32, P, P, P, I32]
         L.tso_moe_forward.restype = I32
         _lib = L
@@ -163,7 +166,7 @@ def softmax(x):
     return out
 
 
-def matmul_int4(x, w_int4, w_scales, w_zp, bias, out_f32: bool):
+def matmul_int4(x, w_int4, w_scales, w_zp, bias, out_f32: bool, scalar: bool = False):
     """y = x @ dequant(W).T + bias.  x: float32 (f32 path) or uint16 (fp16 bits)."""
     x_f32 = x.dtype == np.float32
     x = _c(x, np.float32 if x_f32 else np.uint16)
@@ -171,7 +174,8 @@ def matmul_int4(x, w_int4, w_scales, w_zp, bias, out_f32: bool):
     N = w_int4.shape[0]
     out = np.empty((T, N), np.float32 if out_f32 else np.uint16)
     zp = None if w_zp is None else _c(w_zp, np.uint8)
-    lib().tso_matmul_int4(int(x_f32), int(out_f32), _p(x), _p(_c(w_int4, np.uint8)),
+    fn = lib().tso_matmul_int4_scalar if scalar else lib().tso_matmul_int4
+    fn(int(x_f32), int(out_f32), _p(x), _p(_c(w_int4, np.uint8)),
                           _p(_c(w_scales, np.uint16)), _p(zp), _p(_c(bias, np.uint16)), _p(out), T, N, D)
     return out
 
@@ -278,7 +282,10 @@ class OracleModel:
             _lib.tso_model_destroy(h)
             self._h = None
 
-    def forward(self, ids, mask=None, n_threads=1, trace=False):
+    def forward(self, ids, mask=None, n_threads=1, trace=False, forced_topk=None):
+        """Logits f32 [T, n_classes].  trace=True also returns per-layer
+        residual streams, top-k experts and router inputs; forced_topk
+        (i32 [n_layers, T, top_k]) imposes the expert choice of every layer."""
         ids = _c(ids, np.int32); T = ids.size
         c = self.cfg
         logits = np.empty((T, c["n_classes"]), np.float32)
@@ -288,8 +295,11 @@ class OracleModel:
             ht = np.empty((c["n_layers"] + 1, T, c["d_model"]), np.uint16)
             tk = np.empty((c["n_layers"], T, c["top_k"]), np.int32)
             nt = np.empty((c["n_layers"], T, c["d_model"]), np.float32)
-        rc = lib().tso_model_forward(self._h, _p(ids), _p(m), T, _p(logits), n_threads,
-                                     _p(ht), _p(tk), _p(nt))
+        fk = None if forced_topk is None else _c(forced_topk, np.int32)
+        if fk is not None and fk.shape != (c["n_layers"], T, c["top_k"]):
+            raise ValueError("forced_topk must be [n_layers, T, top_k]")
+        rc = lib().tso_model_forward_forced(self._h, _p(ids), _p(m), T, _p(logits), n_threads,
+                                            _p(ht), _p(tk), _p(nt), _p(fk))
         if rc != 0:
             raise RuntimeError(f"tso_model_forward failed: {rc}")
         if trace:

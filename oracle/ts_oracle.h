@@ -51,6 +51,11 @@ void tso_topk_partial_f32(const float* x, int32_t* out_idx, float* out_val,
 void tso_matmul_int4(int x_is_f32, int out_is_f32, const void* x,
                      const uint8_t* w_int4, const uint16_t* w_scales, const uint8_t* w_zp,
                      const uint16_t* bias, void* out, uint32_t T, uint32_t N, uint32_t D);
+/* The same computation written lane by lane in scalar C (cross-check of the
+ * SIMD form above). */
+void tso_matmul_int4_scalar(int x_is_f32, int out_is_f32, const void* x,
+                            const uint8_t* w_int4, const uint16_t* w_scales, const uint8_t* w_zp,
+                            const uint16_t* bias, void* out, uint32_t T, uint32_t N, uint32_t D);
 void tso_swiglu_clamp_f32(const float* gate_up, float* out, uint32_t T, uint32_t D);
 void tso_softmax_f32(const float* x, float* out, uint32_t rows, uint32_t cols);
 void tso_add_fp16(const uint16_t* a, const uint16_t* b, uint16_t* out, uint32_t n);
@@ -111,6 +116,14 @@ int        tso_model_set(tso_model* m, const char* name, const void* data, size_
 int        tso_model_forward(const tso_model* m, const int32_t* ids, const uint8_t* mask,
                              uint32_t T, float* logits_out, int n_threads,
                              uint16_t* hidden_trace, int32_t* topk_trace, float* normed_trace);
+
+/* As tso_model_forward, with each layer's expert choice forced to
+ * forced_topk i32 [n_layers, T, top_k] (in that order; the routing weights are
+ * the softmax of this forward's own router logits at those experts).  Parity
+ * tooling: it separates arithmetic differences from top-k flips at near-ties. */
+int        tso_model_forward_forced(const tso_model* m, const int32_t* ids, const uint8_t* mask, uint32_t T,
+                                    float* logits_out, int n_threads, uint16_t* hidden_trace, int32_t* topk_trace,
+                                    float* normed_trace, const int32_t* forced_topk);
 
 /* One MoE block half (router + experts), as blockForward runs it after the
  * post-attention norm: normed f32 [T, D] -> moe_out fp16 [T, D] (= fp16(acc*K)),

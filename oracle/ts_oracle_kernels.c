@@ -18,6 +18,7 @@
  */
 #include "ts_oracle.h"
 
+#include <immintrin.h>
 #include <math.h>
 #include <string.h>
 
@@ -272,9 +273,9 @@ static inline void store_out(int out_is_f32, void* out, size_t i, float v) {
  * block sum (v0+v1)+(v2+v3), then sum += bsum*scale (mul, then add).
  * Remaining rows take the tail path (669-707): a0 takes the even 4-chunks,
  * a1 the odd ones, c = a0+a1, acc += ((c0+c1)+(c2+c3))*scale. */
-void tso_matmul_int4(int x_is_f32, int out_is_f32, const void* x,
-                     const uint8_t* w_int4, const uint16_t* w_scales, const uint8_t* w_zp,
-                     const uint16_t* bias, void* out, uint32_t T, uint32_t N, uint32_t D) {
+void tso_matmul_int4_scalar(int x_is_f32, int out_is_f32, const void* x,
+                            const uint8_t* w_int4, const uint16_t* w_scales, const uint8_t* w_zp,
+                            const uint16_t* bias, void* out, uint32_t T, uint32_t N, uint32_t D) {
   const uint32_t BLOCK = 32, TR = 8;
   const uint32_t w_stride = D / 2, s_stride = D / BLOCK, zp_stride = (s_stride + 1) / 2;
   uint32_t tt = 0;
@@ -333,6 +334,100 @@ void tso_matmul_int4(int x_is_f32, int out_is_f32, const void* x,
     float bv = tso_f16_to_f32(bias[n]);
     for (uint32_t ti = 0; ti < m_tail; ti++)
       store_out(out_is_f32, out, (size_t)(tt + ti) * N + n, accs[ti] + bv);
+  }
+}
+
+/* 32 nibbles of one block, minus zp, as eight 4-lane f32 vectors in element
+ * order (int4BlockDecode, wasm_exports.zig:512-540). */
+static inline void decode_block_v(const uint8_t* w_row, uint32_t block_d, uint8_t zp, __m128 q[8]) {
+  const __m128i b = _mm_loadu_si128((const __m128i*)(w_row + block_d / 2));
+  const __m128i m = _mm_set1_epi8(0x0F);
+  const __m128i lo = _mm_and_si128(b, m);
+  const __m128i hi = _mm_and_si128(_mm_srli_epi16(b, 4), m);
+  const __m128i e0 = _mm_unpacklo_epi8(lo, hi); /* elements 0..15 */
+  const __m128i e1 = _mm_unpackhi_epi8(lo, hi); /* elements 16..31 */
+  const __m128i z = _mm_set1_epi32(zp);
+  __m128i src[2] = {e0, e1};
+  for (int h = 0; h < 2; h++) {
+    __m128i v = src[h];
+    for (int c = 0; c < 4; c++) {
+      __m128i w = _mm_cvtepu8_epi32(v);
+      q[h * 4 + c] = _mm_cvtepi32_ps(_mm_sub_epi32(w, z));
+      v = _mm_srli_si128(v, 4);
+    }
+  }
+}
+
+/* (v0 + v1) + (v2 + v3) of one 4-lane vector */
+static inline float hsum_pairs(__m128 v) {
+  __m128 s = _mm_add_ps(v, _mm_shuffle_ps(v, v, _MM_SHUFFLE(2, 3, 0, 1)));
+  return _mm_cvtss_f32(s) + _mm_cvtss_f32(_mm_movehl_ps(s, s));
+}
+
+/* Same contract and bit-identical result as tso_matmul_int4_scalar: the
+ * reference's 4-lane fma4 chains are one SSE fused multiply-add per lane
+ * (the Zig kernel's own vector shape), the horizontal sums keep its
+ * association. */
+void tso_matmul_int4(int x_is_f32, int out_is_f32, const void* x,
+                     const uint8_t* w_int4, const uint16_t* w_scales, const uint8_t* w_zp,
+                     const uint16_t* bias, void* out, uint32_t T, uint32_t N, uint32_t D) {
+  if (!x_is_f32) {
+    tso_matmul_int4_scalar(x_is_f32, out_is_f32, x, w_int4, w_scales, w_zp, bias, out, T, N, D);
+    return;
+  }
+  const float* xf = (const float*)x;
+  const uint32_t BLOCK = 32, TR = 8;
+  const uint32_t w_stride = D / 2, s_stride = D / BLOCK, zp_stride = (s_stride + 1) / 2;
+  uint32_t tt = 0;
+  __m128 q[8];
+  for (; tt + TR <= T; tt += TR) {
+    for (uint32_t n = 0; n < N; n++) {
+      const uint8_t* wr = w_int4 + (size_t)n * w_stride;
+      const uint16_t* sr = w_scales + (size_t)n * s_stride;
+      const uint8_t* zr = w_zp ? w_zp + (size_t)n * zp_stride : NULL;
+      float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (uint32_t b = 0; b < s_stride; b++) {
+        const float scale = tso_f16_to_f32(sr[b]);
+        const uint32_t bd = b * BLOCK;
+        decode_block_v(wr, bd, zr ? extract_zp(zr, b) : 0, q);
+        __m128 v[8];
+        for (int r = 0; r < 8; r++) v[r] = _mm_setzero_ps();
+        for (int c = 0; c < 8; c++)
+          for (int r = 0; r < 8; r++)
+            v[r] = _mm_fmadd_ps(_mm_loadu_ps(xf + (size_t)(tt + r) * D + bd + 4 * c), q[c], v[r]);
+        for (int r = 0; r < 8; r++) {
+          float t = hsum_pairs(v[r]) * scale;
+          sum[r] = sum[r] + t;
+        }
+      }
+      const float bv = tso_f16_to_f32(bias[n]);
+      for (uint32_t r = 0; r < TR; r++) store_out(out_is_f32, out, (size_t)(tt + r) * N + n, sum[r] + bv);
+    }
+  }
+  const uint32_t m_tail = T - tt;
+  if (m_tail == 0) return;
+  for (uint32_t n = 0; n < N; n++) {
+    const uint8_t* wr = w_int4 + (size_t)n * w_stride;
+    const uint16_t* sr = w_scales + (size_t)n * s_stride;
+    const uint8_t* zr = w_zp ? w_zp + (size_t)n * zp_stride : NULL;
+    float accs[7] = {0, 0, 0, 0, 0, 0, 0};
+    for (uint32_t b = 0; b < s_stride; b++) {
+      const float scale = tso_f16_to_f32(sr[b]);
+      const uint32_t bd = b * BLOCK;
+      decode_block_v(wr, bd, zr ? extract_zp(zr, b) : 0, q);
+      for (uint32_t ti = 0; ti < m_tail; ti++) {
+        const float* xr = xf + (size_t)(tt + ti) * D + bd;
+        __m128 a0 = _mm_setzero_ps(), a1 = _mm_setzero_ps();
+        for (int k = 0; k < 4; k++) {
+          a0 = _mm_fmadd_ps(_mm_loadu_ps(xr + 8 * k), q[2 * k], a0);
+          a1 = _mm_fmadd_ps(_mm_loadu_ps(xr + 8 * k + 4), q[2 * k + 1], a1);
+        }
+        float t = hsum_pairs(_mm_add_ps(a0, a1)) * scale;
+        accs[ti] = accs[ti] + t;
+      }
+    }
+    const float bv = tso_f16_to_f32(bias[n]);
+    for (uint32_t ti = 0; ti < m_tail; ti++) store_out(out_is_f32, out, (size_t)(tt + ti) * N + n, accs[ti] + bv);
   }
 }
 
@@ -464,21 +559,27 @@ void tso_cast_f32_to_fp16_scaled(const float* src, uint16_t* dst, uint32_t n, fl
 /* Banded GQA attention with sinks                                     */
 /* ------------------------------------------------------------------ */
 
+/* fp16x4ToF32x4 (math.zig:84-103) on 4 lanes */
+static inline __m128 f16x4_ref(const uint16_t* p) {
+  __m128i u = _mm_cvtepu16_epi32(_mm_loadl_epi64((const __m128i*)p));
+  __m128i sign = _mm_slli_epi32(_mm_and_si128(u, _mm_set1_epi32(0x8000)), 16);
+  __m128i rest = _mm_and_si128(u, _mm_set1_epi32(0x7fff));
+  __m128i biased = _mm_add_epi32(_mm_slli_epi32(rest, 13), _mm_set1_epi32(112 << 23));
+  biased = _mm_andnot_si128(_mm_cmpeq_epi32(rest, _mm_setzero_si128()), biased);
+  return _mm_castsi128_ps(_mm_or_si128(sign, biased));
+}
+
 /* wasm_exports.zig:1232-1267: 4 accumulators x 4 lanes over 16-element
  * steps, then a 4-element step into a0, (a0+a1)+(a2+a3), lane sum left to
  * right, then a scalar mul+add tail. */
 static inline float dot_f16(const uint16_t* a, const uint16_t* b, uint32_t n) {
-  float acc[4][4] = {{0}};
+  __m128 acc[4] = {_mm_setzero_ps(), _mm_setzero_ps(), _mm_setzero_ps(), _mm_setzero_ps()};
   uint32_t i = 0;
   for (; i + 16 <= n; i += 16)
-    for (int u = 0; u < 4; u++)
-      for (int l = 0; l < 4; l++)
-        acc[u][l] = fmaf(tso_f16_to_f32(a[i + 4 * u + l]), tso_f16_to_f32(b[i + 4 * u + l]), acc[u][l]);
-  for (; i + 4 <= n; i += 4)
-    for (int l = 0; l < 4; l++)
-      acc[0][l] = fmaf(tso_f16_to_f32(a[i + l]), tso_f16_to_f32(b[i + l]), acc[0][l]);
+    for (int u = 0; u < 4; u++) acc[u] = _mm_fmadd_ps(f16x4_ref(a + i + 4 * u), f16x4_ref(b + i + 4 * u), acc[u]);
+  for (; i + 4 <= n; i += 4) acc[0] = _mm_fmadd_ps(f16x4_ref(a + i), f16x4_ref(b + i), acc[0]);
   float c[4];
-  for (int l = 0; l < 4; l++) c[l] = (acc[0][l] + acc[1][l]) + (acc[2][l] + acc[3][l]);
+  _mm_storeu_ps(c, _mm_add_ps(_mm_add_ps(acc[0], acc[1]), _mm_add_ps(acc[2], acc[3])));
   float sum = c[0] + c[1];
   sum = sum + c[2];
   sum = sum + c[3];
@@ -535,9 +636,9 @@ void tso_banded_attention(const uint16_t* q, const uint16_t* k, const uint16_t* 
       for (uint32_t j = 0; j < nk; j++) {
         float p = scores[j] * inv;
         const uint16_t* vr = v + (ws + j) * ks + (size_t)hk * D;
+        const __m128 pv4 = _mm_set1_ps(p);
         uint32_t d = 0;
-        for (; d + 4 <= D; d += 4)
-          for (int l = 0; l < 4; l++) acc[d + l] = fmaf(p, tso_f16_to_f32(vr[d + l]), acc[d + l]);
+        for (; d + 4 <= D; d += 4) _mm_storeu_ps(acc + d, _mm_fmadd_ps(pv4, f16x4_ref(vr + d), _mm_loadu_ps(acc + d)));
         for (; d < D; d++) { float pv = p * tso_f16_to_f32(vr[d]); acc[d] = acc[d] + pv; }
       }
       for (uint32_t d = 0; d < D; d++) out[qb + d] = tso_f32_to_f16(acc[d]);

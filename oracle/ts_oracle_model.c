@@ -223,12 +223,22 @@ static void attention_forward(const tso_model* m, const layer_w* lw, const float
 
 /* block.ts:154-207: f32 router logits, top-k, softmax over k, x(1/K) in JS doubles */
 static void router_forward(const tso_model* m, const layer_w* lw, const float* x, int32_t* idx,
-                           float* scores, uint32_t T, int nt) {
+                           float* scores, uint32_t T, int nt, const int32_t* forced) {
   const uint32_t E = m->cfg.n_experts, K = m->cfg.top_k, D = m->cfg.d_model;
   float* logits = (float*)malloc((size_t)T * E * 4);
   float* topv = (float*)malloc((size_t)T * K * 4);
   matmul_rows(nt, 1, 1, x, &lw->router, logits, T, E, D);
-  tso_topk_partial_f32(logits, idx, topv, T, E, K);
+  if (forced) {
+    /* teacher forcing (parity tooling, not a reference path): take the given
+     * experts in the given order, score them with this forward's own logits */
+    for (size_t i = 0; i < (size_t)T * K; i++) {
+      int32_t e = forced[i];
+      idx[i] = e;
+      topv[i] = (e >= 0 && (uint32_t)e < E) ? logits[(i / K) * E + (uint32_t)e] : -INFINITY;
+    }
+  } else {
+    tso_topk_partial_f32(logits, idx, topv, T, E, K);
+  }
   tso_softmax_f32(topv, scores, T, K);
   const double inv_k = 1.0 / (double)K;
   for (size_t i = 0; i < (size_t)T * K; i++) scores[i] = (float)((double)scores[i] * inv_k);
@@ -292,9 +302,9 @@ static void expert_slice(const tso_model* m, const layer_w* lw, const float* x, 
 }
 
 static void moe_forward(const tso_model* m, const layer_w* lw, const float* x, uint32_t T,
-                        uint16_t* moe_out, int32_t* idx, float* sc, int nt) {
+                        uint16_t* moe_out, int32_t* idx, float* sc, int nt, const int32_t* forced) {
   const uint32_t D = m->cfg.d_model, K = m->cfg.top_k;
-  router_forward(m, lw, x, idx, sc, T, nt);
+  router_forward(m, lw, x, idx, sc, T, nt, forced);
   float* acc = (float*)calloc((size_t)T * D, 4);
   if (nt > 1) {
 #pragma omp parallel num_threads(nt)
@@ -320,14 +330,15 @@ static void moe_forward(const tso_model* m, const layer_w* lw, const float* x, u
 int tso_moe_forward(const tso_model* m, uint32_t layer, const float* normed, uint32_t T,
                     uint16_t* moe_out, int32_t* idx_out, float* w_out, int n_threads) {
   if (layer >= m->cfg.n_layers) return -1;
-  moe_forward(m, &m->layers[layer], normed, T, moe_out, idx_out, w_out, n_threads);
+  moe_forward(m, &m->layers[layer], normed, T, moe_out, idx_out, w_out, n_threads, NULL);
   return 0;
 }
 
 /* block.ts:213-302 */
 static void block_forward(const tso_model* m, const layer_w* lw, const uint16_t* in, uint16_t* out,
                           const uint16_t* cos_t, const uint16_t* sin_t, const uint8_t* mask,
-                          uint32_t T, int nt, int32_t* topk_trace, float* normed_trace) {
+                          uint32_t T, int nt, int32_t* topk_trace, float* normed_trace,
+                          const int32_t* forced) {
   const tso_config* c = &m->cfg;
   const uint32_t D = c->d_model, K = c->top_k;
   float* hf = (float*)malloc((size_t)T * D * 4);
@@ -356,7 +367,7 @@ static void block_forward(const tso_model* m, const layer_w* lw, const uint16_t*
     tso_add_rmsnorm_fp16_to_f32(in, attn, lw->post_ln, res2, n2, T, D, c->eps);
   }
   if (normed_trace) memcpy(normed_trace, n2, (size_t)T * D * 4);
-  moe_forward(m, lw, n2, T, moe, idx, sc, nt);
+  moe_forward(m, lw, n2, T, moe, idx, sc, nt, forced);
   if (topk_trace) memcpy(topk_trace, idx, (size_t)T * K * 4);
   tso_add_fp16(res2, moe, out, T * D);
   free(hf); free(attn); free(res2); free(n2); free(idx); free(sc); free(moe);
@@ -366,6 +377,13 @@ static void block_forward(const tso_model* m, const layer_w* lw, const uint16_t*
 int tso_model_forward(const tso_model* m, const int32_t* ids, const uint8_t* mask, uint32_t T,
                       float* logits_out, int n_threads, uint16_t* hidden_trace, int32_t* topk_trace,
                       float* normed_trace) {
+  return tso_model_forward_forced(m, ids, mask, T, logits_out, n_threads, hidden_trace, topk_trace,
+                                  normed_trace, NULL);
+}
+
+int tso_model_forward_forced(const tso_model* m, const int32_t* ids, const uint8_t* mask, uint32_t T,
+                             float* logits_out, int n_threads, uint16_t* hidden_trace, int32_t* topk_trace,
+                             float* normed_trace, const int32_t* forced_topk) {
   const tso_config* c = &m->cfg;
   const uint32_t D = c->d_model, C = c->n_classes, hd = c->head_dim;
   if (T == 0) return 0;
@@ -386,7 +404,8 @@ int tso_model_forward(const tso_model* m, const int32_t* ids, const uint8_t* mas
   for (uint32_t L = 0; L < c->n_layers; L++) {
     block_forward(m, &m->layers[L], src, dst, cos_t, sin_t, mk, T, n_threads,
                   topk_trace ? topk_trace + (size_t)L * T * c->top_k : NULL,
-                  normed_trace ? normed_trace + (size_t)L * T * D : NULL);
+                  normed_trace ? normed_trace + (size_t)L * T * D : NULL,
+                  forced_topk ? forced_topk + (size_t)L * T * c->top_k : NULL);
     uint16_t* tmp = src; src = dst; dst = tmp;
     if (hidden_trace) memcpy(hidden_trace + (size_t)(L + 1) * T * D, src, (size_t)T * D * 2);
   }

@@ -97,3 +97,21 @@ def test_rope_tables_reference_constants(oracle):
     # the first pair rotates at inv_freq[0] = 1 (extrapolation side of the ramp)
     assert c[1, 0] == oracle.f32_to_f16(math.cos(1.0) * msc)
     assert s[1, 0] == oracle.f32_to_f16(math.sin(1.0) * msc)
+
+
+def test_simd_matmul_matches_scalar_restatement(oracle):
+    """The SIMD oracle matmul equals the lane-by-lane scalar restatement bit
+    for bit, on both the 8-row tile path and the tail path."""
+    r = np.random.Generator(np.random.PCG64(5))
+    for T in (1, 7, 8, 19, 64):
+        N, K = 37, 96
+        int4 = r.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
+        sc = r.uniform(1e-3, 1e-2, size=(N, K // 32)).astype(np.float16).view(np.uint16)
+        zp = r.integers(0, 256, size=(N, 2), dtype=np.uint8)
+        b = r.normal(0, 0.1, size=N).astype(np.float16).view(np.uint16)
+        x = r.normal(0, 1, size=(T, K)).astype(np.float32)
+        for out_f32 in (True, False):
+            a = oracle.matmul_int4(x, int4, sc, zp, b, out_f32)
+            s = oracle.matmul_int4(x, int4, sc, zp, b, out_f32, scalar=True)
+            assert np.array_equal(a.view(np.uint32 if out_f32 else np.uint16),
+                                  s.view(np.uint32 if out_f32 else np.uint16))

@@ -20,6 +20,7 @@ TS_ERR_DEVICE = -5
 
 TS_DTYPE_U8, TS_DTYPE_F16, TS_DTYPE_F32, TS_DTYPE_I32 = 0, 1, 2, 3
 TS_MODE_FAST, TS_MODE_EXACT = 0, 1
+PHASES = ("expert_gate_up", "expert_down", "qkv", "attention", "o_proj", "router", "other")
 
 P = ctypes.c_void_p
 U32 = ctypes.c_uint32
@@ -59,8 +60,11 @@ SIGNATURES = [
     ("ts_cuda_forward", ctypes.c_int, [P, P, P, U32, P]),
     ("ts_cuda_forward_packed", ctypes.c_int, [P, P, P, P, U32, P]),
     ("ts_cuda_forward_packed_device", ctypes.c_int, [P, P, P, P, U32, P, P]),
+    ("ts_cuda_forward_trace", ctypes.c_int, [P, P, P, P, U32, P, P]),
     ("ts_cuda_check", ctypes.c_int, [P, P]),
     ("ts_cuda_device_name", ctypes.c_char_p, [P]),
+    ("ts_cuda_profile", ctypes.c_int, [P, I32]),
+    ("ts_cuda_profile_read", ctypes.c_int, [P, P, P, P, P]),
     ("ts_cuda_last_error", ctypes.c_char_p, []),
     ("ts_cuda_destroy", None, [P]),
     ("ts_cuda_op_gather_bq", ctypes.c_int, [P, P, P, P, P, U32, U32, U32, P]),

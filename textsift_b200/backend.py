@@ -130,6 +130,20 @@ class CudaBackend:
             abi.check(abi.lib().ts_cuda_forward(self._h, _ptr(ids), _ptr(mask), T, _ptr(out)))
         return Logits(out, T, self.num_classes)
 
+    def forward_trace(self, token_ids, attention_mask=None):
+        """One sequence; returns (Logits, top-k experts i32 [n_layers, T, top_k])."""
+        if not self._ready:
+            raise RuntimeError("CudaBackend: call warmup() before forward_trace()")
+        ids = np.ascontiguousarray(np.asarray(token_ids, dtype=np.int32))
+        T = ids.size
+        mask = None if attention_mask is None else np.ascontiguousarray(np.asarray(attention_mask, dtype=np.uint8))
+        offs = np.array([0, T], np.uint32)
+        out = np.empty((T * self.num_classes,), dtype=np.float32)
+        topk = np.empty((int(self._cfg.n_layers), T, int(self._cfg.top_k)), dtype=np.int32)
+        abi.check(abi.lib().ts_cuda_forward_trace(self._h, _ptr(ids), _ptr(mask), _ptr(offs), 1, _ptr(out),
+                                                  _ptr(topk)))
+        return Logits(out, T, self.num_classes), topk
+
     def forward_packed(self, chunks: Sequence[np.ndarray], masks: Sequence[np.ndarray] | None = None) -> list[Logits]:
         """Forward many chunks in one launch; returns one Logits per chunk."""
         if not self._ready:

@@ -84,7 +84,7 @@ __global__ void attn_exact_kernel(const AttnArgs a) {
       }
     float sum = __fadd_rn(__fadd_rn(__fadd_rn(sv[0], sv[1]), sv[2]), sv[3]);
     for (; i < total; i++) {
-      float e = expf(__fsub_rn(sc[i], mx));
+      float e = expf_ref(__fsub_rn(sc[i], mx));
       sc[i] = e;
       sum = __fadd_rn(sum, e);
     }
@@ -150,7 +150,8 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
   uint8_t* sK = smem;
   uint8_t* sV = smem + (size_t)band * 128;
   uint8_t* sM = smem + (size_t)band * 256;  // per-key validity of the mask (1 = usable)
-  const uint32_t q0 = blockIdx.x * kAttnRows, hk = blockIdx.y;
+  const int2 tile = a.tiles[blockIdx.x];
+  const uint32_t q0 = (uint32_t)tile.x, q_end = (uint32_t)tile.y, hk = blockIdx.y;
   const uint32_t group = a.Hq / a.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t h = hk * group + (uint32_t)warp;
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
 #pragma unroll
   for (int i = 0; i < 2; i++) {
     const uint32_t t = q0 + g + 8 * i;
-    r_ok[i] = t < a.T;
+    r_ok[i] = t < q_end;
     if (r_ok[i]) {
       const uint32_t s0 = a.sstart ? (uint32_t)a.sstart[t] : 0u;
       const uint32_t L = a.slen ? (uint32_t)a.slen[t] : a.T;
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
         float ev = 0.0f;
         if (key >= r_ws[ri] && key < r_we[ri] && sM[key - kb0]) {
           const float x = __fsub_rn(s[nt][i], mx[ri]);
-          ev = (key - r_ws[ri]) < r_p4[ri] ? exp_approx_ref(x) : expf(x);
+          ev = (key - r_ws[ri]) < r_p4[ri] ? exp_approx_ref(x) : expf_ref(x);
         }
         e[nt][i] = ev;
         lsum[ri] += ev;
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
     const float xs = __fsub_rn(sink, mx[ri]);
-    l += r_nk[ri] < r_p4[ri] ? exp_approx_ref(xs) : expf(xs);  // the sink is entry n_keys
+    l += r_nk[ri] < r_p4[ri] ? exp_approx_ref(xs) : expf_ref(xs);  // the sink is entry n_keys
     inv[ri] = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
   }
 #pragma unroll
@@ -361,9 +362,19 @@ cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st) {
     attr = true;
   }
   if (sm > 200 * 1024) return cudaErrorInvalidValue;
-  dim3 grid((a.T + kAttnRows - 1) / kAttnRows, a.Hkv);
+  if (a.n_tiles == 0) return cudaSuccess;
+  dim3 grid(a.n_tiles, a.Hkv);
   attn_tc_kernel<<<grid, 7 * 32, sm, st>>>(a);
   return cudaGetLastError();
+}
+
+uint32_t attention_max_tiles(uint32_t T, uint32_t n_seqs) { return T / kAttnRows + n_seqs + 1; }
+
+void attention_tiles(const uint32_t* offs, uint32_t n_seqs, int2* out, uint32_t* n_out) {
+  uint32_t n = 0;
+  for (uint32_t s = 0; s < n_seqs; s++)
+    for (uint32_t q = offs[s]; q < offs[s + 1]; q += kAttnRows) out[n++] = make_int2((int)q, (int)offs[s + 1]);
+  *n_out = n;
 }
 
 }  // namespace ts

@@ -9,19 +9,24 @@
 // memory, and the product runs on the 5th-generation tensor core with f32
 // accumulation in TMEM.  Activations enter as fp16.
 //
-// CTA = 128 output rows x BN output columns, 8 warps:
-//   warp 0      producer: TMA tile of A (128 x 64 fp16, 128B swizzle) and one
-//               bulk copy of the packed weight blob per 64-wide K chunk
-//   warp 1      MMA issuer: 4 x tcgen05.mma (K=16) per chunk, commit frees the
-//               stage; a final commit publishes the accumulator
-//   warp 2      TMEM allocator
-//   warps 4..7  dequantise each stage's int4 blob into the swizzled fp16 B
-//               tile, then run the epilogue (tcgen05.ld -> bias -> fused op ->
-//               global stores); warp 4+i owns TMEM lanes 32i..32i+31
+// Persistent, warp-specialized kernel: one CTA per SM walks output tiles of
+// 128 rows x BN columns (dense: row tiles of A; grouped: the 128-row tiles of
+// each expert's segment), 16 warps:
+//   warp 0       producer: TMA tile of A (128 x 64 fp16, 128B swizzle) and one
+//                bulk copy of the packed weight blob per 64-wide K chunk, into
+//                an S-stage ring that runs across tile boundaries
+//   warp 1       MMA issuer: 4 x tcgen05.mma (K=16) per chunk into one of two
+//                TMEM accumulators; commits free the stage / publish the tile
+//   warp 2       TMEM allocator (2 x 256 columns)
+//   warps 4..7   dequantise each stage's int4 blob into the swizzled fp16 B tile
+//   warps 8..15  epilogue of the previous tile while the next one accumulates:
+//                tcgen05.ld -> bias -> fused op -> global stores; warp 8+i
+//                owns TMEM lanes 32(i%4).. and half (i/4) of the columns
 // All waits are bounded (ts_common.cuh) and set the device error flag.
 #include "ts_common.cuh"
 #include "ts_kernels.h"
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -37,10 +42,12 @@ struct GemmCfg {
   static constexpr uint32_t OFF_B = STAGES * A_BYTES;
   static constexpr uint32_t OFF_RAW = OFF_B + STAGES * B_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_RAW + STAGES * RAW_STRIDE;
-  static constexpr uint32_t NUM_BARS = 3 * STAGES + 1;
+  static constexpr uint32_t NUM_BARS = 3 * STAGES + 4;
   static constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
-  static constexpr uint32_t TMEM_COLS = 256;
+  static constexpr uint32_t TMEM_COLS = 512;                    // two accumulators
+  static constexpr uint32_t ACC_STRIDE = 256;                   // column offset of accumulator 1
+  static constexpr int THREADS = 512;
 };
 
 // Bounded wait that also gives up as soon as another role aborted.
@@ -159,9 +166,30 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
   }
 }
 
+struct TileInfo {
+  uint32_t expert, row0, row_end, n_tile;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, uint32_t tile, uint32_t n_ntiles) {
+  TileInfo ti;
+  const uint32_t m = tile / n_ntiles;
+  ti.n_tile = tile % n_ntiles;
+  if (a.tiles) {
+    const int4 t = a.tiles[m];
+    ti.expert = (uint32_t)t.x;
+    ti.row0 = (uint32_t)t.y;
+    ti.row_end = (uint32_t)t.z;
+  } else {
+    ti.expert = a.dense_expert;
+    ti.row0 = m * 128u;
+    ti.row_end = min(a.M, ti.row0 + 128u);
+  }
+  return ti;
+}
+
 template <int BN, int EPI>
-__global__ void __launch_bounds__(256, 1)
-    gemm_w4_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs args) {
+__global__ void __launch_bounds__(512, 1)
+    gemm_w4_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs args, uint32_t n_ntiles) {
   using C = GemmCfg<BN>;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_dyn[];
@@ -173,24 +201,14 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* bready = bars + 2 * S;
-  uint64_t* accum = bars + 3 * S;
+  uint64_t* acc_full = bars + 3 * S;       // [2]
+  uint64_t* acc_empty = bars + 3 * S + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
-  // ---- tile selection (dense or grouped) ----
-  uint32_t expert = args.dense_expert, row0, row_end;
-  if (args.tiles) {
-    if ((int)blockIdx.y >= *args.n_tiles) return;
-    const int4 t = args.tiles[blockIdx.y];
-    expert = (uint32_t)t.x;
-    row0 = (uint32_t)t.y;
-    row_end = (uint32_t)t.z;
-  } else {
-    row0 = blockIdx.y * 128u;
-    row_end = min(args.M, row0 + 128u);
-  }
-  const uint32_t n_tile = blockIdx.x;
-  const uint32_t n0 = n_tile * BN;
+  const uint32_t m_tiles = args.tiles ? (uint32_t)*args.n_tiles : (args.M + 127u) / 128u;
+  const uint32_t total = m_tiles * n_ntiles;
+  if (blockIdx.x >= total) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -199,7 +217,10 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&empty[s], 1);
       mbar_init(&bready[s], 128);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 256);
+    }
     *abort_flag = 0;
     mbar_fence_init();
     fence_proxy_async_smem();
@@ -216,86 +237,114 @@ __global__ void __launch_bounds__(256, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint8_t* wb = args.wblob + (size_t)expert * args.expert_stride + (size_t)n_tile * n_kc * C::RAW_BYTES;
-      for (uint32_t kc = 0; kc < n_kc; kc++) {
-        const int s = kc % S;
-        const uint32_t ph = (kc / S) & 1u;
-        if (!wait_or_abort(&empty[s], ph ^ 1u, args.err, abort_flag)) break;
-        mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::RAW_BYTES);
-        tma_load_2d(sA + s * C::A_BYTES, &tmap_a, (int32_t)(kc * kChunkK), (int32_t)row0, &full[s]);
-        bulk_g2s(sR + s * C::RAW_STRIDE, wb + (size_t)kc * C::RAW_BYTES, C::RAW_BYTES, &full[s]);
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const TileInfo ti = tile_info(args, tile, n_ntiles);
+        const uint8_t* wb = args.wblob + (size_t)ti.expert * args.expert_stride + (size_t)ti.n_tile * n_kc * C::RAW_BYTES;
+        for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!wait_or_abort(&empty[s], ph ^ 1u, args.err, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::RAW_BYTES);
+          tma_load_2d(sA + s * C::A_BYTES, &tmap_a, (int32_t)(kc * kChunkK), (int32_t)ti.row0, &full[s]);
+          bulk_g2s(sR + s * C::RAW_STRIDE, wb + (size_t)kc * C::RAW_BYTES, C::RAW_BYTES, &full[s]);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16_f32(128, BN);
+      uint32_t it = 0, lt = 0;
       bool ok = true;
-      for (uint32_t kc = 0; kc < n_kc && ok; kc++) {
-        const int s = kc % S;
-        const uint32_t ph = (kc / S) & 1u;
-        ok = wait_or_abort(&full[s], ph, args.err, abort_flag) && wait_or_abort(&bready[s], ph, args.err, abort_flag);
-        if (!ok) break;
+      for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x, lt++) {
+        const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
+        if (!wait_or_abort(&acc_empty[b], bph ^ 1u, args.err, abort_flag)) break;
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
-        const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
+        const uint32_t d_tmem = tmem_base + b * C::ACC_STRIDE;
+        for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          ok = wait_or_abort(&full[s], ph, args.err, abort_flag) && wait_or_abort(&bready[s], ph, args.err, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-          tc_mma_f16(tmem_base, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
-                     (kc | (uint32_t)k) != 0u);
-        tc_commit(&empty[s]);
-      }
-      if (ok) tc_commit(accum);
-    }
-  } else if (warp >= 4) {
-    const int t = threadIdx.x - 128;  // 0..127
-    // ---- dequantise: one (or two) B rows per thread per stage ----
-    bool ok = true;
-    for (uint32_t kc = 0; kc < n_kc; kc++) {
-      const int s = kc % S;
-      const uint32_t ph = (kc / S) & 1u;
-      if (!wait_or_abort(&full[s], ph, args.err, abort_flag)) { ok = false; break; }
-      const uint8_t* raw = sR + s * C::RAW_STRIDE;
-      uint8_t* bdst = sB + s * C::B_BYTES;
-#pragma unroll
-      for (int rr = 0; rr < BN / 128; rr++) {
-        const int r = t + rr * 128;
-        const uint4 h0 = *reinterpret_cast<const uint4*>(raw + r * 16);
-        const uint4 h1 = *reinterpret_cast<const uint4*>(raw + BN * 16 + r * 16);
-        const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + BN * 32 + r * 4);
-        const uint32_t z = raw[BN * 36 + r];
-        const uint32_t s0 = (sc & 0xffffu) * 0x00010001u, s1 = (sc >> 16) * 0x00010001u;
-        const uint32_t z0 = (0x6400u | (z & 15u)) * 0x00010001u, z1 = (0x6400u | (z >> 4)) * 0x00010001u;
-        const uint32_t wds[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          const uint32_t w = wds[c];
-          const uint32_t sz = c < 4 ? s0 : s1, zz = c < 4 ? z0 : z1;
-          uint32_t o[4];
-#pragma unroll
-          for (int j = 0; j < 4; j++) {
-            const uint32_t bits = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
-            __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&bits), *reinterpret_cast<const __half2*>(&zz));
-            __half2 d = __hmul2(q, *reinterpret_cast<const __half2*>(&sz));
-            o[j] = *reinterpret_cast<uint32_t*>(&d);
-          }
-          *reinterpret_cast<uint4*>(bdst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          for (int k = 0; k < 4; k++)
+            tc_mma_f16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
+                       (kc | (uint32_t)k) != 0u);
+          tc_commit(&empty[s]);
         }
+        if (ok) tc_commit(&acc_full[b]);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&bready[s]);
     }
-    // ---- epilogue ----
-    if (ok && wait_or_abort(accum, 0, args.err, abort_flag)) {
+  } else if (warp >= 4 && warp < 8) {
+    // ---- dequantise: BN/128 B rows per thread per stage ----
+    const int t = threadIdx.x - 128;  // 0..127
+    uint32_t it = 0;
+    bool ok = true;
+    for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1u;
+        if (!wait_or_abort(&full[s], ph, args.err, abort_flag)) { ok = false; break; }
+        const uint8_t* raw = sR + s * C::RAW_STRIDE;
+        uint8_t* bdst = sB + s * C::B_BYTES;
+#pragma unroll
+        for (int rr = 0; rr < BN / 128; rr++) {
+          const int r = t + rr * 128;
+          const uint4 h0 = *reinterpret_cast<const uint4*>(raw + r * 16);
+          const uint4 h1 = *reinterpret_cast<const uint4*>(raw + BN * 16 + r * 16);
+          const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + BN * 32 + r * 4);
+          const uint32_t z = raw[BN * 36 + r];
+          const uint32_t s0 = (sc & 0xffffu) * 0x00010001u, s1 = (sc >> 16) * 0x00010001u;
+          const uint32_t z0 = (0x6400u | (z & 15u)) * 0x00010001u, z1 = (0x6400u | (z >> 4)) * 0x00010001u;
+          const uint32_t wds[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+          for (int c = 0; c < 8; c++) {
+            const uint32_t w = wds[c];
+            const uint32_t sz = c < 4 ? s0 : s1, zz = c < 4 ? z0 : z1;
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const uint32_t bits = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+              __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&bits), *reinterpret_cast<const __half2*>(&zz));
+              __half2 d = __hmul2(q, *reinterpret_cast<const __half2*>(&sz));
+              o[j] = *reinterpret_cast<uint32_t*>(&d);
+            }
+            *reinterpret_cast<uint4*>(bdst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bready[s]);
+      }
+    }
+  } else if (warp >= 8) {
+    // ---- epilogue: 8 warps, lane quarter (warp % 4), column half ((warp - 8) / 4) ----
+    const uint32_t quarter = (uint32_t)(warp & 3), chalf = (uint32_t)(warp - 8) >> 2;
+    const uint32_t r = quarter * 32u + (uint32_t)lane;
+    uint32_t lt = 0;
+    for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x, lt++) {
+      const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
+      if (!wait_or_abort(&acc_full[b], bph, args.err, abort_flag)) break;
       tc_fence_after();
-      const uint32_t grow = row0 + (uint32_t)t;
-      const bool row_ok = grow < row_end;
-      const uint32_t lane_base = (uint32_t)(warp - 4) * 32u;
-      const uint16_t* bias = args.bias + (size_t)expert * args.N;
+      const TileInfo ti = tile_info(args, tile, n_ntiles);
+      const uint32_t grow = ti.row0 + r;
+      const bool row_ok = grow < ti.row_end;
+      const uint32_t n0 = ti.n_tile * BN;
+      const uint16_t* bias = args.bias + (size_t)ti.expert * args.N;
+      const uint32_t col_lo = chalf * (BN / 2);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (uint32_t c0 = col_lo; c0 < col_lo + BN / 2; c0 += 32) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + (uint32_t)c0, v);
+        tmem_ld_32x32b_x32(tmem_base + b * C::ACC_STRIDE + ((quarter * 32u) << 16) + c0, v);
         tmem_ld_wait();
+        if (c0 + 32 >= col_lo + BN / 2) {
+          // every TMEM read of this buffer by this thread is complete: release it
+          tc_fence_before();
+          mbar_arrive(&acc_empty[b]);
+        }
         if (row_ok && n0 + c0 < args.N) gemm_epilogue_chunk<EPI>(args, grow, n0 + c0, bias, v);
       }
     }
@@ -415,6 +464,16 @@ bool make_act_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K
   return r == CUDA_SUCCESS;
 }
 
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
 template <int BN, int EPI>
 static cudaError_t launch_one(const CUtensorMap& tmap, const GemmArgs& args, uint32_t n_tiles, uint32_t grid_m,
                               cudaStream_t st) {
@@ -426,8 +485,10 @@ static cudaError_t launch_one(const CUtensorMap& tmap, const GemmArgs& args, uin
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  dim3 grid(n_tiles, grid_m);
-  gemm_w4_tc_kernel<BN, EPI><<<grid, 256, C::SMEM_BYTES, st>>>(tmap, args);
+  // persistent: at most one CTA per SM, never more CTAs than tiles can exist
+  const uint64_t max_tiles = (uint64_t)grid_m * n_tiles;
+  const uint32_t grid = (uint32_t)std::min<uint64_t>(max_tiles, (uint64_t)num_sms());
+  gemm_w4_tc_kernel<BN, EPI><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tmap, args, n_tiles);
   return cudaGetLastError();
 }
 

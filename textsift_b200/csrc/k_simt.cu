@@ -127,8 +127,8 @@ __global__ void rmsnorm_kernel(const uint16_t* __restrict__ a, const uint16_t* _
 // otherwise, exactly as the single-thread reference partitions rows.
 // ---------------------------------------------------------------------------
 template <bool X_F32, int OUT>
-__global__ void __launch_bounds__(128) matmul_w4_exact_kernel(const ExactArgs a) {
-  extern __shared__ float xs[];  // [8][K]
+__global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a) {
+  extern __shared__ __align__(16) float xs[];  // [2 groups][8 rows][K]
   const uint32_t K = a.K, nb = K / 32, zs = (nb + 1) / 2;
   uint32_t expert = 0, row0, row_end, seg_start = 0, seg_len = 0;
   const bool grouped = a.tiles != nullptr;
@@ -141,24 +141,28 @@ __global__ void __launch_bounds__(128) matmul_w4_exact_kernel(const ExactArgs a)
     row0 = blockIdx.y * 128u;
     row_end = min(a.M, row0 + 128u);
   }
-  const uint32_t n = blockIdx.x * 128u + threadIdx.x;
+  const uint32_t half = threadIdx.x >> 7;  // which 8-row group of a pair this thread works on
+  const uint32_t n = blockIdx.x * 128u + (threadIdx.x & 127u);
   const bool n_ok = n < a.N;
-  const uint8_t* wr = a.w_int4 + (size_t)expert * a.w_int4_estride + (size_t)n * (K / 2);
-  const uint16_t* sr = a.w_scales + (size_t)expert * a.w_scales_estride + (size_t)n * nb;
-  const uint8_t* zr = a.w_zp ? a.w_zp + (size_t)expert * a.w_zp_estride + (size_t)n * zs : nullptr;
+  const uint8_t* wr = a.w_int4 + (size_t)expert * a.w_int4_estride + (size_t)(n_ok ? n : 0) * (K / 2);
+  const uint16_t* sr = a.w_scales + (size_t)expert * a.w_scales_estride + (size_t)(n_ok ? n : 0) * nb;
+  const uint8_t* zr = a.w_zp ? a.w_zp + (size_t)expert * a.w_zp_estride + (size_t)(n_ok ? n : 0) * zs : nullptr;
   const float bias = n_ok ? f16_ref_to_f32(a.bias[(size_t)expert * a.bias_estride + n]) : 0.0f;
+  float* myx = xs + (size_t)half * 8 * K;
 
-  for (uint32_t g0 = row0; g0 < row_end; g0 += 8) {
-    const uint32_t gr = min(8u, row_end - g0);
+  for (uint32_t gp = row0; gp < row_end; gp += 16) {
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < gr * K; i += blockDim.x) {
-      uint32_t r = i / K, k = i % K;
-      size_t src = (size_t)(g0 + r) * a.ldx + k;
+    const uint32_t rows_pair = min(16u, row_end - gp);
+    for (uint32_t i = threadIdx.x; i < rows_pair * K; i += blockDim.x) {
+      const uint32_t r = i / K, k = i % K;
+      const size_t src = (size_t)(gp + r) * a.ldx + k;
       xs[r * K + k] = X_F32 ? reinterpret_cast<const float*>(a.x)[src]
                             : f16_ref_to_f32(reinterpret_cast<const uint16_t*>(a.x)[src]);
     }
     __syncthreads();
-    if (!n_ok) continue;
+    const uint32_t g0 = gp + half * 8;
+    if (!n_ok || g0 >= row_end) continue;
+    const uint32_t gr = min(8u, row_end - g0);
     bool tile_path[8];
 #pragma unroll
     for (int r = 0; r < 8; r++) {
@@ -188,27 +192,33 @@ __global__ void __launch_bounds__(128) matmul_w4_exact_kernel(const ExactArgs a)
 #pragma unroll
       for (int r = 0; r < 8; r++) {
         if ((uint32_t)r >= gr) break;
-        const float* x = xs + r * K + b * 32;
+        const float4* x4 = reinterpret_cast<const float4*>(myx + r * K + b * 32);
         float bs;
         if (tile_path[r]) {
           float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
 #pragma unroll
           for (int c = 0; c < 8; c++) {
-            v0 = __fmaf_rn(x[4 * c + 0], q[4 * c + 0], v0);
-            v1 = __fmaf_rn(x[4 * c + 1], q[4 * c + 1], v1);
-            v2 = __fmaf_rn(x[4 * c + 2], q[4 * c + 2], v2);
-            v3 = __fmaf_rn(x[4 * c + 3], q[4 * c + 3], v3);
+            const float4 xv = x4[c];
+            v0 = __fmaf_rn(xv.x, q[4 * c + 0], v0);
+            v1 = __fmaf_rn(xv.y, q[4 * c + 1], v1);
+            v2 = __fmaf_rn(xv.z, q[4 * c + 2], v2);
+            v3 = __fmaf_rn(xv.w, q[4 * c + 3], v3);
           }
           bs = __fadd_rn(__fadd_rn(v0, v1), __fadd_rn(v2, v3));
         } else {
           float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int k = 0; k < 4; k++)
-#pragma unroll
-            for (int l = 0; l < 4; l++) {
-              a0[l] = __fmaf_rn(x[8 * k + l], q[8 * k + l], a0[l]);
-              a1[l] = __fmaf_rn(x[8 * k + 4 + l], q[8 * k + 4 + l], a1[l]);
-            }
+          for (int k = 0; k < 4; k++) {
+            const float4 x0 = x4[2 * k], x1 = x4[2 * k + 1];
+            a0[0] = __fmaf_rn(x0.x, q[8 * k + 0], a0[0]);
+            a0[1] = __fmaf_rn(x0.y, q[8 * k + 1], a0[1]);
+            a0[2] = __fmaf_rn(x0.z, q[8 * k + 2], a0[2]);
+            a0[3] = __fmaf_rn(x0.w, q[8 * k + 3], a0[3]);
+            a1[0] = __fmaf_rn(x1.x, q[8 * k + 4], a1[0]);
+            a1[1] = __fmaf_rn(x1.y, q[8 * k + 5], a1[1]);
+            a1[2] = __fmaf_rn(x1.z, q[8 * k + 6], a1[2]);
+            a1[3] = __fmaf_rn(x1.w, q[8 * k + 7], a1[3]);
+          }
           float c0 = __fadd_rn(a0[0], a1[0]), c1 = __fadd_rn(a0[1], a1[1]);
           float c2 = __fadd_rn(a0[2], a1[2]), c3 = __fadd_rn(a0[3], a1[3]);
           bs = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
@@ -259,7 +269,7 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int32_t* __
   float m = ov[0];
   for (uint32_t c = 1; c < K; c++) if (ov[c] > m) m = ov[c];
   float e[8], sum = 0.0f;
-  for (uint32_t c = 0; c < K; c++) { e[c] = expf(__fsub_rn(ov[c], m)); sum = __fadd_rn(sum, e[c]); }
+  for (uint32_t c = 0; c < K; c++) { e[c] = expf_ref(__fsub_rn(ov[c], m)); sum = __fadd_rn(sum, e[c]); }
   const float inv = sum > 0.0f ? __fdiv_rn(1.0f, sum) : __fdiv_rn(1.0f, (float)K);
   for (uint32_t c = 0; c < K; c++) {
     idx[(size_t)t * K + c] = oi[c];
@@ -505,22 +515,26 @@ cudaError_t launch_add_rmsnorm(const uint16_t* a, const uint16_t* b, const uint1
 
 cudaError_t launch_matmul_exact(const ExactArgs& a, bool x_f32, int out_mode, uint32_t grid_m, cudaStream_t st) {
   if (grid_m == 0) return cudaSuccess;
+  if (a.K % 32 || a.K > 2048) return cudaErrorInvalidValue;
   dim3 grid(nblk(a.N, 128), grid_m);
-  const size_t sm = (size_t)8 * a.K * sizeof(float);
-  if (sm > 48 * 1024) {
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16Widen>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  const size_t sm = (size_t)16 * a.K * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    const int mx = 16 * 2048 * 4;
+    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16Widen>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    attr = true;
   }
   if (x_f32) {
-    if (out_mode == kOutF16) matmul_w4_exact_kernel<true, kOutF16><<<grid, 128, sm, st>>>(a);
-    else if (out_mode == kOutF32) matmul_w4_exact_kernel<true, kOutF32><<<grid, 128, sm, st>>>(a);
-    else matmul_w4_exact_kernel<true, kOutF16Widen><<<grid, 128, sm, st>>>(a);
+    if (out_mode == kOutF16) matmul_w4_exact_kernel<true, kOutF16><<<grid, 256, sm, st>>>(a);
+    else if (out_mode == kOutF32) matmul_w4_exact_kernel<true, kOutF32><<<grid, 256, sm, st>>>(a);
+    else matmul_w4_exact_kernel<true, kOutF16Widen><<<grid, 256, sm, st>>>(a);
   } else {
-    if (out_mode == kOutF16) matmul_w4_exact_kernel<false, kOutF16><<<grid, 128, sm, st>>>(a);
-    else if (out_mode == kOutF32) matmul_w4_exact_kernel<false, kOutF32><<<grid, 128, sm, st>>>(a);
+    if (out_mode == kOutF16) matmul_w4_exact_kernel<false, kOutF16><<<grid, 256, sm, st>>>(a);
+    else if (out_mode == kOutF32) matmul_w4_exact_kernel<false, kOutF32><<<grid, 256, sm, st>>>(a);
     else return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

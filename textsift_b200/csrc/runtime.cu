@@ -16,6 +16,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <map>
 #include <memory>
 #include <string>
@@ -207,6 +208,8 @@ struct Workspace {
   DevArr<int32_t> ridx;
   DevArr<int> counts, seg_end, perm_tok, route_pos, n_tiles;
   DevArr<int4> tiles;
+  DevArr<int2> atiles;
+  std::vector<int2> atiles_host;
   DevArr<uint16_t> aperm16, glu16;
   DevArr<float> aperm32, gu32, glu32, down32;
   DevArr<float> logits;
@@ -232,6 +235,17 @@ struct ts_cuda {
   // pinned staging for the host-pointer forward
   uint8_t* pin = nullptr;
   size_t pin_bytes = 0;
+  // when set, each layer's top-k experts are copied here ([n_layers][T][top_k])
+  int32_t* trace_topk = nullptr;
+  // kernel launches issued by forwards / MoE ops (ts_cuda_profile_read)
+  uint64_t n_launch = 0;
+  // optional per-phase CUDA-event timing (ts_cuda_profile)
+  bool prof = false;
+  struct Mark { int phase; cudaEvent_t a, b; uint64_t flops; };
+  std::vector<Mark> marks;
+  std::vector<cudaEvent_t> ev_pool;
+  double ph_ms[TS_PHASE_COUNT] = {0};
+  uint64_t ph_launch[TS_PHASE_COUNT] = {0}, ph_flops[TS_PHASE_COUNT] = {0};
 };
 
 struct ts_cuda_w4 {
@@ -346,11 +360,13 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.glu16.alloc(R * F));
     TS_CUDA_TRY(w.down32.alloc(R * D));
     TS_CUDA_TRY(w.logits.alloc(T * c.n_classes));
+    TS_CUDA_TRY(w.qkv16.alloc(T * (Q + 2 * KV)));
+    TS_CUDA_TRY(w.atiles.alloc(ts::attention_max_tiles((uint32_t)T, (uint32_t)T)));
+    w.atiles_host.resize(ts::attention_max_tiles((uint32_t)T, (uint32_t)T));
     w.cap = (uint32_t)T;
   }
   if (exact && !w.exact_ready) {
     TS_CUDA_TRY(w.hf32.alloc(T * D));
-    TS_CUDA_TRY(w.qkv16.alloc(T * (Q + 2 * KV)));
     TS_CUDA_TRY(w.aperm32.alloc(R * D));
     TS_CUDA_TRY(w.gu32.alloc(R * 2 * F));
     TS_CUDA_TRY(w.glu32.alloc(R * F));
@@ -365,10 +381,45 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     if (e_ != cudaSuccess) return fail(TS_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_));        \
   } while (0)
 
+cudaEvent_t pool_event(ts_cuda* h) {
+  if (!h->ev_pool.empty()) {
+    cudaEvent_t e = h->ev_pool.back();
+    h->ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Brackets the launches of one phase with CUDA events when profiling is on
+// and counts kernel launches always.
+struct Phase {
+  ts_cuda* h;
+  cudaStream_t st;
+  int phase;
+  uint64_t flops;
+  cudaEvent_t a = nullptr;
+  Phase(ts_cuda* h_, cudaStream_t st_, int ph, uint64_t fl, int launches) : h(h_), st(st_), phase(ph), flops(fl) {
+    h->n_launch += (uint64_t)launches;
+    if (h->prof) {
+      a = pool_event(h);
+      cudaEventRecord(a, st);
+    }
+  }
+  ~Phase() {
+    if (a) {
+      cudaEvent_t b = pool_event(h);
+      cudaEventRecord(b, st);
+      h->marks.push_back({phase, a, b, flops});
+    }
+  }
+};
+
 // The MoE half of a block: routing from n32 (f32), experts, deterministic
 // combine.  res == nullptr writes the bare MoE output fp16(K * sum w e(x)).
 int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, const uint16_t* res, uint16_t* out,
-             uint32_t T, const int* rloc, const int* rlen, bool exact, cudaStream_t st) {
+             uint32_t T, const int* rloc, const int* rlen, bool exact, cudaStream_t st, int layer) {
   Workspace& w = h->ws;
   const ts_cuda_cfg& c = h->cfg;
   const uint32_t D = c.d_model, K = c.top_k, E = c.n_experts, F = c.d_ff;
@@ -377,24 +428,40 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
   // router logits in the reference order, then top-k
   ts::ExactArgs ra = L.router.exact();
   ra.x = n32; ra.ldx = D; ra.M = T; ra.rloc = rloc; ra.rlen = rlen; ra.out = w.rlogits.p; ra.ldo = E;
-  TS_K(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
-  TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, T, E, K, st));
-  TS_K(ts::launch_moe_permute(w.ridx.p, T, K, E, w.counts.p, w.perm_tok.p, w.route_pos.p, w.tiles.p, w.n_tiles.p,
-                              w.seg_end.p, st));
+  {
+    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, 4);
+    TS_K(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
+    TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, T, E, K, st));
+    TS_K(ts::launch_moe_permute(w.ridx.p, T, K, E, w.counts.p, w.perm_tok.p, w.route_pos.p, w.tiles.p, w.n_tiles.p,
+                                w.seg_end.p, st));
+  }
+  if (h->trace_topk && layer >= 0)
+    TS_K(cudaMemcpyAsync(h->trace_topk + (size_t)layer * T * K, w.ridx.p, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
+  const uint64_t fl_gu = 2ull * R * (2ull * F) * D, fl_dn = 2ull * R * D * F;
   if (!exact) {
-    TS_K(ts::launch_gather_rows(xn16, w.aperm16.p, w.perm_tok.p, nullptr, R, D * 2, st));
+    {
+      Phase p(h, st, TS_PHASE_OTHER, 0, 1);
+      TS_K(ts::launch_gather_rows(xn16, w.aperm16.p, w.perm_tok.p, nullptr, R, D * 2, st));
+    }
     CUtensorMap ta, tg;
     if (!ts::make_act_tmap(&ta, w.aperm16.p, R, D) || !ts::make_act_tmap(&tg, w.glu16.p, R, F))
       return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the expert operands");
     ts::GemmArgs g;
     g.tiles = w.tiles.p; g.n_tiles = w.n_tiles.p; g.err = h->err.p;
     g.out0 = w.glu16.p; g.ld0 = F;
-    TS_K(ts::launch_gemm_w4_tc(L.gate_up.tiles(), ta, g, ts::kEpiSwiglu, grid_tiles, st));
+    {
+      Phase p(h, st, TS_PHASE_EXPERT_GATE_UP, fl_gu, 1);
+      TS_K(ts::launch_gemm_w4_tc(L.gate_up.tiles(), ta, g, ts::kEpiSwiglu, grid_tiles, st));
+    }
     ts::GemmArgs g2;
     g2.tiles = w.tiles.p; g2.n_tiles = w.n_tiles.p; g2.err = h->err.p;
     g2.out0 = w.down32.p; g2.ld0 = D;
-    TS_K(ts::launch_gemm_w4_tc(L.down.tiles(), tg, g2, ts::kEpiF32, grid_tiles, st));
+    {
+      Phase p(h, st, TS_PHASE_EXPERT_DOWN, fl_dn, 1);
+      TS_K(ts::launch_gemm_w4_tc(L.down.tiles(), tg, g2, ts::kEpiF32, grid_tiles, st));
+    }
   } else {
+    Phase p(h, st, TS_PHASE_EXPERT_GATE_UP, fl_gu + fl_dn, 4);
     TS_K(ts::launch_gather_rows(n32, w.aperm32.p, w.perm_tok.p, nullptr, R, D * 4, st));
     ts::ExactArgs ga = L.gate_up.exact();
     ga.x = w.aperm32.p; ga.ldx = D; ga.tiles = w.tiles.p; ga.n_tiles = w.n_tiles.p; ga.seg_end = w.seg_end.p;
@@ -406,7 +473,10 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
     da.out = w.down32.p; da.ldo = D;
     TS_K(ts::launch_matmul_exact(da, true, ts::kOutF32, grid_tiles, st));
   }
-  TS_K(ts::launch_moe_combine(w.down32.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E, st));
+  {
+    Phase p(h, st, TS_PHASE_OTHER, 0, 1);
+    TS_K(ts::launch_moe_combine(w.down32.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E, st));
+  }
   return TS_OK;
 }
 
@@ -430,8 +500,18 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   const uint32_t D = c.d_model, Q = c.n_heads * c.head_dim, KV = c.n_kv_heads * c.head_dim;
 
   TS_K(cudaMemcpyAsync(w.offs.p, offs, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st));
-  TS_K(ts::launch_seq_info(w.offs.p, n_seqs, T, w.pos.p, w.sstart.p, w.slen.p, st));
-  TS_K(ts::launch_embed(h->embed_int4.p, h->embed_scales.p, h->embed_zp.p, d_ids, w.x0.p, T, c.vocab, D, st));
+  {
+    Phase p(h, st, TS_PHASE_OTHER, 0, 2);
+    TS_K(ts::launch_seq_info(w.offs.p, n_seqs, T, w.pos.p, w.sstart.p, w.slen.p, st));
+    TS_K(ts::launch_embed(h->embed_int4.p, h->embed_scales.p, h->embed_zp.p, d_ids, w.x0.p, T, c.vocab, D, st));
+  }
+  uint64_t band_pairs = 0;  // sum over tokens of the keys each query attends (attention flops)
+  for (uint32_t s = 0; s < n_seqs; s++) {
+    const uint64_t n = offs[s + 1] - offs[s], W = c.window;
+    for (uint64_t t = 0; t < n; t++) band_pairs += std::min<uint64_t>(n, t + W + 1) - (t > W ? t - W : 0);
+  }
+  const uint64_t fl_qkv = 2ull * T * (Q + 2 * KV) * D, fl_o = 2ull * T * D * Q;
+  const uint64_t fl_attn = 4ull * c.n_heads * c.head_dim * band_pairs;
 
   CUtensorMap t_xn, t_attn;
   if (!exact) {
@@ -442,6 +522,13 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   aa.q = w.q.p; aa.k = w.k.p; aa.v = w.v.p; aa.mask = d_mask; aa.out = w.attn.p;
   aa.sstart = w.sstart.p; aa.slen = w.slen.p; aa.T = T; aa.Hq = c.n_heads; aa.Hkv = c.n_kv_heads;
   aa.hd = c.head_dim; aa.window = c.window; aa.err = h->err.p;
+  if (!exact) {
+    uint32_t nt = 0;
+    ts::attention_tiles(offs, n_seqs, w.atiles_host.data(), &nt);
+    TS_K(cudaMemcpyAsync(w.atiles.p, w.atiles_host.data(), (size_t)nt * sizeof(int2), cudaMemcpyHostToDevice, st));
+    aa.tiles = w.atiles.p;
+    aa.n_tiles = nt;
+  }
 
   uint16_t* src = w.x0.p;
   uint16_t* dst = w.x1.p;
@@ -450,18 +537,34 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
     LayerDev& L = *h->layers[li];
     aa.sinks = L.sinks.p;
     if (!exact) {
-      TS_K(ts::launch_rmsnorm(src, L.ln1.p, nullptr, w.xn16.p, T, D, c.eps, st));
+      {
+        Phase p(h, st, TS_PHASE_OTHER, 0, 1);
+        TS_K(ts::launch_rmsnorm(src, L.ln1.p, nullptr, w.xn16.p, T, D, c.eps, st));
+      }
       ts::GemmArgs g;
-      g.M = T; g.err = h->err.p;
-      g.out0 = w.q.p; g.ld0 = Q; g.out1 = w.k.p; g.ld1 = KV; g.out2 = w.v.p; g.ld2 = KV;
-      g.q_cols = Q; g.k_cols = KV; g.pos = w.pos.p; g.rope_cos = h->rope_cos.p; g.rope_sin = h->rope_sin.p;
-      TS_K(ts::launch_gemm_w4_tc(L.qkv.tiles(), t_xn, g, ts::kEpiQkvRope, mt, st));
-      TS_K(ts::launch_attention_tc(aa, st));
+      g.M = T; g.err = h->err.p; g.out0 = w.qkv16.p; g.ld0 = Q + 2 * KV;
+      {
+        Phase p(h, st, TS_PHASE_QKV, fl_qkv, 2);
+        TS_K(ts::launch_gemm_w4_tc(L.qkv.tiles(), t_xn, g, ts::kEpiF16, mt, st));
+        TS_K(ts::launch_split_rope(w.qkv16.p, w.q.p, w.k.p, w.v.p, w.pos.p, h->rope_cos.p, h->rope_sin.p, T, Q, KV,
+                                   KV, c.head_dim, st));
+      }
+      {
+        Phase p(h, st, TS_PHASE_ATTENTION, fl_attn, 1);
+        TS_K(ts::launch_attention_tc(aa, st));
+      }
       ts::GemmArgs go;
       go.M = T; go.err = h->err.p; go.out0 = w.o16.p; go.ld0 = D;
-      TS_K(ts::launch_gemm_w4_tc(L.o.tiles(), t_attn, go, ts::kEpiF16, mt, st));
-      TS_K(ts::launch_add_rmsnorm(src, w.o16.p, L.ln2.p, w.res2.p, w.n32.p, w.xn16.p, T, D, c.eps, st));
+      {
+        Phase p(h, st, TS_PHASE_O, fl_o, 1);
+        TS_K(ts::launch_gemm_w4_tc(L.o.tiles(), t_attn, go, ts::kEpiF16, mt, st));
+      }
+      {
+        Phase p(h, st, TS_PHASE_OTHER, 0, 1);
+        TS_K(ts::launch_add_rmsnorm(src, w.o16.p, L.ln2.p, w.res2.p, w.n32.p, w.xn16.p, T, D, c.eps, st));
+      }
     } else {
+      Phase p(h, st, TS_PHASE_OTHER, fl_qkv + fl_o + fl_attn, 6);
       TS_K(ts::launch_rmsnorm(src, L.ln1.p, w.hf32.p, nullptr, T, D, c.eps, st));
       ts::ExactArgs qa = L.qkv.exact();
       qa.x = w.hf32.p; qa.ldx = D; qa.M = T; qa.rloc = w.pos.p; qa.rlen = w.slen.p; qa.out = w.qkv16.p;
@@ -475,10 +578,11 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
       TS_K(ts::launch_matmul_exact(oa, false, ts::kOutF16, mt, st));
       TS_K(ts::launch_add_rmsnorm(src, w.o16.p, L.ln2.p, w.res2.p, w.n32.p, nullptr, T, D, c.eps, st));
     }
-    rc = moe_half(h, L, w.n32.p, w.xn16.p, w.res2.p, dst, T, w.pos.p, w.slen.p, exact, st);
+    rc = moe_half(h, L, w.n32.p, w.xn16.p, w.res2.p, dst, T, w.pos.p, w.slen.p, exact, st, (int)li);
     if (rc) return rc;
     std::swap(src, dst);
   }
+  Phase p(h, st, TS_PHASE_OTHER, 2ull * T * c.n_classes * D, 2);
   TS_K(ts::launch_rmsnorm(src, h->final_norm.p, w.n32.p, nullptr, T, D, c.eps, st));
   ts::ExactArgs sa = h->score.exact();
   sa.x = w.n32.p; sa.ldx = D; sa.M = T; sa.rloc = w.pos.p; sa.rlen = w.slen.p; sa.out = d_logits; sa.ldo = c.n_classes;
@@ -727,6 +831,15 @@ int ts_cuda_forward_packed(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask
   return TS_OK;
 }
 
+int ts_cuda_forward_trace(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
+                          uint32_t n_seqs, float* logits, int32_t* topk_trace) {
+  if (!h || !topk_trace) return fail(TS_ERR_ARG, "ts_cuda_forward_trace: null argument");
+  h->trace_topk = topk_trace;
+  int rc = ts_cuda_forward_packed(h, ids, mask, seq_offsets, n_seqs, logits);
+  h->trace_topk = nullptr;
+  return rc;
+}
+
 int ts_cuda_forward(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, uint32_t T, float* logits) {
   if (T == 0) return TS_OK;
   const uint32_t offs[2] = {0, T};
@@ -744,12 +857,53 @@ int ts_cuda_check(ts_cuda_t* h, void* stream) {
 
 const char* ts_cuda_device_name(ts_cuda_t* h) { return h ? h->name.c_str() : ""; }
 
+int ts_cuda_profile(ts_cuda_t* h, int32_t enable) {
+  if (!h) return fail(TS_ERR_ARG, "ts_cuda_profile: null handle");
+  DevGuard g(h->cfg.device);
+  cudaStreamSynchronize(h->stream);
+  for (auto& m : h->marks) {
+    h->ev_pool.push_back(m.a);
+    h->ev_pool.push_back(m.b);
+  }
+  h->marks.clear();
+  for (int i = 0; i < TS_PHASE_COUNT; i++) { h->ph_ms[i] = 0; h->ph_launch[i] = 0; h->ph_flops[i] = 0; }
+  h->prof = enable != 0;
+  h->n_launch = 0;
+  return TS_OK;
+}
+
+int ts_cuda_profile_read(ts_cuda_t* h, double* ms, uint64_t* launches, uint64_t* flops, uint64_t* total_launches) {
+  if (!h) return fail(TS_ERR_ARG, "ts_cuda_profile_read: null handle");
+  DevGuard g(h->cfg.device);
+  for (auto& m : h->marks) {
+    float t = 0.0f;
+    cudaError_t e = cudaEventSynchronize(m.b);
+    if (e != cudaSuccess) return fail(TS_ERR_CUDA, "profile event: %s", cudaGetErrorString(e));
+    cudaEventElapsedTime(&t, m.a, m.b);
+    h->ph_ms[m.phase] += t;
+    h->ph_launch[m.phase] += 1;
+    h->ph_flops[m.phase] += m.flops;
+    h->ev_pool.push_back(m.a);
+    h->ev_pool.push_back(m.b);
+  }
+  h->marks.clear();
+  for (int i = 0; i < TS_PHASE_COUNT; i++) {
+    if (ms) ms[i] = h->ph_ms[i];
+    if (launches) launches[i] = h->ph_launch[i];
+    if (flops) flops[i] = h->ph_flops[i];
+  }
+  if (total_launches) *total_launches = h->n_launch;
+  return TS_OK;
+}
+
 void ts_cuda_destroy(ts_cuda_t* h) {
   if (!h) return;
   {
     DevGuard g(h->cfg.device);
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->pin) cudaFreeHost(h->pin);
+    for (auto& m : h->marks) { cudaEventDestroy(m.a); cudaEventDestroy(m.b); }
+    for (auto e : h->ev_pool) cudaEventDestroy(e);
     h->layers.clear();
     if (h->stream) cudaStreamDestroy(h->stream);
     h->stream = nullptr;
@@ -889,7 +1043,7 @@ int ts_cuda_op_moe(ts_cuda_t* h, uint32_t layer, const float* d_x, uint16_t* d_o
   if (rc) return rc;
   const ts_cuda_cfg& c = h->cfg;
   if (!exact) TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, h->ws.xn16.p, (size_t)T * c.d_model, st));
-  rc = moe_half(h, *h->layers[layer], d_x, h->ws.xn16.p, nullptr, d_out, T, nullptr, nullptr, exact, st);
+  rc = moe_half(h, *h->layers[layer], d_x, h->ws.xn16.p, nullptr, d_out, T, nullptr, nullptr, exact, st, -1);
   if (rc) return rc;
   if (d_idx) TS_CUDA_TRY(cudaMemcpyAsync(d_idx, h->ws.ridx.p, (size_t)T * c.top_k * 4, cudaMemcpyDeviceToDevice, st));
   if (d_w) TS_CUDA_TRY(cudaMemcpyAsync(d_w, h->ws.rw.p, (size_t)T * c.top_k * 4, cudaMemcpyDeviceToDevice, st));
@@ -925,7 +1079,16 @@ int ts_cuda_op_banded_attention(const uint16_t* d_q, const uint16_t* d_k, const 
   a.sstart = ss.p; a.slen = sl.p; a.T = T; a.Hq = Hq; a.Hkv = Hkv; a.hd = head_dim; a.window = window;
   if (mode == TS_MODE_FAST) {
     if (head_dim != 64 || Hq / Hkv > 7) return fail(TS_ERR_UNSUPPORTED, "tensor-core attention needs head_dim 64, group <= 7");
+    std::vector<int2> th(ts::attention_max_tiles(T, ns));
+    uint32_t ntl = 0;
+    ts::attention_tiles(ho, ns, th.data(), &ntl);
+    DevArr<int2> td;
+    TS_CUDA_TRY(td.alloc(ntl));
+    TS_CUDA_TRY(cudaMemcpyAsync(td.p, th.data(), (size_t)ntl * sizeof(int2), cudaMemcpyHostToDevice, st));
+    a.tiles = td.p;
+    a.n_tiles = ntl;
     TS_CUDA_TRY(ts::launch_attention_tc(a, st));
+    TS_CUDA_TRY(cudaStreamSynchronize(st));
   } else {
     TS_CUDA_TRY(ts::launch_attention_exact(a, st));
   }

@@ -62,6 +62,13 @@ __device__ __forceinline__ float f16_ieee_to_f32(uint16_t h) {
   return __half2float(__ushort_as_half(h));
 }
 
+// The reference's exact exponential (Zig @exp on f32, a correctly rounded in
+// practice expf) for the few entries that use it: the router softmax over k
+// (wasm_exports.zig:919-958) and the 0-3 tail entries of each attention row
+// (1354-1358).  Computed in double and rounded once to f32, which gives the
+// correctly rounded result.
+__device__ __forceinline__ float expf_ref(float x) { return (float)exp((double)x); }
+
 // wasm_exports.zig:812-838, one lane: exp(x) for x <= 0 via 2^(x*log2 e),
 // floor split, 5th-degree Horner polynomial (fused steps), exponent twiddle.
 // This is the reference's own published approximation, restated.

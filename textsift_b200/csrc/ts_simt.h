@@ -69,9 +69,17 @@ struct AttnArgs {
   uint16_t* out = nullptr;       // [T, Hq*hd]
   const int* sstart = nullptr;
   const int* slen = nullptr;
+  // tensor-core path: 16-query tiles {first query, end of its sequence}, each
+  // tile inside one sequence and aligned to the sequence start, so the key
+  // chunking (and every rounding) is the same however sequences are packed
+  const int2* tiles = nullptr;
+  uint32_t n_tiles = 0;
   uint32_t T = 0, Hq = 0, Hkv = 0, hd = 0, window = 0;
   int* err = nullptr;
 };
+// Host: the tensor-core tile list for packed sequences (offs has n_seqs + 1 entries).
+void attention_tiles(const uint32_t* offs, uint32_t n_seqs, int2* out, uint32_t* n_out);
+uint32_t attention_max_tiles(uint32_t T, uint32_t n_seqs);
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st);     // mma.sync tensor-core path
 cudaError_t launch_attention_exact(const AttnArgs& a, cudaStream_t st);  // reference-order CUDA-core path
 
