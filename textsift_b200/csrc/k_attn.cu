@@ -156,7 +156,9 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t h = hk * group + (uint32_t)warp;
   const int kb0 = (int)q0 - (int)W;  // global key index of smem row 0
-  const size_t kstr = (size_t)a.Hkv * kHD;
+  const size_t kld = a.k_ld ? a.k_ld : (size_t)a.Hkv * kHD;
+  const size_t vld = a.v_ld ? a.v_ld : (size_t)a.Hkv * kHD;
+  const size_t qld = a.q_ld ? a.q_ld : (size_t)a.Hq * kHD;
 
   // ---- stage the K/V band (zero outside [0, T)) ----
   const uint32_t sK_u = smem_u32(sK), sV_u = smem_u32(sV);
@@ -164,9 +166,9 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
     const uint32_t r = i >> 3, c = i & 7u;
     const int key = kb0 + (int)r;
     const bool in = key >= 0 && key < (int)a.T;
-    const size_t g = (size_t)(in ? key : 0) * kstr + (size_t)hk * kHD + c * 8;
-    cp_async16(sK_u + kv_off(r, c), a.k + g, in ? 16u : 0u);
-    cp_async16(sV_u + kv_off(r, c), a.v + g, in ? 16u : 0u);
+    const size_t kr = (size_t)(in ? key : 0);
+    cp_async16(sK_u + kv_off(r, c), a.k + kr * kld + (size_t)hk * kHD + c * 8, in ? 16u : 0u);
+    cp_async16(sV_u + kv_off(r, c), a.v + kr * vld + (size_t)hk * kHD + c * 8, in ? 16u : 0u);
   }
   for (uint32_t r = threadIdx.x; r < band; r += blockDim.x) {
     const int key = kb0 + (int)r;
@@ -222,16 +224,24 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
   // ---- Q fragments (A operand), straight from global ----
   uint32_t qa[4][4];
   {
-    const uint16_t* qg0 = a.q + (size_t)(q0 + g) * a.Hq * kHD + (size_t)h * kHD;
-    const uint16_t* qg1 = a.q + (size_t)(q0 + g + 8) * a.Hq * kHD + (size_t)h * kHD;
+    const uint16_t* qg[2] = {a.q + (size_t)(q0 + g) * qld + (size_t)h * kHD,
+                             a.q + (size_t)(q0 + g + 8) * qld + (size_t)h * kHD};
 #pragma unroll
-    for (int kk = 0; kk < 4; kk++) {
-      const int c0 = kk * 16 + 2 * tq;
-      qa[kk][0] = r_ok[0] ? *reinterpret_cast<const uint32_t*>(qg0 + c0) : 0u;
-      qa[kk][1] = r_ok[1] ? *reinterpret_cast<const uint32_t*>(qg1 + c0) : 0u;
-      qa[kk][2] = r_ok[0] ? *reinterpret_cast<const uint32_t*>(qg0 + c0 + 8) : 0u;
-      qa[kk][3] = r_ok[1] ? *reinterpret_cast<const uint32_t*>(qg1 + c0 + 8) : 0u;
-    }
+    for (int kk = 0; kk < 4; kk++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        // fragment register j: row g + 8*(j&1), columns c, c+1 (one RoPE pair)
+        const int ri = j & 1;
+        const int c = kk * 16 + 2 * tq + 8 * (j >> 1);
+        uint32_t ab = r_ok[ri] ? *reinterpret_cast<const uint32_t*>(qg[ri] + c) : 0u;
+        if (a.q_pos && r_ok[ri]) {
+          const size_t trow = (size_t)a.q_pos[q0 + g + 8 * ri] * (kHD / 2) + (c >> 1);
+          uint16_t lo = (uint16_t)(ab & 0xffffu), hi = (uint16_t)(ab >> 16);
+          rope_pair_ref(lo, hi, a.rope_cos[trow], a.rope_sin[trow]);
+          ab = (uint32_t)lo | ((uint32_t)hi << 16);
+        }
+        qa[kk][j] = ab;
+      }
   }
   const float sink = a.sinks[h];
 
@@ -335,8 +345,8 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
     uint16_t* orow = a.out + (size_t)(q0 + g + 8 * ri) * a.Hq * kHD + (size_t)h * kHD;
 #pragma unroll
     for (int dt = 0; dt < 8; dt++) {
-      const uint16_t lo16 = f32_to_f16_ref(__fmul_rn(o[dt][2 * ri], inv[ri]));
-      const uint16_t hi16 = f32_to_f16_ref(__fmul_rn(o[dt][2 * ri + 1], inv[ri]));
+      const uint16_t lo16 = f32_to_f16_fast(__fmul_rn(o[dt][2 * ri], inv[ri]));
+      const uint16_t hi16 = f32_to_f16_fast(__fmul_rn(o[dt][2 * ri + 1], inv[ri]));
       *reinterpret_cast<uint32_t*>(orow + dt * 8 + 2 * tq) = (uint32_t)lo16 | ((uint32_t)hi16 << 16);
     }
   }

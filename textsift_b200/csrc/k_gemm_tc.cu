@@ -70,19 +70,6 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
 
 __device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
 
-// The reference's RoPE on one (a, b) fp16 pair: three fp16 roundings per
-// output (wasm_exports.zig:1488-1498).
-__device__ __forceinline__ void rope_pair_ref(uint16_t& a16, uint16_t& b16, uint16_t c16, uint16_t s16) {
-  float c = f16_ref_to_f32(c16), s = f16_ref_to_f32(s16);
-  float a = f16_ref_to_f32(a16), b = f16_ref_to_f32(b16);
-  float ac = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(a, c)));
-  float bs = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(b, s)));
-  float bc = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(b, c)));
-  float as = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(a, s)));
-  a16 = f32_to_f16_ref(__fsub_rn(ac, bs));
-  b16 = f32_to_f16_ref(__fadd_rn(bc, as));
-}
-
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t grow, uint32_t ncol0,
                                                     const uint16_t* bias, const uint32_t (&v)[32]) {
@@ -99,13 +86,13 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
     if (full) {
       uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 16; j++) w[j] = pack_h2(f32_to_f16_ref(acc[2 * j]), f32_to_f16_ref(acc[2 * j + 1]));
+      for (int j = 0; j < 16; j++) w[j] = pack_h2(f32_to_f16_fast(acc[2 * j]), f32_to_f16_fast(acc[2 * j + 1]));
       uint4* o4 = reinterpret_cast<uint4*>(o);
 #pragma unroll
       for (int q = 0; q < 4; q++) o4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
     } else {
       for (int j = 0; j < 32; j++)
-        if (ncol0 + j < a.N) o[j] = f32_to_f16_ref(acc[j]);
+        if (ncol0 + j < a.N) o[j] = f32_to_f16_fast(acc[j]);
     }
   } else if constexpr (EPI == kEpiF32) {
     float* o = reinterpret_cast<float*>(a.out0) + (size_t)grow * a.ld0 + ncol0;
@@ -117,12 +104,16 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
       for (int j = 0; j < 32; j++)
         if (ncol0 + j < a.N) o[j] = acc[j];
     }
+  } else if constexpr (EPI == kEpiF16Widen) {
+    float* o = reinterpret_cast<float*>(a.out0) + (size_t)grow * a.ld0 + ncol0;
+    for (int j = 0; j < 32; j++)
+      if (ncol0 + j < a.N) o[j] = f16_ieee_to_f32(f32_to_f16_fast(acc[j]));
   } else if constexpr (EPI == kEpiQkvRope) {
     // Columns [0,q_cols) are Q, [q_cols, q_cols+k_cols) K, the rest V.  Every
     // 32-column chunk lies inside one 64-wide head of one region.
     uint16_t h[32];
 #pragma unroll
-    for (int j = 0; j < 32; j++) h[j] = f32_to_f16_ref(acc[j]);
+    for (int j = 0; j < 32; j++) h[j] = f32_to_f16_fast(acc[j]);
     uint16_t* o;
     if (ncol0 < a.q_cols + a.k_cols) {
       const int p0 = (int)(ncol0 & 63u) >> 1;
@@ -506,6 +497,7 @@ cudaError_t launch_gemm_w4_tc(const W4Tiles& w, const CUtensorMap& tmap_a, GemmA
       case kEpiF32: return launch_one<128, kEpiF32>(tmap_a, args, w.n_tiles, grid_m, st);
       case kEpiQkvRope: return launch_one<128, kEpiQkvRope>(tmap_a, args, w.n_tiles, grid_m, st);
       case kEpiSwiglu: return launch_one<128, kEpiSwiglu>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiF16Widen: return launch_one<128, kEpiF16Widen>(tmap_a, args, w.n_tiles, grid_m, st);
     }
   } else if (w.BN == 256) {
     switch (epi) {

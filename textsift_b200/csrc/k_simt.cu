@@ -81,25 +81,48 @@ __global__ void rmsnorm_kernel(const uint16_t* __restrict__ a, const uint16_t* _
                                const uint16_t* __restrict__ gamma, uint16_t* __restrict__ sum_out,
                                float* __restrict__ out32, uint16_t* __restrict__ out16, uint32_t T, uint32_t D,
                                float eps) {
-  extern __shared__ float rs_smem[];  // [warps][D] f32 (sum before rounding) + [warps][D] f32 (value read back)
+  extern __shared__ float rs_smem[];  // per warp: [D] f32 squared-sum source, [D] f32 value read back
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t row = blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= T) return;
-  float* xs = rs_smem + (size_t)warp * 2 * D;  // squares source
-  float* xr = xs + D;                          // value used by pass 2
-  const uint16_t* ar = a + (size_t)row * D;
-  for (uint32_t d = lane; d < D; d += 32) {
-    float v = f16_ref_to_f32(ar[d]);
+  float* xs = rs_smem + (size_t)warp * 2 * D;
+  float* xr = xs + D;
+  const size_t base = (size_t)row * D;
+  // D is a multiple of 8: 16-byte accesses
+  for (uint32_t c = lane; c < D / 8; c += 32) {
+    const uint4 av = *reinterpret_cast<const uint4*>(a + base + 8 * c);
+    const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+    uint32_t bw[4] = {0, 0, 0, 0}, sw[4];
     if constexpr (ADD) {
-      float sv = __fadd_rn(v, f16_ref_to_f32(b[(size_t)row * D + d]));
-      uint16_t s16 = f32_to_f16_ref(sv);
-      sum_out[(size_t)row * D + d] = s16;
-      xs[d] = sv;
-      xr[d] = f16_ref_to_f32(s16);
-    } else {
-      xs[d] = v;
-      xr[d] = v;
+      const uint4 bv = *reinterpret_cast<const uint4*>(b + base + 8 * c);
+      bw[0] = bv.x; bw[1] = bv.y; bw[2] = bv.z; bw[3] = bv.w;
     }
+    float vs[8], vr[8];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      uint16_t s16[2] = {0, 0};
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        const float v = f16_ref_to_f32((uint16_t)(aw[j] >> (16 * hh)));
+        if constexpr (ADD) {
+          const float sv = __fadd_rn(v, f16_ref_to_f32((uint16_t)(bw[j] >> (16 * hh))));
+          s16[hh] = f32_to_f16_fast(sv);
+          vs[2 * j + hh] = sv;
+          vr[2 * j + hh] = f16_ref_to_f32(s16[hh]);
+        } else {
+          vs[2 * j + hh] = v;
+          vr[2 * j + hh] = v;
+        }
+      }
+      sw[j] = (uint32_t)s16[0] | ((uint32_t)s16[1] << 16);
+    }
+    float4* xs4 = reinterpret_cast<float4*>(xs + 8 * c);
+    float4* xr4 = reinterpret_cast<float4*>(xr + 8 * c);
+    xs4[0] = make_float4(vs[0], vs[1], vs[2], vs[3]);
+    xs4[1] = make_float4(vs[4], vs[5], vs[6], vs[7]);
+    xr4[0] = make_float4(vr[0], vr[1], vr[2], vr[3]);
+    xr4[1] = make_float4(vr[4], vr[5], vr[6], vr[7]);
+    if constexpr (ADD) *reinterpret_cast<uint4*>(sum_out + base + 8 * c) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
   }
   __syncwarp();
   const uint32_t D4 = D & ~3u;  // the 4-lane body covers [0, D4), the scalar tail [D4, D)
@@ -112,24 +135,42 @@ __global__ void rmsnorm_kernel(const uint16_t* __restrict__ a, const uint16_t* _
   for (uint32_t d = D4; d < D; d++) sumsq = __fadd_rn(sumsq, __fmul_rn(xs[d], xs[d]));
   const float d_inv = __fdiv_rn(1.0f, (float)D);
   const float inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(sumsq, d_inv), eps)));
-  for (uint32_t d = lane; d < D; d += 32) {
-    float y = __fmul_rn(__fmul_rn(xr[d], inv_rms), f16_ref_to_f32(gamma[d]));
-    if (out32) out32[(size_t)row * D + d] = y;
-    if (out16) out16[(size_t)row * D + d] = __half_as_ushort(__float2half_rn(y));
+  for (uint32_t c = lane; c < D / 4; c += 32) {
+    const uint2 gv = *reinterpret_cast<const uint2*>(gamma + 4 * c);
+    const uint16_t g[4] = {(uint16_t)(gv.x & 0xffffu), (uint16_t)(gv.x >> 16), (uint16_t)(gv.y & 0xffffu),
+                           (uint16_t)(gv.y >> 16)};
+    const float4 x4 = *reinterpret_cast<const float4*>(xr + 4 * c);
+    const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+    float y[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) y[j] = __fmul_rn(__fmul_rn(xv[j], inv_rms), f16_ref_to_f32(g[j]));
+    if (out32) *reinterpret_cast<float4*>(out32 + base + 4 * c) = make_float4(y[0], y[1], y[2], y[3]);
+    if (out16) {
+      __half2 lo = __floats2half2_rn(y[0], y[1]), hi = __floats2half2_rn(y[2], y[3]);
+      *reinterpret_cast<uint2*>(out16 + base + 4 * c) =
+          make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    }
   }
 }
 
-// ---------------------------------------------------------------------------
-// Exact-order int4 matmul on CUDA cores (wasm_exports.zig:560-708).
-// Block = 128 output columns; each block walks a 128-row tile in groups of 8
-// rows staged in shared memory.  Row r uses the tile-path order when its
-// index inside its sequence is < 8*floor(len/8), the tail-path order
-// otherwise, exactly as the single-thread reference partitions rows.
-// ---------------------------------------------------------------------------
+// Shared-memory layout of the exact kernel: the 128-column weight tile
+// (packed nibbles, rows padded so that eight consecutive rows hit distinct
+// 16-byte bank groups), its scales and zero points, then two groups of 8
+// activation rows in f32.
+__host__ __device__ inline uint32_t exact_wstride(uint32_t K) { return (K / 2 + 31u) / 32u * 32u + 16u; }
+__host__ __device__ inline size_t exact_smem_bytes(uint32_t K) {
+  const size_t w = 128u * exact_wstride(K), sc = 128u * (K / 32) * 2u, zp = 128u * ((K / 32 + 1) / 2);
+  return ((w + sc + zp + 15u) & ~size_t(15)) + 16u * K * sizeof(float);
+}
+
 template <bool X_F32, int OUT>
 __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a) {
-  extern __shared__ __align__(16) float xs[];  // [2 groups][8 rows][K]
-  const uint32_t K = a.K, nb = K / 32, zs = (nb + 1) / 2;
+  extern __shared__ __align__(16) uint8_t ex_smem[];
+  const uint32_t K = a.K, nb = K / 32, zs = (nb + 1) / 2, wst = exact_wstride(K);
+  uint8_t* sw = ex_smem;
+  uint16_t* ssc = reinterpret_cast<uint16_t*>(ex_smem + 128u * wst);
+  uint8_t* szp = ex_smem + 128u * wst + 128u * nb * 2u;
+  float* xs = reinterpret_cast<float*>(ex_smem + ((128u * wst + 128u * nb * 2u + 128u * zs + 15u) & ~15u));
   uint32_t expert = 0, row0, row_end, seg_start = 0, seg_len = 0;
   const bool grouped = a.tiles != nullptr;
   if (grouped) {
@@ -138,15 +179,34 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
     expert = (uint32_t)t.x; row0 = (uint32_t)t.y; row_end = (uint32_t)t.z; seg_start = (uint32_t)t.w;
     seg_len = (uint32_t)a.seg_end[expert] - seg_start;
   } else {
-    row0 = blockIdx.y * 128u;
-    row_end = min(a.M, row0 + 128u);
+    row0 = blockIdx.y * a.rows_per_block;
+    row_end = min(a.M, row0 + a.rows_per_block);
+  }
+  // ---- stage the weight tile of columns [n_base, n_base + 128) ----
+  const uint32_t n_base = blockIdx.x * 128u;
+  const uint32_t ncols = min(128u, a.N - n_base);
+  {
+    const uint8_t* w0 = a.w_int4 + (size_t)expert * a.w_int4_estride + (size_t)n_base * (K / 2);
+    const uint32_t rowb = K / 2;  // a multiple of 16
+    for (uint32_t i = threadIdx.x; i < ncols * (rowb / 16); i += blockDim.x) {
+      const uint32_t r = i / (rowb / 16), c = i % (rowb / 16);
+      *reinterpret_cast<uint4*>(sw + r * wst + c * 16) = *reinterpret_cast<const uint4*>(w0 + (size_t)r * rowb + c * 16);
+    }
+    const uint16_t* s0 = a.w_scales + (size_t)expert * a.w_scales_estride + (size_t)n_base * nb;
+    for (uint32_t i = threadIdx.x; i < ncols * nb; i += blockDim.x) ssc[i] = s0[i];
+    if (a.w_zp) {
+      const uint8_t* z0 = a.w_zp + (size_t)expert * a.w_zp_estride + (size_t)n_base * zs;
+      for (uint32_t i = threadIdx.x; i < ncols * zs; i += blockDim.x) szp[i] = z0[i];
+    }
   }
   const uint32_t half = threadIdx.x >> 7;  // which 8-row group of a pair this thread works on
-  const uint32_t n = blockIdx.x * 128u + (threadIdx.x & 127u);
-  const bool n_ok = n < a.N;
-  const uint8_t* wr = a.w_int4 + (size_t)expert * a.w_int4_estride + (size_t)(n_ok ? n : 0) * (K / 2);
-  const uint16_t* sr = a.w_scales + (size_t)expert * a.w_scales_estride + (size_t)(n_ok ? n : 0) * nb;
-  const uint8_t* zr = a.w_zp ? a.w_zp + (size_t)expert * a.w_zp_estride + (size_t)(n_ok ? n : 0) * zs : nullptr;
+  const uint32_t nl = threadIdx.x & 127u;
+  const uint32_t n = n_base + nl;
+  const bool n_ok = nl < ncols;
+  const uint8_t* wr = sw + (size_t)(n_ok ? nl : 0) * wst;
+  const uint16_t* sr = ssc + (size_t)(n_ok ? nl : 0) * nb;
+  const uint8_t* zr = szp + (size_t)(n_ok ? nl : 0) * zs;
+  const bool has_zp = a.w_zp != nullptr;
   const float bias = n_ok ? f16_ref_to_f32(a.bias[(size_t)expert * a.bias_estride + n]) : 0.0f;
   float* myx = xs + (size_t)half * 8 * K;
 
@@ -179,7 +239,7 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
     for (uint32_t b = 0; b < nb; b++) {
       const float scale = f16_ref_to_f32(sr[b]);
       int zp = 0;
-      if (zr) { uint8_t zb = zr[b >> 1]; zp = (b & 1) ? (zb >> 4) & 15 : zb & 15; }
+      if (has_zp) { uint8_t zb = zr[b >> 1]; zp = (b & 1) ? (zb >> 4) & 15 : zb & 15; }
       const uint4 pk = *reinterpret_cast<const uint4*>(wr + b * 16);
       const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
       float q[32];
@@ -239,106 +299,163 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
 }
 
 // ---------------------------------------------------------------------------
-// Router top-k: insertion top-k (strict '>', ties keep the lower index,
-// output descending), softmax over k with expf, then x (1/k) as the JS
-// caller does in doubles (exact for k a power of two).
+// Router top-k (wasm_exports.zig:367-426 + 919-958, block.ts:201-206): the
+// k largest logits by (value descending, index ascending) -- exactly the set
+// and order the reference's strict-'>' insertion sort produces -- then softmax
+// over the k values in that order and x (1/k) in double like the JS caller.
+// One warp per token (lane l holds logits l, l+32, ...), 128 tokens per block;
+// each block also counts its routes per expert (hist[block][e]) for the
+// permutation.
 // ---------------------------------------------------------------------------
-__global__ void router_topk_kernel(const float* __restrict__ logits, int32_t* __restrict__ idx,
-                                   float* __restrict__ w, uint32_t T, uint32_t E, uint32_t K, double inv_k) {
-  uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= T) return;
-  const float* row = logits + (size_t)t * E;
-  float ov[8];
-  int oi[8];
-  for (uint32_t i = 0; i < K; i++) { oi[i] = (int)i; ov[i] = row[i]; }
-  for (uint32_t s = 1; s < K; s++)
-    for (uint32_t j = s; j > 0 && ov[j] > ov[j - 1]; j--) {
-      float tv = ov[j]; ov[j] = ov[j - 1]; ov[j - 1] = tv;
-      int ti = oi[j]; oi[j] = oi[j - 1]; oi[j - 1] = ti;
+constexpr uint32_t kRouteChunk = 128;  // tokens per top-k block / permutation chunk
+constexpr uint32_t kMaxExperts = 256;
+
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int32_t* __restrict__ idx,
+                                                          float* __restrict__ w, int* __restrict__ hist, uint32_t T,
+                                                          uint32_t E, uint32_t K, double inv_k) {
+  __shared__ int h[kMaxExperts];
+  for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t t0 = blockIdx.x * kRouteChunk;
+  for (uint32_t tl = (uint32_t)warp; tl < kRouteChunk; tl += blockDim.x >> 5) {
+    const uint32_t t = t0 + tl;
+    if (t >= T) break;
+    const float* row = logits + (size_t)t * E;
+    float v[kMaxExperts / 32];
+    bool avail[kMaxExperts / 32];
+#pragma unroll
+    for (int j = 0; j < (int)(kMaxExperts / 32); j++) {
+      const uint32_t c = lane + 32 * j;
+      avail[j] = c < E;
+      v[j] = avail[j] ? row[c] : 0.0f;
     }
-  for (uint32_t c = K; c < E; c++) {
-    float v = row[c];
-    if (v > ov[K - 1]) {
-      ov[K - 1] = v; oi[K - 1] = (int)c;
-      for (uint32_t j = K - 1; j > 0 && ov[j] > ov[j - 1]; j--) {
-        float tv = ov[j]; ov[j] = ov[j - 1]; ov[j - 1] = tv;
-        int ti = oi[j]; oi[j] = oi[j - 1]; oi[j - 1] = ti;
+    float ov[8];
+    int oi[8];
+    for (uint32_t k = 0; k < K; k++) {
+      float bv = 0.0f;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < (int)(kMaxExperts / 32); j++) {
+        const int c = lane + 32 * j;
+        if (avail[j] && (bi == 0x7fffffff || v[j] > bv || (v[j] == bv && c < bi))) { bv = v[j]; bi = c; }
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ovv = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oii = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oii != 0x7fffffff && (bi == 0x7fffffff || ovv > bv || (ovv == bv && oii < bi))) { bv = ovv; bi = oii; }
+      }
+      ov[k] = bv;
+      oi[k] = bi;
+#pragma unroll
+      for (int j = 0; j < (int)(kMaxExperts / 32); j++)
+        if (lane + 32 * j == bi) avail[j] = false;
+    }
+    // softmax over the k values in order (wasm_exports.zig:919-958): lane c
+    // computes exp of entry c, lane 0 sums them in order
+    float m = ov[0];
+    for (uint32_t c = 1; c < K; c++) if (ov[c] > m) m = ov[c];
+    float my_e = 0.0f;
+#pragma unroll
+    for (uint32_t c = 0; c < 8; c++)
+      if (c < K && (uint32_t)lane == c) my_e = expf_ref(__fsub_rn(ov[c], m));
+    float e[8];
+#pragma unroll
+    for (uint32_t c = 0; c < 8; c++) e[c] = __shfl_sync(0xffffffffu, my_e, c);
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (uint32_t c = 0; c < K; c++) sum = __fadd_rn(sum, e[c]);
+      const float inv = sum > 0.0f ? __fdiv_rn(1.0f, sum) : __fdiv_rn(1.0f, (float)K);
+      for (uint32_t c = 0; c < K; c++) {
+        idx[(size_t)t * K + c] = oi[c];
+        w[(size_t)t * K + c] = (float)((double)__fmul_rn(e[c], inv) * inv_k);
+        atomicAdd(&h[oi[c]], 1);
       }
     }
   }
-  float m = ov[0];
-  for (uint32_t c = 1; c < K; c++) if (ov[c] > m) m = ov[c];
-  float e[8], sum = 0.0f;
-  for (uint32_t c = 0; c < K; c++) { e[c] = expf_ref(__fsub_rn(ov[c], m)); sum = __fadd_rn(sum, e[c]); }
-  const float inv = sum > 0.0f ? __fdiv_rn(1.0f, sum) : __fdiv_rn(1.0f, (float)K);
-  for (uint32_t c = 0; c < K; c++) {
-    idx[(size_t)t * K + c] = oi[c];
-    w[(size_t)t * K + c] = (float)((double)__fmul_rn(e[c], inv) * inv_k);
-  }
+  __syncthreads();
+  if (hist)
+    for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) hist[(size_t)blockIdx.x * E + i] = h[i];
 }
 
 // ---------------------------------------------------------------------------
-// MoE permutation.  count: one block per expert counts its routes.  scatter:
-// one block per expert computes its segment offset and tile offset from the
-// counts, writes its 128-row tiles, and compacts its (token, slot) routes in
-// ascending route order (= ascending token, since a token selects an expert
-// at most once), the order expert.ts:137-145 builds.
+// MoE permutation, stable (ascending token within each expert, the order
+// expert.ts:137-145 builds).  scan: one block; thread e walks the chunk
+// histograms to give each (chunk, expert) its base position, then the expert
+// segments, their 128-row GEMM tiles and the tile count.  place: one block per
+// chunk; a route's rank inside its chunk is the number of earlier tokens of
+// the chunk that chose the same expert (a 128-bit token mask per expert).
 // ---------------------------------------------------------------------------
-__global__ void moe_count_kernel(const int32_t* __restrict__ idx, uint32_t n_routes, int* __restrict__ counts) {
-  const int e = blockIdx.x;
-  int c = 0;
-  for (uint32_t i = threadIdx.x; i < n_routes; i += blockDim.x) c += idx[i] == e;
-  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-  __shared__ int ws[32];
-  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = c;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int s = 0;
-    for (uint32_t i = 0; i < blockDim.x / 32; i++) s += ws[i];
-    counts[e] = s;
+// Exclusive scan of hist[c][e] over chunks c, one warp per expert; total[e].
+__global__ void __launch_bounds__(256) moe_chunk_scan_kernel(int* __restrict__ hist, uint32_t n_chunks, uint32_t E,
+                                                             int* __restrict__ counts) {
+  const uint32_t e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (e >= E) return;
+  int run = 0;
+  for (uint32_t c0 = 0; c0 < n_chunks; c0 += 32) {
+    const uint32_t c = c0 + lane;
+    const int v = c < n_chunks ? hist[(size_t)c * E + e] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (c < n_chunks) hist[(size_t)c * E + e] = run + incl - v;
+    run += __shfl_sync(0xffffffffu, incl, 31);
   }
+  if (lane == 0) counts[e] = run;
 }
 
-__global__ void moe_scatter_kernel(const int32_t* __restrict__ idx, uint32_t n_routes, uint32_t K,
-                                   const int* __restrict__ counts, uint32_t E, int* __restrict__ perm_tok,
-                                   int* __restrict__ route_pos, int4* __restrict__ tiles, int* __restrict__ n_tiles,
-                                   int* __restrict__ seg_end) {
-  const int e = blockIdx.x;
-  __shared__ int s_off, s_tile_off, s_base;
-  __shared__ int wsum[32];
-  if (threadIdx.x == 0) {
-    int off = 0, toff = 0, tot_t = 0;
-    for (int i = 0; i < (int)E; i++) {
-      int c = counts[i];
-      int nt = (c + 127) / 128;
-      if (i < e) { off += c; toff += nt; }
-      tot_t += nt;
-    }
-    s_off = off; s_tile_off = toff; s_base = 0;
-    if (e == 0) *n_tiles = tot_t;
-    seg_end[e] = off + counts[e];
+// Expert segments, their 128-row GEMM tiles and the tile count from counts.
+__global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __restrict__ counts, uint32_t E,
+                                                                   int4* __restrict__ tiles, int* __restrict__ n_tiles,
+                                                                   int* __restrict__ seg_start,
+                                                                   int* __restrict__ seg_end) {
+  __shared__ int off[kMaxExperts + 1], toff[kMaxExperts + 1];
+  const uint32_t e = threadIdx.x;
+  if (e < E) { off[e + 1] = counts[e]; toff[e + 1] = (counts[e] + 127) / 128; }
+  if (e == 0) { off[0] = 0; toff[0] = 0; }
+  __syncthreads();
+  if (e == 0)
+    for (uint32_t i = 1; i <= E; i++) { off[i] += off[i - 1]; toff[i] += toff[i - 1]; }
+  __syncthreads();
+  if (e < E) {
+    const int base = off[e], cnt = off[e + 1] - off[e];
+    seg_start[e] = base;
+    seg_end[e] = off[e + 1];
+    for (int tt = 0; tt * 128 < cnt; tt++)
+      tiles[toff[e] + tt] = make_int4((int)e, base + tt * 128, base + min(cnt, tt * 128 + 128), base);
+  }
+  if (e == 0) *n_tiles = toff[E];
+}
+
+__global__ void __launch_bounds__(kRouteChunk) moe_place_kernel(const int32_t* __restrict__ idx,
+                                                                const int* __restrict__ hist,
+                                                                const int* __restrict__ seg_start, uint32_t T,
+                                                                uint32_t K, uint32_t E, int* __restrict__ perm_tok,
+                                                                int* __restrict__ route_pos) {
+  __shared__ uint32_t mask[kMaxExperts][kRouteChunk / 32];
+  const uint32_t tl = threadIdx.x, t = blockIdx.x * kRouteChunk + tl;
+  for (uint32_t i = threadIdx.x; i < E * (kRouteChunk / 32); i += blockDim.x) mask[i / 4][i % 4] = 0;
+  __syncthreads();
+  int ek[8];
+  const bool ok = t < T;
+  for (uint32_t k = 0; k < K; k++) {
+    ek[k] = ok ? idx[(size_t)t * K + k] : -1;
+    if (ek[k] >= 0 && (uint32_t)ek[k] < E) atomicOr(&mask[ek[k]][tl >> 5], 1u << (tl & 31));
   }
   __syncthreads();
-  const int cnt = counts[e];
-  for (int tt = threadIdx.x; tt * 128 < cnt; tt += blockDim.x)
-    tiles[s_tile_off + tt] = make_int4(e, s_off + tt * 128, s_off + min(cnt, tt * 128 + 128), s_off);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (uint32_t base = 0; base < n_routes; base += blockDim.x) {
-    const uint32_t i = base + threadIdx.x;
-    const bool hit = i < n_routes && idx[i] == e;
-    const uint32_t bal = __ballot_sync(0xffffffffu, hit);
-    if (lane == 0) wsum[warp] = __popc(bal);
-    __syncthreads();
-    int before = 0, total = 0;
-    for (int w = 0; w < nw; w++) { int c = wsum[w]; if (w < warp) before += c; total += c; }
-    if (hit) {
-      const int p = s_off + s_base + before + __popc(bal & ((1u << lane) - 1u));
-      perm_tok[p] = (int)(i / K);
-      route_pos[i] = p;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) s_base += total;
-    __syncthreads();
+  if (!ok) return;
+  for (uint32_t k = 0; k < K; k++) {
+    const int e = ek[k];
+    if (e < 0 || (uint32_t)e >= E) { route_pos[(size_t)t * K + k] = -1; continue; }
+    int rank = __popc(mask[e][tl >> 5] & ((1u << (tl & 31)) - 1u));
+    for (uint32_t wdx = 0; wdx < (tl >> 5); wdx++) rank += __popc(mask[e][wdx]);
+    const int p = seg_start[e] + hist[(size_t)blockIdx.x * E + e] + rank;
+    perm_tok[p] = (int)t;
+    route_pos[(size_t)t * K + k] = p;
   }
 }
 
@@ -379,12 +496,30 @@ __global__ void moe_combine_kernel(const float* __restrict__ down, const int32_t
     }
   }
   const float kf = (float)K;
-  for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc = 0.0f;
-    for (uint32_t j = 0; j < n; j++) acc = __fmaf_rn(wk[j], down[(size_t)pk[j] * D + d], acc);
-    const uint16_t m16 = f32_to_f16_ref(__fmul_rn(acc, kf));
-    const size_t o = (size_t)t * D + d;
-    out[o] = res ? f32_to_f16_ref(__fadd_rn(f16_ref_to_f32(res[o]), f16_ref_to_f32(m16))) : m16;
+  for (uint32_t c = threadIdx.x; c < D / 4; c += blockDim.x) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (uint32_t j = 0; j < n; j++) {
+      const float4 v = *reinterpret_cast<const float4*>(down + (size_t)pk[j] * D + 4 * c);
+      acc[0] = __fmaf_rn(wk[j], v.x, acc[0]);
+      acc[1] = __fmaf_rn(wk[j], v.y, acc[1]);
+      acc[2] = __fmaf_rn(wk[j], v.z, acc[2]);
+      acc[3] = __fmaf_rn(wk[j], v.w, acc[3]);
+    }
+    const size_t o = (size_t)t * D + 4 * c;
+    uint16_t r16[4];
+    if (res) {
+      const uint2 rv = *reinterpret_cast<const uint2*>(res + o);
+      r16[0] = (uint16_t)(rv.x & 0xffffu); r16[1] = (uint16_t)(rv.x >> 16);
+      r16[2] = (uint16_t)(rv.y & 0xffffu); r16[3] = (uint16_t)(rv.y >> 16);
+    }
+    uint16_t o16[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const uint16_t m16 = f32_to_f16_fast(__fmul_rn(acc[j], kf));
+      o16[j] = res ? f32_to_f16_fast(__fadd_rn(f16_ref_to_f32(r16[j]), f16_ref_to_f32(m16))) : m16;
+    }
+    *reinterpret_cast<uint2*>(out + o) =
+        make_uint2((uint32_t)o16[0] | ((uint32_t)o16[1] << 16), (uint32_t)o16[2] | ((uint32_t)o16[3] << 16));
   }
 }
 
@@ -408,26 +543,47 @@ __global__ void split_rope_kernel(const uint16_t* __restrict__ qkv, uint16_t* __
   const uint32_t pairs = W / 2;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)T * pairs; i += (size_t)gridDim.x * blockDim.x) {
     const uint32_t t = (uint32_t)(i / pairs), c = (uint32_t)(i % pairs) * 2;
-    uint16_t a16 = qkv[(size_t)t * W + c], b16 = qkv[(size_t)t * W + c + 1];
+    const uint32_t ab = *reinterpret_cast<const uint32_t*>(qkv + (size_t)t * W + c);
+    uint16_t a16 = (uint16_t)(ab & 0xffffu), b16 = (uint16_t)(ab >> 16);
     if (c < qc + kc) {
       const uint32_t p = (c % hd) / 2;
-      const uint16_t c16 = cos_t[(size_t)pos[t] * half + p], s16 = sin_t[(size_t)pos[t] * half + p];
-      float cf = f16_ref_to_f32(c16), sf = f16_ref_to_f32(s16);
-      float af = f16_ref_to_f32(a16), bf = f16_ref_to_f32(b16);
-      float ac = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(af, cf)));
-      float bs = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(bf, sf)));
-      float bc = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(bf, cf)));
-      float as = f16_ref_to_f32(f32_to_f16_ref(__fmul_rn(af, sf)));
-      a16 = f32_to_f16_ref(__fsub_rn(ac, bs));
-      b16 = f32_to_f16_ref(__fadd_rn(bc, as));
+      rope_pair_ref(a16, b16, cos_t[(size_t)pos[t] * half + p], sin_t[(size_t)pos[t] * half + p]);
     }
     uint16_t* dst;
     uint32_t col, ld;
     if (c < qc) { dst = q; col = c; ld = qc; }
     else if (c < qc + kc) { dst = k; col = c - qc; ld = kc; }
     else { dst = v; col = c - qc - kc; ld = vc; }
-    dst[(size_t)t * ld + col] = a16;
-    dst[(size_t)t * ld + col + 1] = b16;
+    if (dst) *reinterpret_cast<uint32_t*>(dst + (size_t)t * ld + col) = (uint32_t)a16 | ((uint32_t)b16 << 16);
+  }
+}
+
+// RoPE of the q and k heads of a fused [T, ld] projection (q columns
+// [0, qc), k columns [qc, qc+kc)) into q [T, qc] and k [T, kc]; v stays in
+// the fused buffer.  One thread per 8 consecutive columns (4 pairs).
+__global__ void rope_qk_kernel(const uint16_t* __restrict__ qkv, uint32_t ld, uint16_t* __restrict__ q, uint32_t qc,
+                               uint16_t* __restrict__ k, uint32_t kc, const int* __restrict__ pos,
+                               const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t, uint32_t T,
+                               uint32_t hd) {
+  const uint32_t half = hd / 2, oct = (qc + kc) / 8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)T * oct; i += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t t = (uint32_t)(i / oct), c = (uint32_t)(i % oct) * 8;
+    const uint4 v = *reinterpret_cast<const uint4*>(qkv + (size_t)t * ld + c);
+    uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t p0 = (c % hd) / 2;
+    const size_t trow = (size_t)pos[t] * half + p0;
+    const uint2 cv = *reinterpret_cast<const uint2*>(cos_t + trow);
+    const uint2 sv = *reinterpret_cast<const uint2*>(sin_t + trow);
+    const uint16_t cs[4] = {(uint16_t)(cv.x & 0xffffu), (uint16_t)(cv.x >> 16), (uint16_t)(cv.y & 0xffffu), (uint16_t)(cv.y >> 16)};
+    const uint16_t sn[4] = {(uint16_t)(sv.x & 0xffffu), (uint16_t)(sv.x >> 16), (uint16_t)(sv.y & 0xffffu), (uint16_t)(sv.y >> 16)};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      uint16_t a16 = (uint16_t)(wd[j] & 0xffffu), b16 = (uint16_t)(wd[j] >> 16);
+      rope_pair_ref(a16, b16, cs[j], sn[j]);
+      wd[j] = (uint32_t)a16 | ((uint32_t)b16 << 16);
+    }
+    uint16_t* dst = c < qc ? q + (size_t)t * qc + c : k + (size_t)t * kc + (c - qc);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
 }
 
@@ -498,6 +654,7 @@ cudaError_t launch_embed(const uint8_t* w, const uint16_t* sc, const uint8_t* zp
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gamma, float* out32, uint16_t* out16, uint32_t T,
                            uint32_t D, float eps, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
+  if (D % 8) return cudaErrorInvalidValue;
   const unsigned warps = 4;
   rmsnorm_kernel<false><<<nblk(T, warps), warps * 32, warps * 2 * D * sizeof(float), st>>>(
       x, nullptr, gamma, nullptr, out32, out16, T, D, eps);
@@ -507,26 +664,33 @@ cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gamma, float* out3
 cudaError_t launch_add_rmsnorm(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
                                float* out32, uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
+  if (D % 8) return cudaErrorInvalidValue;
   const unsigned warps = 4;
   rmsnorm_kernel<true><<<nblk(T, warps), warps * 32, warps * 2 * D * sizeof(float), st>>>(a, b, gamma, sum_out, out32,
                                                                                          out16, T, D, eps);
   return cudaGetLastError();
 }
 
-cudaError_t launch_matmul_exact(const ExactArgs& a, bool x_f32, int out_mode, uint32_t grid_m, cudaStream_t st) {
+cudaError_t launch_matmul_exact(const ExactArgs& a_in, bool x_f32, int out_mode, uint32_t grid_m, cudaStream_t st) {
   if (grid_m == 0) return cudaSuccess;
-  if (a.K % 32 || a.K > 2048) return cudaErrorInvalidValue;
+  if (a_in.K % 32 || a_in.K > 1024) return cudaErrorInvalidValue;
+  ExactArgs a = a_in;
+  if (a.rows_per_block == 0) a.rows_per_block = 128;
+  if (!a.tiles) grid_m = (a.M + a.rows_per_block - 1) / a.rows_per_block;
   dim3 grid(nblk(a.N, 128), grid_m);
-  const size_t sm = (size_t)16 * a.K * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    const int mx = 16 * 2048 * 4;
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16Widen>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    attr = true;
+  const size_t sm = exact_smem_bytes(a.K);
+  if (sm > 227 * 1024) return cudaErrorInvalidValue;
+  static size_t attr_bytes = 0;
+  if (sm > 48 * 1024 && sm > attr_bytes) {
+    const int v = (int)sm;
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, v)) ||
+        (e = cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, v)) ||
+        (e = cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16Widen>, cudaFuncAttributeMaxDynamicSharedMemorySize, v)) ||
+        (e = cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, v)) ||
+        (e = cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, v)))
+      return e;
+    attr_bytes = sm;
   }
   if (x_f32) {
     if (out_mode == kOutF16) matmul_w4_exact_kernel<true, kOutF16><<<grid, 256, sm, st>>>(a);
@@ -540,19 +704,24 @@ cudaError_t launch_matmul_exact(const ExactArgs& a, bool x_f32, int out_mode, ui
   return cudaGetLastError();
 }
 
-cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, uint32_t T, uint32_t E, uint32_t K,
-                               cudaStream_t st) {
+uint32_t route_chunks(uint32_t T) { return (T + kRouteChunk - 1) / kRouteChunk; }
+
+cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, int* hist, uint32_t T, uint32_t E,
+                               uint32_t K, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  if (K > 8 || K > E) return cudaErrorInvalidValue;
-  router_topk_kernel<<<nblk(T, 128), 128, 0, st>>>(logits, idx, w, T, E, K, 1.0 / (double)K);
+  if (K > 8 || K > E || E > kMaxExperts) return cudaErrorInvalidValue;
+  router_topk_kernel<<<route_chunks(T), 256, 0, st>>>(logits, idx, w, hist, T, E, K, 1.0 / (double)K);
   return cudaGetLastError();
 }
 
-cudaError_t launch_moe_permute(const int32_t* idx, uint32_t T, uint32_t K, uint32_t E, int* counts, int* perm_tok,
-                               int* route_pos, int4* tiles, int* n_tiles, int* seg_end, cudaStream_t st) {
-  const uint32_t n_routes = T * K;
-  moe_count_kernel<<<E, 256, 0, st>>>(idx, n_routes, counts);
-  moe_scatter_kernel<<<E, 256, 0, st>>>(idx, n_routes, K, counts, E, perm_tok, route_pos, tiles, n_tiles, seg_end);
+cudaError_t launch_moe_permute(const int32_t* idx, int* hist, uint32_t T, uint32_t K, uint32_t E, int* counts,
+                               int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int* seg_start, int* seg_end,
+                               cudaStream_t st) {
+  if (E > kMaxExperts || K > 8) return cudaErrorInvalidValue;
+  const uint32_t nc = route_chunks(T);
+  moe_chunk_scan_kernel<<<(E + 7) / 8, 256, 0, st>>>(hist, nc, E, counts);
+  moe_segments_kernel<<<1, kMaxExperts, 0, st>>>(counts, E, tiles, n_tiles, seg_start, seg_end);
+  moe_place_kernel<<<nc, kRouteChunk, 0, st>>>(idx, hist, seg_start, T, K, E, perm_tok, route_pos);
   return cudaGetLastError();
 }
 
@@ -568,6 +737,7 @@ cudaError_t launch_moe_combine(const float* down, const int32_t* idx, const floa
                                const uint16_t* res, uint16_t* out, uint32_t T, uint32_t D, uint32_t K, uint32_t E,
                                cudaStream_t st) {
   if (T == 0) return cudaSuccess;
+  if (D % 4) return cudaErrorInvalidValue;
   moe_combine_kernel<<<T, 160, 0, st>>>(down, idx, w, route_pos, res, out, T, D, K, E);
   return cudaGetLastError();
 }
@@ -585,6 +755,16 @@ cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uin
   if (T == 0) return cudaSuccess;
   split_rope_kernel<<<gs_blocks((size_t)T * (qc + kc + vc) / 2, 256), 256, 0, st>>>(qkv, q, k, v, pos, cos_t, sin_t, T,
                                                                                    qc, kc, vc, hd);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_qk(const uint16_t* qkv, uint32_t ld, uint16_t* q, uint32_t qc, uint16_t* k, uint32_t kc,
+                           const int* pos, const uint16_t* cos_t, const uint16_t* sin_t, uint32_t T, uint32_t hd,
+                           cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (qc % 8 || kc % 8 || hd % 8 || ld % 8) return cudaErrorInvalidValue;
+  rope_qk_kernel<<<gs_blocks((size_t)T * (qc + kc) / 8, 256), 256, 0, st>>>(qkv, ld, q, qc, k, kc, pos, cos_t, sin_t,
+                                                                            T, hd);
   return cudaGetLastError();
 }
 

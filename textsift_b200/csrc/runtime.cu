@@ -206,7 +206,7 @@ struct Workspace {
   DevArr<uint16_t> x0, x1, xn16, q, k, v, attn, o16, res2, qkv16;
   DevArr<float> n32, hf32, rlogits, rw;
   DevArr<int32_t> ridx;
-  DevArr<int> counts, seg_end, perm_tok, route_pos, n_tiles;
+  DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, hist;
   DevArr<int4> tiles;
   DevArr<int2> atiles;
   std::vector<int2> atiles_host;
@@ -351,7 +351,9 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.ridx.alloc(R));
     TS_CUDA_TRY(w.rw.alloc(R));
     TS_CUDA_TRY(w.counts.alloc(E));
+    TS_CUDA_TRY(w.hist.alloc((size_t)ts::route_chunks((uint32_t)T) * E));
     TS_CUDA_TRY(w.seg_end.alloc(E));
+    TS_CUDA_TRY(w.seg_start.alloc(E));
     TS_CUDA_TRY(w.perm_tok.alloc(R));
     TS_CUDA_TRY(w.route_pos.alloc(R));
     TS_CUDA_TRY(w.n_tiles.alloc(1));
@@ -429,11 +431,20 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
   ts::ExactArgs ra = L.router.exact();
   ra.x = n32; ra.ldx = D; ra.M = T; ra.rloc = rloc; ra.rlen = rlen; ra.out = w.rlogits.p; ra.ldo = E;
   {
-    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, 4);
-    TS_K(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
-    TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, T, E, K, st));
-    TS_K(ts::launch_moe_permute(w.ridx.p, T, K, E, w.counts.p, w.perm_tok.p, w.route_pos.p, w.tiles.p, w.n_tiles.p,
-                                w.seg_end.p, st));
+    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, 5);
+    if (exact) {
+      TS_K(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
+    } else {
+      // fast mode: router logits on the tensor cores from the fp16 operand
+      CUtensorMap tx;
+      if (!ts::make_act_tmap(&tx, xn16, T, D)) return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed (router)");
+      ts::GemmArgs gr;
+      gr.M = T; gr.err = h->err.p; gr.out0 = w.rlogits.p; gr.ld0 = E;
+      TS_K(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiF32, (T + 127) / 128, st));
+    }
+    TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, w.hist.p, T, E, K, st));
+    TS_K(ts::launch_moe_permute(w.ridx.p, w.hist.p, T, K, E, w.counts.p, w.perm_tok.p, w.route_pos.p, w.tiles.p,
+                                w.n_tiles.p, w.seg_start.p, w.seg_end.p, st));
   }
   if (h->trace_topk && layer >= 0)
     TS_K(cudaMemcpyAsync(h->trace_topk + (size_t)layer * T * K, w.ridx.p, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
@@ -528,6 +539,8 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
     TS_K(cudaMemcpyAsync(w.atiles.p, w.atiles_host.data(), (size_t)nt * sizeof(int2), cudaMemcpyHostToDevice, st));
     aa.tiles = w.atiles.p;
     aa.n_tiles = nt;
+    // v straight from the fused projection (q and k are rotated copies)
+    aa.v = w.qkv16.p + Q + KV; aa.v_ld = Q + 2 * KV;
   }
 
   uint16_t* src = w.x0.p;
@@ -546,8 +559,8 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
       {
         Phase p(h, st, TS_PHASE_QKV, fl_qkv, 2);
         TS_K(ts::launch_gemm_w4_tc(L.qkv.tiles(), t_xn, g, ts::kEpiF16, mt, st));
-        TS_K(ts::launch_split_rope(w.qkv16.p, w.q.p, w.k.p, w.v.p, w.pos.p, h->rope_cos.p, h->rope_sin.p, T, Q, KV,
-                                   KV, c.head_dim, st));
+        TS_K(ts::launch_rope_qk(w.qkv16.p, Q + 2 * KV, w.q.p, Q, w.k.p, KV, w.pos.p, h->rope_cos.p, h->rope_sin.p, T,
+                                c.head_dim, st));
       }
       {
         Phase p(h, st, TS_PHASE_ATTENTION, fl_attn, 1);
@@ -583,6 +596,13 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
     std::swap(src, dst);
   }
   Phase p(h, st, TS_PHASE_OTHER, 2ull * T * c.n_classes * D, 2);
+  if (!exact) {
+    TS_K(ts::launch_rmsnorm(src, h->final_norm.p, nullptr, w.xn16.p, T, D, c.eps, st));
+    ts::GemmArgs gs;
+    gs.M = T; gs.err = h->err.p; gs.out0 = d_logits; gs.ld0 = c.n_classes;
+    TS_K(ts::launch_gemm_w4_tc(h->score.tiles(), t_xn, gs, ts::kEpiF16Widen, mt, st));
+    return TS_OK;
+  }
   TS_K(ts::launch_rmsnorm(src, h->final_norm.p, w.n32.p, nullptr, T, D, c.eps, st));
   ts::ExactArgs sa = h->score.exact();
   sa.x = w.n32.p; sa.ldx = D; sa.M = T; sa.rloc = w.pos.p; sa.rlen = w.slen.p; sa.out = d_logits; sa.ldo = c.n_classes;
@@ -650,7 +670,8 @@ ts_cuda_t* ts_cuda_create(const ts_cuda_cfg* cfg, char* err, size_t err_cap) {
   const ts_cuda_cfg& c = *cfg;
   if (c.d_model % 64 || c.d_ff % 64 || (c.n_heads * c.head_dim) % 64 || c.head_dim != 64 || c.n_kv_heads == 0 ||
       c.n_heads % c.n_kv_heads || c.n_heads / c.n_kv_heads > 7 || c.top_k == 0 || c.top_k > 8 ||
-      c.top_k > c.n_experts || c.n_classes == 0 || c.max_tokens == 0 || c.max_seq_len == 0 || c.n_layers == 0)
+      c.top_k > c.n_experts || c.n_experts > 256 || c.d_model > 1024 || c.d_ff > 1024 ||
+      c.n_heads * c.head_dim > 1024 || c.n_classes == 0 || c.max_tokens == 0 || c.max_seq_len == 0 || c.n_layers == 0)
     return bad("ts_cuda_create: unsupported configuration (head_dim must be 64, d_model/d_ff multiples of 64, "
                "GQA group <= 7, top_k <= 8)");
   int ndev = 0;
@@ -715,12 +736,12 @@ int ts_cuda_finalize(ts_cuda_t* h) {
     return rc;
   auto p8 = [&](const std::string& n) { return staged_ptr(h, n); };
   auto p16 = [&](const std::string& n) { return reinterpret_cast<const uint16_t*>(staged_ptr(h, n)); };
-  rc = w4_upload(h->score, p8("score.int4"), p16("score.scales"), p8("score.zp"),
-                 h->staged.count("score.bias") ? p16("score.bias") : nullptr, 1, c.n_classes, D, 128, false, nullptr, st);
-  if (rc) return rc;
   DevArr<int> bad;
   TS_CUDA_TRY(bad.alloc(1));
   TS_CUDA_TRY(cudaMemsetAsync(bad.p, 0, 4, st));
+  rc = w4_upload(h->score, p8("score.int4"), p16("score.scales"), p8("score.zp"),
+                 h->staged.count("score.bias") ? p16("score.bias") : nullptr, 1, c.n_classes, D, 128, true, bad.p, st);
+  if (rc) return rc;
   h->layers.clear();
   for (uint32_t li = 0; li < c.n_layers; li++) {
     auto L = std::make_unique<LayerDev>();
@@ -749,7 +770,7 @@ int ts_cuda_finalize(ts_cuda_t* h) {
     if ((rc = w4_upload(L->o, p8(p + "attn.o_proj.int4"), p16(p + "attn.o_proj.scales"), p8(p + "attn.o_proj.zp"),
                         p16(p + "attn.o_proj.bias"), 1, D, Q, 128, true, bad.p, st)) ||
         (rc = w4_upload(L->router, p8(p + "router.int4"), p16(p + "router.scales"), p8(p + "router.zp"),
-                        p16(p + "router.bias"), 1, E, D, 128, false, nullptr, st)) ||
+                        p16(p + "router.bias"), 1, E, D, 128, true, bad.p, st)) ||
         (rc = w4_upload(L->gate_up, p8(p + "experts.gate_up.int4"), p16(p + "experts.gate_up.scales"),
                         p8(p + "experts.gate_up.zp"), p16(p + "experts.gate_up.bias"), E, 2 * F, D, 256, true, bad.p,
                         st)) ||
@@ -926,7 +947,7 @@ int ts_cuda_op_gather_bq(const uint8_t* d_int4, const uint16_t* d_scales, const 
 int ts_cuda_op_rmsnorm(const uint16_t* d_a, const uint16_t* d_b, const uint16_t* d_gamma, uint16_t* d_sum, float* d_out,
                        uint32_t T, uint32_t D, float eps, void* stream) {
   if (!d_a || !d_gamma || !d_out || (d_b && !d_sum)) return fail(TS_ERR_ARG, "ts_cuda_op_rmsnorm: null pointer");
-  if (D > 8192) return fail(TS_ERR_UNSUPPORTED, "D=%u too large", D);
+  if (D > 8192 || D % 8) return fail(TS_ERR_UNSUPPORTED, "D=%u must be a multiple of 8, at most 8192", D);
   cudaStream_t st = (cudaStream_t)stream;
   if (d_b) TS_CUDA_TRY(ts::launch_add_rmsnorm(d_a, d_b, d_gamma, d_sum, d_out, nullptr, T, D, eps, st));
   else TS_CUDA_TRY(ts::launch_rmsnorm(d_a, d_gamma, d_out, nullptr, T, D, eps, st));
@@ -1026,7 +1047,7 @@ int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32
   ts::ExactArgs ra = h->layers[layer]->router.exact();
   ra.x = d_x; ra.ldx = c.d_model; ra.M = T; ra.out = h->ws.rlogits.p; ra.ldo = c.n_experts;
   TS_CUDA_TRY(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
-  TS_CUDA_TRY(ts::launch_router_topk(h->ws.rlogits.p, d_idx, d_w, T, c.n_experts, c.top_k, st));
+  TS_CUDA_TRY(ts::launch_router_topk(h->ws.rlogits.p, d_idx, d_w, nullptr, T, c.n_experts, c.top_k, st));
   return TS_OK;
 }
 

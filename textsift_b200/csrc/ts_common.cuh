@@ -56,6 +56,28 @@ __device__ __forceinline__ uint16_t f32_to_f16_ref(float f) {
   return (uint16_t)(sign | (ue << 10) | m10);
 }
 
+// Same result as f32_to_f16_ref for every input: hardware round-to-nearest-
+// even is the reference's rounding for normal results, zero and overflow; the
+// reference routine itself handles subnormal results (half-up) and NaN.
+__device__ __forceinline__ uint16_t f32_to_f16_fast(float f) {
+  const float a = fabsf(f);
+  if (a >= 6.103515625e-05f && a < 65520.0f) return __half_as_ushort(__float2half_rn(f));
+  return f32_to_f16_ref(f);
+}
+
+// The reference's RoPE on one interleaved (a, b) fp16 pair with its cos/sin
+// table entries: three fp16 roundings per output (wasm_exports.zig:1488-1498).
+__device__ __forceinline__ void rope_pair_ref(uint16_t& a16, uint16_t& b16, uint16_t c16, uint16_t s16) {
+  const float c = f16_ref_to_f32(c16), s = f16_ref_to_f32(s16);
+  const float a = f16_ref_to_f32(a16), b = f16_ref_to_f32(b16);
+  const float ac = f16_ref_to_f32(f32_to_f16_fast(__fmul_rn(a, c)));
+  const float bs = f16_ref_to_f32(f32_to_f16_fast(__fmul_rn(b, s)));
+  const float bc = f16_ref_to_f32(f32_to_f16_fast(__fmul_rn(b, c)));
+  const float as = f16_ref_to_f32(f32_to_f16_fast(__fmul_rn(a, s)));
+  a16 = f32_to_f16_fast(__fsub_rn(ac, bs));
+  b16 = f32_to_f16_fast(__fadd_rn(bc, as));
+}
+
 // Exact fp16 -> f32 (IEEE, subnormals included): packages/textsift/src/
 // browser/backends/wasm.ts:776-797 widens the final logits this way.
 __device__ __forceinline__ float f16_ieee_to_f32(uint16_t h) {

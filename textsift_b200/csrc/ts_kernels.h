@@ -50,6 +50,7 @@ enum GemmEpi : int {
   kEpiF32 = 1,     // out0 f32  [row][ld0] = acc + bias
   kEpiQkvRope = 2, // q/k with the reference's 3-rounding RoPE, v plain (fp16)
   kEpiSwiglu = 3,  // out0 fp16 [row][N/2] = f16(swiglu(gate, up))
+  kEpiF16Widen = 4,  // out0 f32 [row][ld0] = f32(f16(acc + bias)) (logits, wasm.ts:776-797)
 };
 
 struct GemmArgs {

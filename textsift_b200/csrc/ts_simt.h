@@ -28,6 +28,7 @@ struct ExactArgs {
   const int* seg_end = nullptr;   // grouped: end row of each expert segment
   void* out = nullptr;
   uint32_t ldo = 0;
+  uint32_t rows_per_block = 128;  // dense mode
 };
 
 cudaError_t launch_seq_info(const uint32_t* offs, uint32_t n_seqs, uint32_t T, int* pos, int* sstart, int* slen,
@@ -39,10 +40,15 @@ cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gamma, float* out3
 cudaError_t launch_add_rmsnorm(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
                                float* out32, uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st);
 cudaError_t launch_matmul_exact(const ExactArgs& a, bool x_f32, int out_mode, uint32_t grid_m, cudaStream_t st);
-cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, uint32_t T, uint32_t E, uint32_t K,
+// Top-k of each token's router logits; hist (may be null) receives the
+// per-chunk expert counts that launch_moe_permute consumes.
+uint32_t route_chunks(uint32_t T);
+cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, int* hist, uint32_t T, uint32_t E,
+                               uint32_t K, cudaStream_t st);
+// Stable expert permutation from idx and the top-k kernel's hist (overwritten).
+cudaError_t launch_moe_permute(const int32_t* idx, int* hist, uint32_t T, uint32_t K, uint32_t E, int* counts,
+                               int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int* seg_start, int* seg_end,
                                cudaStream_t st);
-cudaError_t launch_moe_permute(const int32_t* idx, uint32_t T, uint32_t K, uint32_t E, int* counts, int* perm_tok,
-                               int* route_pos, int4* tiles, int* n_tiles, int* seg_end, cudaStream_t st);
 cudaError_t launch_gather_rows(const void* src, void* dst, const int* perm_tok, const int* n_rows_dev,
                                uint32_t max_rows, uint32_t row_bytes, cudaStream_t st);
 cudaError_t launch_moe_combine(const float* down, const int32_t* idx, const float* w, const int* route_pos,
@@ -53,6 +59,9 @@ cudaError_t launch_swiglu_exact(const float* gu, float* out, const int* n_rows_d
 cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uint16_t* v, const int* pos,
                               const uint16_t* cos_t, const uint16_t* sin_t, uint32_t T, uint32_t qc, uint32_t kc,
                               uint32_t vc, uint32_t hd, cudaStream_t st);
+cudaError_t launch_rope_qk(const uint16_t* qkv, uint32_t ld, uint16_t* q, uint32_t qc, uint16_t* k, uint32_t kc,
+                           const int* pos, const uint16_t* cos_t, const uint16_t* sin_t, uint32_t T, uint32_t hd,
+                           cudaStream_t st);
 cudaError_t launch_f16_to_f32_ref(const uint16_t* src, float* dst, size_t n, cudaStream_t st);
 cudaError_t launch_f32_to_f16(const float* src, uint16_t* dst, size_t n, cudaStream_t st);
 cudaError_t launch_dequant_tiles(const uint8_t* blobs, uint32_t N, uint32_t K, uint32_t BN, uint32_t n_kc,
@@ -61,9 +70,15 @@ cudaError_t launch_dequant_tiles(const uint8_t* blobs, uint32_t N, uint32_t K, u
 // Banded GQA attention with sinks (k_attn.cu).  Sequences are packed along
 // T; sstart/slen give each token's sequence (null: one sequence of T tokens).
 struct AttnArgs {
-  const uint16_t* q = nullptr;   // [T, Hq*hd]
-  const uint16_t* k = nullptr;   // [T, Hkv*hd]
-  const uint16_t* v = nullptr;   // [T, Hkv*hd]
+  const uint16_t* q = nullptr;   // [T, Hq*hd], row stride q_ld
+  const uint16_t* k = nullptr;   // [T, Hkv*hd], row stride k_ld
+  const uint16_t* v = nullptr;   // [T, Hkv*hd], row stride v_ld
+  uint32_t q_ld = 0, k_ld = 0, v_ld = 0;  // 0 = dense (Hq*hd, Hkv*hd)
+  // tensor-core path: when set, the reference RoPE is applied to q as it is
+  // loaded (q is then the projection before rotation)
+  const int* q_pos = nullptr;
+  const uint16_t* rope_cos = nullptr;
+  const uint16_t* rope_sin = nullptr;
   const float* sinks = nullptr;  // [Hq]
   const uint8_t* mask = nullptr; // [T] or null
   uint16_t* out = nullptr;       // [T, Hq*hd]
