@@ -42,12 +42,16 @@ struct GemmCfg {
   static constexpr uint32_t OFF_B = STAGES * A_BYTES;
   static constexpr uint32_t OFF_RAW = OFF_B + STAGES * B_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_RAW + STAGES * RAW_STRIDE;
-  static constexpr uint32_t NUM_BARS = 3 * STAGES + 4;
-  static constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr uint32_t NUM_BARS = 3 * STAGES + 6;
+  // f32 [2][BN], decoded bias of the tile; read as float4, so 16-byte aligned
+  static constexpr uint32_t OFF_BIAS = (OFF_BAR + NUM_BARS * 8 + 127u) & ~127u;
+  static constexpr uint32_t OFF_MISC = OFF_BIAS + 2 * BN * 4;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;                    // two accumulators
   static constexpr uint32_t ACC_STRIDE = 256;                   // column offset of accumulator 1
   static constexpr int THREADS = 512;
+  static_assert(OFF_BIAS % 16 == 0 && OFF_MISC % 16 == 0, "smem regions read with 16-byte accesses");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
 // Bounded wait that also gives up as soon as another role aborted.
@@ -72,13 +76,16 @@ __device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) { return (
 
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t grow, uint32_t ncol0,
-                                                    const uint16_t* bias, const uint32_t (&v)[32]) {
+                                                    const float* sbias, const uint32_t (&v)[32]) {
+  // sbias: the decoded bias of columns ncol0..ncol0+31 (zero past N), in smem
   float acc[32];
 #pragma unroll
-  for (int j = 0; j < 32; j++) {
-    uint32_t n = ncol0 + j;
-    float b = n < a.N ? f16_ref_to_f32(bias[n]) : 0.0f;
-    acc[j] = __fadd_rn(__uint_as_float(v[j]), b);
+  for (int q = 0; q < 8; q++) {
+    const float4 b4 = reinterpret_cast<const float4*>(sbias)[q];
+    acc[4 * q + 0] = __fadd_rn(__uint_as_float(v[4 * q + 0]), b4.x);
+    acc[4 * q + 1] = __fadd_rn(__uint_as_float(v[4 * q + 1]), b4.y);
+    acc[4 * q + 2] = __fadd_rn(__uint_as_float(v[4 * q + 2]), b4.z);
+    acc[4 * q + 3] = __fadd_rn(__uint_as_float(v[4 * q + 3]), b4.w);
   }
   const bool full = ncol0 + 32 <= a.N;
   if constexpr (EPI == kEpiF16) {
@@ -140,9 +147,8 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
     uint32_t w[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      float g0 = swiglu_ref(acc[4 * j], acc[4 * j + 1]);
-      float g1 = swiglu_ref(acc[4 * j + 2], acc[4 * j + 3]);
-      w[j] = pack_h2(__half_as_ushort(__float2half_rn(g0)), __half_as_ushort(__float2half_rn(g1)));
+      const __half2 hv = __floats2half2_rn(swiglu_fast(acc[4 * j], acc[4 * j + 1]), swiglu_fast(acc[4 * j + 2], acc[4 * j + 3]));
+      w[j] = *reinterpret_cast<const uint32_t*>(&hv);
     }
     if (full) {
       uint4* o4 = reinterpret_cast<uint4*>(o);
@@ -194,6 +200,7 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* bready = bars + 2 * S;
   uint64_t* acc_full = bars + 3 * S;       // [2]
   uint64_t* acc_empty = bars + 3 * S + 2;  // [2]
+  uint64_t* bias_full = bars + 3 * S + 4;  // [2] the tile's bias is staged
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -211,6 +218,7 @@ __global__ void __launch_bounds__(512, 1)
     for (int b = 0; b < 2; b++) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 256);
+      mbar_init(&bias_full[b], 256);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -315,16 +323,26 @@ __global__ void __launch_bounds__(512, 1)
     // ---- epilogue: 8 warps, lane quarter (warp % 4), column half ((warp - 8) / 4) ----
     const uint32_t quarter = (uint32_t)(warp & 3), chalf = (uint32_t)(warp - 8) >> 2;
     const uint32_t r = quarter * 32u + (uint32_t)lane;
+    const uint32_t et = threadIdx.x - 256;  // 0..255 across the 8 epilogue warps
+    float* sbias_all = reinterpret_cast<float*>(smem + C::OFF_BIAS);
     uint32_t lt = 0;
     for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x, lt++) {
       const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
+      const TileInfo ti = tile_info(args, tile, n_ntiles);
+      const uint32_t n0 = ti.n_tile * BN;
+      // stage this tile's decoded bias (two buffers: a tile's buffer is only
+      // rewritten after every epilogue warp has passed the next tile's barrier)
+      float* sbias = sbias_all + b * BN;
+      if (et < BN) {
+        const uint32_t n = n0 + et;
+        sbias[et] = n < args.N ? f16_ref_to_f32(args.bias[(size_t)ti.expert * args.N + n]) : 0.0f;
+      }
+      mbar_arrive(&bias_full[b]);
+      if (!wait_or_abort(&bias_full[b], bph, args.err, abort_flag)) break;
       if (!wait_or_abort(&acc_full[b], bph, args.err, abort_flag)) break;
       tc_fence_after();
-      const TileInfo ti = tile_info(args, tile, n_ntiles);
       const uint32_t grow = ti.row0 + r;
       const bool row_ok = grow < ti.row_end;
-      const uint32_t n0 = ti.n_tile * BN;
-      const uint16_t* bias = args.bias + (size_t)ti.expert * args.N;
       const uint32_t col_lo = chalf * (BN / 2);
 #pragma unroll 1
       for (uint32_t c0 = col_lo; c0 < col_lo + BN / 2; c0 += 32) {
@@ -336,7 +354,7 @@ __global__ void __launch_bounds__(512, 1)
           tc_fence_before();
           mbar_arrive(&acc_empty[b]);
         }
-        if (row_ok && n0 + c0 < args.N) gemm_epilogue_chunk<EPI>(args, grow, n0 + c0, bias, v);
+        if (row_ok && n0 + c0 < args.N) gemm_epilogue_chunk<EPI>(args, grow, n0 + c0, sbias + c0, v);
       }
     }
   }

@@ -130,6 +130,19 @@ __device__ __forceinline__ float swiglu_ref(float g, float u) {
   return __fmul_rn(__fadd_rn(up, 1.0f), glu);
 }
 
+// The same gate with the sigmoid's division done by the fast reciprocal (at
+// most 2 ulp from the correctly rounded quotient); used by the tensor-core
+// path, whose output is rounded to fp16 anyway.
+__device__ __forceinline__ float swiglu_fast(float g, float u) {
+  const float gate = fminf(g, 7.0f);
+  const float up = fmaxf(fminf(u, 7.0f), -7.0f);
+  const float x = __fmul_rn(gate, 1.702f);
+  const float e = exp_approx_ref(-fabsf(x));
+  const float sig_neg = __fdividef(e, __fadd_rn(1.0f, e));
+  const float sig = x >= 0.0f ? __fsub_rn(1.0f, sig_neg) : sig_neg;
+  return __fmul_rn(__fadd_rn(up, 1.0f), __fmul_rn(gate, sig));
+}
+
 // ---------------------------------------------------------------------------
 // Error flag shared by every kernel (bounded waits, bad indices)
 // ---------------------------------------------------------------------------
