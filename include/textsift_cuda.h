@@ -194,6 +194,28 @@ int ts_cuda_op_banded_attention(const uint16_t* d_q, const uint16_t* d_k, const 
                                 uint32_t head_dim, uint32_t window, const uint32_t* seq_offsets, uint32_t n_seqs,
                                 int32_t mode, void* stream);
 
+/* The banded attention above with no device allocation.  No counterpart in
+ * the reference: ts_cuda_op_banded_attention allocates its scratch (sequence
+ * offsets, per-token sequence info, tile list) with cudaMalloc on every call,
+ * which callers that own all device memory under a fixed budget (an embedding
+ * runtime, a serving loop) or that cannot afford cudaMalloc/cudaFree's
+ * implicit device-wide synchronisation between their kernels cannot allow.
+ * This variant keeps that scratch in one static device array of ~221 KB per
+ * GPU (held until the process exits) and calls no allocator.
+ * Limits: T <= 16384 tokens, n_seqs <= 1024 sequences per call, otherwise
+ * TS_ERR_UNSUPPORTED.  Every call on a GPU shares the array: calls that
+ * overlap on the GPU (e.g. on two streams at once) race and must be
+ * serialized by the caller.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  Same arguments and results as
+ * ts_cuda_op_banded_attention, except that it returns once the work is
+ * queued on `stream` (no synchronize): synchronize the stream before reading
+ * d_out. */
+int ts_cuda_op_banded_attention_noalloc(const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v,
+                                        const float* d_sinks, const uint8_t* d_mask, uint16_t* d_out, uint32_t T,
+                                        uint32_t Hq, uint32_t Hkv, uint32_t head_dim, uint32_t window,
+                                        const uint32_t* seq_offsets, uint32_t n_seqs, int32_t mode, void* stream);
+
 /* YaRN RoPE tables of the handle (browser/inference/rope.ts:348-356), fp16
  * [rows, head_dim/2] each, copied to host. */
 int ts_cuda_rope_tables(ts_cuda_t* h, uint32_t rows, uint16_t* cos_out, uint16_t* sin_out);

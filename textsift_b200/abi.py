@@ -76,6 +76,8 @@ SIGNATURES = [
     ("ts_cuda_op_router_topk", ctypes.c_int, [P, U32, P, P, P, U32, P]),
     ("ts_cuda_op_moe", ctypes.c_int, [P, U32, P, P, P, P, U32, P]),
     ("ts_cuda_op_banded_attention", ctypes.c_int, [P, P, P, P, P, P, U32, U32, U32, U32, U32, P, U32, I32, P]),
+    ("ts_cuda_op_banded_attention_noalloc", ctypes.c_int, [P, P, P, P, P, P, U32, U32, U32, U32, U32, P, U32, I32,
+                                                           P]),
     ("ts_cuda_rope_tables", ctypes.c_int, [P, U32, P, P]),
 ]
 

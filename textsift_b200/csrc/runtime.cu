@@ -625,6 +625,10 @@ int check_dev_err(int* d_err, cudaStream_t st) {
 
 }  // namespace
 
+namespace ts {
+void set_last_error(const char* msg) { g_err = msg ? msg : ""; }
+}  // namespace ts
+
 // =============================================================================
 // extern "C" ABI
 // =============================================================================

@@ -98,4 +98,7 @@ uint32_t attention_max_tiles(uint32_t T, uint32_t n_seqs);
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st);     // mma.sync tensor-core path
 cudaError_t launch_attention_exact(const AttnArgs& a, cudaStream_t st);  // reference-order CUDA-core path
 
+// Sets the calling thread's message returned by ts_cuda_last_error().
+void set_last_error(const char* msg);
+
 }  // namespace ts
