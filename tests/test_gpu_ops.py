@@ -188,6 +188,27 @@ def test_banded_attention(L, oracle, T, mode):
         assert d.max() <= 4e-3 and d.mean() < 3e-4, (d.max(), d.mean())
 
 
+@pytest.mark.parametrize("Hq,Hkv,W", [(12, 2, 128), (4, 2, 16), (7, 7, 64), (14, 2, 0), (14, 2, 200)])
+def test_banded_attention_shapes(L, oracle, Hq, Hkv, W):
+    """Tensor-core path over GQA groups 1..7 and windows 0..128 (tcgen05
+    kernel) and a window past 128 (the mma.sync kernel), packed sequences."""
+    lens = [100, 3, 157, 40]
+    T = sum(lens)
+    q, k, v, sinks, mask = _attn_inputs(8 + Hq + W, T, Hq=Hq, Hkv=Hkv, mask_tail=0.0)
+    mask[np.random.Generator(np.random.PCG64(1)).integers(0, T, size=20)] = 0
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+    out = empty((T, Hq * 64), np.uint16)
+    assert L.ts_cuda_op_banded_attention(ptr(dev(q)), ptr(dev(k)), ptr(dev(v)), ptr(dev(sinks)), ptr(dev(mask)),
+                                         ptr(out), T, Hq, Hkv, 64, W, offs.ctypes.data, len(lens), 0,
+                                         stream()) == 0, L.ts_cuda_last_error()
+    got = host(out, F16)
+    for s in range(len(lens)):
+        a, b = offs[s], offs[s + 1]
+        ref = oracle.banded_attention(q[a:b], k[a:b], v[a:b], sinks, mask[a:b], b - a, Hq, Hkv, 64, W)
+        d = np.abs(f16(got[a:b]) - f16(ref))
+        assert d.max() <= 4e-3 and d.mean() < 3e-4, (s, d.max(), d.mean())
+
+
 @pytest.mark.parametrize("mode", [0, 1])
 def test_banded_attention_packed(L, oracle, mode):
     lens = [5, 130, 257, 64, 400, 1]

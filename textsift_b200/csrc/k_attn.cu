@@ -362,6 +362,7 @@ cudaError_t launch_attention_exact(const AttnArgs& a, cudaStream_t st) {
 
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st) {
   if (a.T == 0) return cudaSuccess;
+  if (attention_umma_supported(a)) return launch_attention_umma(a, st);
   if (a.hd != kHD || a.Hq % a.Hkv != 0 || a.Hq / a.Hkv > 7) return cudaErrorInvalidValue;
   const uint32_t band = (kAttnRows + 2 * a.window + 15) & ~15u;
   const size_t sm = (size_t)band * 256 + band + 16;

@@ -54,24 +54,6 @@ struct GemmCfg {
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-// Bounded wait that also gives up as soon as another role aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  uint32_t it = 0;
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++it & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        set_dev_err(err, kDevErrWaitTimeout);
-        *abort_flag = 1;
-        return false;
-      }
-    }
-  }
-}
-
 __device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
 
 template <int EPI>
@@ -460,6 +442,21 @@ static PFN_tmapEncodeTiled get_encode_fn() {
   return fn;
 }
 
+bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+                  uint32_t box_rows) {
+  PFN_tmapEncodeTiled enc = get_encode_fn();
+  if (!enc || rows == 0 || cols == 0 || (reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 2) & 15u) || ld < cols)
+    return false;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_act_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K) {
   PFN_tmapEncodeTiled enc = get_encode_fn();
   if (!enc || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15u) || ((K * 2) & 15u)) return false;
@@ -473,7 +470,7 @@ bool make_act_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K
   return r == CUDA_SUCCESS;
 }
 
-static int num_sms() {
+int num_sms() {
   static int n = 0;
   if (n == 0) {
     int dev = 0;

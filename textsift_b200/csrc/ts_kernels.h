@@ -75,6 +75,12 @@ struct GemmArgs {
 // Build a 2-D TMA descriptor for an fp16 row-major [rows, K] activation
 // matrix, box 128 rows x 64 K, 128-byte swizzle.
 bool make_act_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K);
+// 2-D fp16 tensor map with the 128-byte swizzle: `rows` rows of `cols`
+// elements, `ld` elements apart, copied in boxes of box_cols x box_rows.
+bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+                  uint32_t box_rows);
+// Streaming multiprocessors of the current device.
+int num_sms();
 
 // Tensor-core int4 GEMM: y = A(fp16 [M,K]) x dequant(W)^T.  grid_m = number
 // of 128-row tiles (dense) or an upper bound on the grouped tile count.

@@ -92,6 +92,10 @@ struct AttnArgs {
   uint32_t T = 0, Hq = 0, Hkv = 0, hd = 0, window = 0;
   int* err = nullptr;
 };
+// tcgen05 attention (k_attn_umma.cu): head_dim 64, group <= 8, window <= 128,
+// no fused q rotation, 16-byte aligned operands.
+bool attention_umma_supported(const AttnArgs& a);
+cudaError_t launch_attention_umma(const AttnArgs& a, cudaStream_t st);
 // Host: the tensor-core tile list for packed sequences (offs has n_seqs + 1 entries).
 void attention_tiles(const uint32_t* offs, uint32_t n_seqs, int2* out, uint32_t* n_out);
 uint32_t attention_max_tiles(uint32_t T, uint32_t n_seqs);
