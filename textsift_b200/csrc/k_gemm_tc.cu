@@ -54,7 +54,6 @@ struct GemmCfg {
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-__device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
 
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t grow, uint32_t ncol0,
@@ -75,13 +74,13 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
     if (full) {
       uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 16; j++) w[j] = pack_h2(f32_to_f16_fast(acc[2 * j]), f32_to_f16_fast(acc[2 * j + 1]));
+      for (int j = 0; j < 16; j++) w[j] = f32x2_to_h2(acc[2 * j], acc[2 * j + 1]);
       uint4* o4 = reinterpret_cast<uint4*>(o);
 #pragma unroll
       for (int q = 0; q < 4; q++) o4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
     } else {
       for (int j = 0; j < 32; j++)
-        if (ncol0 + j < a.N) o[j] = f32_to_f16_fast(acc[j]);
+        if (ncol0 + j < a.N) o[j] = __half_as_ushort(__float2half_rn(acc[j]));
     }
   } else if constexpr (EPI == kEpiF32) {
     float* o = reinterpret_cast<float*>(a.out0) + (size_t)grow * a.ld0 + ncol0;
@@ -96,21 +95,29 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
   } else if constexpr (EPI == kEpiF16Widen) {
     float* o = reinterpret_cast<float*>(a.out0) + (size_t)grow * a.ld0 + ncol0;
     for (int j = 0; j < 32; j++)
-      if (ncol0 + j < a.N) o[j] = f16_ieee_to_f32(f32_to_f16_fast(acc[j]));
+      if (ncol0 + j < a.N) o[j] = __half2float(__float2half_rn(acc[j]));
   } else if constexpr (EPI == kEpiQkvRope) {
     // Columns [0,q_cols) are Q, [q_cols, q_cols+k_cols) K, the rest V.  Every
     // 32-column chunk lies inside one 64-wide head of one region.
-    uint16_t h[32];
+    uint32_t h[16];
 #pragma unroll
-    for (int j = 0; j < 32; j++) h[j] = f32_to_f16_fast(acc[j]);
+    for (int j = 0; j < 16; j++) h[j] = f32x2_to_h2(acc[2 * j], acc[2 * j + 1]);
     uint16_t* o;
     if (ncol0 < a.q_cols + a.k_cols) {
       const int p0 = (int)(ncol0 & 63u) >> 1;
       const size_t trow = (size_t)a.pos[grow] * 32;
-      const uint16_t* cr = a.rope_cos + trow + p0;
-      const uint16_t* sr = a.rope_sin + trow + p0;
+      const uint4* cr = reinterpret_cast<const uint4*>(a.rope_cos + trow + p0);
+      const uint4* sr = reinterpret_cast<const uint4*>(a.rope_sin + trow + p0);
 #pragma unroll
-      for (int p = 0; p < 16; p++) rope_pair_ref(h[2 * p], h[2 * p + 1], cr[p], sr[p]);
+      for (int q = 0; q < 2; q++) {
+        const uint4 c4 = cr[q], s4 = sr[q];
+        const uint32_t cw[4] = {c4.x, c4.y, c4.z, c4.w}, sw[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const int p = 8 * q + e;
+          h[p] = rope_h2(h[p], (uint16_t)(cw[e >> 1] >> (16 * (e & 1))), (uint16_t)(sw[e >> 1] >> (16 * (e & 1))));
+        }
+      }
       if (ncol0 < a.q_cols)
         o = reinterpret_cast<uint16_t*>(a.out0) + (size_t)grow * a.ld0 + ncol0;
       else
@@ -120,9 +127,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
     }
     uint4* o4 = reinterpret_cast<uint4*>(o);
 #pragma unroll
-    for (int q = 0; q < 4; q++)
-      o4[q] = make_uint4(pack_h2(h[8 * q], h[8 * q + 1]), pack_h2(h[8 * q + 2], h[8 * q + 3]),
-                         pack_h2(h[8 * q + 4], h[8 * q + 5]), pack_h2(h[8 * q + 6], h[8 * q + 7]));
+    for (int q = 0; q < 4; q++) o4[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
   } else if constexpr (EPI == kEpiSwiglu) {
     // gate = even column, up = odd column (wasm_exports.zig:855-903).
     uint16_t* o = reinterpret_cast<uint16_t*>(a.out0) + (size_t)grow * a.ld0 + (ncol0 >> 1);

@@ -558,35 +558,6 @@ __global__ void split_rope_kernel(const uint16_t* __restrict__ qkv, uint16_t* __
   }
 }
 
-// RoPE of the q and k heads of a fused [T, ld] projection (q columns
-// [0, qc), k columns [qc, qc+kc)) into q [T, qc] and k [T, kc]; v stays in
-// the fused buffer.  One thread per 8 consecutive columns (4 pairs).
-__global__ void rope_qk_kernel(const uint16_t* __restrict__ qkv, uint32_t ld, uint16_t* __restrict__ q, uint32_t qc,
-                               uint16_t* __restrict__ k, uint32_t kc, const int* __restrict__ pos,
-                               const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t, uint32_t T,
-                               uint32_t hd) {
-  const uint32_t half = hd / 2, oct = (qc + kc) / 8;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)T * oct; i += (size_t)gridDim.x * blockDim.x) {
-    const uint32_t t = (uint32_t)(i / oct), c = (uint32_t)(i % oct) * 8;
-    const uint4 v = *reinterpret_cast<const uint4*>(qkv + (size_t)t * ld + c);
-    uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-    const uint32_t p0 = (c % hd) / 2;
-    const size_t trow = (size_t)pos[t] * half + p0;
-    const uint2 cv = *reinterpret_cast<const uint2*>(cos_t + trow);
-    const uint2 sv = *reinterpret_cast<const uint2*>(sin_t + trow);
-    const uint16_t cs[4] = {(uint16_t)(cv.x & 0xffffu), (uint16_t)(cv.x >> 16), (uint16_t)(cv.y & 0xffffu), (uint16_t)(cv.y >> 16)};
-    const uint16_t sn[4] = {(uint16_t)(sv.x & 0xffffu), (uint16_t)(sv.x >> 16), (uint16_t)(sv.y & 0xffffu), (uint16_t)(sv.y >> 16)};
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      uint16_t a16 = (uint16_t)(wd[j] & 0xffffu), b16 = (uint16_t)(wd[j] >> 16);
-      rope_pair_ref(a16, b16, cs[j], sn[j]);
-      wd[j] = (uint32_t)a16 | ((uint32_t)b16 << 16);
-    }
-    uint16_t* dst = c < qc ? q + (size_t)t * qc + c : k + (size_t)t * kc + (c - qc);
-    *reinterpret_cast<uint4*>(dst) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-  }
-}
-
 // fp16 -> f32 widen with the reference decode (wasm_exports.zig:1106-1116).
 __global__ void f16_to_f32_ref_kernel(const uint16_t* __restrict__ src, float* __restrict__ dst, size_t n) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -755,16 +726,6 @@ cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uin
   if (T == 0) return cudaSuccess;
   split_rope_kernel<<<gs_blocks((size_t)T * (qc + kc + vc) / 2, 256), 256, 0, st>>>(qkv, q, k, v, pos, cos_t, sin_t, T,
                                                                                    qc, kc, vc, hd);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_rope_qk(const uint16_t* qkv, uint32_t ld, uint16_t* q, uint32_t qc, uint16_t* k, uint32_t kc,
-                           const int* pos, const uint16_t* cos_t, const uint16_t* sin_t, uint32_t T, uint32_t hd,
-                           cudaStream_t st) {
-  if (T == 0) return cudaSuccess;
-  if (qc % 8 || kc % 8 || hd % 8 || ld % 8) return cudaErrorInvalidValue;
-  rope_qk_kernel<<<gs_blocks((size_t)T * (qc + kc) / 8, 256), 256, 0, st>>>(qkv, ld, q, qc, k, kc, pos, cos_t, sin_t,
-                                                                            T, hd);
   return cudaGetLastError();
 }
 

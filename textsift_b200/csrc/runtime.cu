@@ -539,8 +539,6 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
     TS_K(cudaMemcpyAsync(w.atiles.p, w.atiles_host.data(), (size_t)nt * sizeof(int2), cudaMemcpyHostToDevice, st));
     aa.tiles = w.atiles.p;
     aa.n_tiles = nt;
-    // v straight from the fused projection (q and k are rotated copies)
-    aa.v = w.qkv16.p + Q + KV; aa.v_ld = Q + 2 * KV;
   }
 
   uint16_t* src = w.x0.p;
@@ -555,12 +553,13 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
         TS_K(ts::launch_rmsnorm(src, L.ln1.p, nullptr, w.xn16.p, T, D, c.eps, st));
       }
       ts::GemmArgs g;
-      g.M = T; g.err = h->err.p; g.out0 = w.qkv16.p; g.ld0 = Q + 2 * KV;
+      g.M = T; g.err = h->err.p;
       {
-        Phase p(h, st, TS_PHASE_QKV, fl_qkv, 2);
-        TS_K(ts::launch_gemm_w4_tc(L.qkv.tiles(), t_xn, g, ts::kEpiF16, mt, st));
-        TS_K(ts::launch_rope_qk(w.qkv16.p, Q + 2 * KV, w.q.p, Q, w.k.p, KV, w.pos.p, h->rope_cos.p, h->rope_sin.p, T,
-                                c.head_dim, st));
+        // RoPE in the GEMM epilogue: q, k (rotated) and v to their own buffers
+        g.out0 = w.q.p; g.ld0 = Q; g.out1 = w.k.p; g.ld1 = KV; g.out2 = w.v.p; g.ld2 = KV;
+        g.q_cols = Q; g.k_cols = KV; g.pos = w.pos.p; g.rope_cos = h->rope_cos.p; g.rope_sin = h->rope_sin.p;
+        Phase p(h, st, TS_PHASE_QKV, fl_qkv, 1);
+        TS_K(ts::launch_gemm_w4_tc(L.qkv.tiles(), t_xn, g, ts::kEpiQkvRope, mt, st));
       }
       {
         Phase p(h, st, TS_PHASE_ATTENTION, fl_attn, 1);

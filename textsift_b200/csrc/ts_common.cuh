@@ -78,6 +78,31 @@ __device__ __forceinline__ void rope_pair_ref(uint16_t& a16, uint16_t& b16, uint
   b16 = f32_to_f16_fast(__fadd_rn(bc, as));
 }
 
+// The same RoPE on an fp16x2 word (a in the low half, b in the high half):
+// (a c - b s, b c + a s) with every product and the sum rounded to fp16 by
+// the half-precision unit (no contraction into fma).  Products of two fp16
+// values and sums of two fp16 values are exact in f32 (or, for sums, too far
+// from an fp16 tie to matter), so this equals rope_pair_ref bit for bit
+// whenever no input, product or result is an fp16 subnormal; it differs from
+// it only there (the reference decodes subnormals as if normal and rounds
+// subnormal results half-up).
+__device__ __forceinline__ uint32_t rope_h2(uint32_t ab, uint16_t c16, uint16_t s16) {
+  const uint32_t cc = (uint32_t)c16 * 0x00010001u, ss = (uint32_t)s16 * 0x00010001u;
+  const uint32_t ba = __byte_perm(ab, 0u, 0x1032);
+  const __half2 x = __hmul2_rn(*reinterpret_cast<const __half2*>(&ab), *reinterpret_cast<const __half2*>(&cc));
+  const __half2 y0 = __hmul2_rn(*reinterpret_cast<const __half2*>(&ba), *reinterpret_cast<const __half2*>(&ss));
+  const uint32_t yn = *reinterpret_cast<const uint32_t*>(&y0) ^ 0x00008000u;  // (-b s, a s)
+  const __half2 r = __hadd2_rn(x, *reinterpret_cast<const __half2*>(&yn));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// Two f32 values as an fp16x2 word, hardware round-to-nearest-even (the
+// tensor-core path's output conversion).
+__device__ __forceinline__ uint32_t f32x2_to_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // Exact fp16 -> f32 (IEEE, subnormals included): packages/textsift/src/
 // browser/backends/wasm.ts:776-797 widens the final logits this way.
 __device__ __forceinline__ float f16_ieee_to_f32(uint16_t h) {
