@@ -523,6 +523,139 @@ __global__ void moe_combine_kernel(const float* __restrict__ down, const int32_t
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fast-mode (tensor-core path) norms and combine: any summation order,
+// hardware round-to-nearest-even conversions, everything held in registers.
+// ---------------------------------------------------------------------------
+
+// One warp per row, D <= 1024 and a multiple of 8.  With ADD: sum_out =
+// fp16(a + b); the squares are taken of the f32 sum and the normalised value
+// is the fp16-rounded sum (as in the reference-order kernel above).
+template <bool ADD>
+__global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __restrict__ a,
+                                                           const uint16_t* __restrict__ b,
+                                                           const uint16_t* __restrict__ gamma,
+                                                           uint16_t* __restrict__ sum_out,
+                                                           uint16_t* __restrict__ out16, uint32_t T, uint32_t D,
+                                                           float eps) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const uint32_t nc = D / 8;
+  const size_t base = (size_t)row * D;
+  uint4 xr[4];  // the value to normalise (fp16x2 words), chunks lane, lane+32, ...
+  float ss = 0.0f;
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const uint32_t c = (uint32_t)lane + 32u * r;
+    if (c >= nc) break;
+    uint4 av = *reinterpret_cast<const uint4*>(a + base + 8 * c);
+    if constexpr (ADD) {
+      const uint4 bv = *reinterpret_cast<const uint4*>(b + base + 8 * c);
+      uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+      const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
+        const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
+        const float s0 = fa.x + fb.x, s1 = fa.y + fb.y;
+        ss = fmaf(s0, s0, ss);
+        ss = fmaf(s1, s1, ss);
+        aw[j] = f32x2_to_h2(s0, s1);
+      }
+      av = make_uint4(aw[0], aw[1], aw[2], aw[3]);
+      *reinterpret_cast<uint4*>(sum_out + base + 8 * c) = av;
+    } else {
+      const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+    xr[r] = av;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv_rms = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const uint32_t c = (uint32_t)lane + 32u * r;
+    if (c >= nc) break;
+    const uint4 gv = *reinterpret_cast<const uint4*>(gamma + 8 * c);
+    const uint32_t xw[4] = {xr[r].x, xr[r].y, xr[r].z, xr[r].w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t ow[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&xw[j]));
+      const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
+      ow[j] = f32x2_to_h2(x.x * inv_rms * g.x, x.y * inv_rms * g.y);
+    }
+    *reinterpret_cast<uint4*>(out16 + base + 8 * c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  }
+}
+
+// MoE combine from fp16 expert outputs, one thread per (token, 8 columns):
+// acc = sum over the token's experts in ascending id of w * v (fma, from 0);
+// out = fp16(res + fp16(acc * K)) (or fp16(acc * K) without a residual).
+__global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* __restrict__ down,
+                                                               const int32_t* __restrict__ idx,
+                                                               const float* __restrict__ w,
+                                                               const int* __restrict__ route_pos,
+                                                               const uint16_t* __restrict__ res,
+                                                               uint16_t* __restrict__ out, uint32_t T, uint32_t D,
+                                                               uint32_t K, uint32_t E) {
+  const uint32_t nc = D / 8;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)T * nc) return;
+  const uint32_t t = (uint32_t)(i / nc), c = (uint32_t)(i % nc);
+  int ek[8], pk[8];
+  float wk[8];
+  uint32_t n = 0;
+  for (uint32_t k = 0; k < K; k++) {
+    const int e = idx[(size_t)t * K + k];
+    if (e < 0 || (uint32_t)e >= E) continue;
+    uint32_t j = n++;
+    ek[j] = e; wk[j] = w[(size_t)t * K + k]; pk[j] = route_pos[(size_t)t * K + k];
+    while (j > 0 && ek[j] < ek[j - 1]) {
+      int te = ek[j]; ek[j] = ek[j - 1]; ek[j - 1] = te;
+      float tw = wk[j]; wk[j] = wk[j - 1]; wk[j - 1] = tw;
+      int tp = pk[j]; pk[j] = pk[j - 1]; pk[j - 1] = tp;
+      j--;
+    }
+  }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (uint32_t j = 0; j < n; j++) {
+    const uint4 v = *reinterpret_cast<const uint4*>(down + (size_t)pk[j] * D + 8 * c);
+    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vw[q]));
+      acc[2 * q] = fmaf(wk[j], f.x, acc[2 * q]);
+      acc[2 * q + 1] = fmaf(wk[j], f.y, acc[2 * q + 1]);
+    }
+  }
+  const float kf = (float)K;
+  const size_t o = (size_t)t * D + 8 * c;
+  uint32_t ow[4];
+  if (res) {
+    const uint4 rv = *reinterpret_cast<const uint4*>(res + o);
+    const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint32_t m = f32x2_to_h2(acc[2 * q] * kf, acc[2 * q + 1] * kf);
+      const float2 mf = __half22float2(*reinterpret_cast<const __half2*>(&m));
+      const float2 rf = __half22float2(*reinterpret_cast<const __half2*>(&rw[q]));
+      ow[q] = f32x2_to_h2(rf.x + mf.x, rf.y + mf.y);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; q++) ow[q] = f32x2_to_h2(acc[2 * q] * kf, acc[2 * q + 1] * kf);
+  }
+  *reinterpret_cast<uint4*>(out + o) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
 // SwiGLU-clamp on f32 (gate even, up odd), 4-lane polynomial body.
 __global__ void swiglu_exact_kernel(const float* __restrict__ gu, float* __restrict__ out,
                                     const int* __restrict__ n_rows_dev, uint32_t n_rows, uint32_t D) {
@@ -726,6 +859,26 @@ cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uin
   if (T == 0) return cudaSuccess;
   split_rope_kernel<<<gs_blocks((size_t)T * (qc + kc + vc) / 2, 256), 256, 0, st>>>(qkv, q, k, v, pos, cos_t, sin_t, T,
                                                                                    qc, kc, vc, hd);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
+                                uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (D % 8 || D > 1024 || !out16 || (b && !sum_out)) return cudaErrorInvalidValue;
+  const uint32_t blocks = (T + 7) / 8;
+  if (b) rmsnorm_fast_kernel<true><<<blocks, 256, 0, st>>>(a, b, gamma, sum_out, out16, T, D, eps);
+  else rmsnorm_fast_kernel<false><<<blocks, 256, 0, st>>>(a, nullptr, gamma, nullptr, out16, T, D, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,
+                                    const uint16_t* res, uint16_t* out, uint32_t T, uint32_t D, uint32_t K,
+                                    uint32_t E, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (D % 8 || K > 8) return cudaErrorInvalidValue;
+  const size_t n = (size_t)T * (D / 8);
+  moe_combine_fast_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(down, idx, w, route_pos, res, out, T, D, K, E);
   return cudaGetLastError();
 }
 

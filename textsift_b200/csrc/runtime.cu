@@ -203,7 +203,7 @@ struct Workspace {
   DevArr<uint8_t> mask;
   DevArr<uint32_t> offs;
   DevArr<int> pos, sstart, slen;
-  DevArr<uint16_t> x0, x1, xn16, q, k, v, attn, o16, res2, qkv16;
+  DevArr<uint16_t> x0, x1, xn16, q, k, v, attn, o16, res2, qkv16, down16;
   DevArr<float> n32, hf32, rlogits, rw;
   DevArr<int32_t> ridx;
   DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, hist;
@@ -361,6 +361,7 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.aperm16.alloc(R * D));
     TS_CUDA_TRY(w.glu16.alloc(R * F));
     TS_CUDA_TRY(w.down32.alloc(R * D));
+    TS_CUDA_TRY(w.down16.alloc(R * D));
     TS_CUDA_TRY(w.logits.alloc(T * c.n_classes));
     TS_CUDA_TRY(w.qkv16.alloc(T * (Q + 2 * KV)));
     TS_CUDA_TRY(w.atiles.alloc(ts::attention_max_tiles((uint32_t)T, (uint32_t)T)));
@@ -418,7 +419,8 @@ struct Phase {
   }
 };
 
-// The MoE half of a block: routing from n32 (f32), experts, deterministic
+// The MoE half of a block: routing from n32 (f32, exact mode) or xn16 (fp16,
+// fast mode), experts, deterministic
 // combine.  res == nullptr writes the bare MoE output fp16(K * sum w e(x)).
 int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, const uint16_t* res, uint16_t* out,
              uint32_t T, const int* rloc, const int* rlen, bool exact, cudaStream_t st, int layer) {
@@ -466,10 +468,10 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
     }
     ts::GemmArgs g2;
     g2.tiles = w.tiles.p; g2.n_tiles = w.n_tiles.p; g2.err = h->err.p;
-    g2.out0 = w.down32.p; g2.ld0 = D;
+    g2.out0 = w.down16.p; g2.ld0 = D;
     {
       Phase p(h, st, TS_PHASE_EXPERT_DOWN, fl_dn, 1);
-      TS_K(ts::launch_gemm_w4_tc(L.down.tiles(), tg, g2, ts::kEpiF32, grid_tiles, st));
+      TS_K(ts::launch_gemm_w4_tc(L.down.tiles(), tg, g2, ts::kEpiF16, grid_tiles, st));
     }
   } else {
     Phase p(h, st, TS_PHASE_EXPERT_GATE_UP, fl_gu + fl_dn, 4);
@@ -486,7 +488,8 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
   }
   {
     Phase p(h, st, TS_PHASE_OTHER, 0, 1);
-    TS_K(ts::launch_moe_combine(w.down32.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E, st));
+    if (exact) TS_K(ts::launch_moe_combine(w.down32.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E, st));
+    else TS_K(ts::launch_moe_combine_fast(w.down16.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E, st));
   }
   return TS_OK;
 }
@@ -550,7 +553,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
     if (!exact) {
       {
         Phase p(h, st, TS_PHASE_OTHER, 0, 1);
-        TS_K(ts::launch_rmsnorm(src, L.ln1.p, nullptr, w.xn16.p, T, D, c.eps, st));
+        TS_K(ts::launch_rmsnorm_fast(src, nullptr, L.ln1.p, nullptr, w.xn16.p, T, D, c.eps, st));
       }
       ts::GemmArgs g;
       g.M = T; g.err = h->err.p;
@@ -573,7 +576,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
       }
       {
         Phase p(h, st, TS_PHASE_OTHER, 0, 1);
-        TS_K(ts::launch_add_rmsnorm(src, w.o16.p, L.ln2.p, w.res2.p, w.n32.p, w.xn16.p, T, D, c.eps, st));
+        TS_K(ts::launch_rmsnorm_fast(src, w.o16.p, L.ln2.p, w.res2.p, w.xn16.p, T, D, c.eps, st));
       }
     } else {
       Phase p(h, st, TS_PHASE_OTHER, fl_qkv + fl_o + fl_attn, 6);
@@ -596,7 +599,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   }
   Phase p(h, st, TS_PHASE_OTHER, 2ull * T * c.n_classes * D, 2);
   if (!exact) {
-    TS_K(ts::launch_rmsnorm(src, h->final_norm.p, nullptr, w.xn16.p, T, D, c.eps, st));
+    TS_K(ts::launch_rmsnorm_fast(src, nullptr, h->final_norm.p, nullptr, w.xn16.p, T, D, c.eps, st));
     ts::GemmArgs gs;
     gs.M = T; gs.err = h->err.p; gs.out0 = d_logits; gs.ld0 = c.n_classes;
     TS_K(ts::launch_gemm_w4_tc(h->score.tiles(), t_xn, gs, ts::kEpiF16Widen, mt, st));

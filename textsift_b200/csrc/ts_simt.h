@@ -59,6 +59,13 @@ cudaError_t launch_swiglu_exact(const float* gu, float* out, const int* n_rows_d
 cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uint16_t* v, const int* pos,
                               const uint16_t* cos_t, const uint16_t* sin_t, uint32_t T, uint32_t qc, uint32_t kc,
                               uint32_t vc, uint32_t hd, cudaStream_t st);
+// Fast mode: RMSNorm (b != nullptr: of a + b, the sum written to sum_out)
+// to fp16, any summation order; MoE combine from fp16 expert outputs.
+cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
+                                uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st);
+cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,
+                                    const uint16_t* res, uint16_t* out, uint32_t T, uint32_t D, uint32_t K,
+                                    uint32_t E, cudaStream_t st);
 cudaError_t launch_f16_to_f32_ref(const uint16_t* src, float* dst, size_t n, cudaStream_t st);
 cudaError_t launch_f32_to_f16(const float* src, uint16_t* dst, size_t n, cudaStream_t st);
 cudaError_t launch_dequant_tiles(const uint8_t* blobs, uint32_t N, uint32_t K, uint32_t BN, uint32_t n_kc,
