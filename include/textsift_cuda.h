@@ -108,6 +108,18 @@ int ts_cuda_forward_packed_device(ts_cuda_t* h, const int32_t* d_ids, const uint
 int ts_cuda_forward_trace(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
                           uint32_t n_seqs, float* logits, int32_t* topk_trace);
 
+/* As ts_cuda_forward_packed, but each sequence's logits are decoded on the
+ * GPU into BIOES tags (host, u8 [T], class ids 0..32) and only the tags are
+ * copied back.  Replaces the per-chunk pair backend.forward +
+ * ViterbiDecoder.decode of runDetection (browser/privacy-filter.ts:497-500;
+ * browser/inference/viterbi.ts:75-145), bit-identical to the decoder.
+ * calibration (host, 6 values, calibration.ts:29-36): background_stay,
+ * background_to_start, inside_to_continue, inside_to_end,
+ * end_to_background, end_to_start; each finite with |value| < 1e20.
+ * Needs the 33-class head; sequences of at most 7044 tokens. */
+int ts_cuda_forward_packed_tags(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
+                                uint32_t n_seqs, const float* calibration, uint8_t* tags);
+
 /* Synchronize the handle's work on `stream` and report a device-side error
  * flag (bounded waits that timed out, bad indices) as TS_ERR_DEVICE. */
 int ts_cuda_check(ts_cuda_t* h, void* stream);
@@ -193,6 +205,13 @@ int ts_cuda_op_banded_attention(const uint16_t* d_q, const uint16_t* d_k, const 
                                 const uint8_t* d_mask, uint16_t* d_out, uint32_t T, uint32_t Hq, uint32_t Hkv,
                                 uint32_t head_dim, uint32_t window, const uint32_t* seq_offsets, uint32_t n_seqs,
                                 int32_t mode, void* stream);
+
+/* BIOES Viterbi decoding alone (ViterbiDecoder.decode,
+ * browser/inference/viterbi.ts:75-145): d_logits f32 [T, 33] (device) with
+ * sequences at seq_offsets (host, n_seqs + 1) -> d_tags u8 [T] (device).
+ * Calibration as for ts_cuda_forward_packed_tags.  Synchronizes `stream`. */
+int ts_cuda_op_viterbi(const float* d_logits, const uint32_t* seq_offsets, uint32_t n_seqs, const float* calibration,
+                       uint8_t* d_tags, void* stream);
 
 /* The banded attention above with no device allocation.  No counterpart in
  * the reference: ts_cuda_op_banded_attention allocates its scratch (sequence

@@ -92,6 +92,10 @@ def lib():
         L.tso_model_forward_forced.restype = I32
         L.tso_moe_forward.argtypes = [P, U32, P, U32, P, P, P, I32]
         L.tso_moe_forward.restype = I32
+        L.tso_viterbi_tables.argtypes = [P, P, P]
+        L.tso_viterbi.argtypes = [P, U32, P, P, P, P]
+        L.tso_bioes_spans.argtypes = [P, U32, P, U32]
+        L.tso_bioes_spans.restype = U32
         _lib = L
     return _lib
 
@@ -238,6 +242,37 @@ def embed_lookup_int4(embed_int4, embed_scales, embed_zp, ids, V, D):
 
 def exp_approx(x: float) -> float:
     return lib().tso_exp_approx(float(x))
+
+
+ZERO_CALIBRATION = (0.0, 0.0, 0.0, 0.0, 0.0, 0.0)
+
+
+def viterbi_tables(cal=ZERO_CALIBRATION):
+    """browser/inference/viterbi.ts:155-225: (trans [to, from] f32[33,33], start f32[33])."""
+    trans = np.zeros((33, 33), np.float32)
+    start = np.zeros(33, np.float32)
+    lib().tso_viterbi_tables(_p(np.asarray(cal, np.float32)), _p(trans), _p(start))
+    return trans, start
+
+
+def viterbi(logits, cal=ZERO_CALIBRATION):
+    """browser/inference/viterbi.ts:75-145: BIOES tags u8[T] of logits f32[T,33]."""
+    lg = _c(logits, np.float32).reshape(-1, 33)
+    T = lg.shape[0]
+    tags = np.zeros(T, np.uint8)
+    alpha = np.zeros(max(T, 1) * 33, np.float32)
+    back = np.zeros(max(T, 1) * 33, np.uint8)
+    lib().tso_viterbi(_p(lg), T, _p(np.asarray(cal, np.float32)), _p(tags), _p(alpha), _p(back))
+    return tags
+
+
+def bioes_spans(tags):
+    """browser/inference/spans.ts:29-104 at token level: [(first, last, label)]."""
+    tg = _c(tags, np.uint8)
+    cap = max(int(tg.size), 1)
+    out = np.zeros((cap, 3), np.int32)
+    n = lib().tso_bioes_spans(_p(tg), tg.size, _p(out), cap)
+    return [tuple(int(v) for v in out[i]) for i in range(n)]
 
 
 def rope_cfg(head_dim=64, theta=150000.0, factor=32.0, orig=4096.0, beta_fast=32.0,

@@ -86,6 +86,14 @@ typedef struct {
   double original_max_pos, beta_fast, beta_slow;
   int truncate;
 } tso_rope_cfg;
+/* Span decoding (ts_oracle_decode.c): browser/inference/viterbi.ts and
+ * spans.ts.  cal = {background_stay, background_to_start,
+ * inside_to_continue, inside_to_end, end_to_background, end_to_start}. */
+void tso_viterbi_tables(const float cal[6], float* trans /* [33*33], [to*33+from] */, float* start /* [33] */);
+void tso_viterbi(const float* logits, uint32_t T, const float cal[6], uint8_t* tags, float* alpha_scratch,
+                 uint8_t* back_scratch);
+uint32_t tso_bioes_spans(const uint8_t* tags, uint32_t T, int32_t* out /* [cap][3] */, uint32_t cap);
+
 void tso_build_rope_tables(const tso_rope_cfg* cfg, uint32_t T, uint16_t* cos_out, uint16_t* sin_out);
 
 /* ---- model composition (model.ts / block.ts / attention.ts / expert.ts) ---- */

@@ -60,6 +60,7 @@ SIGNATURES = [
     ("ts_cuda_forward", ctypes.c_int, [P, P, P, U32, P]),
     ("ts_cuda_forward_packed", ctypes.c_int, [P, P, P, P, U32, P]),
     ("ts_cuda_forward_packed_device", ctypes.c_int, [P, P, P, P, U32, P, P]),
+    ("ts_cuda_forward_packed_tags", ctypes.c_int, [P, P, P, P, U32, P, P]),
     ("ts_cuda_forward_trace", ctypes.c_int, [P, P, P, P, U32, P, P]),
     ("ts_cuda_check", ctypes.c_int, [P, P]),
     ("ts_cuda_device_name", ctypes.c_char_p, [P]),
@@ -76,6 +77,7 @@ SIGNATURES = [
     ("ts_cuda_op_router_topk", ctypes.c_int, [P, U32, P, P, P, U32, P]),
     ("ts_cuda_op_moe", ctypes.c_int, [P, U32, P, P, P, P, U32, P]),
     ("ts_cuda_op_banded_attention", ctypes.c_int, [P, P, P, P, P, P, U32, U32, U32, U32, U32, P, U32, I32, P]),
+    ("ts_cuda_op_viterbi", ctypes.c_int, [P, P, U32, P, P, P]),
     ("ts_cuda_op_banded_attention_noalloc", ctypes.c_int, [P, P, P, P, P, P, U32, U32, U32, U32, U32, P, U32, I32,
                                                            P]),
     ("ts_cuda_rope_tables", ctypes.c_int, [P, U32, P, P]),

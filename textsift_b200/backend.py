@@ -165,3 +165,28 @@ class CudaBackend:
             o = int(offs[s]) * self.num_classes
             res.append(Logits(out[o:o + n * self.num_classes].copy(), n, self.num_classes))
         return res
+
+    def forward_packed_tags(self, chunks: Sequence[np.ndarray], calibration: Sequence[float],
+                            masks: Sequence[np.ndarray] | None = None) -> list[np.ndarray]:
+        """Forward many chunks and decode each on the GPU with the BIOES
+        Viterbi decoder (ViterbiDecoder.decode, browser/inference/viterbi.ts):
+        one u8 tag array per chunk.  calibration: the six transition biases of
+        ViterbiCalibration (browser/model/calibration.ts:29-36) in field order."""
+        if not self._ready:
+            raise RuntimeError("CudaBackend: call warmup() before forward_packed_tags()")
+        cal = np.ascontiguousarray(np.asarray(calibration, dtype=np.float32))
+        if cal.size != 6:
+            raise ValueError("forward_packed_tags: calibration needs 6 values")
+        lens = [int(np.asarray(c).size) for c in chunks]
+        offs = np.zeros(len(lens) + 1, dtype=np.uint32)
+        offs[1:] = np.cumsum(lens)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(c, dtype=np.int32) for c in chunks]))
+        mask = None
+        if masks is not None:
+            mask = np.ascontiguousarray(np.concatenate([np.asarray(m, dtype=np.uint8) for m in masks]))
+            if mask.size != ids.size:
+                raise ValueError("forward_packed_tags: masks and chunks differ in length")
+        tags = np.empty(ids.size, dtype=np.uint8)
+        abi.check(abi.lib().ts_cuda_forward_packed_tags(self._h, _ptr(ids), _ptr(mask), _ptr(offs), len(lens),
+                                                        _ptr(cal), _ptr(tags)))
+        return [tags[int(offs[s]):int(offs[s + 1])].copy() for s in range(len(lens))]

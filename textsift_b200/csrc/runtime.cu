@@ -200,7 +200,7 @@ struct LayerDev {
 struct Workspace {
   uint32_t cap = 0;  // tokens
   DevArr<int32_t> ids;
-  DevArr<uint8_t> mask;
+  DevArr<uint8_t> mask, tags;
   DevArr<uint32_t> offs;
   DevArr<int> pos, sstart, slen;
   DevArr<uint16_t> x0, x1, xn16, q, k, v, attn, o16, res2, qkv16, down16;
@@ -334,6 +334,7 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.ids.alloc(T));
     TS_CUDA_TRY(w.mask.alloc(T));
     TS_CUDA_TRY(w.offs.alloc(T + 1));
+    TS_CUDA_TRY(w.tags.alloc(T));
     TS_CUDA_TRY(w.pos.alloc(T));
     TS_CUDA_TRY(w.sstart.alloc(T));
     TS_CUDA_TRY(w.slen.alloc(T));
@@ -858,6 +859,66 @@ int ts_cuda_forward_packed(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask
   return TS_OK;
 }
 
+// Viterbi arguments: calibration values finite and below 1e20 in magnitude
+// (the range in which the kernel's restricted candidate scan equals the
+// reference's full one), sequences non-empty and short enough for the
+// per-warp back-pointer table in shared memory.
+static int check_viterbi_args(const uint32_t* offs, uint32_t n_seqs, const float* cal, uint32_t* max_len) {
+  if (!cal) return fail(TS_ERR_ARG, "calibration must hold 6 values");
+  for (int i = 0; i < 6; i++)
+    if (!(std::fabs(cal[i]) < 1e20f)) return fail(TS_ERR_ARG, "calibration[%d] is not a finite value below 1e20", i);
+  if (offs[0] != 0) return fail(TS_ERR_ARG, "seq_offsets[0] must be 0");
+  uint32_t m = 0;
+  for (uint32_t s = 0; s < n_seqs; s++) {
+    if (offs[s + 1] <= offs[s]) return fail(TS_ERR_ARG, "sequence %u is empty", s);
+    m = std::max(m, offs[s + 1] - offs[s]);
+  }
+  if (m > ts::viterbi_max_len())
+    return fail(TS_ERR_UNSUPPORTED, "sequence of %u tokens > %u for Viterbi decoding", m, ts::viterbi_max_len());
+  *max_len = m;
+  return TS_OK;
+}
+
+int ts_cuda_forward_packed_tags(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
+                                uint32_t n_seqs, const float* calibration, uint8_t* tags) {
+  if (!h || !ids || !tags || !seq_offsets || n_seqs == 0)
+    return fail(TS_ERR_ARG, "ts_cuda_forward_packed_tags: null argument");
+  if (!h->finalized) return fail(TS_ERR_STATE, "ts_cuda_finalize has not succeeded");
+  uint32_t max_len = 0;
+  int rc = check_viterbi_args(seq_offsets, n_seqs, calibration, &max_len);
+  if (rc) return rc;
+  const uint32_t T = seq_offsets[n_seqs];
+  if (T > h->cfg.max_tokens) return fail(TS_ERR_UNSUPPORTED, "%u tokens > max_tokens %u", T, h->cfg.max_tokens);
+  if (h->cfg.n_classes != 33) return fail(TS_ERR_UNSUPPORTED, "Viterbi decoding needs the 33-class BIOES head");
+  DevGuard g(h->cfg.device);
+  cudaStream_t st = h->stream;
+  Workspace& w = h->ws;
+  uint8_t* pin_ids = h->pin;
+  uint8_t* pin_mask = h->pin + (size_t)h->cfg.max_tokens * 4;
+  uint8_t* pin_tags = pin_mask + h->cfg.max_tokens + 16 - ((uintptr_t)(pin_mask + h->cfg.max_tokens) & 15u);
+  memcpy(pin_ids, ids, (size_t)T * 4);
+  TS_CUDA_TRY(cudaMemcpyAsync(w.ids.p, pin_ids, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+  const uint8_t* dmask = nullptr;
+  if (mask) {
+    memcpy(pin_mask, mask, T);
+    TS_CUDA_TRY(cudaMemcpyAsync(w.mask.p, pin_mask, T, cudaMemcpyHostToDevice, st));
+    dmask = w.mask.p;
+  }
+  rc = forward_device(h, w.ids.p, dmask, seq_offsets, n_seqs, w.logits.p, st);
+  if (rc) {
+    cudaStreamSynchronize(st);
+    return rc;
+  }
+  // forward_device left the sequence offsets in w.offs
+  TS_CUDA_TRY(ts::launch_viterbi(w.logits.p, reinterpret_cast<const int*>(w.offs.p), n_seqs, max_len, calibration,
+                                 w.tags.p, st));
+  TS_CUDA_TRY(cudaMemcpyAsync(pin_tags, w.tags.p, T, cudaMemcpyDeviceToHost, st));
+  rc = check_dev_err(h->err.p, st);
+  if (rc) return rc;
+  memcpy(tags, pin_tags, T);
+  return TS_OK;
+}
+
 int ts_cuda_forward_trace(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
                           uint32_t n_seqs, float* logits, int32_t* topk_trace) {
   if (!h || !topk_trace) return fail(TS_ERR_ARG, "ts_cuda_forward_trace: null argument");
@@ -1119,6 +1180,22 @@ int ts_cuda_op_banded_attention(const uint16_t* d_q, const uint16_t* d_k, const 
   } else {
     TS_CUDA_TRY(ts::launch_attention_exact(a, st));
   }
+  TS_CUDA_TRY(cudaStreamSynchronize(st));  // scratch above is freed on return
+  return TS_OK;
+}
+
+int ts_cuda_op_viterbi(const float* d_logits, const uint32_t* seq_offsets, uint32_t n_seqs, const float* calibration,
+                       uint8_t* d_tags, void* stream) {
+  if (!d_logits || !d_tags || !seq_offsets || n_seqs == 0) return fail(TS_ERR_ARG, "ts_cuda_op_viterbi: null argument");
+  uint32_t max_len = 0;
+  int rc = check_viterbi_args(seq_offsets, n_seqs, calibration, &max_len);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  DevArr<uint32_t> offs;  // a scratch allocation per call: this is a test/benchmark entry point
+  TS_CUDA_TRY(offs.alloc(n_seqs + 1));
+  TS_CUDA_TRY(cudaMemcpyAsync(offs.p, seq_offsets, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st));
+  TS_CUDA_TRY(ts::launch_viterbi(d_logits, reinterpret_cast<const int*>(offs.p), n_seqs, max_len, calibration, d_tags,
+                                 st));
   TS_CUDA_TRY(cudaStreamSynchronize(st));  // scratch above is freed on return
   return TS_OK;
 }

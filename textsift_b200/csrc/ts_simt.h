@@ -59,6 +59,11 @@ cudaError_t launch_swiglu_exact(const float* gu, float* out, const int* n_rows_d
 cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uint16_t* v, const int* pos,
                               const uint16_t* cos_t, const uint16_t* sin_t, uint32_t T, uint32_t qc, uint32_t kc,
                               uint32_t vc, uint32_t hd, cudaStream_t st);
+// BIOES Viterbi decoding (k_viterbi.cu): one warp per sequence of logits
+// f32 [len][33] starting at offs_dev[s]; max_len <= viterbi_max_len().
+uint32_t viterbi_max_len();
+cudaError_t launch_viterbi(const float* logits, const int* offs_dev, uint32_t n_seqs, uint32_t max_len,
+                           const float cal[6], uint8_t* tags, cudaStream_t st);
 // Fast mode: RMSNorm (b != nullptr: of a + b, the sum written to sum_out)
 // to fp16, any summation order; MoE combine from fp16 expert outputs.
 cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
