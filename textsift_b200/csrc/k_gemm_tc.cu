@@ -49,7 +49,7 @@ struct GemmCfg {
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;                    // two accumulators
   static constexpr uint32_t ACC_STRIDE = 256;                   // column offset of accumulator 1
-  static constexpr int THREADS = 512;
+  static constexpr int THREADS = 640;  // TMA, MMA, TMEM alloc, idle, 8 dequant warps, 8 epilogue warps
   static_assert(OFF_BIAS % 16 == 0 && OFF_MISC % 16 == 0, "smem regions read with 16-byte accesses");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
@@ -172,7 +172,7 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, uint32_t tile, 
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(640, 1)
     gemm_w4_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs args, uint32_t n_ntiles) {
   using C = GemmCfg<BN>;
   constexpr int S = C::STAGES;
@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(512, 1)
     for (int s = 0; s < S; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&bready[s], 128);
+      mbar_init(&bready[s], 256);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&acc_full[b], 1);
@@ -265,9 +265,9 @@ __global__ void __launch_bounds__(512, 1)
         if (ok) tc_commit(&acc_full[b]);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ---- dequantise: BN/128 B rows per thread per stage ----
-    const int t = threadIdx.x - 128;  // 0..127
+  } else if (warp >= 4 && warp < 12) {
+    // ---- dequantise: half rows (32 K values, one scale and zero point) ----
+    const int t = threadIdx.x - 128;  // 0..255
     uint32_t it = 0;
     bool ok = true;
     for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
@@ -278,19 +278,19 @@ __global__ void __launch_bounds__(512, 1)
         const uint8_t* raw = sR + s * C::RAW_STRIDE;
         uint8_t* bdst = sB + s * C::B_BYTES;
 #pragma unroll
-        for (int rr = 0; rr < BN / 128; rr++) {
-          const int r = t + rr * 128;
-          const uint4 h0 = *reinterpret_cast<const uint4*>(raw + r * 16);
-          const uint4 h1 = *reinterpret_cast<const uint4*>(raw + BN * 16 + r * 16);
-          const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + BN * 32 + r * 4);
-          const uint32_t z = raw[BN * 36 + r];
-          const uint32_t s0 = (sc & 0xffffu) * 0x00010001u, s1 = (sc >> 16) * 0x00010001u;
-          const uint32_t z0 = (0x6400u | (z & 15u)) * 0x00010001u, z1 = (0x6400u | (z >> 4)) * 0x00010001u;
-          const uint32_t wds[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        for (int uu = 0; uu < BN / 128; uu++) {
+          // unit u: row u % BN, K half u / BN (a warp takes 32 consecutive rows)
+          const int u = t + uu * 256;
+          const int r = u % BN, hf = u / BN;
+          const uint4 hw = *reinterpret_cast<const uint4*>(raw + hf * BN * 16 + r * 16);
+          const uint32_t sc = *reinterpret_cast<const uint16_t*>(raw + BN * 32 + r * 4 + hf * 2);
+          const uint32_t z = (raw[BN * 36 + r] >> (4 * hf)) & 15u;
+          const uint32_t sz = sc * 0x00010001u, zz = (0x6400u | z) * 0x00010001u;
+          const uint32_t wds[4] = {hw.x, hw.y, hw.z, hw.w};
 #pragma unroll
-          for (int c = 0; c < 8; c++) {
-            const uint32_t w = wds[c];
-            const uint32_t sz = c < 4 ? s0 : s1, zz = c < 4 ? z0 : z1;
+          for (int cc = 0; cc < 4; cc++) {
+            const uint32_t w = wds[cc];
+            const int c = 4 * hf + cc;
             uint32_t o[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -306,11 +306,11 @@ __global__ void __launch_bounds__(512, 1)
         mbar_arrive(&bready[s]);
       }
     }
-  } else if (warp >= 8) {
-    // ---- epilogue: 8 warps, lane quarter (warp % 4), column half ((warp - 8) / 4) ----
-    const uint32_t quarter = (uint32_t)(warp & 3), chalf = (uint32_t)(warp - 8) >> 2;
+  } else if (warp >= 12) {
+    // ---- epilogue: 8 warps, lane quarter (warp % 4), column half ((warp - 12) / 4) ----
+    const uint32_t quarter = (uint32_t)(warp & 3), chalf = (uint32_t)(warp - 12) >> 2;
     const uint32_t r = quarter * 32u + (uint32_t)lane;
-    const uint32_t et = threadIdx.x - 256;  // 0..255 across the 8 epilogue warps
+    const uint32_t et = threadIdx.x - 384;  // 0..255 across the 8 epilogue warps
     float* sbias_all = reinterpret_cast<float*>(smem + C::OFF_BIAS);
     uint32_t lt = 0;
     for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x, lt++) {

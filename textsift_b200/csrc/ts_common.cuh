@@ -123,9 +123,19 @@ __device__ __forceinline__ float exp_approx_ref(float x) {
   const float LOG2_E = 1.44269504088896340736f;
   float cl = x > -88.0f ? x : -88.0f;
   float y = __fmul_rn(cl, LOG2_E);
-  float fl = floorf(y);
-  int iv = (int)fl;
-  float frac = __fsub_rn(y, (float)iv);
+  // floor(y) and its integer without the conversion unit: adding 1.5 * 2^23
+  // rounds y to the nearest integer in the low mantissa bits (|y| < 2^22),
+  // one step down where that rounded up.  Same result as floorf and the int
+  // conversions for every x < 60, NaN included (checked over all such
+  // floats); callers pass x <= 0.
+  const float t = __fadd_rn(y, 12582912.0f);
+  float fl = __fsub_rn(t, 12582912.0f);
+  int iv = __float_as_int(t) - 0x4B400000;
+  if (fl > y) {
+    fl = __fsub_rn(fl, 1.0f);
+    iv -= 1;
+  }
+  float frac = __fsub_rn(y, fl);
   float p = __fmaf_rn(0.001333355f, frac, 0.009679494f);
   p = __fmaf_rn(p, frac, 0.055053319f);
   p = __fmaf_rn(p, frac, 0.240226522f);
