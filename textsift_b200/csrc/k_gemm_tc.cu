@@ -10,18 +10,22 @@
 // accumulation in TMEM.  Activations enter as fp16.
 //
 // Persistent, warp-specialized kernel: one CTA per SM walks output tiles of
-// 128 rows x BN columns (dense: row tiles of A; grouped: the 128-row tiles of
-// each expert's segment), 16 warps:
-//   warp 0       producer: TMA tile of A (128 x 64 fp16, 128B swizzle) and one
-//                bulk copy of the packed weight blob per 64-wide K chunk, into
-//                an S-stage ring that runs across tile boundaries
-//   warp 1       MMA issuer: 4 x tcgen05.mma (K=16) per chunk into one of two
-//                TMEM accumulators; commits free the stage / publish the tile
-//   warp 2       TMEM allocator (2 x 256 columns)
-//   warps 4..7   dequantise each stage's int4 blob into the swizzled fp16 B tile
-//   warps 8..15  epilogue of the previous tile while the next one accumulates:
-//                tcgen05.ld -> bias -> fused op -> global stores; warp 8+i
-//                owns TMEM lanes 32(i%4).. and half (i/4) of the columns
+// BM = 256 rows x BN = 128 columns (dense: row tiles of A; grouped: the
+// 256-row tiles of each expert's segment), 20 warps:
+//   warp 0       producer: two TMA boxes of A (2 x 128 rows x 64 fp16, 128B
+//                swizzle) and one bulk copy of the packed weight blob per
+//                64-wide K chunk, into an S-stage ring that runs across tiles
+//   warp 1       MMA issuer: per K=16 step two tcgen05.mma (M=128 each, the
+//                two row halves) sharing the dequantised B tile, into one of
+//                two TMEM tile buffers; commits free the stage / publish a tile
+//   warp 2       TMEM allocator (2 buffers x 2 accumulators x 128 columns)
+//   warps 4..11  dequantise each stage's int4 blob into the swizzled fp16 B
+//                tile (one 32-K half row per thread)
+//   warps 12..19 epilogue of the previous tile while the next one accumulates:
+//                tcgen05.ld -> bias -> fused op -> global stores; warp 12+i
+//                owns TMEM lanes 32(i%4).. of row half i/4
+// Sharing each dequantised B tile between two 128-row accumulators halves the
+// dequantisation work per flop, which bounds this kernel's tensor-core rate.
 // All waits are bounded (ts_common.cuh) and set the device error flag.
 #include "ts_common.cuh"
 #include "ts_kernels.h"
@@ -32,10 +36,12 @@
 
 namespace ts {
 
-template <int BN>
+template <int BN, int BM>
 struct GemmCfg {
-  static constexpr int STAGES = BN == 256 ? 3 : 4;
-  static constexpr uint32_t A_BYTES = 128 * 128;            // 128 rows x 64 fp16
+  static_assert(BM == 128 || BM == 256, "row tile");
+  static_assert(BM == 128 || BN == 128, "two 128-row accumulators of BN columns per tile buffer");
+  static constexpr int STAGES = (BN == 256 || BM == 256) ? (BM == 256 ? 4 : 3) : 4;
+  static constexpr uint32_t A_BYTES = BM * 128;             // BM rows x 64 fp16
   static constexpr uint32_t B_BYTES = BN * 128;             // BN rows x 64 fp16
   static constexpr uint32_t RAW_BYTES = BN * 37;            // packed blob
   static constexpr uint32_t RAW_STRIDE = (RAW_BYTES + 1023) & ~1023u;
@@ -48,7 +54,8 @@ struct GemmCfg {
   static constexpr uint32_t OFF_MISC = OFF_BIAS + 2 * BN * 4;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;                    // two accumulators
-  static constexpr uint32_t ACC_STRIDE = 256;                   // column offset of accumulator 1
+  static constexpr uint32_t ACC_STRIDE = 256;                   // column offset of tile buffer 1
+  static constexpr uint32_t ACC_ROWS = BM / 128;                // 128-row accumulators per tile buffer
   static constexpr int THREADS = 640;  // TMA, MMA, TMEM alloc, idle, 8 dequant warps, 8 epilogue warps
   static_assert(OFF_BIAS % 16 == 0 && OFF_MISC % 16 == 0, "smem regions read with 16-byte accesses");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -154,6 +161,7 @@ struct TileInfo {
   uint32_t expert, row0, row_end, n_tile;
 };
 
+template <int BM>
 __device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, uint32_t tile, uint32_t n_ntiles) {
   TileInfo ti;
   const uint32_t m = tile / n_ntiles;
@@ -165,16 +173,16 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, uint32_t tile, 
     ti.row_end = (uint32_t)t.z;
   } else {
     ti.expert = a.dense_expert;
-    ti.row0 = m * 128u;
-    ti.row_end = min(a.M, ti.row0 + 128u);
+    ti.row0 = m * (uint32_t)BM;
+    ti.row_end = min(a.M, ti.row0 + (uint32_t)BM);
   }
   return ti;
 }
 
-template <int BN, int EPI>
+template <int BN, int BM, int EPI>
 __global__ void __launch_bounds__(640, 1)
     gemm_w4_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs args, uint32_t n_ntiles) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, BM>;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(640, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
-  const uint32_t m_tiles = args.tiles ? (uint32_t)*args.n_tiles : (args.M + 127u) / 128u;
+  const uint32_t m_tiles = args.tiles ? (uint32_t)*args.n_tiles : (args.M + (uint32_t)BM - 1u) / (uint32_t)BM;
   const uint32_t total = m_tiles * n_ntiles;
   if (blockIdx.x >= total) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -226,14 +234,17 @@ __global__ void __launch_bounds__(640, 1)
       uint32_t it = 0;
       bool ok = true;
       for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const TileInfo ti = tile_info(args, tile, n_ntiles);
+        const TileInfo ti = tile_info<BM>(args, tile, n_ntiles);
         const uint8_t* wb = args.wblob + (size_t)ti.expert * args.expert_stride + (size_t)ti.n_tile * n_kc * C::RAW_BYTES;
         for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!wait_or_abort(&empty[s], ph ^ 1u, args.err, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::RAW_BYTES);
-          tma_load_2d(sA + s * C::A_BYTES, &tmap_a, (int32_t)(kc * kChunkK), (int32_t)ti.row0, &full[s]);
+#pragma unroll
+          for (uint32_t h = 0; h < C::ACC_ROWS; h++)
+            tma_load_2d(sA + s * C::A_BYTES + h * 16384u, &tmap_a, (int32_t)(kc * kChunkK), (int32_t)(ti.row0 + 128u * h),
+                        &full[s]);
           bulk_g2s(sR + s * C::RAW_STRIDE, wb + (size_t)kc * C::RAW_BYTES, C::RAW_BYTES, &full[s]);
         }
       }
@@ -258,8 +269,10 @@ __global__ void __launch_bounds__(640, 1)
           const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < 4; k++)
-            tc_mma_f16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
-                       (kc | (uint32_t)k) != 0u);
+#pragma unroll
+            for (uint32_t h = 0; h < C::ACC_ROWS; h++)
+              tc_mma_f16(d_tmem + h * BN, umma_desc_sw128(a_addr + h * 16384u + k * 32),
+                         umma_desc_sw128(b_addr + k * 32), idesc, (kc | (uint32_t)k) != 0u);
           tc_commit(&empty[s]);
         }
         if (ok) tc_commit(&acc_full[b]);
@@ -307,15 +320,18 @@ __global__ void __launch_bounds__(640, 1)
       }
     }
   } else if (warp >= 12) {
-    // ---- epilogue: 8 warps, lane quarter (warp % 4), column half ((warp - 12) / 4) ----
-    const uint32_t quarter = (uint32_t)(warp & 3), chalf = (uint32_t)(warp - 12) >> 2;
-    const uint32_t r = quarter * 32u + (uint32_t)lane;
+    // ---- epilogue: 8 warps, lane quarter (warp % 4); warp group g = (warp - 12) / 4
+    // takes the column half g (BM = 128) or the 128-row accumulator g (BM = 256) ----
+    const uint32_t quarter = (uint32_t)(warp & 3), g = (uint32_t)(warp - 12) >> 2;
+    const uint32_t rh = BM == 256 ? g : 0u, chalf = BM == 256 ? 0u : g;
+    constexpr uint32_t kCols = BM == 256 ? BN : BN / 2;
+    const uint32_t r = rh * 128u + quarter * 32u + (uint32_t)lane;
     const uint32_t et = threadIdx.x - 384;  // 0..255 across the 8 epilogue warps
     float* sbias_all = reinterpret_cast<float*>(smem + C::OFF_BIAS);
     uint32_t lt = 0;
     for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x, lt++) {
       const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
-      const TileInfo ti = tile_info(args, tile, n_ntiles);
+      const TileInfo ti = tile_info<BM>(args, tile, n_ntiles);
       const uint32_t n0 = ti.n_tile * BN;
       // stage this tile's decoded bias (two buffers: a tile's buffer is only
       // rewritten after every epilogue warp has passed the next tile's barrier)
@@ -331,12 +347,13 @@ __global__ void __launch_bounds__(640, 1)
       const uint32_t grow = ti.row0 + r;
       const bool row_ok = grow < ti.row_end;
       const uint32_t col_lo = chalf * (BN / 2);
+      const uint32_t acc = tmem_base + b * C::ACC_STRIDE + rh * BN + ((quarter * 32u) << 16);
 #pragma unroll 1
-      for (uint32_t c0 = col_lo; c0 < col_lo + BN / 2; c0 += 32) {
+      for (uint32_t c0 = col_lo; c0 < col_lo + kCols; c0 += 32) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + b * C::ACC_STRIDE + ((quarter * 32u) << 16) + c0, v);
+        tmem_ld_32x32b_x32(acc + c0, v);
         tmem_ld_wait();
-        if (c0 + 32 >= col_lo + BN / 2) {
+        if (c0 + 32 >= col_lo + kCols) {
           // every TMEM read of this buffer by this thread is complete: release it
           tc_fence_before();
           mbar_arrive(&acc_empty[b]);
@@ -485,21 +502,21 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int EPI>
+template <int BN, int BM, int EPI>
 static cudaError_t launch_one(const CUtensorMap& tmap, const GemmArgs& args, uint32_t n_tiles, uint32_t grid_m,
                               cudaStream_t st) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, BM>;
   static bool attr_done = false;
   if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_w4_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(gemm_w4_tc_kernel<BN, BM, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
   // persistent: at most one CTA per SM, never more CTAs than tiles can exist
   const uint64_t max_tiles = (uint64_t)grid_m * n_tiles;
   const uint32_t grid = (uint32_t)std::min<uint64_t>(max_tiles, (uint64_t)num_sms());
-  gemm_w4_tc_kernel<BN, EPI><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tmap, args, n_tiles);
+  gemm_w4_tc_kernel<BN, BM, EPI><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tmap, args, n_tiles);
   return cudaGetLastError();
 }
 
@@ -511,19 +528,14 @@ cudaError_t launch_gemm_w4_tc(const W4Tiles& w, const CUtensorMap& tmap_a, GemmA
   args.bias = w.bias;
   args.N = w.N;
   args.n_kc = w.n_kc;
+  // 256-row tiles: two 128-row accumulators share each dequantised weight tile
   if (w.BN == 128) {
     switch (epi) {
-      case kEpiF16: return launch_one<128, kEpiF16>(tmap_a, args, w.n_tiles, grid_m, st);
-      case kEpiF32: return launch_one<128, kEpiF32>(tmap_a, args, w.n_tiles, grid_m, st);
-      case kEpiQkvRope: return launch_one<128, kEpiQkvRope>(tmap_a, args, w.n_tiles, grid_m, st);
-      case kEpiSwiglu: return launch_one<128, kEpiSwiglu>(tmap_a, args, w.n_tiles, grid_m, st);
-      case kEpiF16Widen: return launch_one<128, kEpiF16Widen>(tmap_a, args, w.n_tiles, grid_m, st);
-    }
-  } else if (w.BN == 256) {
-    switch (epi) {
-      case kEpiF16: return launch_one<256, kEpiF16>(tmap_a, args, w.n_tiles, grid_m, st);
-      case kEpiF32: return launch_one<256, kEpiF32>(tmap_a, args, w.n_tiles, grid_m, st);
-      case kEpiSwiglu: return launch_one<256, kEpiSwiglu>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiF16: return launch_one<128, 256, kEpiF16>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiF32: return launch_one<128, 256, kEpiF32>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiQkvRope: return launch_one<128, 256, kEpiQkvRope>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiSwiglu: return launch_one<128, 256, kEpiSwiglu>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiF16Widen: return launch_one<128, 256, kEpiF16Widen>(tmap_a, args, w.n_tiles, grid_m, st);
     }
   }
   return cudaErrorInvalidValue;

@@ -408,18 +408,29 @@ __global__ void __launch_bounds__(256) moe_chunk_scan_kernel(int* __restrict__ h
   if (lane == 0) counts[e] = run;
 }
 
-// Expert segments, their 128-row GEMM tiles and the tile count from counts.
+// Expert segments, their 128-row GEMM tiles (exact path) and 256-row GEMM
+// tiles (tensor-core path), and both tile counts, from counts.
 __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __restrict__ counts, uint32_t E,
                                                                    int4* __restrict__ tiles, int* __restrict__ n_tiles,
+                                                                   int4* __restrict__ tiles256,
+                                                                   int* __restrict__ n_tiles256,
                                                                    int* __restrict__ seg_start,
                                                                    int* __restrict__ seg_end) {
-  __shared__ int off[kMaxExperts + 1], toff[kMaxExperts + 1];
+  __shared__ int off[kMaxExperts + 1], toff[kMaxExperts + 1], toff2[kMaxExperts + 1];
   const uint32_t e = threadIdx.x;
-  if (e < E) { off[e + 1] = counts[e]; toff[e + 1] = (counts[e] + 127) / 128; }
-  if (e == 0) { off[0] = 0; toff[0] = 0; }
+  if (e < E) {
+    off[e + 1] = counts[e];
+    toff[e + 1] = (counts[e] + 127) / 128;
+    toff2[e + 1] = (counts[e] + 255) / 256;
+  }
+  if (e == 0) { off[0] = 0; toff[0] = 0; toff2[0] = 0; }
   __syncthreads();
   if (e == 0)
-    for (uint32_t i = 1; i <= E; i++) { off[i] += off[i - 1]; toff[i] += toff[i - 1]; }
+    for (uint32_t i = 1; i <= E; i++) {
+      off[i] += off[i - 1];
+      toff[i] += toff[i - 1];
+      toff2[i] += toff2[i - 1];
+    }
   __syncthreads();
   if (e < E) {
     const int base = off[e], cnt = off[e + 1] - off[e];
@@ -427,8 +438,14 @@ __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __
     seg_end[e] = off[e + 1];
     for (int tt = 0; tt * 128 < cnt; tt++)
       tiles[toff[e] + tt] = make_int4((int)e, base + tt * 128, base + min(cnt, tt * 128 + 128), base);
+    if (tiles256)
+      for (int tt = 0; tt * 256 < cnt; tt++)
+        tiles256[toff2[e] + tt] = make_int4((int)e, base + tt * 256, base + min(cnt, tt * 256 + 256), base);
   }
-  if (e == 0) *n_tiles = toff[E];
+  if (e == 0) {
+    *n_tiles = toff[E];
+    if (n_tiles256) *n_tiles256 = toff2[E];
+  }
 }
 
 __global__ void __launch_bounds__(kRouteChunk) moe_place_kernel(const int32_t* __restrict__ idx,
@@ -819,12 +836,12 @@ cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, int*
 }
 
 cudaError_t launch_moe_permute(const int32_t* idx, int* hist, uint32_t T, uint32_t K, uint32_t E, int* counts,
-                               int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int* seg_start, int* seg_end,
-                               cudaStream_t st) {
+                               int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int4* tiles256,
+                               int* n_tiles256, int* seg_start, int* seg_end, cudaStream_t st) {
   if (E > kMaxExperts || K > 8) return cudaErrorInvalidValue;
   const uint32_t nc = route_chunks(T);
   moe_chunk_scan_kernel<<<(E + 7) / 8, 256, 0, st>>>(hist, nc, E, counts);
-  moe_segments_kernel<<<1, kMaxExperts, 0, st>>>(counts, E, tiles, n_tiles, seg_start, seg_end);
+  moe_segments_kernel<<<1, kMaxExperts, 0, st>>>(counts, E, tiles, n_tiles, tiles256, n_tiles256, seg_start, seg_end);
   moe_place_kernel<<<nc, kRouteChunk, 0, st>>>(idx, hist, seg_start, T, K, E, perm_tok, route_pos);
   return cudaGetLastError();
 }

@@ -206,8 +206,8 @@ struct Workspace {
   DevArr<uint16_t> x0, x1, xn16, q, k, v, attn, o16, res2, qkv16, down16;
   DevArr<float> n32, hf32, rlogits, rw;
   DevArr<int32_t> ridx;
-  DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, hist;
-  DevArr<int4> tiles;
+  DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, n_tiles256, hist;
+  DevArr<int4> tiles, tiles256;
   DevArr<int2> atiles;
   std::vector<int2> atiles_host;
   DevArr<uint16_t> aperm16, glu16;
@@ -359,6 +359,8 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.route_pos.alloc(R));
     TS_CUDA_TRY(w.n_tiles.alloc(1));
     TS_CUDA_TRY(w.tiles.alloc(R / 128 + E + 1));
+    TS_CUDA_TRY(w.n_tiles256.alloc(1));
+    TS_CUDA_TRY(w.tiles256.alloc(R / 256 + E + 1));
     TS_CUDA_TRY(w.aperm16.alloc(R * D));
     TS_CUDA_TRY(w.glu16.alloc(R * F));
     TS_CUDA_TRY(w.down32.alloc(R * D));
@@ -447,7 +449,7 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
     }
     TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, w.hist.p, T, E, K, st));
     TS_K(ts::launch_moe_permute(w.ridx.p, w.hist.p, T, K, E, w.counts.p, w.perm_tok.p, w.route_pos.p, w.tiles.p,
-                                w.n_tiles.p, w.seg_start.p, w.seg_end.p, st));
+                                w.n_tiles.p, w.tiles256.p, w.n_tiles256.p, w.seg_start.p, w.seg_end.p, st));
   }
   if (h->trace_topk && layer >= 0)
     TS_K(cudaMemcpyAsync(h->trace_topk + (size_t)layer * T * K, w.ridx.p, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
@@ -461,14 +463,14 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
     if (!ts::make_act_tmap(&ta, w.aperm16.p, R, D) || !ts::make_act_tmap(&tg, w.glu16.p, R, F))
       return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the expert operands");
     ts::GemmArgs g;
-    g.tiles = w.tiles.p; g.n_tiles = w.n_tiles.p; g.err = h->err.p;
+    g.tiles = w.tiles256.p; g.n_tiles = w.n_tiles256.p; g.err = h->err.p;
     g.out0 = w.glu16.p; g.ld0 = F;
     {
       Phase p(h, st, TS_PHASE_EXPERT_GATE_UP, fl_gu, 1);
       TS_K(ts::launch_gemm_w4_tc(L.gate_up.tiles(), ta, g, ts::kEpiSwiglu, grid_tiles, st));
     }
     ts::GemmArgs g2;
-    g2.tiles = w.tiles.p; g2.n_tiles = w.n_tiles.p; g2.err = h->err.p;
+    g2.tiles = w.tiles256.p; g2.n_tiles = w.n_tiles256.p; g2.err = h->err.p;
     g2.out0 = w.down16.p; g2.ld0 = D;
     {
       Phase p(h, st, TS_PHASE_EXPERT_DOWN, fl_dn, 1);
@@ -779,7 +781,7 @@ int ts_cuda_finalize(ts_cuda_t* h) {
         (rc = w4_upload(L->router, p8(p + "router.int4"), p16(p + "router.scales"), p8(p + "router.zp"),
                         p16(p + "router.bias"), 1, E, D, 128, true, bad.p, st)) ||
         (rc = w4_upload(L->gate_up, p8(p + "experts.gate_up.int4"), p16(p + "experts.gate_up.scales"),
-                        p8(p + "experts.gate_up.zp"), p16(p + "experts.gate_up.bias"), E, 2 * F, D, 256, true, bad.p,
+                        p8(p + "experts.gate_up.zp"), p16(p + "experts.gate_up.bias"), E, 2 * F, D, 128, true, bad.p,
                         st)) ||
         (rc = w4_upload(L->down, p8(p + "experts.down.int4"), p16(p + "experts.down.scales"),
                         p8(p + "experts.down.zp"), p16(p + "experts.down.bias"), E, D, F, 128, true, bad.p, st)))
@@ -1038,7 +1040,7 @@ ts_cuda_w4_t* ts_cuda_w4_create(int32_t device, const uint8_t* int4, const uint1
     return bad("ts_cuda_w4_create: CUDA initialisation failed");
   }
   DevArr<int> nb;
-  const uint32_t BN = N >= 256 && N % 256 == 0 ? 256 : 128;
+  const uint32_t BN = 128;
   int rc = nb.alloc(1) == cudaSuccess && cudaMemsetAsync(nb.p, 0, 4, w->stream) == cudaSuccess
                ? w4_upload(w->w, int4, scales, zp, bias, E, N, K, BN, true, nb.p, w->stream)
                : TS_ERR_CUDA;
