@@ -11,7 +11,7 @@ import ctypes
 import numpy as np
 import pytest
 
-from gpu_util import dev, empty, f16, host, ptr, stream, ulp_diff
+from gpu_util import dev, empty, f16, host, ptr, rand_w4, stream, ulp_diff, w4_handle
 
 pytestmark = pytest.mark.gpu
 
@@ -27,24 +27,6 @@ def L(cuda_lib):
 
 def rng(seed):
     return np.random.Generator(np.random.PCG64(seed))
-
-
-def rand_w4(r, E, N, K, zp_random=True, scale_range=(1e-3, 1e-2)):
-    int4 = r.integers(0, 256, size=(E, N, K // 2), dtype=np.uint8)
-    sc = r.uniform(*scale_range, size=(E, N, K // 32)).astype(np.float16).view(F16)
-    zb = (K // 32 + 1) // 2
-    zp = r.integers(0, 256, size=(E, N, zb), dtype=np.uint8) if zp_random else np.full((E, N, zb), 0x88, np.uint8)
-    bias = r.normal(0, 0.05, size=(E, N)).astype(np.float16).view(F16)
-    return int4, sc, zp, bias
-
-
-def w4_handle(L, int4, sc, zp, bias):
-    E, N, K2 = int4.shape
-    err = ctypes.create_string_buffer(512)
-    h = L.ts_cuda_w4_create(0, int4.ctypes.data, sc.ctypes.data, zp.ctypes.data if zp is not None else None,
-                            bias.ctypes.data, E, N, K2 * 2, err, 512)
-    assert h, err.value
-    return h
 
 
 # ----------------------------------------------------------------- embedding
