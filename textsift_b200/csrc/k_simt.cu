@@ -310,6 +310,12 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
 constexpr uint32_t kRouteChunk = 128;  // tokens per top-k block / permutation chunk
 constexpr uint32_t kMaxExperts = 256;
 
+// One warp per token: K rounds of a warp arg-max (value desc, index asc: the
+// reference's insertion order, wasm_exports.zig:367-426) over SLOTS logits
+// per lane, then the softmax over the K values in order
+// (wasm_exports.zig:919-958) with the K exact exponentials computed at once
+// on lanes 0..K-1.  hist: per-chunk expert counts for the permutation.
+template <int SLOTS>
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int32_t* __restrict__ idx,
                                                           float* __restrict__ w, int* __restrict__ hist, uint32_t T,
                                                           uint32_t E, uint32_t K, double inv_k) {
@@ -322,24 +328,29 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     const uint32_t t = t0 + tl;
     if (t >= T) break;
     const float* row = logits + (size_t)t * E;
-    float v[kMaxExperts / 32];
-    bool avail[kMaxExperts / 32];
+    float v[SLOTS];
+    bool avail[SLOTS];
 #pragma unroll
-    for (int j = 0; j < (int)(kMaxExperts / 32); j++) {
+    for (int j = 0; j < SLOTS; j++) {
       const uint32_t c = lane + 32 * j;
       avail[j] = c < E;
       v[j] = avail[j] ? row[c] : 0.0f;
     }
     float ov[8];
     int oi[8];
-    for (uint32_t k = 0; k < K; k++) {
+#pragma unroll
+    for (uint32_t k = 0; k < 8; k++) {
+      ov[k] = 0.0f;
+      oi[k] = 0;
+      if (k >= K) continue;
       float bv = 0.0f;
       int bi = 0x7fffffff;
 #pragma unroll
-      for (int j = 0; j < (int)(kMaxExperts / 32); j++) {
+      for (int j = 0; j < SLOTS; j++) {
         const int c = lane + 32 * j;
         if (avail[j] && (bi == 0x7fffffff || v[j] > bv || (v[j] == bv && c < bi))) { bv = v[j]; bi = c; }
       }
+#pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ovv = __shfl_xor_sync(0xffffffffu, bv, o);
         const int oii = __shfl_xor_sync(0xffffffffu, bi, o);
@@ -348,17 +359,17 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
       ov[k] = bv;
       oi[k] = bi;
 #pragma unroll
-      for (int j = 0; j < (int)(kMaxExperts / 32); j++)
+      for (int j = 0; j < SLOTS; j++)
         if (lane + 32 * j == bi) avail[j] = false;
     }
-    // softmax over the k values in order (wasm_exports.zig:919-958): lane c
-    // computes exp of entry c, lane 0 sums them in order
     float m = ov[0];
     for (uint32_t c = 1; c < K; c++) if (ov[c] > m) m = ov[c];
-    float my_e = 0.0f;
+    // lane c < K: exp of entry c (one exact exponential per lane, no divergence)
+    float mine = ov[0];
 #pragma unroll
-    for (uint32_t c = 0; c < 8; c++)
-      if (c < K && (uint32_t)lane == c) my_e = expf_ref(__fsub_rn(ov[c], m));
+    for (int c = 1; c < 8; c++)
+      if (lane == c) mine = ov[c];
+    const float my_e = expf_ref(__fsub_rn(mine, m));
     float e[8];
 #pragma unroll
     for (uint32_t c = 0; c < 8; c++) e[c] = __shfl_sync(0xffffffffu, my_e, c);
@@ -408,6 +419,24 @@ __global__ void __launch_bounds__(256) moe_chunk_scan_kernel(int* __restrict__ h
   if (lane == 0) counts[e] = run;
 }
 
+// Exclusive prefix sum of one int per thread over a block of up to
+// kMaxExperts threads (warp shuffles, then the warp totals).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int base = 0;
+  for (int i = 0; i < warp; i++) base += warp_tot[i];
+  __syncthreads();  // warp_tot may be reused by the caller
+  return base + incl - v;
+}
+
 // Expert segments, their 128-row GEMM tiles (exact path) and 256-row GEMM
 // tiles (tensor-core path), and both tile counts, from counts.
 __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __restrict__ counts, uint32_t E,
@@ -416,35 +445,25 @@ __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __
                                                                    int* __restrict__ n_tiles256,
                                                                    int* __restrict__ seg_start,
                                                                    int* __restrict__ seg_end) {
-  __shared__ int off[kMaxExperts + 1], toff[kMaxExperts + 1], toff2[kMaxExperts + 1];
+  __shared__ int wt[kMaxExperts / 32];
   const uint32_t e = threadIdx.x;
+  const int cnt = e < E ? counts[e] : 0;
+  const int t1 = (cnt + 127) / 128, t2 = (cnt + 255) / 256;
+  const int base = block_exclusive_scan(cnt, wt);
+  const int tb1 = block_exclusive_scan(t1, wt);
+  const int tb2 = block_exclusive_scan(t2, wt);
   if (e < E) {
-    off[e + 1] = counts[e];
-    toff[e + 1] = (counts[e] + 127) / 128;
-    toff2[e + 1] = (counts[e] + 255) / 256;
-  }
-  if (e == 0) { off[0] = 0; toff[0] = 0; toff2[0] = 0; }
-  __syncthreads();
-  if (e == 0)
-    for (uint32_t i = 1; i <= E; i++) {
-      off[i] += off[i - 1];
-      toff[i] += toff[i - 1];
-      toff2[i] += toff2[i - 1];
-    }
-  __syncthreads();
-  if (e < E) {
-    const int base = off[e], cnt = off[e + 1] - off[e];
     seg_start[e] = base;
-    seg_end[e] = off[e + 1];
-    for (int tt = 0; tt * 128 < cnt; tt++)
-      tiles[toff[e] + tt] = make_int4((int)e, base + tt * 128, base + min(cnt, tt * 128 + 128), base);
+    seg_end[e] = base + cnt;
+    for (int tt = 0; tt < t1; tt++)
+      tiles[tb1 + tt] = make_int4((int)e, base + tt * 128, base + min(cnt, tt * 128 + 128), base);
     if (tiles256)
-      for (int tt = 0; tt * 256 < cnt; tt++)
-        tiles256[toff2[e] + tt] = make_int4((int)e, base + tt * 256, base + min(cnt, tt * 256 + 256), base);
+      for (int tt = 0; tt < t2; tt++)
+        tiles256[tb2 + tt] = make_int4((int)e, base + tt * 256, base + min(cnt, tt * 256 + 256), base);
   }
-  if (e == 0) {
-    *n_tiles = toff[E];
-    if (n_tiles256) *n_tiles256 = toff2[E];
+  if (e == E - 1) {
+    *n_tiles = tb1 + t1;
+    if (n_tiles256) *n_tiles256 = tb2 + t2;
   }
 }
 
@@ -613,9 +632,11 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
   }
 }
 
-// MoE combine from fp16 expert outputs, one thread per (token, 8 columns):
-// acc = sum over the token's experts in ascending id of w * v (fma, from 0);
-// out = fp16(res + fp16(acc * K)) (or fp16(acc * K) without a residual).
+// MoE combine from fp16 expert outputs, one warp per token: lanes 0..K-1
+// read the token's routes and order them by expert id (ties by slot), the
+// warp then streams the rows in 8-column chunks: acc = sum over the experts
+// in ascending id of w * v (fma, from 0); out = fp16(res + fp16(acc * K))
+// (or fp16(acc * K) without a residual).
 __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* __restrict__ down,
                                                                const int32_t* __restrict__ idx,
                                                                const float* __restrict__ w,
@@ -623,54 +644,73 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
                                                                const uint16_t* __restrict__ res,
                                                                uint16_t* __restrict__ out, uint32_t T, uint32_t D,
                                                                uint32_t K, uint32_t E) {
-  const uint32_t nc = D / 8;
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (size_t)T * nc) return;
-  const uint32_t t = (uint32_t)(i / nc), c = (uint32_t)(i % nc);
-  int ek[8], pk[8];
-  float wk[8];
-  uint32_t n = 0;
-  for (uint32_t k = 0; k < K; k++) {
-    const int e = idx[(size_t)t * K + k];
-    if (e < 0 || (uint32_t)e >= E) continue;
-    uint32_t j = n++;
-    ek[j] = e; wk[j] = w[(size_t)t * K + k]; pk[j] = route_pos[(size_t)t * K + k];
-    while (j > 0 && ek[j] < ek[j - 1]) {
-      int te = ek[j]; ek[j] = ek[j - 1]; ek[j - 1] = te;
-      float tw = wk[j]; wk[j] = wk[j - 1]; wk[j - 1] = tw;
-      int tp = pk[j]; pk[j] = pk[j - 1]; pk[j - 1] = tp;
-      j--;
+  const uint32_t t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  int my_e = 0x7fffffff, my_p = 0;
+  float my_w = 0.0f;
+  if ((uint32_t)lane < K) {
+    const int e = idx[(size_t)t * K + lane];
+    if (e >= 0 && (uint32_t)e < E) {
+      my_e = e;
+      my_w = w[(size_t)t * K + lane];
+      my_p = route_pos[(size_t)t * K + lane];
     }
   }
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (uint32_t j = 0; j < n; j++) {
-    const uint4 v = *reinterpret_cast<const uint4*>(down + (size_t)pk[j] * D + 8 * c);
-    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+  // rank of this lane's route among the valid ones: (expert id, slot) order
+  int rank = 0, n = 0;
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vw[q]));
-      acc[2 * q] = fmaf(wk[j], f.x, acc[2 * q]);
-      acc[2 * q + 1] = fmaf(wk[j], f.y, acc[2 * q + 1]);
+  for (int j = 0; j < 8; j++) {
+    const int ej = __shfl_sync(0xffffffffu, my_e, j);
+    if ((uint32_t)j < K && ej != 0x7fffffff) {
+      n++;
+      rank += (ej < my_e || (ej == my_e && j < lane)) ? 1 : 0;
     }
+  }
+  int pk[8];
+  float wk[8];
+#pragma unroll
+  for (int r = 0; r < 8; r++) {
+    // the lane whose route has rank r
+    const unsigned sel = __ballot_sync(0xffffffffu, (uint32_t)lane < K && my_e != 0x7fffffff && rank == r);
+    const int src = sel ? __ffs(sel) - 1 : 0;
+    pk[r] = __shfl_sync(0xffffffffu, my_p, src);
+    wk[r] = __shfl_sync(0xffffffffu, my_w, src);
   }
   const float kf = (float)K;
-  const size_t o = (size_t)t * D + 8 * c;
-  uint32_t ow[4];
-  if (res) {
-    const uint4 rv = *reinterpret_cast<const uint4*>(res + o);
-    const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+  const uint32_t nc = D / 8;
+  for (uint32_t c = (uint32_t)lane; c < nc; c += 32) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const uint32_t m = f32x2_to_h2(acc[2 * q] * kf, acc[2 * q + 1] * kf);
-      const float2 mf = __half22float2(*reinterpret_cast<const __half2*>(&m));
-      const float2 rf = __half22float2(*reinterpret_cast<const __half2*>(&rw[q]));
-      ow[q] = f32x2_to_h2(rf.x + mf.x, rf.y + mf.y);
+    for (int j = 0; j < 8; j++) {
+      if (j >= n) break;
+      const uint4 v = *reinterpret_cast<const uint4*>(down + (size_t)pk[j] * D + 8 * c);
+      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vw[q]));
+        acc[2 * q] = fmaf(wk[j], f.x, acc[2 * q]);
+        acc[2 * q + 1] = fmaf(wk[j], f.y, acc[2 * q + 1]);
+      }
     }
-  } else {
+    const size_t o = (size_t)t * D + 8 * c;
+    uint32_t ow[4];
+    if (res) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(res + o);
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-    for (int q = 0; q < 4; q++) ow[q] = f32x2_to_h2(acc[2 * q] * kf, acc[2 * q + 1] * kf);
+      for (int q = 0; q < 4; q++) {
+        const uint32_t m = f32x2_to_h2(acc[2 * q] * kf, acc[2 * q + 1] * kf);
+        const float2 mf = __half22float2(*reinterpret_cast<const __half2*>(&m));
+        const float2 rf = __half22float2(*reinterpret_cast<const __half2*>(&rw[q]));
+        ow[q] = f32x2_to_h2(rf.x + mf.x, rf.y + mf.y);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; q++) ow[q] = f32x2_to_h2(acc[2 * q] * kf, acc[2 * q + 1] * kf);
+    }
+    *reinterpret_cast<uint4*>(out + o) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
-  *reinterpret_cast<uint4*>(out + o) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }
 
 // SwiGLU-clamp on f32 (gate even, up odd), 4-lane polynomial body.
@@ -831,7 +871,11 @@ cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, int*
                                uint32_t K, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (K > 8 || K > E || E > kMaxExperts) return cudaErrorInvalidValue;
-  router_topk_kernel<<<route_chunks(T), 256, 0, st>>>(logits, idx, w, hist, T, E, K, 1.0 / (double)K);
+  if (E <= 128)
+    router_topk_kernel<4><<<route_chunks(T), 256, 0, st>>>(logits, idx, w, hist, T, E, K, 1.0 / (double)K);
+  else
+    router_topk_kernel<kMaxExperts / 32><<<route_chunks(T), 256, 0, st>>>(logits, idx, w, hist, T, E, K,
+                                                                           1.0 / (double)K);
   return cudaGetLastError();
 }
 
@@ -894,8 +938,7 @@ cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, co
                                     uint32_t E, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (D % 8 || K > 8) return cudaErrorInvalidValue;
-  const size_t n = (size_t)T * (D / 8);
-  moe_combine_fast_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(down, idx, w, route_pos, res, out, T, D, K, E);
+  moe_combine_fast_kernel<<<(T + 7) / 8, 256, 0, st>>>(down, idx, w, route_pos, res, out, T, D, K, E);
   return cudaGetLastError();
 }
 
