@@ -78,6 +78,25 @@ ts_cuda_t* ts_cuda_create(const ts_cuda_cfg* cfg, char* err, size_t err_cap);
 int ts_cuda_load_tensor(ts_cuda_t* h, const char* name, int32_t dtype, const int64_t* shape, int32_t ndim,
                         const void* host_data, size_t nbytes);
 
+/* Upload every weight from the model's ONNX files: graph = the bytes of
+ * onnx/model_q4f16.onnx, ext_data = the bytes of onnx/model_q4f16.onnx_data
+ * (may be NULL when no initializer is stored externally).  Replaces
+ * loadOnnxWeights (browser/backends/wasm.ts:328-453): the same initializer
+ * names, layer-count probe and conversions (router scales and bias f32 ->
+ * fp16, expert zero points 0x88, zero classifier bias, sinks flattened to
+ * [Hq]), each tensor then loaded as by ts_cuda_load_tensor.  On failure
+ * returns TS_ERR_ARG (or the load error) with a message in err. */
+int ts_cuda_load_onnx(ts_cuda_t* h, const uint8_t* graph, size_t graph_len, const uint8_t* ext_data, size_t ext_len,
+                      char* err, size_t err_cap);
+
+/* Host-only (no device): one initializer of an ONNX graph as the loader sees
+ * it -- ONNX data type, dims (up to 8 written, *ndim = their count), whether
+ * it is external, and its byte offset (in ext_data, or in graph for inline
+ * data) and length.  TS_ERR_ARG if the graph does not parse or has no such
+ * tensor.  Parser check for the loader (onnx-reader.ts:158-240). */
+int ts_cuda_onnx_tensor_info(const uint8_t* graph, size_t graph_len, const char* name, int32_t* onnx_dtype,
+                             int64_t* dims, int32_t* ndim, int32_t* external, uint64_t* offset, uint64_t* nbytes);
+
 /* Check that every tensor is present, repack the int4 GEMM weights into
  * tensor-core tiles and build the YaRN RoPE tables.  Idempotent, like
  * InferenceBackend.warmup (browser/backends/abstract.ts:44). */

@@ -55,6 +55,8 @@ SIGNATURES = [
     ("ts_cuda_create", P, [ctypes.POINTER(Cfg), ctypes.c_char_p, ctypes.c_size_t]),
     ("ts_cuda_load_tensor", ctypes.c_int, [P, ctypes.c_char_p, I32, ctypes.POINTER(ctypes.c_int64), I32, P,
                                            ctypes.c_size_t]),
+    ("ts_cuda_load_onnx", ctypes.c_int, [P, P, ctypes.c_size_t, P, ctypes.c_size_t, P, ctypes.c_size_t]),
+    ("ts_cuda_onnx_tensor_info", ctypes.c_int, [P, ctypes.c_size_t, ctypes.c_char_p, P, P, P, P, P, P]),
     ("ts_cuda_finalize", ctypes.c_int, [P]),
     ("ts_cuda_set_mode", ctypes.c_int, [P, I32]),
     ("ts_cuda_forward", ctypes.c_int, [P, P, P, U32, P]),

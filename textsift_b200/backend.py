@@ -67,10 +67,26 @@ class CudaBackend:
     def __init__(self, tensors: Mapping[str, np.ndarray], cfg: Mapping | None = None, *, device: int = 0,
                  max_tokens: int = 65536, max_seq_len: int = 8192, mode: int = abi.TS_MODE_FAST):
         self._tensors = tensors
+        self._onnx = None  # (graph bytes, external-data bytes) for from_onnx
         self._cfg = make_cfg(cfg, device=device, max_tokens=max_tokens, max_seq_len=max_seq_len, mode=mode)
         self.num_classes = int(self._cfg.n_classes)
         self._h = None
         self._ready = False
+
+    @classmethod
+    def from_onnx(cls, graph: bytes | str, ext_data: bytes | str | None = None, cfg: Mapping | None = None,
+                  **kw) -> "CudaBackend":
+        """Weights from the model's ONNX files (onnx/model_q4f16.onnx and
+        onnx/model_q4f16.onnx_data; bytes or paths), mapped and converted by
+        the addon the way loadOnnxWeights does (browser/backends/wasm.ts)."""
+        def _bytes(x):
+            if x is None or isinstance(x, (bytes, bytearray)):
+                return x
+            with open(x, "rb") as f:
+                return f.read()
+        b = cls({}, cfg, **kw)
+        b._onnx = (_bytes(graph), _bytes(ext_data))
+        return b
 
     # -- lifecycle -------------------------------------------------------
     def warmup(self) -> None:
@@ -84,6 +100,15 @@ class CudaBackend:
             if not h:
                 raise abi.TextsiftCudaError(abi.TS_ERR_CUDA, err.value.decode(errors="replace"))
             self._h = h
+        if self._onnx is not None:
+            graph, ext = self._onnx
+            g = np.frombuffer(graph, dtype=np.uint8)
+            e = np.frombuffer(ext, dtype=np.uint8) if ext else None
+            err = ctypes.create_string_buffer(1024)
+            rc = L.ts_cuda_load_onnx(self._h, _ptr(g), g.size, _ptr(e), 0 if e is None else e.size, err, 1024)
+            if rc != 0:
+                raise abi.TextsiftCudaError(rc, err.value.decode(errors="replace"))
+            self._onnx = None
         for name, arr in self._tensors.items():
             a = np.ascontiguousarray(arr)
             shape = (ctypes.c_int64 * a.ndim)(*a.shape)
