@@ -209,7 +209,6 @@ struct Workspace {
   DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, n_tiles256, hist;
   DevArr<int4> tiles, tiles256;
   DevArr<int2> atiles;
-  std::vector<int2> atiles_host;
   DevArr<uint16_t> aperm16, glu16;
   DevArr<float> aperm32, gu32, glu32, down32;
   DevArr<float> logits;
@@ -235,6 +234,12 @@ struct ts_cuda {
   // pinned staging for the host-pointer forward
   uint8_t* pin = nullptr;
   size_t pin_bytes = 0;
+  // pinned ring for each forward's small host -> device copies (sequence
+  // offsets, attention tile list): a slot is reused only after the copies
+  // queued from it have executed, so the host can run forwards ahead
+  struct Stage { uint8_t* p = nullptr; size_t cap = 0; cudaEvent_t done = nullptr; };
+  Stage stage[4];
+  uint32_t stage_next = 0;
   // when set, each layer's top-k experts are copied here ([n_layers][T][top_k])
   int32_t* trace_topk = nullptr;
   // kernel launches issued by forwards / MoE ops (ts_cuda_profile_read)
@@ -368,7 +373,6 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.logits.alloc(T * c.n_classes));
     TS_CUDA_TRY(w.qkv16.alloc(T * (Q + 2 * KV)));
     TS_CUDA_TRY(w.atiles.alloc(ts::attention_max_tiles((uint32_t)T, (uint32_t)T)));
-    w.atiles_host.resize(ts::attention_max_tiles((uint32_t)T, (uint32_t)T));
     w.cap = (uint32_t)T;
   }
   if (exact && !w.exact_ready) {
@@ -497,6 +501,23 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
   return TS_OK;
 }
 
+// Next slot of the pinned staging ring with room for `bytes`, once the copies
+// queued from it by an earlier forward have executed.
+static int next_stage(ts_cuda* h, size_t bytes, ts_cuda::Stage** out) {
+  ts_cuda::Stage& sg = h->stage[h->stage_next++ % 4];
+  if (sg.done) TS_CUDA_TRY(cudaEventSynchronize(sg.done));
+  else TS_CUDA_TRY(cudaEventCreateWithFlags(&sg.done, cudaEventDisableTiming));
+  if (sg.cap < bytes) {
+    if (sg.p) cudaFreeHost(sg.p);
+    sg.p = nullptr;
+    sg.cap = 0;
+    TS_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&sg.p), bytes, cudaHostAllocDefault));
+    sg.cap = bytes;
+  }
+  *out = &sg;
+  return TS_OK;
+}
+
 int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, const uint32_t* offs, uint32_t n_seqs,
                    float* d_logits, cudaStream_t st) {
   if (!h->finalized) return fail(TS_ERR_STATE, "ts_cuda_finalize has not succeeded");
@@ -516,7 +537,14 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   Workspace& w = h->ws;
   const uint32_t D = c.d_model, Q = c.n_heads * c.head_dim, KV = c.n_kv_heads * c.head_dim;
 
-  TS_K(cudaMemcpyAsync(w.offs.p, offs, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st));
+  // small host -> device copies through the pinned ring (offsets, then the
+  // attention tile list at a 16-byte aligned offset)
+  const size_t offs_bytes = ((size_t)(n_seqs + 1) * 4 + 15) & ~size_t(15);
+  ts_cuda::Stage* sg = nullptr;
+  int rc0 = next_stage(h, offs_bytes + (size_t)ts::attention_max_tiles(T, n_seqs) * sizeof(int2), &sg);
+  if (rc0) return rc0;
+  memcpy(sg->p, offs, (size_t)(n_seqs + 1) * 4);
+  TS_K(cudaMemcpyAsync(w.offs.p, sg->p, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st));
   {
     Phase p(h, st, TS_PHASE_OTHER, 0, 2);
     TS_K(ts::launch_seq_info(w.offs.p, n_seqs, T, w.pos.p, w.sstart.p, w.slen.p, st));
@@ -541,11 +569,13 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   aa.hd = c.head_dim; aa.window = c.window; aa.err = h->err.p;
   if (!exact) {
     uint32_t nt = 0;
-    ts::attention_tiles(offs, n_seqs, w.atiles_host.data(), &nt);
-    TS_K(cudaMemcpyAsync(w.atiles.p, w.atiles_host.data(), (size_t)nt * sizeof(int2), cudaMemcpyHostToDevice, st));
+    int2* th = reinterpret_cast<int2*>(sg->p + offs_bytes);
+    ts::attention_tiles(offs, n_seqs, th, &nt);
+    TS_K(cudaMemcpyAsync(w.atiles.p, th, (size_t)nt * sizeof(int2), cudaMemcpyHostToDevice, st));
     aa.tiles = w.atiles.p;
     aa.n_tiles = nt;
   }
+  TS_K(cudaEventRecord(sg->done, st));  // the staging slot is free once this passes
 
   uint16_t* src = w.x0.p;
   uint16_t* dst = w.x1.p;
@@ -992,6 +1022,10 @@ void ts_cuda_destroy(ts_cuda_t* h) {
     DevGuard g(h->cfg.device);
     if (h->stream) cudaStreamSynchronize(h->stream);
     if (h->pin) cudaFreeHost(h->pin);
+    for (auto& sg : h->stage) {
+      if (sg.p) cudaFreeHost(sg.p);
+      if (sg.done) cudaEventDestroy(sg.done);
+    }
     for (auto& m : h->marks) { cudaEventDestroy(m.a); cudaEventDestroy(m.b); }
     for (auto e : h->ev_pool) cudaEventDestroy(e);
     h->layers.clear();
