@@ -203,9 +203,11 @@ int ts_cuda_op_dequant(const ts_cuda_w4_t* w, uint32_t expert, uint16_t* d_out, 
 int ts_cuda_op_matmul_nbits(const ts_cuda_w4_t* w, uint32_t expert, const void* d_x, int32_t x_dtype, void* d_out,
                             int32_t out_dtype, uint32_t M, int32_t mode, void* stream);
 
-/* Router of layer `layer`: f32 logits in the reference order, top-k with the
- * reference tie rule, softmax over k, x 1/k (browser/inference/block.ts:
- * 154-207).  d_x: f32 [T, d_model]; d_idx: i32 [T, k]; d_w: f32 [T, k]. */
+/* Router of layer `layer`: logits, top-k with the reference tie rule,
+ * softmax over k, x 1/k (browser/inference/block.ts:154-207).  Exact mode:
+ * f32 logits in the reference order.  Fast mode (the forward's fast path):
+ * logits on the tensor cores from fp16(x), top-k in the GEMM epilogue.
+ * d_x: f32 [T, d_model]; d_idx: i32 [T, k]; d_w: f32 [T, k]. */
 int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32_t* d_idx, float* d_w, uint32_t T,
                            void* stream);
 

@@ -17,7 +17,7 @@ token's first disagreement is a near-tie of the reference's own router logits.
 import numpy as np
 import pytest
 
-from gpu_util import dev, empty, f16, host, ptr, stream, ulp_diff
+from gpu_util import dev, empty, f16, host, ptr, stream, ulp_diff, w4_handle
 
 pytestmark = pytest.mark.gpu
 
@@ -60,18 +60,63 @@ def f32_ulps(a, b):
 
 
 def test_router_topk_bit_exact(small_backend, small_oracle, cuda_lib):
+    from textsift_b200 import abi
     T = 1000
     x = rng(1).normal(0, 1, size=(T, 640)).astype(np.float32)
     idx = empty((T, 4), np.int32)
     w = empty((T, 4), np.float32)
+    small_backend.set_mode(abi.TS_MODE_EXACT)
+    try:
+        for layer in (0, 1):
+            assert cuda_lib.ts_cuda_op_router_topk(small_backend.handle, layer, ptr(dev(x)), ptr(idx), ptr(w), T,
+                                                   stream()) == 0
+            _, ridx, rw = small_oracle.moe(layer, x)
+            assert np.array_equal(host(idx, np.int32), ridx)
+            # weights: softmax over 4 with exp -> CUDA expf vs the C library's
+            # expf may differ by an ulp
+            assert f32_ulps(host(w, np.float32), rw).max() <= 1
+    finally:
+        small_backend.set_mode(abi.TS_MODE_FAST)
+
+
+@pytest.mark.parametrize("T", [1000, 4097])
+def test_router_topk_fast_fused(small, small_backend, cuda_lib, oracle, T):
+    """Fast mode: the top-k fused into the router GEMM's epilogue selects
+    and weights exactly as the reference top-k does on that GEMM's own f32
+    logits (the same tensor-core kernel writing logits instead)."""
+    from textsift_b200 import abi
+    cfg, wts = small
+    x = rng(5).normal(0, 1, size=(T, 640)).astype(np.float32)
+    # duplicate rows: equal logits in one row stay in ascending expert order
+    x[7] = x[3]
+    x16 = x.astype(np.float16).view(np.uint16)
+    idx = empty((T, 4), np.int32)
+    w = empty((T, 4), np.float32)
+    small_backend.set_mode(abi.TS_MODE_FAST)
     for layer in (0, 1):
+        p = f"layers.{layer}.router."
+        h = w4_handle(cuda_lib, wts[p + "int4"][None], wts[p + "scales"][None], wts[p + "zp"][None], wts[p + "bias"][None])
+        try:
+            lg = empty((T, cfg["n_experts"]), np.float32)
+            assert cuda_lib.ts_cuda_op_matmul_nbits(h, 0, ptr(dev(x16)), abi.TS_DTYPE_F16, ptr(lg), abi.TS_DTYPE_F32, T,
+                                                    abi.TS_MODE_FAST, stream()) == 0, abi.last_error()
+            logits = host(lg, np.float32)
+        finally:
+            cuda_lib.ts_cuda_w4_destroy(h)
         assert cuda_lib.ts_cuda_op_router_topk(small_backend.handle, layer, ptr(dev(x)), ptr(idx), ptr(w), T,
-                                               stream()) == 0
-        _, ridx, rw = small_oracle.moe(layer, x)
+                                               stream()) == 0, abi.last_error()
+        ridx, val = oracle.topk(logits, 4)
+        got_w = host(w, np.float32)
         assert np.array_equal(host(idx, np.int32), ridx)
-        # weights: softmax over 4 with exp -> CUDA expf vs the C library's
-        # expf may differ by an ulp
-        assert f32_ulps(host(w, np.float32), rw).max() <= 1
+        # the kernel's weights: e_c = f32(exp(f64(v_c - v_0))), sequential f32
+        # sum, w_c = f32(e_c * f32(1 / sum)) / 4 -- bit-exact restatement
+        e = np.exp((val - val[:, :1]).astype(np.float64)).astype(np.float32)
+        ssum = ((e[:, 0] + e[:, 1]) + e[:, 2]) + e[:, 3]
+        inv = (np.float32(1.0) / ssum).astype(np.float32)
+        assert np.array_equal(got_w, (e * inv[:, None]) * np.float32(0.25))
+        # and the reference's softmax (its exp, a division per weight): <= 2 ulps
+        rw = oracle.softmax(val) * np.float32(0.25)
+        assert f32_ulps(got_w, rw).max() <= 2
 
 
 def router_logits(oracle, weights, layer, normed):

@@ -157,6 +157,60 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
   }
 }
 
+// Router top-k on the accumulator row of one token (BM = 256: the thread owns
+// all BN = 128 expert columns of its row).  The same selection and weights as
+// router_topk_kernel (wasm_exports.zig:367-426 + 919-958, block.ts:201-206):
+// the top 4 logits in descending order, equal logits in ascending expert
+// order, softmax over them with the exact exponential, each weight scaled by
+// 1/4.  Expert counts go to hist[row / 128] (the permutation's chunks).
+__device__ __forceinline__ void router_topk_epilogue(const GemmArgs& a, uint32_t acc, uint32_t grow, bool row_ok,
+                                                     const float* sbias, uint64_t* acc_empty) {
+  float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f, t3 = 0.0f;
+  int i0 = -1, i1 = -1, i2 = -1, i3 = -1;
+#pragma unroll 1
+  for (uint32_t c0 = 0; c0 < 128; c0 += 32) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(acc + c0, v);
+    tmem_ld_wait();
+    if (c0 == 96) {
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const int c = (int)c0 + j;
+      if ((uint32_t)c >= a.N) break;
+      const float x = __fadd_rn(__uint_as_float(v[j]), sbias[c]);
+      // strict '>' in ascending column order: equal logits keep the lower expert first
+      if (i3 < 0 || x > t3) {
+        if (i2 < 0 || x > t2) {
+          t3 = t2; i3 = i2;
+          if (i1 < 0 || x > t1) {
+            t2 = t1; i2 = i1;
+            if (i0 < 0 || x > t0) { t1 = t0; i1 = i0; t0 = x; i0 = c; }
+            else { t1 = x; i1 = c; }
+          } else { t2 = x; i2 = c; }
+        } else { t3 = x; i3 = c; }
+      }
+    }
+  }
+  if (!row_ok) return;
+  const float e0 = expf_ref(__fsub_rn(t0, t0)), e1 = expf_ref(__fsub_rn(t1, t0));
+  const float e2 = expf_ref(__fsub_rn(t2, t0)), e3 = expf_ref(__fsub_rn(t3, t0));
+  const float sum = __fadd_rn(__fadd_rn(__fadd_rn(e0, e1), e2), e3);
+  const float inv = sum > 0.0f ? __fdiv_rn(1.0f, sum) : __fdiv_rn(1.0f, 4.0f);
+  const double inv_k = 0.25;
+  reinterpret_cast<int4*>(a.out0)[grow] = make_int4(i0, i1, i2, i3);
+  reinterpret_cast<float4*>(a.out1)[grow] =
+      make_float4((float)((double)__fmul_rn(e0, inv) * inv_k), (float)((double)__fmul_rn(e1, inv) * inv_k),
+                  (float)((double)__fmul_rn(e2, inv) * inv_k), (float)((double)__fmul_rn(e3, inv) * inv_k));
+  int* h = a.hist + (size_t)(grow >> 7) * a.N;
+  atomicAdd(h + i0, 1);
+  atomicAdd(h + i1, 1);
+  atomicAdd(h + i2, 1);
+  atomicAdd(h + i3, 1);
+}
+
 struct TileInfo {
   uint32_t expert, row0, row_end, n_tile;
 };
@@ -348,17 +402,21 @@ __global__ void __launch_bounds__(640, 1)
       const bool row_ok = grow < ti.row_end;
       const uint32_t col_lo = chalf * (BN / 2);
       const uint32_t acc = tmem_base + b * C::ACC_STRIDE + rh * BN + ((quarter * 32u) << 16);
+      if constexpr (EPI == kEpiRouterTopk) {
+        router_topk_epilogue(args, acc, grow, row_ok, sbias, &acc_empty[b]);
+      } else {
 #pragma unroll 1
-      for (uint32_t c0 = col_lo; c0 < col_lo + kCols; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(acc + c0, v);
-        tmem_ld_wait();
-        if (c0 + 32 >= col_lo + kCols) {
-          // every TMEM read of this buffer by this thread is complete: release it
-          tc_fence_before();
-          mbar_arrive(&acc_empty[b]);
+        for (uint32_t c0 = col_lo; c0 < col_lo + kCols; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(acc + c0, v);
+          tmem_ld_wait();
+          if (c0 + 32 >= col_lo + kCols) {
+            // every TMEM read of this buffer by this thread is complete: release it
+            tc_fence_before();
+            mbar_arrive(&acc_empty[b]);
+          }
+          if (row_ok && n0 + c0 < args.N) gemm_epilogue_chunk<EPI>(args, grow, n0 + c0, sbias + c0, v);
         }
-        if (row_ok && n0 + c0 < args.N) gemm_epilogue_chunk<EPI>(args, grow, n0 + c0, sbias + c0, v);
       }
     }
   }
@@ -536,6 +594,9 @@ cudaError_t launch_gemm_w4_tc(const W4Tiles& w, const CUtensorMap& tmap_a, GemmA
       case kEpiQkvRope: return launch_one<128, 256, kEpiQkvRope>(tmap_a, args, w.n_tiles, grid_m, st);
       case kEpiSwiglu: return launch_one<128, 256, kEpiSwiglu>(tmap_a, args, w.n_tiles, grid_m, st);
       case kEpiF16Widen: return launch_one<128, 256, kEpiF16Widen>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiRouterTopk:
+        if (w.N > 128 || w.n_tiles != 1 || !args.hist) return cudaErrorInvalidValue;
+        return launch_one<128, 256, kEpiRouterTopk>(tmap_a, args, w.n_tiles, grid_m, st);
     }
   }
   return cudaErrorInvalidValue;

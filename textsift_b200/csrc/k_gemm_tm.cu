@@ -1,0 +1,357 @@
+// k_gemm_tm.cu — MatMulNBits (uint4, block 32, fp16 scale, uint4 zero point)
+// as a tcgen05 GEMM whose dequantised weight operand lives in tensor memory.
+//
+// Reference semantics: packages/textsift/src/zig/wasm_exports.zig:560-766
+// (matmulInt4BlockImpl), y = x . dequant(W)^T + bias, dequant(W)[n,k] =
+// fp16((q - zp) * scale) (bit-identical to the reference helper for every
+// normal scale), f32 accumulation.
+//
+// The product is computed transposed, D^T[n, m] = W[n, :] . x[m, :]: the
+// weight tile (128 output rows x 64 K per chunk) is the MMA's A operand and
+// is written by the dequantising warps straight into TMEM with tcgen05.st
+// (lane = output row, two fp16 of consecutive k per 32-bit column); the
+// activations (192 token rows x 64 K, 128B swizzle, one TMA box per chunk)
+// are the B operand in shared memory.  Per chunk the shared-memory traffic
+// is the activation tile (written by TMA, read once by one M=128 x N=192
+// MMA per K=16 step) and the 4.6 KB packed blob; the dequantised weights
+// never touch shared memory.
+//
+// Persistent, warp-specialized: one CTA per SM walks (token tile, 128-wide
+// output tile) pairs, 20 warps:
+//   warp 0       producer: TMA box of x + bulk copy of the blob per chunk
+//   warp 1       MMA issuer: 4 x tcgen05.mma (A from TMEM) per chunk
+//   warp 2       TMEM allocator: 2 accumulators x 192 columns + 4 A stages
+//                x 32 columns = 512
+//   warps 4..11  dequantise: warp w owns TMEM lanes 32(w%4).. (output rows)
+//                and K half (w-4)/4 of each chunk
+//   warps 12..19 epilogue of the previous tile: warp w reads lanes 32(w%4)..
+//                (one output column per thread) for tokens 96((w-12)/4)..;
+//                lane pairs exchange values so each store is 32 bits
+// All waits are bounded (ts_common.cuh) and set the device error flag.
+#include "ts_common.cuh"
+#include "ts_kernels.h"
+
+#include <algorithm>
+
+namespace ts {
+
+namespace tm {
+constexpr int S = 4;                      // stages: smem (x tile + blob) and TMEM A
+constexpr uint32_t TOK = 192;             // tokens per tile = MMA N
+constexpr uint32_t X_BYTES = TOK * 128;   // 192 rows x 64 fp16
+constexpr uint32_t RAW_BYTES = 128 * 37;  // packed blob of a 128-row x 64-K chunk (w4_blob_bytes(128))
+constexpr uint32_t RAW_STRIDE = 5120;
+constexpr uint32_t OFF_RAW = S * X_BYTES;
+constexpr uint32_t OFF_BAR = OFF_RAW + S * RAW_STRIDE;
+constexpr uint32_t NUM_BARS = 3 * S + 4;
+constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_A = 2 * TOK;  // first A stage column, after the two accumulators
+constexpr int THREADS = 640;
+static_assert(X_BYTES % 1024 == 0, "swizzle atoms");
+static_assert(COL_A + S * 32 <= TMEM_COLS, "TMEM budget");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+}  // namespace tm
+
+struct TmTile {
+  uint32_t expert, row0, row_end, n_tile;
+};
+
+__device__ __forceinline__ TmTile tm_tile(const GemmArgs& a, uint32_t tile, uint32_t n_ntiles) {
+  TmTile ti;
+  const uint32_t m = tile / n_ntiles;
+  ti.n_tile = tile % n_ntiles;
+  if (a.tiles) {
+    const int4 t = a.tiles[m];
+    ti.expert = (uint32_t)t.x;
+    ti.row0 = (uint32_t)t.y;
+    ti.row_end = (uint32_t)t.z;
+  } else {
+    ti.expert = a.dense_expert;
+    ti.row0 = m * tm::TOK;
+    ti.row_end = min(a.M, ti.row0 + tm::TOK);
+  }
+  return ti;
+}
+
+// One 32-token slice of the accumulator column of output n: v[j] is token
+// m0 + j.  Lanes 2i and 2i+1 hold outputs n and n+1; one exchange gives the
+// even lane both outputs of token m0+2jj and the odd lane those of m0+2jj+1.
+template <int EPI>
+__device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTile& ti, uint32_t m0, uint32_t n,
+                                                  float bv, const uint32_t (&v)[32], int lane) {
+  const uint32_t odd = (uint32_t)lane & 1u;
+  const uint32_t ncol = n & ~1u;
+  const bool col_ok = ncol < a.N;
+  if constexpr (EPI == kEpiF16) {
+    uint16_t* o = reinterpret_cast<uint16_t*>(a.out0) + ncol;
+#pragma unroll
+    for (int jj = 0; jj < 16; jj++) {
+      const float x0 = __fadd_rn(__uint_as_float(v[2 * jj]), bv);
+      const float x1 = __fadd_rn(__uint_as_float(v[2 * jj + 1]), bv);
+      const float r = __shfl_xor_sync(0xffffffffu, odd ? x0 : x1, 1);
+      const uint32_t m = m0 + 2u * jj + odd;
+      if (col_ok && m < ti.row_end)
+        *reinterpret_cast<uint32_t*>(o + (size_t)m * a.ld0) = odd ? f32x2_to_h2(r, x1) : f32x2_to_h2(x0, r);
+    }
+  } else if constexpr (EPI == kEpiSwiglu) {
+    // gate = even output column, up = odd (wasm_exports.zig:855-903); output i = n / 2
+    const uint32_t bit1 = ((uint32_t)lane >> 1) & 1u;
+    const uint32_t icol = (n >> 1) & ~1u;
+    uint16_t* o = reinterpret_cast<uint16_t*>(a.out0) + icol;
+    const bool ok = icol < (a.N >> 1);
+#pragma unroll
+    for (int jq = 0; jq < 8; jq++) {
+      float y[2];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int t = 4 * jq + 2 * h;
+        const float g0 = __fadd_rn(__uint_as_float(v[t]), bv);
+        const float g1 = __fadd_rn(__uint_as_float(v[t + 1]), bv);
+        const float r = __shfl_xor_sync(0xffffffffu, odd ? g0 : g1, 1);
+        y[h] = odd ? swiglu_fast(r, g1) : swiglu_fast(g0, r);  // token t + odd
+      }
+      // lanes 4a+{0,1} hold output i (even), 4a+{2,3} output i+1
+      const float r2 = __shfl_xor_sync(0xffffffffu, bit1 ? y[0] : y[1], 2);
+      const uint32_t m = m0 + 4u * jq + 2u * bit1 + odd;
+      if (ok && m < ti.row_end)
+        *reinterpret_cast<uint32_t*>(o + (size_t)m * a.ld0) = bit1 ? f32x2_to_h2(r2, y[1]) : f32x2_to_h2(y[0], r2);
+    }
+  } else if constexpr (EPI == kEpiQkvRope) {
+    // the whole 128-column tile lies in one of Q, K, V (launcher checks)
+    const uint32_t n0 = ti.n_tile * 128u;
+    const bool rope = n0 < a.q_cols + a.k_cols;
+    uint16_t* o;
+    uint32_t ld;
+    if (n0 < a.q_cols) { o = reinterpret_cast<uint16_t*>(a.out0) + ncol; ld = a.ld0; }
+    else if (rope) { o = reinterpret_cast<uint16_t*>(a.out1) + (ncol - a.q_cols); ld = a.ld1; }
+    else { o = reinterpret_cast<uint16_t*>(a.out2) + (ncol - a.q_cols - a.k_cols); ld = a.ld2; }
+    uint16_t cs[16], sn[16];
+    if (rope) {
+      // position of token m0 + lane, then each lane's (cos, sin) of pair (n % 64) / 2
+      const uint32_t ml = m0 + (uint32_t)lane;
+      const int mypos = ml < ti.row_end ? a.pos[ml] : 0;
+      const uint32_t p = (n & 63u) >> 1;
+#pragma unroll
+      for (int jj = 0; jj < 16; jj++) {
+        const int ps = __shfl_sync(0xffffffffu, mypos, 2 * jj + (int)odd);
+        cs[jj] = a.rope_cos[(size_t)ps * 32 + p];
+        sn[jj] = a.rope_sin[(size_t)ps * 32 + p];
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < 16; jj++) {
+      const float x0 = __fadd_rn(__uint_as_float(v[2 * jj]), bv);
+      const float x1 = __fadd_rn(__uint_as_float(v[2 * jj + 1]), bv);
+      const float r = __shfl_xor_sync(0xffffffffu, odd ? x0 : x1, 1);
+      const uint32_t m = m0 + 2u * jj + odd;
+      uint32_t h2 = odd ? f32x2_to_h2(r, x1) : f32x2_to_h2(x0, r);
+      if (rope) h2 = rope_h2(h2, cs[jj], sn[jj]);
+      if (col_ok && m < ti.row_end) *reinterpret_cast<uint32_t*>(o + (size_t)m * ld) = h2;
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(640, 1)
+    gemm_w4_tm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args, uint32_t n_ntiles) {
+  using namespace tm;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* sX = smem;
+  uint8_t* sR = smem + OFF_RAW;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* aready = bars + 2 * S;
+  uint64_t* acc_full = bars + 3 * S;       // [2]
+  uint64_t* acc_empty = bars + 3 * S + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+
+  const uint32_t m_tiles = args.tiles ? (uint32_t)*args.n_tiles : (args.M + TOK - 1u) / TOK;
+  const uint32_t total = m_tiles * n_ntiles;
+  if (blockIdx.x >= total) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&aready[s], 256);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 256);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t n_kc = args.n_kc;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const TmTile ti = tm_tile(args, tile, n_ntiles);
+        const uint8_t* wb = args.wblob + (size_t)ti.expert * args.expert_stride + (size_t)ti.n_tile * n_kc * RAW_BYTES;
+        for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!wait_or_abort(&empty[s], ph ^ 1u, args.err, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], X_BYTES + RAW_BYTES);
+          tma_load_2d(sX + s * X_BYTES, &tmap_x, (int32_t)(kc * kChunkK), (int32_t)ti.row0, &full[s]);
+          bulk_g2s(sR + s * RAW_STRIDE, wb + (size_t)kc * RAW_BYTES, RAW_BYTES, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16_f32(128, TOK);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x, lt++) {
+        const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
+        if (!wait_or_abort(&acc_empty[b], bph ^ 1u, args.err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * TOK;
+        for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          ok = wait_or_abort(&full[s], ph, args.err, abort_flag) && wait_or_abort(&aready[s], ph, args.err, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t x_addr = smem_u32(sX + s * X_BYTES);
+          const uint32_t a_tmem = tmem_base + COL_A + (uint32_t)s * 32u;
+#pragma unroll
+          for (int k = 0; k < 4; k++)
+            tc_mma_f16_ts(d_tmem, a_tmem + 8u * k, umma_desc_sw128(x_addr + k * 32), idesc, (kc | (uint32_t)k) != 0u);
+          tc_commit(&empty[s]);
+        }
+        if (ok) tc_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ---- dequantise one (output row, K half) of each chunk into TMEM ----
+    const uint32_t q = (uint32_t)(warp & 3), hf = (uint32_t)(warp - 4) >> 2;
+    const uint32_t r = q * 32u + (uint32_t)lane;
+    const uint32_t tcol = tmem_base + ((q * 32u) << 16) + COL_A + hf * 16u;
+    uint32_t it = 0;
+    bool ok = true;
+    for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1u;
+        // full[s] of this use follows the MMAs of the stage's previous use
+        // (the producer waited for their commit), so its TMEM A stage is free
+        if (!wait_or_abort(&full[s], ph, args.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint8_t* raw = sR + s * RAW_STRIDE;
+        const uint4 hw = *reinterpret_cast<const uint4*>(raw + hf * 128u * 16u + r * 16u);
+        const uint32_t sc = *reinterpret_cast<const uint16_t*>(raw + 128u * 32u + r * 4u + hf * 2u);
+        const uint32_t z = (raw[128u * 36u + r] >> (4u * hf)) & 15u;
+        const uint32_t sz = sc * 0x00010001u, zz = (0x6400u | z) * 0x00010001u;
+        const uint32_t wds[4] = {hw.x, hw.y, hw.z, hw.w};
+        uint32_t o[16];
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            // word cc holds k = 8cc..8cc+7 of this half: (k, k+1) = low/high nibble lanes
+            const uint32_t bits = ((wds[cc] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+            __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&bits), *reinterpret_cast<const __half2*>(&zz));
+            __half2 d = __hmul2(qv, *reinterpret_cast<const __half2*>(&sz));
+            o[4 * cc + j] = *reinterpret_cast<uint32_t*>(&d);
+          }
+        }
+        tmem_st_32x32b_x16(tcol + (uint32_t)s * 32u, o);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&aready[s]);
+      }
+    }
+  } else if (warp >= 12) {
+    // ---- epilogue: lanes 32(warp%4).. = output columns, token half (warp-12)/4 ----
+    const uint32_t q = (uint32_t)(warp & 3), g = (uint32_t)(warp - 12) >> 2;
+    const uint32_t nl = q * 32u + (uint32_t)lane;
+    uint32_t lt = 0;
+    for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x, lt++) {
+      const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
+      const TmTile ti = tm_tile(args, tile, n_ntiles);
+      const uint32_t n = ti.n_tile * 128u + nl;
+      const float bv = n < args.N ? f16_ref_to_f32(args.bias[(size_t)ti.expert * args.N + n]) : 0.0f;
+      if (!wait_or_abort(&acc_full[b], bph, args.err, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t acc = tmem_base + ((q * 32u) << 16) + b * TOK + g * (TOK / 2);
+#pragma unroll 1
+      for (uint32_t c0 = 0; c0 < TOK / 2; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(acc + c0, v);
+        tmem_ld_wait();
+        if (c0 + 32 >= TOK / 2) {
+          // every TMEM read of this buffer by this thread is complete: release it
+          tc_fence_before();
+          mbar_arrive(&acc_empty[b]);
+        }
+        tm_epilogue_slice<EPI>(args, ti, ti.row0 + g * (TOK / 2) + c0, n, bv, v, lane);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int EPI>
+static cudaError_t launch_tm(const CUtensorMap& tmap, const GemmArgs& args, uint32_t n_tiles, uint32_t grid_m,
+                             cudaStream_t st) {
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_w4_tm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)tm::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  const uint64_t max_tiles = (uint64_t)grid_m * n_tiles;
+  const uint32_t grid = (uint32_t)std::min<uint64_t>(max_tiles, (uint64_t)num_sms());
+  gemm_w4_tm_kernel<EPI><<<grid, tm::THREADS, tm::SMEM_BYTES, st>>>(tmap, args, n_tiles);
+  return cudaGetLastError();
+}
+
+uint32_t gemm_tm_rows() { return tm::TOK; }
+
+cudaError_t launch_gemm_w4_tm(const W4Tiles& w, const void* x, uint64_t x_rows, GemmArgs args, int epi,
+                              uint32_t grid_m, cudaStream_t st) {
+  if (grid_m == 0 || x_rows == 0) return cudaSuccess;
+  if (w.BN != 128 || (w.N & 1u)) return cudaErrorInvalidValue;
+  if (epi == kEpiQkvRope && ((args.q_cols | args.k_cols) & 127u)) return cudaErrorInvalidValue;
+  args.wblob = w.blobs;
+  args.expert_stride = w.expert_stride;
+  args.bias = w.bias;
+  args.N = w.N;
+  args.n_kc = w.n_kc;
+  CUtensorMap tmap;
+  if (!make_tmap_2d(&tmap, x, w.K, x_rows, w.K, 64, tm::TOK)) return cudaErrorInvalidValue;
+  switch (epi) {
+    case kEpiF16: return launch_tm<kEpiF16>(tmap, args, w.n_tiles, grid_m, st);
+    case kEpiSwiglu: return launch_tm<kEpiSwiglu>(tmap, args, w.n_tiles, grid_m, st);
+    case kEpiQkvRope: return launch_tm<kEpiQkvRope>(tmap, args, w.n_tiles, grid_m, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ts

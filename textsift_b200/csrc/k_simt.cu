@@ -437,18 +437,18 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
   return base + incl - v;
 }
 
-// Expert segments, their 128-row GEMM tiles (exact path) and 256-row GEMM
-// tiles (tensor-core path), and both tile counts, from counts.
+// Expert segments, their 128-row GEMM tiles (exact path) and rows_tc-row
+// GEMM tiles (tensor-core path), and both tile counts, from counts.
 __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __restrict__ counts, uint32_t E,
                                                                    int4* __restrict__ tiles, int* __restrict__ n_tiles,
-                                                                   int4* __restrict__ tiles256,
-                                                                   int* __restrict__ n_tiles256,
+                                                                   int4* __restrict__ tiles_tc,
+                                                                   int* __restrict__ n_tiles_tc, int rows_tc,
                                                                    int* __restrict__ seg_start,
                                                                    int* __restrict__ seg_end) {
   __shared__ int wt[kMaxExperts / 32];
   const uint32_t e = threadIdx.x;
   const int cnt = e < E ? counts[e] : 0;
-  const int t1 = (cnt + 127) / 128, t2 = (cnt + 255) / 256;
+  const int t1 = (cnt + 127) / 128, t2 = (cnt + rows_tc - 1) / rows_tc;
   const int base = block_exclusive_scan(cnt, wt);
   const int tb1 = block_exclusive_scan(t1, wt);
   const int tb2 = block_exclusive_scan(t2, wt);
@@ -457,13 +457,13 @@ __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __
     seg_end[e] = base + cnt;
     for (int tt = 0; tt < t1; tt++)
       tiles[tb1 + tt] = make_int4((int)e, base + tt * 128, base + min(cnt, tt * 128 + 128), base);
-    if (tiles256)
+    if (tiles_tc)
       for (int tt = 0; tt < t2; tt++)
-        tiles256[tb2 + tt] = make_int4((int)e, base + tt * 256, base + min(cnt, tt * 256 + 256), base);
+        tiles_tc[tb2 + tt] = make_int4((int)e, base + tt * rows_tc, base + min(cnt, (tt + 1) * rows_tc), base);
   }
   if (e == E - 1) {
     *n_tiles = tb1 + t1;
-    if (n_tiles256) *n_tiles256 = tb2 + t2;
+    if (n_tiles_tc) *n_tiles_tc = tb2 + t2;
   }
 }
 
@@ -880,12 +880,13 @@ cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, int*
 }
 
 cudaError_t launch_moe_permute(const int32_t* idx, int* hist, uint32_t T, uint32_t K, uint32_t E, int* counts,
-                               int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int4* tiles256,
-                               int* n_tiles256, int* seg_start, int* seg_end, cudaStream_t st) {
-  if (E > kMaxExperts || K > 8) return cudaErrorInvalidValue;
+                               int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int4* tiles_tc,
+                               int* n_tiles_tc, uint32_t rows_tc, int* seg_start, int* seg_end, cudaStream_t st) {
+  if (E > kMaxExperts || K > 8 || (tiles_tc && rows_tc == 0)) return cudaErrorInvalidValue;
   const uint32_t nc = route_chunks(T);
   moe_chunk_scan_kernel<<<(E + 7) / 8, 256, 0, st>>>(hist, nc, E, counts);
-  moe_segments_kernel<<<1, kMaxExperts, 0, st>>>(counts, E, tiles, n_tiles, tiles256, n_tiles256, seg_start, seg_end);
+  moe_segments_kernel<<<1, kMaxExperts, 0, st>>>(counts, E, tiles, n_tiles, tiles_tc, n_tiles_tc, (int)rows_tc,
+                                                 seg_start, seg_end);
   moe_place_kernel<<<nc, kRouteChunk, 0, st>>>(idx, hist, seg_start, T, K, E, perm_tok, route_pos);
   return cudaGetLastError();
 }

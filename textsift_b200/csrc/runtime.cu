@@ -206,8 +206,8 @@ struct Workspace {
   DevArr<uint16_t> x0, x1, xn16, q, k, v, attn, o16, res2, qkv16, down16;
   DevArr<float> n32, hf32, rlogits, rw;
   DevArr<int32_t> ridx;
-  DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, n_tiles256, hist;
-  DevArr<int4> tiles, tiles256;
+  DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, n_tiles_tc, hist;
+  DevArr<int4> tiles, tiles_tc;  // 128-row tiles (exact path), gemm_tm_rows()-row tiles (tensor cores)
   DevArr<int2> atiles;
   DevArr<uint16_t> aperm16, glu16;
   DevArr<float> aperm32, gu32, glu32, down32;
@@ -364,8 +364,8 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.route_pos.alloc(R));
     TS_CUDA_TRY(w.n_tiles.alloc(1));
     TS_CUDA_TRY(w.tiles.alloc(R / 128 + E + 1));
-    TS_CUDA_TRY(w.n_tiles256.alloc(1));
-    TS_CUDA_TRY(w.tiles256.alloc(R / 256 + E + 1));
+    TS_CUDA_TRY(w.n_tiles_tc.alloc(1));
+    TS_CUDA_TRY(w.tiles_tc.alloc(R / ts::gemm_tm_rows() + E + 1));
     TS_CUDA_TRY(w.aperm16.alloc(R * D));
     TS_CUDA_TRY(w.glu16.alloc(R * F));
     TS_CUDA_TRY(w.down32.alloc(R * D));
@@ -440,7 +440,8 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
   ts::ExactArgs ra = L.router.exact();
   ra.x = n32; ra.ldx = D; ra.M = T; ra.rloc = rloc; ra.rlen = rlen; ra.out = w.rlogits.p; ra.ldo = E;
   {
-    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, 5);
+    // kernels: logits GEMM (+ top-k kernel unless fused) + 3 permutation kernels
+    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, (!exact && K == 4 && E <= 128) ? 4 : 5);
     if (exact) {
       TS_K(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
     } else {
@@ -448,12 +449,22 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
       CUtensorMap tx;
       if (!ts::make_act_tmap(&tx, xn16, T, D)) return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed (router)");
       ts::GemmArgs gr;
-      gr.M = T; gr.err = h->err.p; gr.out0 = w.rlogits.p; gr.ld0 = E;
-      TS_K(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiF32, (T + 127) / 128, st));
+      gr.M = T; gr.err = h->err.p;
+      if (K == 4 && E <= 128) {
+        // top-k and the permutation's expert counts in the GEMM epilogue
+        TS_K(cudaMemsetAsync(w.hist.p, 0, (size_t)ts::route_chunks(T) * E * sizeof(int), st));
+        gr.out0 = w.ridx.p; gr.out1 = w.rw.p; gr.hist = w.hist.p;
+        TS_K(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiRouterTopk, (T + 127) / 128, st));
+      } else {
+        gr.out0 = w.rlogits.p; gr.ld0 = E;
+        TS_K(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiF32, (T + 127) / 128, st));
+        TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, w.hist.p, T, E, K, st));
+      }
     }
-    TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, w.hist.p, T, E, K, st));
+    if (exact) TS_K(ts::launch_router_topk(w.rlogits.p, w.ridx.p, w.rw.p, w.hist.p, T, E, K, st));
     TS_K(ts::launch_moe_permute(w.ridx.p, w.hist.p, T, K, E, w.counts.p, w.perm_tok.p, w.route_pos.p, w.tiles.p,
-                                w.n_tiles.p, w.tiles256.p, w.n_tiles256.p, w.seg_start.p, w.seg_end.p, st));
+                                w.n_tiles.p, w.tiles_tc.p, w.n_tiles_tc.p, ts::gemm_tm_rows(), w.seg_start.p,
+                                w.seg_end.p, st));
   }
   if (h->trace_topk && layer >= 0)
     TS_K(cudaMemcpyAsync(h->trace_topk + (size_t)layer * T * K, w.ridx.p, (size_t)T * K * 4, cudaMemcpyDeviceToHost, st));
@@ -463,22 +474,20 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
       Phase p(h, st, TS_PHASE_OTHER, 0, 1);
       TS_K(ts::launch_gather_rows(xn16, w.aperm16.p, w.perm_tok.p, nullptr, R, D * 2, st));
     }
-    CUtensorMap ta, tg;
-    if (!ts::make_act_tmap(&ta, w.aperm16.p, R, D) || !ts::make_act_tmap(&tg, w.glu16.p, R, F))
-      return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the expert operands");
+    const uint32_t grid_tc = R / ts::gemm_tm_rows() + E + 1;
     ts::GemmArgs g;
-    g.tiles = w.tiles256.p; g.n_tiles = w.n_tiles256.p; g.err = h->err.p;
+    g.tiles = w.tiles_tc.p; g.n_tiles = w.n_tiles_tc.p; g.err = h->err.p;
     g.out0 = w.glu16.p; g.ld0 = F;
     {
       Phase p(h, st, TS_PHASE_EXPERT_GATE_UP, fl_gu, 1);
-      TS_K(ts::launch_gemm_w4_tc(L.gate_up.tiles(), ta, g, ts::kEpiSwiglu, grid_tiles, st));
+      TS_K(ts::launch_gemm_w4_tm(L.gate_up.tiles(), w.aperm16.p, R, g, ts::kEpiSwiglu, grid_tc, st));
     }
     ts::GemmArgs g2;
-    g2.tiles = w.tiles256.p; g2.n_tiles = w.n_tiles256.p; g2.err = h->err.p;
+    g2.tiles = w.tiles_tc.p; g2.n_tiles = w.n_tiles_tc.p; g2.err = h->err.p;
     g2.out0 = w.down16.p; g2.ld0 = D;
     {
       Phase p(h, st, TS_PHASE_EXPERT_DOWN, fl_dn, 1);
-      TS_K(ts::launch_gemm_w4_tc(L.down.tiles(), tg, g2, ts::kEpiF16, grid_tiles, st));
+      TS_K(ts::launch_gemm_w4_tm(L.down.tiles(), w.glu16.p, R, g2, ts::kEpiF16, grid_tc, st));
     }
   } else {
     Phase p(h, st, TS_PHASE_EXPERT_GATE_UP, fl_gu + fl_dn, 4);
@@ -558,9 +567,9 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   const uint64_t fl_qkv = 2ull * T * (Q + 2 * KV) * D, fl_o = 2ull * T * D * Q;
   const uint64_t fl_attn = 4ull * c.n_heads * c.head_dim * band_pairs;
 
-  CUtensorMap t_xn, t_attn;
+  CUtensorMap t_xn;  // the classifier's operand (the other GEMMs build their own maps)
   if (!exact) {
-    if (!ts::make_act_tmap(&t_xn, w.xn16.p, T, D) || !ts::make_act_tmap(&t_attn, w.attn.p, T, Q))
+    if (!ts::make_act_tmap(&t_xn, w.xn16.p, T, D))
       return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation operands");
   }
   ts::AttnArgs aa;
@@ -580,6 +589,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   uint16_t* src = w.x0.p;
   uint16_t* dst = w.x1.p;
   const uint32_t mt = (T + 127) / 128;
+  const uint32_t mt_tc = (T + ts::gemm_tm_rows() - 1) / ts::gemm_tm_rows();
   for (uint32_t li = 0; li < c.n_layers; li++) {
     LayerDev& L = *h->layers[li];
     aa.sinks = L.sinks.p;
@@ -595,7 +605,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
         g.out0 = w.q.p; g.ld0 = Q; g.out1 = w.k.p; g.ld1 = KV; g.out2 = w.v.p; g.ld2 = KV;
         g.q_cols = Q; g.k_cols = KV; g.pos = w.pos.p; g.rope_cos = h->rope_cos.p; g.rope_sin = h->rope_sin.p;
         Phase p(h, st, TS_PHASE_QKV, fl_qkv, 1);
-        TS_K(ts::launch_gemm_w4_tc(L.qkv.tiles(), t_xn, g, ts::kEpiQkvRope, mt, st));
+        TS_K(ts::launch_gemm_w4_tm(L.qkv.tiles(), w.xn16.p, T, g, ts::kEpiQkvRope, mt_tc, st));
       }
       {
         Phase p(h, st, TS_PHASE_ATTENTION, fl_attn, 1);
@@ -605,7 +615,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
       go.M = T; go.err = h->err.p; go.out0 = w.o16.p; go.ld0 = D;
       {
         Phase p(h, st, TS_PHASE_O, fl_o, 1);
-        TS_K(ts::launch_gemm_w4_tc(L.o.tiles(), t_attn, go, ts::kEpiF16, mt, st));
+        TS_K(ts::launch_gemm_w4_tm(L.o.tiles(), w.attn.p, T, go, ts::kEpiF16, mt_tc, st));
       }
       {
         Phase p(h, st, TS_PHASE_OTHER, 0, 1);
@@ -1117,10 +1127,18 @@ int ts_cuda_op_matmul_nbits(const ts_cuda_w4_t* w, uint32_t expert, const void* 
   cudaStream_t st = (cudaStream_t)stream;
   if (mode == TS_MODE_FAST) {
     if (x_dtype != TS_DTYPE_F16) return fail(TS_ERR_UNSUPPORTED, "the tensor-core path takes fp16 activations");
-    CUtensorMap tm;
-    if (!ts::make_act_tmap(&tm, d_x, M, w->w.K)) return fail(TS_ERR_UNSUPPORTED, "activation tensor map (16-byte alignment)");
+    if ((reinterpret_cast<uintptr_t>(d_x) & 15u) || ((w->w.K * 2) & 15u))
+      return fail(TS_ERR_UNSUPPORTED, "activation tensor map (16-byte alignment)");
     ts::GemmArgs g;
     g.M = M; g.dense_expert = expert; g.err = w->err.p; g.out0 = d_out; g.ld0 = w->w.N;
+    if (out_dtype == TS_DTYPE_F16 && !(w->w.N & 1u) && !(reinterpret_cast<uintptr_t>(d_out) & 3u)) {
+      // fp16 output: the GEMM with the weights in TMEM, as the forward runs it
+      const uint32_t rows = ts::gemm_tm_rows();
+      TS_CUDA_TRY(ts::launch_gemm_w4_tm(w->w.tiles(), d_x, M, g, ts::kEpiF16, (M + rows - 1) / rows, st));
+      return TS_OK;
+    }
+    CUtensorMap tm;
+    if (!ts::make_act_tmap(&tm, d_x, M, w->w.K)) return fail(TS_ERR_UNSUPPORTED, "activation tensor map (16-byte alignment)");
     TS_CUDA_TRY(ts::launch_gemm_w4_tc(w->w.tiles(), tm, g, out_dtype == TS_DTYPE_F16 ? ts::kEpiF16 : ts::kEpiF32,
                                       (M + 127) / 128, st));
     return TS_OK;
@@ -1147,6 +1165,22 @@ int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32
   int rc = ensure_workspace(h, false);
   if (rc) return rc;
   const ts_cuda_cfg& c = h->cfg;
+  if (T == 0) return TS_OK;
+  if (c.mode != TS_MODE_EXACT && c.top_k == 4 && c.n_experts <= 128) {
+    // fast mode, as the forward runs it: fp16 operand, tensor-core logits,
+    // top-k in the GEMM epilogue
+    Workspace& w = h->ws;
+    TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, w.xn16.p, (size_t)T * c.d_model, st));
+    CUtensorMap tx;
+    if (!ts::make_act_tmap(&tx, w.xn16.p, T, c.d_model)) return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed (router)");
+    TS_CUDA_TRY(cudaMemsetAsync(w.hist.p, 0, (size_t)ts::route_chunks(T) * c.n_experts * sizeof(int), st));
+    ts::GemmArgs gr;
+    gr.M = T; gr.err = h->err.p; gr.out0 = w.ridx.p; gr.out1 = w.rw.p; gr.hist = w.hist.p;
+    TS_CUDA_TRY(ts::launch_gemm_w4_tc(h->layers[layer]->router.tiles(), tx, gr, ts::kEpiRouterTopk, (T + 127) / 128, st));
+    TS_CUDA_TRY(cudaMemcpyAsync(d_idx, w.ridx.p, (size_t)T * 4 * 4, cudaMemcpyDeviceToDevice, st));
+    TS_CUDA_TRY(cudaMemcpyAsync(d_w, w.rw.p, (size_t)T * 4 * 4, cudaMemcpyDeviceToDevice, st));
+    return TS_OK;
+  }
   ts::ExactArgs ra = h->layers[layer]->router.exact();
   ra.x = d_x; ra.ldx = c.d_model; ra.M = T; ra.out = h->ws.rlogits.p; ra.ldo = c.n_experts;
   TS_CUDA_TRY(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));

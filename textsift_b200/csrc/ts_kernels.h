@@ -51,6 +51,8 @@ enum GemmEpi : int {
   kEpiQkvRope = 2, // q/k with the reference's 3-rounding RoPE, v plain (fp16)
   kEpiSwiglu = 3,  // out0 fp16 [row][N/2] = f16(swiglu(gate, up))
   kEpiF16Widen = 4,  // out0 f32 [row][ld0] = f32(f16(acc + bias)) (logits, wasm.ts:776-797)
+  kEpiRouterTopk = 5,  // router logits -> top-4 experts: out0 int32 [row][4] ids, out1 f32 [row][4]
+                       // weights, hist [row / 128][N] += 1 per route (block.ts:201-206)
 };
 
 struct GemmArgs {
@@ -69,6 +71,7 @@ struct GemmArgs {
   const int* pos = nullptr;         // kEpiQkvRope: position of each row in its sequence
   const uint16_t* rope_cos = nullptr;
   const uint16_t* rope_sin = nullptr;
+  int* hist = nullptr;               // kEpiRouterTopk: per 128-row chunk expert counts (zeroed)
   int* err = nullptr;
 };
 
@@ -85,6 +88,14 @@ int num_sms();
 // Tensor-core int4 GEMM: y = A(fp16 [M,K]) x dequant(W)^T.  grid_m = number
 // of 128-row tiles (dense) or an upper bound on the grouped tile count.
 cudaError_t launch_gemm_w4_tc(const W4Tiles& w, const CUtensorMap& tmap_a, GemmArgs args, int epi,
+                              uint32_t grid_m, cudaStream_t st);
+
+// Tensor-core int4 GEMM with the dequantised weights in TMEM (epilogues
+// kEpiF16, kEpiSwiglu, kEpiQkvRope; BN = 128 blobs).  Token tiles of
+// gemm_tm_rows() rows; x is fp16 [x_rows, K]; grid_m = number of token tiles
+// (dense) or an upper bound on the grouped tile count (args.tiles).
+uint32_t gemm_tm_rows();
+cudaError_t launch_gemm_w4_tm(const W4Tiles& w, const void* x, uint64_t x_rows, GemmArgs args, int epi,
                               uint32_t grid_m, cudaStream_t st);
 
 }  // namespace ts

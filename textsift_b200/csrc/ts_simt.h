@@ -46,11 +46,11 @@ uint32_t route_chunks(uint32_t T);
 cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, int* hist, uint32_t T, uint32_t E,
                                uint32_t K, cudaStream_t st);
 // Stable expert permutation from idx and the top-k kernel's hist
-// (overwritten), the 128-row and (when tiles256 is set) 256-row grouped-GEMM
-// tile lists and their device tile counts.
+// (overwritten), the 128-row and (when tiles_tc is set) rows_tc-row
+// grouped-GEMM tile lists and their device tile counts.
 cudaError_t launch_moe_permute(const int32_t* idx, int* hist, uint32_t T, uint32_t K, uint32_t E, int* counts,
-                               int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int4* tiles256,
-                               int* n_tiles256, int* seg_start, int* seg_end, cudaStream_t st);
+                               int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int4* tiles_tc,
+                               int* n_tiles_tc, uint32_t rows_tc, int* seg_start, int* seg_end, cudaStream_t st);
 cudaError_t launch_gather_rows(const void* src, void* dst, const int* perm_tok, const int* n_rows_dev,
                                uint32_t max_rows, uint32_t row_bytes, cudaStream_t st);
 cudaError_t launch_moe_combine(const float* down, const int32_t* idx, const float* w, const int* route_pos,
