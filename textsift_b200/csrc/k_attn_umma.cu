@@ -251,37 +251,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t j = lt > 2u ? lt - 2u : 0u; j < lt; j++) mbar_wait(&full[j & 1u], (j >> 1) & 1u, a.err);
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t n1 = band > 256u ? 128u : band, n2 = band - n1;
-      const uint32_t idesc1 = umma_idesc_f16_f32(128, n1);
-      const uint32_t idesc2 = umma_idesc_f16_f32(128, n2 > 0u ? n2 : 16u);
-      const uint32_t idesc_pv = umma_idesc_f16_f32(128, 64) | (1u << 16);  // B (V) is MN-major
-      const uint32_t nks = band / 16u;
-      auto issue_pv = [&](uint32_t s) {
-        const uint32_t va = smem_u32(smem + s * kStageBytes + kQBytes + kKVBytes);
-        for (uint32_t j = 0; j < nks; j++)
-          tc_mma_f16_ts(tmem + kColO, tmem + kColP + 8u * j, umma_desc_sw128_mn(va + 2048u * j), idesc_pv, j > 0u);
-      };
-      uint32_t lt = 0, prev_s = 0;
-      bool ok = true;
-      for (uint32_t item = blockIdx.x; item < items; item += gridDim.x, lt++) {
-        const uint32_t s = lt & 1u;
-        if (!wait_or_abort(&full[s], (lt >> 1) & 1u, a.err, abort_flag)) { ok = false; break; }
-        // the softmax of the previous item is done with S (and has written P)
-        if (lt > 0 && !wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag)) { ok = false; break; }
-        tc_fence_after();
+    // The whole warp runs the loop in lockstep (warp-uniform state keeps the
+    // issue cheap beside the softmax warps of this scheduler); one elected
+    // lane issues.  Descriptor address fields step by bytes / 16.
+    const uint32_t n1 = band > 256u ? 128u : band, n2 = band - n1;
+    const uint32_t idesc1 = umma_idesc_f16_f32(128, n1);
+    const uint32_t idesc2 = umma_idesc_f16_f32(128, n2 > 0u ? n2 : 16u);
+    const uint32_t idesc_pv = umma_idesc_f16_f32(128, 64) | (1u << 16);  // B (V) is MN-major
+    const uint32_t nks = band / 16u;
+    const uint64_t qd0 = umma_desc_sw128(smem_u32(smem));
+    const uint64_t kd0 = umma_desc_sw128(smem_u32(smem + kQBytes));
+    const uint64_t vd0 = umma_desc_sw128_mn(smem_u32(smem + kQBytes + kKVBytes));
+    constexpr uint32_t kStageUnits = kStageBytes >> 4;
+    auto issue_pv = [&](uint32_t s) {
+      const uint64_t vd = vd0 + (uint64_t)(s * kStageUnits);
+      for (uint32_t j = 0; j < nks; j++) tc_mma_f16_ts(tmem + kColO, tmem + kColP + 8u * j, vd + 128u * j, idesc_pv, j > 0u);
+    };
+    uint32_t lt = 0, prev_s = 0;
+    bool ok = true;
+    for (uint32_t item = blockIdx.x; item < items; item += gridDim.x, lt++) {
+      const uint32_t s = lt & 1u;
+      // the stage has landed, and the softmax of the previous item is done
+      // with S (and has written P)
+      ok = __all_sync(0xffffffffu, wait_or_abort(&full[s], (lt >> 1) & 1u, a.err, abort_flag) &&
+                                       (lt == 0 || wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag)));
+      if (!ok) break;
+      tc_fence_after();
+      if (elect_one()) {
         // S of this item first, so its softmax starts while P.V of the
         // previous item runs behind it on the tensor core
-        const uint32_t qa = smem_u32(smem + s * kStageBytes);
-        const uint32_t ka = qa + kQBytes;
+        const uint64_t qd = qd0 + (uint64_t)(s * kStageUnits), kd = kd0 + (uint64_t)(s * kStageUnits);
 #pragma unroll
-        for (uint32_t k = 0; k < 4; k++)
-          tc_mma_f16(tmem + kColS, umma_desc_sw128(qa + 32u * k), umma_desc_sw128(ka + 32u * k), idesc1, k > 0u);
+        for (uint32_t k = 0; k < 4; k++) tc_mma_f16(tmem + kColS, qd + 2u * k, kd + 2u * k, idesc1, k > 0u);
         if (n2 > 0u) {
 #pragma unroll
           for (uint32_t k = 0; k < 4; k++)
-            tc_mma_f16(tmem + kColS + n1, umma_desc_sw128(qa + 32u * k), umma_desc_sw128(ka + n1 * 128u + 32u * k),
-                       idesc2, k > 0u);
+            tc_mma_f16(tmem + kColS + n1, qd + 2u * k, kd + n1 * 8u + 2u * k, idesc2, k > 0u);
         }
         tc_commit(s_full);
         if (lt > 0) {
@@ -289,18 +294,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit(o_full);
           tc_commit(&empty[prev_s]);
         }
-        prev_s = s;
       }
-      if (ok && lt > 0 && wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag)) {
-        tc_fence_after();
+      __syncwarp();
+      prev_s = s;
+    }
+    if (ok && lt > 0 && __all_sync(0xffffffffu, wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag))) {
+      tc_fence_after();
+      if (elect_one()) {
         issue_pv(prev_s);
         tc_commit(o_full);
         tc_commit(&empty[prev_s]);
       }
-      // every MMA issued above has completed before TMEM is freed
-      tc_commit(drain);
-      mbar_wait(drain, 0, a.err);
+      __syncwarp();
     }
+    // every MMA issued above has completed before TMEM is freed
+    if (elect_one()) tc_commit(drain);
+    __syncwarp();
+    if (lane == 0) mbar_wait(drain, 0, a.err);
   } else if (warp >= 4) {
     // ---------------- softmax + epilogue ----------------
     // Two warps per TMEM lane quarter: warp (4 + quad + 4 * hh) owns rows

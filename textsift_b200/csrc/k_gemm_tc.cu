@@ -304,33 +304,40 @@ __global__ void __launch_bounds__(640, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16_f32(128, BN);
-      uint32_t it = 0, lt = 0;
-      bool ok = true;
-      for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x, lt++) {
-        const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
-        if (!wait_or_abort(&acc_empty[b], bph ^ 1u, args.err, abort_flag)) break;
+    // The whole warp runs the loop in lockstep (cheap issue beside the busy
+    // warps of this scheduler); one elected lane issues the MMAs.
+    constexpr uint32_t idesc = umma_idesc_f16_f32(128, BN);
+    const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA)), bdesc0 = umma_desc_sw128(smem_u32(sB));
+    uint32_t it = 0, lt = 0;
+    bool ok = true;
+    for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x, lt++) {
+      const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&acc_empty[b], bph ^ 1u, args.err, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + b * C::ACC_STRIDE;
+      for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1u;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&full[s], ph, args.err, abort_flag) &&
+                                         wait_or_abort(&bready[s], ph, args.err, abort_flag));
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + b * C::ACC_STRIDE;
-        for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1u;
-          ok = wait_or_abort(&full[s], ph, args.err, abort_flag) && wait_or_abort(&bready[s], ph, args.err, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
+        if (elect_one()) {
+          // descriptor address fields step by bytes / 16
+          const uint64_t ad = adesc0 + (uint64_t)((uint32_t)s * (C::A_BYTES >> 4));
+          const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)s * (C::B_BYTES >> 4));
 #pragma unroll
           for (int k = 0; k < 4; k++)
 #pragma unroll
             for (uint32_t h = 0; h < C::ACC_ROWS; h++)
-              tc_mma_f16(d_tmem + h * BN, umma_desc_sw128(a_addr + h * 16384u + k * 32),
-                         umma_desc_sw128(b_addr + k * 32), idesc, (kc | (uint32_t)k) != 0u);
+              tc_mma_f16(d_tmem + h * BN, ad + h * 1024u + 2u * k, bd + 2u * k, idesc, (kc | (uint32_t)k) != 0u);
           tc_commit(&empty[s]);
         }
-        if (ok) tc_commit(&acc_full[b]);
+        __syncwarp();
       }
+      if (ok && elect_one()) tc_commit(&acc_full[b]);
+      __syncwarp();
     }
   } else if (warp >= 4 && warp < 12) {
     // ---- dequantise: half rows (32 K values, one scale and zero point) ----

@@ -19,11 +19,12 @@
 // Persistent, warp-specialized: one CTA per SM walks (token tile, 128-wide
 // output tile) pairs, 20 warps:
 //   warp 0       producer: TMA box of x + bulk copy of the blob per chunk
-//   warp 1       MMA issuer: 4 x tcgen05.mma (A from TMEM) per chunk
+//   warp 1       MMA issuer: 4 x tcgen05.mma (A from TMEM) per chunk, from
+//                one elected lane of a warp that runs the loop in lockstep
 //   warp 2       TMEM allocator: 2 accumulators x 192 columns + 4 A stages
 //                x 32 columns = 512
-//   warps 4..11  dequantise: warp w owns TMEM lanes 32(w%4).. (output rows)
-//                and K half (w-4)/4 of each chunk
+//   warps 4..11  dequantise: warp w owns TMEM lanes 32(w%4).. (output rows);
+//                warps 4..7 take the even chunks, 8..11 the odd ones
 //   warps 12..19 epilogue of the previous tile: warp w reads lanes 32(w%4)..
 //                (one output column per thread) for tokens 96((w-12)/4)..;
 //                lane pairs exchange values so each store is 32 bits
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(640, 1)
     for (int s = 0; s < S; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&aready[s], 256);
+      mbar_init(&aready[s], 128);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&acc_full[b], 1);
@@ -217,40 +218,51 @@ __global__ void __launch_bounds__(640, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16_f32(128, TOK);
-      uint32_t it = 0, lt = 0;
-      bool ok = true;
-      for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x, lt++) {
-        const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
-        if (!wait_or_abort(&acc_empty[b], bph ^ 1u, args.err, abort_flag)) break;
+    // The whole warp runs the loop (warp-uniform state, cheap to issue next to
+    // the busy dequantising/epilogue warps of this scheduler); one elected
+    // lane issues the MMAs and commits.  Descriptors: stage s's x tile starts
+    // s * X_BYTES / 16 descriptor units after stage 0's, K step k 2 units.
+    constexpr uint32_t idesc = umma_idesc_f16_f32(128, TOK);
+    const uint64_t xdesc0 = umma_desc_sw128(smem_u32(sX));
+    uint32_t it = 0, lt = 0;
+    bool ok = true;
+    for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x, lt++) {
+      const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&acc_empty[b], bph ^ 1u, args.err, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + b * TOK;
+      for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1u;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&full[s], ph, args.err, abort_flag) &&
+                                         wait_or_abort(&aready[s], ph, args.err, abort_flag));
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + b * TOK;
-        for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1u;
-          ok = wait_or_abort(&full[s], ph, args.err, abort_flag) && wait_or_abort(&aready[s], ph, args.err, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t x_addr = smem_u32(sX + s * X_BYTES);
+        if (elect_one()) {
+          const uint64_t xd = xdesc0 + (uint64_t)((uint32_t)s * (X_BYTES >> 4));
           const uint32_t a_tmem = tmem_base + COL_A + (uint32_t)s * 32u;
 #pragma unroll
           for (int k = 0; k < 4; k++)
-            tc_mma_f16_ts(d_tmem, a_tmem + 8u * k, umma_desc_sw128(x_addr + k * 32), idesc, (kc | (uint32_t)k) != 0u);
+            tc_mma_f16_ts(d_tmem, a_tmem + 8u * k, xd + 2u * k, idesc, (kc | (uint32_t)k) != 0u);
           tc_commit(&empty[s]);
         }
-        if (ok) tc_commit(&acc_full[b]);
+        __syncwarp();
       }
+      if (ok && elect_one()) tc_commit(&acc_full[b]);
+      __syncwarp();
     }
   } else if (warp >= 4 && warp < 12) {
-    // ---- dequantise one (output row, K half) of each chunk into TMEM ----
-    const uint32_t q = (uint32_t)(warp & 3), hf = (uint32_t)(warp - 4) >> 2;
+    // ---- dequantise: warps 4..7 take the even chunks, 8..11 the odd ones, so
+    // two chunks are in flight; thread = one output row, both K halves ----
+    const uint32_t q = (uint32_t)(warp & 3), grp = (uint32_t)(warp - 4) >> 2;
     const uint32_t r = q * 32u + (uint32_t)lane;
-    const uint32_t tcol = tmem_base + ((q * 32u) << 16) + COL_A + hf * 16u;
+    const uint32_t tcol = tmem_base + ((q * 32u) << 16) + COL_A;
     uint32_t it = 0;
     bool ok = true;
     for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
       for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+        if ((it & 1u) != grp) continue;
         const int s = it % S;
         const uint32_t ph = (it / S) & 1u;
         // full[s] of this use follows the MMAs of the stage's previous use
@@ -258,24 +270,30 @@ __global__ void __launch_bounds__(640, 1)
         if (!wait_or_abort(&full[s], ph, args.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint8_t* raw = sR + s * RAW_STRIDE;
-        const uint4 hw = *reinterpret_cast<const uint4*>(raw + hf * 128u * 16u + r * 16u);
-        const uint32_t sc = *reinterpret_cast<const uint16_t*>(raw + 128u * 32u + r * 4u + hf * 2u);
-        const uint32_t z = (raw[128u * 36u + r] >> (4u * hf)) & 15u;
-        const uint32_t sz = sc * 0x00010001u, zz = (0x6400u | z) * 0x00010001u;
-        const uint32_t wds[4] = {hw.x, hw.y, hw.z, hw.w};
-        uint32_t o[16];
+        const uint4 h0 = *reinterpret_cast<const uint4*>(raw + r * 16u);
+        const uint4 h1 = *reinterpret_cast<const uint4*>(raw + 128u * 16u + r * 16u);
+        const uint32_t sc2 = *reinterpret_cast<const uint32_t*>(raw + 128u * 32u + r * 4u);
+        const uint32_t zb = raw[128u * 36u + r];
+        uint32_t o[32];
 #pragma unroll
-        for (int cc = 0; cc < 4; cc++) {
+        for (int hf = 0; hf < 2; hf++) {
+          const uint32_t sz = ((sc2 >> (16 * hf)) & 0xffffu) * 0x00010001u;
+          const uint32_t zz = (0x6400u | ((zb >> (4 * hf)) & 15u)) * 0x00010001u;
+          const uint4 hw = hf ? h1 : h0;
+          const uint32_t wds[4] = {hw.x, hw.y, hw.z, hw.w};
 #pragma unroll
-          for (int j = 0; j < 4; j++) {
-            // word cc holds k = 8cc..8cc+7 of this half: (k, k+1) = low/high nibble lanes
-            const uint32_t bits = ((wds[cc] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
-            __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&bits), *reinterpret_cast<const __half2*>(&zz));
-            __half2 d = __hmul2(qv, *reinterpret_cast<const __half2*>(&sz));
-            o[4 * cc + j] = *reinterpret_cast<uint32_t*>(&d);
+          for (int cc = 0; cc < 4; cc++) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              // word cc holds k = 8cc..8cc+7 of this half: (k, k+1) = low/high nibble lanes
+              const uint32_t bits = ((wds[cc] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+              __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&bits), *reinterpret_cast<const __half2*>(&zz));
+              __half2 d = __hmul2(qv, *reinterpret_cast<const __half2*>(&sz));
+              o[16 * hf + 4 * cc + j] = *reinterpret_cast<uint32_t*>(&d);
+            }
           }
         }
-        tmem_st_32x32b_x16(tcol + (uint32_t)s * 32u, o);
+        tmem_st_32x32b_x32(tcol + (uint32_t)s * 32u, o);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&aready[s]);
