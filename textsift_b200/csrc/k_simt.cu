@@ -680,12 +680,18 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
   const float kf = (float)K;
   const uint32_t nc = D / 8;
   for (uint32_t c = (uint32_t)lane; c < nc; c += 32) {
+    // every route's 16 bytes (and the residual's) in flight before the math
+    const size_t o = (size_t)t * D + 8 * c;
+    uint4 vv[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      vv[j] = j < n ? __ldg(reinterpret_cast<const uint4*>(down + (size_t)pk[j] * D + 8 * c)) : make_uint4(0, 0, 0, 0);
+    const uint4 rv = res ? __ldg(reinterpret_cast<const uint4*>(res + o)) : make_uint4(0, 0, 0, 0);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       if (j >= n) break;
-      const uint4 v = *reinterpret_cast<const uint4*>(down + (size_t)pk[j] * D + 8 * c);
-      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+      const uint32_t vw[4] = {vv[j].x, vv[j].y, vv[j].z, vv[j].w};
 #pragma unroll
       for (int q = 0; q < 4; q++) {
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vw[q]));
@@ -693,10 +699,8 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
         acc[2 * q + 1] = fmaf(wk[j], f.y, acc[2 * q + 1]);
       }
     }
-    const size_t o = (size_t)t * D + 8 * c;
     uint32_t ow[4];
     if (res) {
-      const uint4 rv = *reinterpret_cast<const uint4*>(res + o);
       const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
       for (int q = 0; q < 4; q++) {
