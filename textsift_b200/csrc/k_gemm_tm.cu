@@ -85,12 +85,16 @@ __device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTil
   const uint32_t odd = (uint32_t)lane & 1u;
   const uint32_t ncol = n & ~1u;
   const bool col_ok = ncol < a.N;
+  // bias on tokens 2jj, 2jj+1 with one packed add (fp16 and SwiGLU epilogues)
+  auto biased = [&](int jj, float& x0, float& x1) {
+    f2unpack(add_f32x2(f2pack(__uint_as_float(v[2 * jj]), __uint_as_float(v[2 * jj + 1])), f2pack(bv, bv)), x0, x1);
+  };
   if constexpr (EPI == kEpiF16) {
     uint16_t* o = reinterpret_cast<uint16_t*>(a.out0) + ncol;
 #pragma unroll
     for (int jj = 0; jj < 16; jj++) {
-      const float x0 = __fadd_rn(__uint_as_float(v[2 * jj]), bv);
-      const float x1 = __fadd_rn(__uint_as_float(v[2 * jj + 1]), bv);
+      float x0, x1;
+      biased(jj, x0, x1);
       const float r = __shfl_xor_sync(0xffffffffu, odd ? x0 : x1, 1);
       const uint32_t m = m0 + 2u * jj + odd;
       if (col_ok && m < ti.row_end)
@@ -104,15 +108,16 @@ __device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTil
     const bool ok = icol < (a.N >> 1);
 #pragma unroll
     for (int jq = 0; jq < 8; jq++) {
-      float y[2];
+      float gg[2], uu[2], y[2];
 #pragma unroll
       for (int h = 0; h < 2; h++) {
-        const int t = 4 * jq + 2 * h;
-        const float g0 = __fadd_rn(__uint_as_float(v[t]), bv);
-        const float g1 = __fadd_rn(__uint_as_float(v[t + 1]), bv);
+        float g0, g1;
+        biased(2 * jq + h, g0, g1);
         const float r = __shfl_xor_sync(0xffffffffu, odd ? g0 : g1, 1);
-        y[h] = odd ? swiglu_fast(r, g1) : swiglu_fast(g0, r);  // token t + odd
+        gg[h] = odd ? r : g0;  // token 4jq + 2h + odd
+        uu[h] = odd ? g1 : r;
       }
+      swiglu_fast2(gg[0], uu[0], gg[1], uu[1], y[0], y[1]);
       // lanes 4a+{0,1} hold output i (even), 4a+{2,3} output i+1
       const float r2 = __shfl_xor_sync(0xffffffffu, bit1 ? y[0] : y[1], 2);
       const uint32_t m = m0 + 4u * jq + 2u * bit1 + odd;

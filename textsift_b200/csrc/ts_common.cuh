@@ -185,6 +185,41 @@ __device__ __forceinline__ float swiglu_fast(float g, float u) {
   return (up + 1.0f) * (gate * sig);
 }
 
+// Packed f32x2 arithmetic (sm_100): one instruction for two round-to-nearest
+// f32 adds or multiplies, same results as two scalar ones.
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Two swiglu_fast evaluations with the adds and multiplies packed: results
+// identical to swiglu_fast(g0, u0) and swiglu_fast(g1, u1).
+__device__ __forceinline__ void swiglu_fast2(float g0, float u0, float g1, float u1, float& y0, float& y1) {
+  const uint64_t gate = f2pack(fminf(g0, 7.0f), fminf(g1, 7.0f));
+  const uint64_t up = f2pack(fmaxf(fminf(u0, 7.0f), -7.0f), fmaxf(fminf(u1, 7.0f), -7.0f));
+  const uint64_t one = f2pack(1.0f, 1.0f);
+  float t0, t1;
+  f2unpack(mul_f32x2(gate, f2pack(-2.45546696f, -2.45546696f)), t0, t1);  // -1.702 * log2(e)
+  float d0, d1;
+  f2unpack(add_f32x2(f2pack(ex2_approx(t0), ex2_approx(t1)), one), d0, d1);
+  const uint64_t gs = mul_f32x2(gate, f2pack(__fdividef(1.0f, d0), __fdividef(1.0f, d1)));
+  f2unpack(mul_f32x2(add_f32x2(up, one), gs), y0, y1);
+}
+
 // ---------------------------------------------------------------------------
 // Error flag shared by every kernel (bounded waits, bad indices)
 // ---------------------------------------------------------------------------
