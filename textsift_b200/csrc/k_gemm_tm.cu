@@ -133,7 +133,7 @@ __device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTil
     if (n0 < a.q_cols) { o = reinterpret_cast<uint16_t*>(a.out0) + ncol; ld = a.ld0; }
     else if (rope) { o = reinterpret_cast<uint16_t*>(a.out1) + (ncol - a.q_cols); ld = a.ld1; }
     else { o = reinterpret_cast<uint16_t*>(a.out2) + (ncol - a.q_cols - a.k_cols); ld = a.ld2; }
-    uint16_t cs[16], sn[16];
+    uint32_t csn[16];  // cos | sin << 16
     if (rope) {
       // position of token m0 + lane, then each lane's (cos, sin) of pair (n % 64) / 2
       const uint32_t ml = m0 + (uint32_t)lane;
@@ -142,8 +142,7 @@ __device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTil
 #pragma unroll
       for (int jj = 0; jj < 16; jj++) {
         const int ps = __shfl_sync(0xffffffffu, mypos, 2 * jj + (int)odd);
-        cs[jj] = a.rope_cos[(size_t)ps * 32 + p];
-        sn[jj] = a.rope_sin[(size_t)ps * 32 + p];
+        csn[jj] = a.rope_cs[(size_t)ps * 32 + p];
       }
     }
 #pragma unroll
@@ -153,7 +152,7 @@ __device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTil
       const float r = __shfl_xor_sync(0xffffffffu, odd ? x0 : x1, 1);
       const uint32_t m = m0 + 2u * jj + odd;
       uint32_t h2 = odd ? f32x2_to_h2(r, x1) : f32x2_to_h2(x0, r);
-      if (rope) h2 = rope_h2(h2, cs[jj], sn[jj]);
+      if (rope) h2 = rope_h2(h2, (uint16_t)(csn[jj] & 0xffffu), (uint16_t)(csn[jj] >> 16));
       if (col_ok && m < ti.row_end) *reinterpret_cast<uint32_t*>(o + (size_t)m * ld) = h2;
     }
   }
@@ -361,7 +360,8 @@ cudaError_t launch_gemm_w4_tm(const W4Tiles& w, const void* x, uint64_t x_rows, 
                               uint32_t grid_m, cudaStream_t st) {
   if (grid_m == 0 || x_rows == 0) return cudaSuccess;
   if (w.BN != 128 || (w.N & 1u)) return cudaErrorInvalidValue;
-  if (epi == kEpiQkvRope && ((args.q_cols | args.k_cols) & 127u)) return cudaErrorInvalidValue;
+  if (epi == kEpiQkvRope && (((args.q_cols | args.k_cols) & 127u) || !args.rope_cs || !args.pos))
+    return cudaErrorInvalidValue;
   args.wblob = w.blobs;
   args.expert_stride = w.expert_stride;
   args.bias = w.bias;

@@ -229,6 +229,7 @@ struct ts_cuda {
   W4Dev score;
   std::vector<std::unique_ptr<LayerDev>> layers;
   DevArr<uint16_t> rope_cos, rope_sin;
+  DevArr<uint32_t> rope_cs;  // cos | sin << 16 per (position, pair): one load in the QKV epilogue
   DevArr<int> err;
   Workspace ws;
   // pinned staging for the host-pointer forward
@@ -604,6 +605,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
         // RoPE in the GEMM epilogue: q, k (rotated) and v to their own buffers
         g.out0 = w.q.p; g.ld0 = Q; g.out1 = w.k.p; g.ld1 = KV; g.out2 = w.v.p; g.ld2 = KV;
         g.q_cols = Q; g.k_cols = KV; g.pos = w.pos.p; g.rope_cos = h->rope_cos.p; g.rope_sin = h->rope_sin.p;
+        g.rope_cs = h->rope_cs.p;
         Phase p(h, st, TS_PHASE_QKV, fl_qkv, 1);
         TS_K(ts::launch_gemm_w4_tm(L.qkv.tiles(), w.xn16.p, T, g, ts::kEpiQkvRope, mt_tc, st));
       }
@@ -834,6 +836,10 @@ int ts_cuda_finalize(ts_cuda_t* h) {
   TS_CUDA_TRY(h->rope_sin.alloc(sn.size()));
   TS_CUDA_TRY(cudaMemcpyAsync(h->rope_cos.p, cs.data(), cs.size() * 2, cudaMemcpyHostToDevice, st));
   TS_CUDA_TRY(cudaMemcpyAsync(h->rope_sin.p, sn.data(), sn.size() * 2, cudaMemcpyHostToDevice, st));
+  std::vector<uint32_t> csn(cs.size());
+  for (size_t i = 0; i < cs.size(); i++) csn[i] = (uint32_t)cs[i] | ((uint32_t)sn[i] << 16);
+  TS_CUDA_TRY(h->rope_cs.alloc(csn.size()));
+  TS_CUDA_TRY(cudaMemcpyAsync(h->rope_cs.p, csn.data(), csn.size() * 4, cudaMemcpyHostToDevice, st));
   int nbad = 0;
   TS_CUDA_TRY(cudaMemcpyAsync(&nbad, bad.p, 4, cudaMemcpyDeviceToHost, st));
   TS_CUDA_TRY(cudaStreamSynchronize(st));

@@ -71,6 +71,7 @@ struct GemmArgs {
   const int* pos = nullptr;         // kEpiQkvRope: position of each row in its sequence
   const uint16_t* rope_cos = nullptr;
   const uint16_t* rope_sin = nullptr;
+  const uint32_t* rope_cs = nullptr;  // kEpiQkvRope (launch_gemm_w4_tm): cos | sin << 16, [pos][32]
   int* hist = nullptr;               // kEpiRouterTopk: per 128-row chunk expert counts (zeroed)
   int* err = nullptr;
 };
