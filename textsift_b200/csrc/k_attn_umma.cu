@@ -19,10 +19,12 @@
 //   * the MMA warp (warp 1) computes S = Q K^T into TMEM (columns kColS..)
 //     and, behind the next item's S, O = P V with P read from TMEM and V
 //     from smem (an MN-major operand);
-//   * four softmax warps (one thread per row) find the row max over the
-//     usable keys, write P = 2^((s - max) log2 e) as fp16 into TMEM (kColP..)
-//     and keep the row sum; one item later they read O, divide by
-//     (sum + sink term) and store fp16.
+//   * sixteen softmax warps, four per TMEM lane quarter (one thread per row,
+//     each warp a quarter of the band's columns), find the row max over the
+//     usable keys (the four partial maxima meet in smem), write
+//     P = 2^((s - max) log2 e) as fp16 into TMEM (kColP..) and keep partial
+//     row sums; one item later each reads 16 columns of O, divides by
+//     (sum of the four partial sums + sink term) and stores fp16.
 // Every wait is bounded; on a timeout the kernel records kDevErrWaitTimeout,
 // drains its copies and MMAs in flight and frees TMEM.
 #include "ts_common.cuh"
@@ -42,11 +44,11 @@ constexpr uint32_t kStageBytes = kQBytes + 2u * kKVBytes;
 constexpr uint32_t kStages = 2;
 constexpr uint32_t kOffBar = kStages * kStageBytes;
 constexpr uint32_t kOffMeta = kOffBar + 128u;             // ItemMeta[kStages]
-constexpr uint32_t kOffRed = kOffMeta + 128u;             // float red_max[2][128], red_sum[2][2][128]
-constexpr uint32_t kSmemBytes = kOffRed + 6u * 128u * 4u + 1024u;  // + alignment slack
+constexpr uint32_t kOffRed = kOffMeta + 128u;             // float red_max[4][128], red_sum[2][4][128]
+constexpr uint32_t kSmemBytes = kOffRed + 12u * 128u * 4u + 1024u;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 288, kColO = 448;  // S: band cols, P: band/2, O: 64
-constexpr int kThreads = 384;  // producer, MMA, TMEM allocator, idle, 8 softmax warps
+constexpr int kThreads = 640;  // producer, MMA, TMEM allocator, idle, 16 softmax warps
 static_assert(kColP >= kColS + kMaxBand && kColO >= kColP + kMaxBand / 2 && kColO + 64 <= kTmemCols, "TMEM map");
 static_assert(kSmemBytes <= 227u * 1024u, "shared memory budget");
 static_assert(kStageBytes % 1024u == 0 && kQBytes % 1024u == 0 && kKVBytes % 1024u == 0, "SW128 alignment");
@@ -128,10 +130,10 @@ __device__ __forceinline__ void exp_pack(const uint32_t (&v)[N], uint32_t rm, fl
   }
 }
 
-// Half an output row: 32 f32 of O times 1/l, as fp16 (round to nearest even).
-__device__ __forceinline__ void store_half_row(uint16_t* dst, const uint32_t (&o)[32], float inv) {
+// A quarter output row: 16 f32 of O times 1/l, as fp16 (round to nearest even).
+__device__ __forceinline__ void store_quarter_row(uint16_t* dst, const uint32_t (&o)[16], float inv) {
 #pragma unroll
-  for (int c = 0; c < 32; c += 8) {
+  for (int c = 0; c < 16; c += 8) {
     uint4 w;
     w.x = pack_half2(__uint_as_float(o[c]) * inv, __uint_as_float(o[c + 1]) * inv);
     w.y = pack_half2(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
@@ -153,11 +155,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = bars + 5;
   uint64_t* o_full = bars + 6;
   uint64_t* drain = bars + 7;
-  uint64_t* pair_bar = bars + 8;  // [4] the two softmax warps of a lane quarter exchanged row maxima
+  uint64_t* pair_bar = bars + 8;  // [4] the four softmax warps of a lane quarter exchanged row maxima
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 12) + 1;
   float* red_max = reinterpret_cast<float*>(smem + kOffRed);
-  float* red_sum = red_max + 256;
+  float* red_sum = red_max + 512;
   ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + kOffMeta);
 
   const uint32_t group = a.Hq / a.Hkv;
@@ -170,8 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 256);
-    for (int q = 0; q < 4; q++) mbar_init(&pair_bar[q], 64);
+    mbar_init(p_full, 512);
+    for (int q = 0; q < 4; q++) mbar_init(&pair_bar[q], 128);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -313,25 +315,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) mbar_wait(drain, 0, a.err);
   } else if (warp >= 4) {
     // ---------------- softmax + epilogue ----------------
-    // Two warps per TMEM lane quarter: warp (4 + quad + 4 * hh) owns rows
-    // quad * 32 .. +31 and column half hh of the band (and of O).
-    const uint32_t quad = (uint32_t)warp & 3u, hh = ((uint32_t)warp - 4u) >> 2;
+    // Four warps per TMEM lane quarter: warp (4 + quad + 4 * cq) owns rows
+    // quad * 32 .. +31, column part cq of the band (its 16-column groups split
+    // in four) and columns 16 cq .. +15 of O.
+    const uint32_t quad = (uint32_t)warp & 3u, cq = ((uint32_t)warp - 4u) >> 2;
     const uint32_t r = quad * 32u + (uint32_t)lane;
     const uint32_t hl = r >> 4, i = r & 15u;
     const uint32_t trow = tmem + ((quad * 32u) << 16);
     const int W = (int)a.window;
     constexpr float kL2E = 1.4426950408889634f;
     const size_t out_ld = (size_t)a.Hq * 64u;
-    const uint32_t g0 = (band / 16u + 1u) / 2u;  // 16-column groups of half 0
-    const uint32_t col_begin = hh == 0u ? 0u : g0 * 16u;
-    const uint32_t col_end = hh == 0u ? g0 * 16u : band;
+    const uint32_t ng = band / 16u;  // 16-column groups of the band
+    const uint32_t col_begin = (ng * cq / 4u) * 16u;
+    const uint32_t col_end = (ng * (cq + 1u) / 4u) * 16u;
     const uint32_t n32 = (col_end - col_begin) / 32u;
     const bool tail = ((col_end - col_begin) & 31u) != 0u;
     const uint32_t c_tail = col_begin + 32u * n32;
     uint32_t lt = 0;
     bool ok = true;
     bool prev_ok = false;
-    float prev_l = 0.0f, prev_sink_term = 0.0f;
+    float prev_sink_term = 0.0f;
     uint16_t* prev_out = nullptr;
     for (uint32_t item = blockIdx.x; item < items; item += gridDim.x, lt++) {
       const uint32_t s = lt & 1u;
@@ -375,10 +378,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int b = 0; b < 16; b++) m0 = fmaxf(m0, ((rm >> b) & 1u) ? __uint_as_float(v[b]) : -INFINITY);
       }
       const float mh = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
-      red_max[hh * 128u + r] = mh;
+      red_max[cq * 128u + r] = mh;
       mbar_arrive(&pair_bar[quad]);
       if (!wait_or_abort(&pair_bar[quad], lt & 1u, a.err, abort_flag)) { ok = false; break; }
-      const float m = fmaxf(mh, red_max[(hh ^ 1u) * 128u + r]);
+      const float m = fmaxf(fmaxf(red_max[r], red_max[128u + r]), fmaxf(red_max[256u + r], red_max[384u + r]));
       const float mb = m * kL2E;
 
       // ---- pass 2: P = exp(s - max) as fp16 into TMEM, this half's row sum ----
@@ -409,37 +412,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_32x32b_x8(trow + kColP + c_tail / 2u, pk);
       }
       tmem_st_wait();
-      red_sum[s * 256u + hh * 128u + r] = l0 + l1;
+      red_sum[s * 512u + cq * 128u + r] = l0 + l1;
 
-      // ---- the previous item's O, this half's 32 columns ----
-      uint32_t o[32];
+      // ---- the previous item's O, this warp's 16 columns ----
+      uint32_t o[16];
       float inv = 0.0f;
       if (lt > 0) {
-        tmem_ld_32x32b_x32(trow + kColO + 32u * hh, o);
-        // p_full of the previous item has completed (its P.V ran), so the
-        // partner's row sum for it is in red_sum
+        tmem_ld_32x32b_x16(trow + kColO + 16u * cq, o);
+        // p_full of the previous item has completed (its P.V ran), so every
+        // part's row sum for it is in red_sum
         if (!wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag)) { ok = false; break; }
-        inv = __fdiv_rn(1.0f, prev_l + red_sum[(s ^ 1u) * 256u + (hh ^ 1u) * 128u + r] + prev_sink_term);
+        const float* ps = red_sum + (s ^ 1u) * 512u + r;
+        inv = __fdiv_rn(1.0f, ((ps[0] + ps[128]) + ps[256]) + ps[384] + prev_sink_term);
         tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(p_full);
-      if (lt > 0 && prev_ok) store_half_row(prev_out, o, inv);
+      if (lt > 0 && prev_ok) store_quarter_row(prev_out, o, inv);
       prev_ok = row_ok;
-      prev_l = l0 + l1;
       prev_sink_term = ex2_approx(fmaf(sink, kL2E, -mb));
       prev_out = a.out + (size_t)(row_ok ? t : 0) * out_ld + (size_t)(hk * group + (row_ok ? hl : 0u)) * 64u +
-                 32u * hh;
+                 16u * cq;
     }
     if (ok && lt > 0 && wait_or_abort(o_full, (lt - 1u) & 1u, a.err, abort_flag) &&
         wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag)) {
       tc_fence_after();
-      uint32_t o[32];
-      tmem_ld_32x32b_x32(trow + kColO + 32u * hh, o);
-      const float inv =
-          __fdiv_rn(1.0f, prev_l + red_sum[((lt - 1u) & 1u) * 256u + (hh ^ 1u) * 128u + r] + prev_sink_term);
+      uint32_t o[16];
+      tmem_ld_32x32b_x16(trow + kColO + 16u * cq, o);
+      const float* ps = red_sum + ((lt - 1u) & 1u) * 512u + r;
+      const float inv = __fdiv_rn(1.0f, ((ps[0] + ps[128]) + ps[256]) + ps[384] + prev_sink_term);
       tmem_ld_wait();
-      if (prev_ok) store_half_row(prev_out, o, inv);
+      if (prev_ok) store_quarter_row(prev_out, o, inv);
     }
   }
   tc_fence_before();
