@@ -175,9 +175,10 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i)
     abi.check(L.ts_cuda_check(h, sp))
-    abi.check(L.ts_cuda_profile(h, 1))
     barrier()
     torch.cuda.synchronize()
+    # Headline pass: no per-phase events inside the steps (an event recorded
+    # between two kernels serialises their programmatic launch).
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         e0.record(st)
@@ -188,6 +189,16 @@ def run_ours(args):
     barrier()
     abi.check(L.ts_cuda_check(h, sp))
     ms = e0.elapsed_time(e1)
+    # Second timed pass of the same steps with CUDA events around each phase:
+    # per-kernel durations for the phase table and the roofline.
+    abi.check(L.ts_cuda_profile(h, 1))
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.warmup, need):
+        step(i)
+    torch.cuda.synchronize()
+    barrier()
+    abi.check(L.ts_cuda_check(h, sp))
     ph_ms = (ctypes.c_double * 7)()
     ph_n = (ctypes.c_uint64 * 7)()
     ph_fl = (ctypes.c_uint64 * 7)()
@@ -263,7 +274,9 @@ def run_ours(args):
                              "achieved": achieved, "peak": pk["tflops_sustained"], "unit": "TFLOP/s",
                              "frac": achieved / pk["tflops_sustained"], "peak_source":
                                  f"{pk['source']} bf16 sustained", "traffic": traffic,
-                             "avg_launch_ms": dur_ms, "flops_per_launch": fl},
+                             "avg_launch_ms": dur_ms, "flops_per_launch": fl,
+                             "timing": "CUDA events around each expert-GEMM launch on a second timed pass of the "
+                                       "same steps (per-phase events kept out of the headline pass)"},
                 "phases": phases,
                 "cpu_baseline": cpu,
                 "e2e": {"value": toks_all / e2e_max, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),

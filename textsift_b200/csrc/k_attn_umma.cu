@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv, const AttnArgs a, uint32_t band) {
   extern __shared__ uint8_t smem_raw[];
+  // inputs come from the previous kernel of the stream (programmatic launch)
+  pdl_trigger();
+  pdl_wait();
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* full = bars;       // [2] Q/K/V of a stage landed
@@ -488,8 +491,7 @@ cudaError_t launch_attention_umma(const AttnArgs& a, cudaStream_t st) {
   }
   const uint64_t items = (uint64_t)a.n_tiles * a.Hkv;
   const uint32_t grid = (uint32_t)std::min<uint64_t>(items, (uint64_t)num_sms());
-  attn_umma_kernel<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, tv, a, band);
-  return cudaGetLastError();
+  return launch_pdl(attn_umma_kernel, dim3(grid), dim3(kThreads), kSmemBytes, st, tq, tk, tv, a, band);
 }
 
 }  // namespace ts

@@ -239,6 +239,9 @@ __global__ void __launch_bounds__(640, 1)
   using C = GemmCfg<BN, BM>;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_dyn[];
+  // inputs come from the previous kernel of the stream (programmatic launch)
+  pdl_trigger();
+  pdl_wait();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::OFF_B;
@@ -581,8 +584,8 @@ static cudaError_t launch_one(const CUtensorMap& tmap, const GemmArgs& args, uin
   // persistent: at most one CTA per SM, never more CTAs than tiles can exist
   const uint64_t max_tiles = (uint64_t)grid_m * n_tiles;
   const uint32_t grid = (uint32_t)std::min<uint64_t>(max_tiles, (uint64_t)num_sms());
-  gemm_w4_tc_kernel<BN, BM, EPI><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tmap, args, n_tiles);
-  return cudaGetLastError();
+  return launch_pdl(gemm_w4_tc_kernel<BN, BM, EPI>, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, st, tmap, args,
+                    n_tiles);
 }
 
 cudaError_t launch_gemm_w4_tc(const W4Tiles& w, const CUtensorMap& tmap_a, GemmArgs args, int epi, uint32_t grid_m,

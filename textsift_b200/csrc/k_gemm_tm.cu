@@ -163,6 +163,9 @@ __global__ void __launch_bounds__(640, 1)
     gemm_w4_tm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args, uint32_t n_ntiles) {
   using namespace tm;
   extern __shared__ uint8_t smem_dyn[];
+  // inputs come from the previous kernel of the stream (programmatic launch)
+  pdl_trigger();
+  pdl_wait();
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint8_t* sX = smem;
   uint8_t* sR = smem + OFF_RAW;
@@ -350,8 +353,7 @@ static cudaError_t launch_tm(const CUtensorMap& tmap, const GemmArgs& args, uint
   }
   const uint64_t max_tiles = (uint64_t)grid_m * n_tiles;
   const uint32_t grid = (uint32_t)std::min<uint64_t>(max_tiles, (uint64_t)num_sms());
-  gemm_w4_tm_kernel<EPI><<<grid, tm::THREADS, tm::SMEM_BYTES, st>>>(tmap, args, n_tiles);
-  return cudaGetLastError();
+  return launch_pdl(gemm_w4_tm_kernel<EPI>, dim3(grid), dim3(tm::THREADS), tm::SMEM_BYTES, st, tmap, args, n_tiles);
 }
 
 uint32_t gemm_tm_rows() { return tm::TOK; }

@@ -24,6 +24,8 @@ namespace ts {
 // ---------------------------------------------------------------------------
 __global__ void seq_info_kernel(const uint32_t* __restrict__ offs, uint32_t n_seqs, uint32_t T, int* __restrict__ pos,
                                 int* __restrict__ sstart, int* __restrict__ slen) {
+  pdl_trigger();
+  pdl_wait();
   uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   uint32_t lo = 0, hi = n_seqs;  // find s with offs[s] <= t < offs[s+1]
@@ -43,6 +45,8 @@ __global__ void seq_info_kernel(const uint32_t* __restrict__ offs, uint32_t n_se
 __global__ void embed_gather_kernel(const uint8_t* __restrict__ w, const uint16_t* __restrict__ sc,
                                     const uint8_t* __restrict__ zp, const int32_t* __restrict__ ids,
                                     uint16_t* __restrict__ out, uint32_t T, uint32_t V, uint32_t D) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t nb = D / 32, zs = (nb + 1) / 2;
   uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x;
   if (gid >= T * nb) return;
@@ -400,6 +404,8 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 // Exclusive scan of hist[c][e] over chunks c, one warp per expert; total[e].
 __global__ void __launch_bounds__(256) moe_chunk_scan_kernel(int* __restrict__ hist, uint32_t n_chunks, uint32_t E,
                                                              int* __restrict__ counts) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (e >= E) return;
@@ -445,6 +451,8 @@ __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __
                                                                    int* __restrict__ n_tiles_tc, int rows_tc,
                                                                    int* __restrict__ seg_start,
                                                                    int* __restrict__ seg_end) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int wt[kMaxExperts / 32];
   const uint32_t e = threadIdx.x;
   const int cnt = e < E ? counts[e] : 0;
@@ -468,11 +476,13 @@ __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __
 }
 
 __global__ void __launch_bounds__(kRouteChunk) moe_place_kernel(const int32_t* __restrict__ idx,
-                                                                const int* __restrict__ hist,
+                                                                int* __restrict__ hist,
                                                                 const int* __restrict__ seg_start, uint32_t T,
                                                                 uint32_t K, uint32_t E, int* __restrict__ perm_tok,
                                                                 int* __restrict__ route_pos) {
   __shared__ uint32_t mask[kMaxExperts][kRouteChunk / 32];
+  pdl_trigger();
+  pdl_wait();
   const uint32_t tl = threadIdx.x, t = blockIdx.x * kRouteChunk + tl;
   for (uint32_t i = threadIdx.x; i < E * (kRouteChunk / 32); i += blockDim.x) mask[i / 4][i % 4] = 0;
   __syncthreads();
@@ -483,8 +493,7 @@ __global__ void __launch_bounds__(kRouteChunk) moe_place_kernel(const int32_t* _
     if (ek[k] >= 0 && (uint32_t)ek[k] < E) atomicOr(&mask[ek[k]][tl >> 5], 1u << (tl & 31));
   }
   __syncthreads();
-  if (!ok) return;
-  for (uint32_t k = 0; k < K; k++) {
+  for (uint32_t k = 0; k < K && ok; k++) {
     const int e = ek[k];
     if (e < 0 || (uint32_t)e >= E) { route_pos[(size_t)t * K + k] = -1; continue; }
     int rank = __popc(mask[e][tl >> 5] & ((1u << (tl & 31)) - 1u));
@@ -493,12 +502,18 @@ __global__ void __launch_bounds__(kRouteChunk) moe_place_kernel(const int32_t* _
     perm_tok[p] = (int)t;
     route_pos[(size_t)t * K + k] = p;
   }
+  // this chunk's row is consumed: leave it zero for the next fused top-k,
+  // which accumulates expert counts into it
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) hist[(size_t)blockIdx.x * E + i] = 0;
 }
 
 // dst[p, :] = src[perm_tok[p], :] (row bytes a multiple of 16)
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                    const int* __restrict__ perm_tok, const int* __restrict__ n_rows_dev,
                                    uint32_t n_rows, uint32_t row_bytes) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t rows = n_rows_dev ? (uint32_t)*n_rows_dev : n_rows;
   const uint32_t per_row = row_bytes / 16;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < rows * per_row; i += gridDim.x * blockDim.x) {
@@ -574,6 +589,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
                                                            uint16_t* __restrict__ sum_out,
                                                            uint16_t* __restrict__ out16, uint32_t T, uint32_t D,
                                                            float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const uint32_t row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= T) return;
@@ -644,6 +661,8 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
                                                                const uint16_t* __restrict__ res,
                                                                uint16_t* __restrict__ out, uint32_t T, uint32_t D,
                                                                uint32_t K, uint32_t E) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -805,15 +824,14 @@ static inline unsigned gs_blocks(size_t n, unsigned b) {
 cudaError_t launch_seq_info(const uint32_t* offs, uint32_t n_seqs, uint32_t T, int* pos, int* sstart, int* slen,
                             cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  seq_info_kernel<<<nblk(T, 256), 256, 0, st>>>(offs, n_seqs, T, pos, sstart, slen);
-  return cudaGetLastError();
+  return launch_pdl(seq_info_kernel, dim3(nblk(T, 256)), dim3(256), 0, st, offs, n_seqs, T, pos, sstart, slen);
 }
 
 cudaError_t launch_embed(const uint8_t* w, const uint16_t* sc, const uint8_t* zp, const int32_t* ids, uint16_t* out,
                          uint32_t T, uint32_t V, uint32_t D, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  embed_gather_kernel<<<nblk((size_t)T * (D / 32), 128), 128, 0, st>>>(w, sc, zp, ids, out, T, V, D);
-  return cudaGetLastError();
+  return launch_pdl(embed_gather_kernel, dim3(nblk((size_t)T * (D / 32), 128)), dim3(128), 0, st, w, sc, zp, ids, out, T,
+                    V, D);
 }
 
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gamma, float* out32, uint16_t* out16, uint32_t T,
@@ -888,19 +906,20 @@ cudaError_t launch_moe_permute(const int32_t* idx, int* hist, uint32_t T, uint32
                                int* n_tiles_tc, uint32_t rows_tc, int* seg_start, int* seg_end, cudaStream_t st) {
   if (E > kMaxExperts || K > 8 || (tiles_tc && rows_tc == 0)) return cudaErrorInvalidValue;
   const uint32_t nc = route_chunks(T);
-  moe_chunk_scan_kernel<<<(E + 7) / 8, 256, 0, st>>>(hist, nc, E, counts);
-  moe_segments_kernel<<<1, kMaxExperts, 0, st>>>(counts, E, tiles, n_tiles, tiles_tc, n_tiles_tc, (int)rows_tc,
-                                                 seg_start, seg_end);
-  moe_place_kernel<<<nc, kRouteChunk, 0, st>>>(idx, hist, seg_start, T, K, E, perm_tok, route_pos);
-  return cudaGetLastError();
+  cudaError_t e = launch_pdl(moe_chunk_scan_kernel, dim3((E + 7) / 8), dim3(256), 0, st, hist, nc, E, counts);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(moe_segments_kernel, dim3(1), dim3(kMaxExperts), 0, st, counts, E, tiles, n_tiles, tiles_tc, n_tiles_tc,
+                 (int)rows_tc, seg_start, seg_end);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(moe_place_kernel, dim3(nc), dim3(kRouteChunk), 0, st, idx, hist, seg_start, T, K, E, perm_tok,
+                    route_pos);
 }
 
 cudaError_t launch_gather_rows(const void* src, void* dst, const int* perm_tok, const int* n_rows_dev,
                                uint32_t max_rows, uint32_t row_bytes, cudaStream_t st) {
   if (max_rows == 0) return cudaSuccess;
-  gather_rows_kernel<<<gs_blocks((size_t)max_rows * row_bytes / 16, 256), 256, 0, st>>>(
-      (const uint8_t*)src, (uint8_t*)dst, perm_tok, n_rows_dev, max_rows, row_bytes);
-  return cudaGetLastError();
+  return launch_pdl(gather_rows_kernel, dim3(gs_blocks((size_t)max_rows * row_bytes / 16, 256)), dim3(256), 0, st,
+                    (const uint8_t*)src, (uint8_t*)dst, perm_tok, n_rows_dev, max_rows, row_bytes);
 }
 
 cudaError_t launch_moe_combine(const float* down, const int32_t* idx, const float* w, const int* route_pos,
@@ -933,9 +952,9 @@ cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint
   if (T == 0) return cudaSuccess;
   if (D % 8 || D > 1024 || !out16 || (b && !sum_out)) return cudaErrorInvalidValue;
   const uint32_t blocks = (T + 7) / 8;
-  if (b) rmsnorm_fast_kernel<true><<<blocks, 256, 0, st>>>(a, b, gamma, sum_out, out16, T, D, eps);
-  else rmsnorm_fast_kernel<false><<<blocks, 256, 0, st>>>(a, nullptr, gamma, nullptr, out16, T, D, eps);
-  return cudaGetLastError();
+  if (b) return launch_pdl(rmsnorm_fast_kernel<true>, dim3(blocks), dim3(256), 0, st, a, b, gamma, sum_out, out16, T, D, eps);
+  return launch_pdl(rmsnorm_fast_kernel<false>, dim3(blocks), dim3(256), 0, st, a, (const uint16_t*)nullptr, gamma,
+                    (uint16_t*)nullptr, out16, T, D, eps);
 }
 
 cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,
@@ -943,8 +962,8 @@ cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, co
                                     uint32_t E, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (D % 8 || K > 8) return cudaErrorInvalidValue;
-  moe_combine_fast_kernel<<<(T + 7) / 8, 256, 0, st>>>(down, idx, w, route_pos, res, out, T, D, K, E);
-  return cudaGetLastError();
+  return launch_pdl(moe_combine_fast_kernel, dim3((T + 7) / 8), dim3(256), 0, st, down, idx, w, route_pos, res, out, T, D,
+                    K, E);
 }
 
 cudaError_t launch_f16_to_f32_ref(const uint16_t* src, float* dst, size_t n, cudaStream_t st) {

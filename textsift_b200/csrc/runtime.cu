@@ -452,8 +452,9 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
       ts::GemmArgs gr;
       gr.M = T; gr.err = h->err.p;
       if (K == 4 && E <= 128) {
-        // top-k and the permutation's expert counts in the GEMM epilogue
-        TS_K(cudaMemsetAsync(w.hist.p, 0, (size_t)ts::route_chunks(T) * E * sizeof(int), st));
+        // top-k and the permutation's expert counts in the GEMM epilogue; the
+        // counts start from zero (the forward or the op zeroes them once, and
+        // moe_place zeroes each chunk's row after consuming it)
         gr.out0 = w.ridx.p; gr.out1 = w.rw.p; gr.hist = w.hist.p;
         TS_K(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiRouterTopk, (T + 127) / 128, st));
       } else {
@@ -555,6 +556,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   if (rc0) return rc0;
   memcpy(sg->p, offs, (size_t)(n_seqs + 1) * 4);
   TS_K(cudaMemcpyAsync(w.offs.p, sg->p, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st));
+  TS_K(cudaMemsetAsync(w.hist.p, 0, (size_t)ts::route_chunks(T) * c.n_experts * sizeof(int), st));
   {
     Phase p(h, st, TS_PHASE_OTHER, 0, 2);
     TS_K(ts::launch_seq_info(w.offs.p, n_seqs, T, w.pos.p, w.sstart.p, w.slen.p, st));
@@ -1206,7 +1208,10 @@ int ts_cuda_op_moe(ts_cuda_t* h, uint32_t layer, const float* d_x, uint16_t* d_o
   int rc = ensure_workspace(h, exact);
   if (rc) return rc;
   const ts_cuda_cfg& c = h->cfg;
-  if (!exact) TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, h->ws.xn16.p, (size_t)T * c.d_model, st));
+  if (!exact) {
+    TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, h->ws.xn16.p, (size_t)T * c.d_model, st));
+    TS_CUDA_TRY(cudaMemsetAsync(h->ws.hist.p, 0, (size_t)ts::route_chunks(T) * c.n_experts * sizeof(int), st));
+  }
   rc = moe_half(h, *h->layers[layer], d_x, h->ws.xn16.p, nullptr, d_out, T, nullptr, nullptr, exact, st, -1);
   if (rc) return rc;
   if (d_idx) TS_CUDA_TRY(cudaMemcpyAsync(d_idx, h->ws.ridx.p, (size_t)T * c.top_k * 4, cudaMemcpyDeviceToDevice, st));

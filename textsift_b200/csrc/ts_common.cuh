@@ -221,6 +221,34 @@ __device__ __forceinline__ void swiglu_fast2(float g0, float u0, float g1, float
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Kernels of the forward are launched with
+// programmatic stream serialisation: the next grid may be scheduled once every
+// block of the running one has called pdl_trigger(), and its blocks run their
+// set-up until pdl_wait(), which returns when the previous grid has completed
+// and its memory is visible.  Every such kernel calls pdl_trigger() and then
+// pdl_wait() before its first access to global memory; launched without the
+// attribute both are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------
 // Error flag shared by every kernel (bounded waits, bad indices)
 // ---------------------------------------------------------------------------
 enum DevErr : int {
