@@ -28,6 +28,8 @@
 //   warps 12..19 epilogue of the previous tile: warp w reads lanes 32(w%4)..
 //                (one output column per thread) for tokens 96((w-12)/4)..;
 //                lane pairs exchange values so each store is 32 bits
+// With the RoPE epilogue (QKV) warps 4..7 dequantise every chunk and warps
+// 8..19 run the epilogue, 64 tokens each.
 // All waits are bounded (ts_common.cuh) and set the device error flag.
 #include "ts_common.cuh"
 #include "ts_kernels.h"
@@ -162,6 +164,12 @@ template <int EPI>
 __global__ void __launch_bounds__(640, 1)
     gemm_w4_tm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args, uint32_t n_ntiles) {
   using namespace tm;
+  // the 16 role warps: the RoPE epilogue (loads of the rotation table) gets
+  // 12 warps and dequantisation 4; the other epilogues 8 and 8
+  constexpr uint32_t kDqWarps = EPI == kEpiQkvRope ? 4 : 8;
+  constexpr uint32_t kEpiWarps = 16 - kDqWarps;
+  constexpr uint32_t kPartTok = TOK / (kEpiWarps / 4);  // tokens per epilogue warp
+  static_assert(kPartTok % 32 == 0, "32-token slices");
   extern __shared__ uint8_t smem_dyn[];
   // inputs come from the previous kernel of the stream (programmatic launch)
   pdl_trigger();
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(640, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 256);
+      mbar_init(&acc_empty[b], 32u * kEpiWarps);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -259,9 +267,10 @@ __global__ void __launch_bounds__(640, 1)
       if (ok && elect_one()) tc_commit(&acc_full[b]);
       __syncwarp();
     }
-  } else if (warp >= 4 && warp < 12) {
-    // ---- dequantise: warps 4..7 take the even chunks, 8..11 the odd ones, so
-    // two chunks are in flight; thread = one output row, both K halves ----
+  } else if (warp >= 4 && warp < 4 + kDqWarps) {
+    // ---- dequantise; thread = one output row, both K halves.  With 8 warps,
+    // 4..7 take the even chunks and 8..11 the odd ones (two chunks in flight);
+    // with 4 warps each takes every chunk. ----
     const uint32_t q = (uint32_t)(warp & 3), grp = (uint32_t)(warp - 4) >> 2;
     const uint32_t r = q * 32u + (uint32_t)lane;
     const uint32_t tcol = tmem_base + ((q * 32u) << 16) + COL_A;
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(640, 1)
     bool ok = true;
     for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
       for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
-        if ((it & 1u) != grp) continue;
+        if (kDqWarps == 8 && (it & 1u) != grp) continue;
         const int s = it % S;
         const uint32_t ph = (it / S) & 1u;
         // full[s] of this use follows the MMAs of the stage's previous use
@@ -306,9 +315,9 @@ __global__ void __launch_bounds__(640, 1)
         mbar_arrive(&aready[s]);
       }
     }
-  } else if (warp >= 12) {
-    // ---- epilogue: lanes 32(warp%4).. = output columns, token half (warp-12)/4 ----
-    const uint32_t q = (uint32_t)(warp & 3), g = (uint32_t)(warp - 12) >> 2;
+  } else if (warp >= 4 + kDqWarps) {
+    // ---- epilogue: lanes 32(warp%4).. = output columns, token part g of kParts ----
+    const uint32_t q = (uint32_t)(warp & 3), g = (uint32_t)(warp - 4 - kDqWarps) >> 2;
     const uint32_t nl = q * 32u + (uint32_t)lane;
     uint32_t lt = 0;
     for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x, lt++) {
@@ -318,18 +327,18 @@ __global__ void __launch_bounds__(640, 1)
       const float bv = n < args.N ? f16_ref_to_f32(args.bias[(size_t)ti.expert * args.N + n]) : 0.0f;
       if (!wait_or_abort(&acc_full[b], bph, args.err, abort_flag)) break;
       tc_fence_after();
-      const uint32_t acc = tmem_base + ((q * 32u) << 16) + b * TOK + g * (TOK / 2);
+      const uint32_t acc = tmem_base + ((q * 32u) << 16) + b * TOK + g * kPartTok;
 #pragma unroll 1
-      for (uint32_t c0 = 0; c0 < TOK / 2; c0 += 32) {
+      for (uint32_t c0 = 0; c0 < kPartTok; c0 += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(acc + c0, v);
         tmem_ld_wait();
-        if (c0 + 32 >= TOK / 2) {
+        if (c0 + 32 >= kPartTok) {
           // every TMEM read of this buffer by this thread is complete: release it
           tc_fence_before();
           mbar_arrive(&acc_empty[b]);
         }
-        tm_epilogue_slice<EPI>(args, ti, ti.row0 + g * (TOK / 2) + c0, n, bv, v, lane);
+        tm_epilogue_slice<EPI>(args, ti, ti.row0 + g * kPartTok + c0, n, bv, v, lane);
       }
     }
   }
