@@ -144,6 +144,9 @@ def run_ours(args):
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
+        # stdout carries exactly one JSON line: NCCL's own messages (printed
+        # when NCCL_DEBUG is set, e.g. its version line) go to stderr
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     L = abi.lib()
