@@ -260,6 +260,46 @@ int ts_cuda_op_banded_attention_noalloc(const uint16_t* d_q, const uint16_t* d_k
  * [rows, head_dim/2] each, copied to host. */
 int ts_cuda_rope_tables(ts_cuda_t* h, uint32_t rows, uint16_t* cos_out, uint16_t* sin_out);
 
+/* ---------------------------------------------------------------------
+ * Tokenizer (host CPU): the native counterpart of textsift's o200k-style
+ * byte-level BPE Tokenizer (src/browser/model/tokenizer.ts), so tokenizing
+ * keeps up with the GPU forward.  Same token ids and tokenToCharOffset
+ * (UTF-16 code units) as Tokenizer.encode; input is UTF-8.  Calls on one
+ * handle must not overlap (ts_tok_encode_batch spreads one batch over its
+ * own threads).
+ * ------------------------------------------------------------------- */
+typedef struct ts_tok ts_tok_t;
+
+/* Tokenizer.fromBundle (tokenizer.ts:134-221): parses tokenizer.json
+ * (model.type "BPE", model.vocab, model.merges as [a, b] pairs,
+ * added_tokens).  NULL on error, message in err (and ts_cuda_last_error). */
+ts_tok_t* ts_tok_create(const char* tokenizer_json, size_t len, char* err, size_t err_cap);
+void ts_tok_destroy(ts_tok_t* t);
+/* Largest token id + 1 (Tokenizer.vocabSize, tokenizer.ts:233-236). */
+uint32_t ts_tok_vocab_size(const ts_tok_t* t);
+
+/* Tokenizer.encode (tokenizer.ts:238-291) of one UTF-8 text.  *n_tokens =
+ * the token count; ids [n], char_offsets [n + 1] (UTF-16 start of each token
+ * and the end of the last: tokenToCharOffset) and byte_offsets [n + 1] (the
+ * same in UTF-8 bytes) are written when non-NULL, if n <= cap (else
+ * TS_ERR_ARG).  All three NULL: size query.  Invalid UTF-8 -> TS_ERR_ARG. */
+int ts_tok_encode(ts_tok_t* t, const char* utf8, size_t len, int32_t* ids, uint32_t* char_offsets,
+                  uint32_t* byte_offsets, size_t cap, size_t* n_tokens);
+
+/* Many texts on up to n_threads threads (0: one per hardware thread).
+ * token_begin [n_texts + 1]: text i's tokens are [token_begin[i],
+ * token_begin[i + 1]) of ids, starts and ends (UTF-16 start and end of
+ * each token within its text), written when non-NULL if the total <= cap.
+ * All three NULL: size query. */
+int ts_tok_encode_batch(ts_tok_t* t, const char* const* texts, const size_t* lens, uint32_t n_texts,
+                        uint32_t n_threads, int32_t* ids, uint32_t* starts, uint32_t* ends, size_t cap,
+                        uint64_t* token_begin);
+
+/* Tokenizer.decode (tokenizer.ts:294-334) to UTF-8: *out_len = bytes;
+ * written to out when non-NULL and *out_len <= cap.  Unknown ids are
+ * skipped. */
+int ts_tok_decode(const ts_tok_t* t, const int32_t* ids, size_t n, char* out, size_t cap, size_t* out_len);
+
 #ifdef __cplusplus
 }
 #endif

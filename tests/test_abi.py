@@ -14,7 +14,7 @@ HEADER = os.path.join(ROOT, "include", "textsift_cuda.h")
 def declared_functions():
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(ts_cuda_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(ts_(?:cuda|tok)_\w+)\s*\(", src)))
 
 
 def test_header_declares_the_boundary():

@@ -83,6 +83,13 @@ SIGNATURES = [
     ("ts_cuda_op_banded_attention_noalloc", ctypes.c_int, [P, P, P, P, P, P, U32, U32, U32, U32, U32, P, U32, I32,
                                                            P]),
     ("ts_cuda_rope_tables", ctypes.c_int, [P, U32, P, P]),
+    # host tokenizer
+    ("ts_tok_create", P, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t]),
+    ("ts_tok_destroy", None, [P]),
+    ("ts_tok_vocab_size", U32, [P]),
+    ("ts_tok_encode", ctypes.c_int, [P, ctypes.c_char_p, ctypes.c_size_t, P, P, P, ctypes.c_size_t, P]),
+    ("ts_tok_encode_batch", ctypes.c_int, [P, P, P, U32, U32, P, P, P, ctypes.c_size_t, P]),
+    ("ts_tok_decode", ctypes.c_int, [P, P, ctypes.c_size_t, P, ctypes.c_size_t, P]),
 ]
 
 
