@@ -660,7 +660,9 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
                                                                const int* __restrict__ route_pos,
                                                                const uint16_t* __restrict__ res,
                                                                uint16_t* __restrict__ out, uint32_t T, uint32_t D,
-                                                               uint32_t K, uint32_t E) {
+                                                               uint32_t K, uint32_t E,
+                                                               const uint16_t* __restrict__ norm_gamma,
+                                                               uint16_t* __restrict__ norm_out, float eps) {
   pdl_trigger();
   pdl_wait();
   const uint32_t t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -698,7 +700,12 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
   }
   const float kf = (float)K;
   const uint32_t nc = D / 8;
-  for (uint32_t c = (uint32_t)lane; c < nc; c += 32) {
+  uint4 xr[4];      // this lane's output chunks, kept for the fused norm
+  float ss = 0.0f;  // their sum of squares, in rmsnorm_fast_kernel's order
+#pragma unroll
+  for (int rr = 0; rr < 4; rr++) {
+    const uint32_t c = (uint32_t)lane + 32u * rr;
+    if (c >= nc) break;
     // every route's 16 bytes (and the residual's) in flight before the math
     const size_t o = (size_t)t * D + 8 * c;
     uint4 vv[8];
@@ -733,6 +740,35 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
       for (int q = 0; q < 4; q++) ow[q] = f32x2_to_h2(acc[2 * q] * kf, acc[2 * q + 1] * kf);
     }
     *reinterpret_cast<uint4*>(out + o) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    if (norm_gamma) {
+      xr[rr] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ow[q]));
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+  }
+  if (!norm_gamma) return;
+  // the next RMSNorm of this token's new residual, exactly as rmsnorm_fast_kernel<false>
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv_rms = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int rr = 0; rr < 4; rr++) {
+    const uint32_t c = (uint32_t)lane + 32u * rr;
+    if (c >= nc) break;
+    const uint4 gv = *reinterpret_cast<const uint4*>(norm_gamma + 8 * c);
+    const uint32_t xw[4] = {xr[rr].x, xr[rr].y, xr[rr].z, xr[rr].w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t nw[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&xw[j]));
+      const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
+      nw[j] = f32x2_to_h2(x.x * inv_rms * g.x, x.y * inv_rms * g.y);
+    }
+    *reinterpret_cast<uint4*>(norm_out + (size_t)t * D + 8 * c) = make_uint4(nw[0], nw[1], nw[2], nw[3]);
   }
 }
 
@@ -959,11 +995,12 @@ cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint
 
 cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,
                                     const uint16_t* res, uint16_t* out, uint32_t T, uint32_t D, uint32_t K,
-                                    uint32_t E, cudaStream_t st) {
+                                    uint32_t E, const uint16_t* norm_gamma, uint16_t* norm_out, float eps,
+                                    cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  if (D % 8 || K > 8) return cudaErrorInvalidValue;
+  if (D % 8 || K > 8 || D > 8 * 32 * 4 || (norm_gamma && !norm_out)) return cudaErrorInvalidValue;
   return launch_pdl(moe_combine_fast_kernel, dim3((T + 7) / 8), dim3(256), 0, st, down, idx, w, route_pos, res, out, T, D,
-                    K, E);
+                    K, E, norm_gamma, norm_out, eps);
 }
 
 cudaError_t launch_f16_to_f32_ref(const uint16_t* src, float* dst, size_t n, cudaStream_t st) {

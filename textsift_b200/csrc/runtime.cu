@@ -430,8 +430,11 @@ struct Phase {
 // The MoE half of a block: routing from n32 (f32, exact mode) or xn16 (fp16,
 // fast mode), experts, deterministic
 // combine.  res == nullptr writes the bare MoE output fp16(K * sum w e(x)).
+// next_gamma (fast mode) fuses the next RMSNorm into the combine: xn16 then
+// holds RMSNorm(out) * next_gamma on return.
 int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, const uint16_t* res, uint16_t* out,
-             uint32_t T, const int* rloc, const int* rlen, bool exact, cudaStream_t st, int layer) {
+             uint32_t T, const int* rloc, const int* rlen, bool exact, cudaStream_t st, int layer,
+             const uint16_t* next_gamma = nullptr) {
   Workspace& w = h->ws;
   const ts_cuda_cfg& c = h->cfg;
   const uint32_t D = c.d_model, K = c.top_k, E = c.n_experts, F = c.d_ff;
@@ -507,7 +510,9 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
   {
     Phase p(h, st, TS_PHASE_OTHER, 0, 1);
     if (exact) TS_K(ts::launch_moe_combine(w.down32.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E, st));
-    else TS_K(ts::launch_moe_combine_fast(w.down16.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E, st));
+    else
+      TS_K(ts::launch_moe_combine_fast(w.down16.p, w.ridx.p, w.rw.p, w.route_pos.p, res, out, T, D, K, E,
+                                       next_gamma, w.xn16.p, c.eps, st));
   }
   return TS_OK;
 }
@@ -597,7 +602,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
     LayerDev& L = *h->layers[li];
     aa.sinks = L.sinks.p;
     if (!exact) {
-      {
+      if (li == 0) {  // later layers' ln1 comes fused with the previous combine
         Phase p(h, st, TS_PHASE_OTHER, 0, 1);
         TS_K(ts::launch_rmsnorm_fast(src, nullptr, L.ln1.p, nullptr, w.xn16.p, T, D, c.eps, st));
       }
@@ -640,13 +645,15 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
       TS_K(ts::launch_matmul_exact(oa, false, ts::kOutF16, mt, st));
       TS_K(ts::launch_add_rmsnorm(src, w.o16.p, L.ln2.p, w.res2.p, w.n32.p, nullptr, T, D, c.eps, st));
     }
-    rc = moe_half(h, L, w.n32.p, w.xn16.p, w.res2.p, dst, T, w.pos.p, w.slen.p, exact, st, (int)li);
+    const uint16_t* next_gamma = exact ? nullptr : li + 1 < c.n_layers ? h->layers[li + 1]->ln1.p : h->final_norm.p;
+    rc = moe_half(h, L, w.n32.p, w.xn16.p, w.res2.p, dst, T, w.pos.p, w.slen.p, exact, st, (int)li, next_gamma);
     if (rc) return rc;
     std::swap(src, dst);
   }
-  Phase p(h, st, TS_PHASE_OTHER, 2ull * T * c.n_classes * D, 2);
+  Phase p(h, st, TS_PHASE_OTHER, 2ull * T * c.n_classes * D, (!exact && c.n_layers > 0) ? 1 : 2);
   if (!exact) {
-    TS_K(ts::launch_rmsnorm_fast(src, nullptr, h->final_norm.p, nullptr, w.xn16.p, T, D, c.eps, st));
+    // the final norm comes fused with the last layer's combine
+    if (c.n_layers == 0) TS_K(ts::launch_rmsnorm_fast(src, nullptr, h->final_norm.p, nullptr, w.xn16.p, T, D, c.eps, st));
     ts::GemmArgs gs;
     gs.M = T; gs.err = h->err.p; gs.out0 = d_logits; gs.ld0 = c.n_classes;
     TS_K(ts::launch_gemm_w4_tc(h->score.tiles(), t_xn, gs, ts::kEpiF16Widen, mt, st));

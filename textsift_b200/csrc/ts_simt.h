@@ -70,9 +70,12 @@ cudaError_t launch_viterbi(const float* logits, const int* offs_dev, uint32_t n_
 // to fp16, any summation order; MoE combine from fp16 expert outputs.
 cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
                                 uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st);
+// With norm_gamma set it also writes norm_out = RMSNorm(out) * norm_gamma, the
+// same bits as launch_rmsnorm_fast on out (D <= 1024).
 cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,
                                     const uint16_t* res, uint16_t* out, uint32_t T, uint32_t D, uint32_t K,
-                                    uint32_t E, cudaStream_t st);
+                                    uint32_t E, const uint16_t* norm_gamma, uint16_t* norm_out, float eps,
+                                    cudaStream_t st);
 cudaError_t launch_f16_to_f32_ref(const uint16_t* src, float* dst, size_t n, cudaStream_t st);
 cudaError_t launch_f32_to_f16(const float* src, uint16_t* dst, size_t n, cudaStream_t st);
 cudaError_t launch_dequant_tiles(const uint8_t* blobs, uint32_t N, uint32_t K, uint32_t BN, uint32_t n_kc,
