@@ -654,7 +654,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
 // warp then streams the rows in 8-column chunks: acc = sum over the experts
 // in ascending id of w * v (fma, from 0); out = fp16(res + fp16(acc * K))
 // (or fp16(acc * K) without a residual).
-__global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* __restrict__ down,
+template <int KMAX>
+__global__ void __launch_bounds__(256, 4) moe_combine_fast_kernel(const uint16_t* __restrict__ down,
                                                                const int32_t* __restrict__ idx,
                                                                const float* __restrict__ w,
                                                                const int* __restrict__ route_pos,
@@ -681,17 +682,17 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
   // rank of this lane's route among the valid ones: (expert id, slot) order
   int rank = 0, n = 0;
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
+  for (int j = 0; j < KMAX; j++) {
     const int ej = __shfl_sync(0xffffffffu, my_e, j);
     if ((uint32_t)j < K && ej != 0x7fffffff) {
       n++;
       rank += (ej < my_e || (ej == my_e && j < lane)) ? 1 : 0;
     }
   }
-  int pk[8];
-  float wk[8];
+  int pk[KMAX];
+  float wk[KMAX];
 #pragma unroll
-  for (int r = 0; r < 8; r++) {
+  for (int r = 0; r < KMAX; r++) {
     // the lane whose route has rank r
     const unsigned sel = __ballot_sync(0xffffffffu, (uint32_t)lane < K && my_e != 0x7fffffff && rank == r);
     const int src = sel ? __ffs(sel) - 1 : 0;
@@ -700,22 +701,19 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
   }
   const float kf = (float)K;
   const uint32_t nc = D / 8;
-  uint4 xr[4];      // this lane's output chunks, kept for the fused norm
-  float ss = 0.0f;  // their sum of squares, in rmsnorm_fast_kernel's order
-#pragma unroll
-  for (int rr = 0; rr < 4; rr++) {
-    const uint32_t c = (uint32_t)lane + 32u * rr;
-    if (c >= nc) break;
+  float ss = 0.0f;  // sum of squares of this lane's outputs, in rmsnorm_fast_kernel's order
+#pragma unroll 1
+  for (uint32_t c = (uint32_t)lane; c < nc; c += 32) {
     // every route's 16 bytes (and the residual's) in flight before the math
     const size_t o = (size_t)t * D + 8 * c;
-    uint4 vv[8];
+    uint4 vv[KMAX];
 #pragma unroll
-    for (int j = 0; j < 8; j++)
+    for (int j = 0; j < KMAX; j++)
       vv[j] = j < n ? __ldg(reinterpret_cast<const uint4*>(down + (size_t)pk[j] * D + 8 * c)) : make_uint4(0, 0, 0, 0);
     const uint4 rv = res ? __ldg(reinterpret_cast<const uint4*>(res + o)) : make_uint4(0, 0, 0, 0);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
+    for (int j = 0; j < KMAX; j++) {
       if (j >= n) break;
       const uint32_t vw[4] = {vv[j].x, vv[j].y, vv[j].z, vv[j].w};
 #pragma unroll
@@ -741,7 +739,6 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
     }
     *reinterpret_cast<uint4*>(out + o) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
     if (norm_gamma) {
-      xr[rr] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
 #pragma unroll
       for (int q = 0; q < 4; q++) {
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ow[q]));
@@ -755,12 +752,13 @@ __global__ void __launch_bounds__(256) moe_combine_fast_kernel(const uint16_t* _
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float inv_rms = rsqrtf(ss / (float)D + eps);
-#pragma unroll
-  for (int rr = 0; rr < 4; rr++) {
-    const uint32_t c = (uint32_t)lane + 32u * rr;
-    if (c >= nc) break;
-    const uint4 gv = *reinterpret_cast<const uint4*>(norm_gamma + 8 * c);
-    const uint32_t xw[4] = {xr[rr].x, xr[rr].y, xr[rr].z, xr[rr].w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+  // each lane reads back the chunks it wrote above (L2-resident): cheaper than
+  // holding them in registers across the loop, which halves the occupancy
+#pragma unroll 1
+  for (uint32_t c = (uint32_t)lane; c < nc; c += 32) {
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(norm_gamma + 8 * c));
+    const uint4 xv = *reinterpret_cast<const uint4*>(out + (size_t)t * D + 8 * c);
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
     uint32_t nw[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -999,8 +997,11 @@ cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, co
                                     cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (D % 8 || K > 8 || D > 8 * 32 * 4 || (norm_gamma && !norm_out)) return cudaErrorInvalidValue;
-  return launch_pdl(moe_combine_fast_kernel, dim3((T + 7) / 8), dim3(256), 0, st, down, idx, w, route_pos, res, out, T, D,
-                    K, E, norm_gamma, norm_out, eps);
+  if (K <= 4)
+    return launch_pdl(moe_combine_fast_kernel<4>, dim3((T + 7) / 8), dim3(256), 0, st, down, idx, w, route_pos, res, out,
+                      T, D, K, E, norm_gamma, norm_out, eps);
+  return launch_pdl(moe_combine_fast_kernel<8>, dim3((T + 7) / 8), dim3(256), 0, st, down, idx, w, route_pos, res, out, T,
+                    D, K, E, norm_gamma, norm_out, eps);
 }
 
 cudaError_t launch_f16_to_f32_ref(const uint16_t* src, float* dst, size_t n, cudaStream_t st) {
