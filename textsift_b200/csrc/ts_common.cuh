@@ -305,6 +305,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a waiting thread sleeps (issuing nothing)
+// until the phase completes or about kSuspendHintNs pass, so warps parked on a
+// barrier leave the scheduler's issue slots to the warps sharing it.
+#ifndef TS_SUSPEND_HINT_NS
+#define TS_SUSPEND_HINT_NS 20000
+#endif
+constexpr uint32_t kSuspendHintNs = TS_SUSPEND_HINT_NS;
+
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait.  Returns false (and records kDevErrWaitTimeout) if the phase
 // did not complete within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -312,7 +332,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   const unsigned long long t0 = globaltimer_ns();
   uint32_t it = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if ((++it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
       set_dev_err(err, kDevErrWaitTimeout);
       return false;
@@ -326,7 +346,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
   const unsigned long long t0 = globaltimer_ns();
   uint32_t it = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if ((++it & 63u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
