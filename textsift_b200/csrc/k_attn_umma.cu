@@ -21,10 +21,13 @@
 //     from smem (an MN-major operand);
 //   * sixteen softmax warps, four per TMEM lane quarter (one thread per row,
 //     each warp a quarter of the band's columns), find the row max over the
-//     usable keys (the four partial maxima meet in smem), write
-//     P = 2^((s - max) log2 e) as fp16 into TMEM (kColP..) and keep partial
-//     row sums; one item later each reads 16 columns of O, divides by
-//     (sum of the four partial sums + sink term) and stores fp16.
+//     usable keys (the four partial maxima meet in smem) and write
+//     P = 2^((s - max) log2 e) into TMEM (kColP..), two exponentials per
+//     fp16x2 SFU instruction; one item later each reads 16 columns of O and
+//     the row sum, divides by (row sum + sink term) and stores fp16;
+//   * the row sums come from the tensor core: beside each K step of P.V the
+//     MMA warp issues P times a 16-column block of ones (kColL..), so the
+//     normaliser is the sum of exactly the fp16 P that entered P.V.
 // Every wait is bounded; on a timeout the kernel records kDevErrWaitTimeout,
 // drains its copies and MMAs in flight and frees TMEM.
 #include "ts_common.cuh"
@@ -42,14 +45,18 @@ constexpr uint32_t kQBytes = 128u * 128u;           // 128 rows x 64 fp16
 constexpr uint32_t kKVBytes = kMaxBand * 128u;      // one K or V band
 constexpr uint32_t kStageBytes = kQBytes + 2u * kKVBytes;
 constexpr uint32_t kStages = 2;
-constexpr uint32_t kOffBar = kStages * kStageBytes;
+constexpr uint32_t kOffOnes = kStages * kStageBytes;  // 16 rows x 64 fp16 ones: the row-sum MMA's B operand
+constexpr uint32_t kOffBar = kOffOnes + 2048u;
 constexpr uint32_t kOffMeta = kOffBar + 128u;             // ItemMeta[kStages]
-constexpr uint32_t kOffRed = kOffMeta + 128u;             // float red_max[4][128], red_sum[2][4][128]
-constexpr uint32_t kSmemBytes = kOffRed + 12u * 128u * 4u + 1024u;  // + alignment slack
+constexpr uint32_t kOffRed = kOffMeta + 128u;             // float red_max[4][128]
+constexpr uint32_t kSmemBytes = kOffRed + 4u * 128u * 4u + 1024u;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColP = 288, kColO = 448;  // S: band cols, P: band/2, O: 64
+// S: band columns; P: band / 2 (fp16 pairs); O: 64; row sums: 16 (equal) columns
+constexpr uint32_t kColS = 0, kColP = 272, kColO = 416, kColL = 480;
 constexpr int kThreads = 640;  // producer, MMA, TMEM allocator, idle, 16 softmax warps
-static_assert(kColP >= kColS + kMaxBand && kColO >= kColP + kMaxBand / 2 && kColO + 64 <= kTmemCols, "TMEM map");
+static_assert(kColP >= kColS + kMaxBand && kColO >= kColP + kMaxBand / 2 && kColL >= kColO + 64 &&
+                  kColL + 16 <= kTmemCols, "TMEM map");
+static_assert(kOffOnes % 1024u == 0, "SW128 alignment");
 static_assert(kSmemBytes <= 227u * 1024u, "shared memory budget");
 static_assert(kStageBytes % 1024u == 0 && kQBytes % 1024u == 0 && kKVBytes % 1024u == 0, "SW128 alignment");
 
@@ -82,11 +89,11 @@ __device__ __forceinline__ void max32(const uint32_t (&v)[32], uint32_t rm, floa
   if (rm == 0u) return;
   if (rm == 0xffffffffu) {
 #pragma unroll
-    for (int b = 0; b < 32; b += 4) {
-      m0 = fmaxf(m0, __uint_as_float(v[b]));
-      m1 = fmaxf(m1, __uint_as_float(v[b + 1]));
-      m2 = fmaxf(m2, __uint_as_float(v[b + 2]));
-      m3 = fmaxf(m3, __uint_as_float(v[b + 3]));
+    for (int b = 0; b < 32; b += 8) {
+      m0 = fmax3(m0, __uint_as_float(v[b]), __uint_as_float(v[b + 1]));
+      m1 = fmax3(m1, __uint_as_float(v[b + 2]), __uint_as_float(v[b + 3]));
+      m2 = fmax3(m2, __uint_as_float(v[b + 4]), __uint_as_float(v[b + 5]));
+      m3 = fmax3(m3, __uint_as_float(v[b + 6]), __uint_as_float(v[b + 7]));
     }
   } else {
 #pragma unroll
@@ -97,36 +104,28 @@ __device__ __forceinline__ void max32(const uint32_t (&v)[32], uint32_t rm, floa
   }
 }
 
-// P = 2^(s log2 e - m log2 e) for N columns (0 where rm has no bit), packed
-// as fp16 pairs; adds the row sum into l0 + l1.
+// P = 2^(s log2 e - m log2 e) for N columns as fp16 pairs, 0 where rm has no
+// bit: one packed FMA, one conversion and one fp16x2 SFU exponential per pair.
+// nmb2 holds -m log2 e twice.
 template <int N>
-__device__ __forceinline__ void exp_pack(const uint32_t (&v)[N], uint32_t rm, float mb, float& l0, float& l1,
-                                         uint32_t (&pk)[N / 2]) {
-  constexpr float kL2E = 1.4426950408889634f;
+__device__ __forceinline__ void exp_pack(const uint32_t (&v)[N], uint32_t rm, uint64_t nmb2, uint32_t (&pk)[N / 2]) {
+  const uint64_t l2e2 = f2pack(1.4426950408889634f, 1.4426950408889634f);
   const uint32_t full = N == 32 ? 0xffffffffu : ((1u << N) - 1u);
   if (rm == 0u) {
 #pragma unroll
     for (int b = 0; b < N / 2; b++) pk[b] = 0u;
-  } else if (rm == full) {
+    return;
+  }
 #pragma unroll
-    for (int b = 0; b < N; b += 2) {
-      const float p0 = ex2_approx(fmaf(__uint_as_float(v[b]), kL2E, -mb));
-      const float p1 = ex2_approx(fmaf(__uint_as_float(v[b + 1]), kL2E, -mb));
-      l0 += p0;
-      l1 += p1;
-      pk[b >> 1] = pack_half2(p0, p1);
-    }
-  } else {
+  for (int b = 0; b < N; b += 2) {
+    float x0, x1;
+    f2unpack(fma_f32x2(f2pack(__uint_as_float(v[b]), __uint_as_float(v[b + 1])), l2e2, nmb2), x0, x1);
+    pk[b >> 1] = ex2_h2(f32x2_to_h2(x0, x1));
+  }
+  if (rm != full) {
 #pragma unroll
-    for (int b = 0; b < N; b += 2) {
-      float p0 = ex2_approx(fmaf(__uint_as_float(v[b]), kL2E, -mb));
-      float p1 = ex2_approx(fmaf(__uint_as_float(v[b + 1]), kL2E, -mb));
-      p0 = ((rm >> b) & 1u) ? p0 : 0.0f;
-      p1 = ((rm >> (b + 1)) & 1u) ? p1 : 0.0f;
-      l0 += p0;
-      l1 += p1;
-      pk[b >> 1] = pack_half2(p0, p1);
-    }
+    for (int b = 0; b < N; b += 2)
+      pk[b >> 1] &= (((rm >> b) & 1u) ? 0x0000ffffu : 0u) | (((rm >> (b + 1)) & 1u) ? 0xffff0000u : 0u);
   }
 }
 
@@ -162,7 +161,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 12) + 1;
   float* red_max = reinterpret_cast<float*>(smem + kOffRed);
-  float* red_sum = red_max + 512;
   ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + kOffMeta);
 
   const uint32_t group = a.Hq / a.Hkv;
@@ -187,6 +185,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s = i / (kQBytes / 16u), o = i % (kQBytes / 16u);
     *reinterpret_cast<uint4*>(smem + s * kStageBytes + o * 16u) = make_uint4(0u, 0u, 0u, 0u);
   }
+  // fp16 1.0 everywhere: any layout reads the block as ones
+  for (uint32_t i = threadIdx.x; i < 2048u / 16u; i += blockDim.x)
+    *reinterpret_cast<uint4*>(smem + kOffOnes + i * 16u) = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
   fence_proxy_async_smem();
   if (warp == 2) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -263,6 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t idesc1 = umma_idesc_f16_f32(128, n1);
     const uint32_t idesc2 = umma_idesc_f16_f32(128, n2 > 0u ? n2 : 16u);
     const uint32_t idesc_pv = umma_idesc_f16_f32(128, 64) | (1u << 16);  // B (V) is MN-major
+    const uint32_t idesc_l = umma_idesc_f16_f32(128, 16);                 // P x ones: row sums
+    const uint64_t ones_d = umma_desc_sw128(smem_u32(smem + kOffOnes));
     const uint32_t nks = band / 16u;
     const uint64_t qd0 = umma_desc_sw128(smem_u32(smem));
     const uint64_t kd0 = umma_desc_sw128(smem_u32(smem + kQBytes));
@@ -270,7 +273,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t kStageUnits = kStageBytes >> 4;
     auto issue_pv = [&](uint32_t s) {
       const uint64_t vd = vd0 + (uint64_t)(s * kStageUnits);
-      for (uint32_t j = 0; j < nks; j++) tc_mma_f16_ts(tmem + kColO, tmem + kColP + 8u * j, vd + 128u * j, idesc_pv, j > 0u);
+      for (uint32_t j = 0; j < nks; j++) {
+        tc_mma_f16_ts(tmem + kColO, tmem + kColP + 8u * j, vd + 128u * j, idesc_pv, j > 0u);
+        tc_mma_f16_ts(tmem + kColL, tmem + kColP + 8u * j, ones_d, idesc_l, j > 0u);
+      }
     };
     uint32_t lt = 0, prev_s = 0;
     bool ok = true;
@@ -386,14 +392,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!wait_or_abort(&pair_bar[quad], lt & 1u, a.err, abort_flag)) { ok = false; break; }
       const float m = fmaxf(fmaxf(red_max[r], red_max[128u + r]), fmaxf(red_max[256u + r], red_max[384u + r]));
       const float mb = m * kL2E;
+      const uint64_t nmb2 = f2pack(-mb, -mb);
 
-      // ---- pass 2: P = exp(s - max) as fp16 into TMEM, this half's row sum ----
-      // (P of the previous item must have been consumed by its P.V first)
+      // ---- pass 2: P = exp(s - max) as fp16 into TMEM ----
+      // (P of the previous item must have been consumed by its P.V first; that
+      // also completes the previous item's O and row sums)
       if (lt > 0) {
         if (!wait_or_abort(o_full, (lt - 1u) & 1u, a.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
       }
-      float l0 = 0.0f, l1 = 0.0f;
 #pragma unroll 1
       for (uint32_t j = 0; j < n32; j++) {
         const uint32_t c = col_begin + 32u * j;
@@ -402,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t rm = row_mask(c);
         tmem_ld_wait();
         uint32_t pk[16];
-        exp_pack<32>(v, rm, mb, l0, l1, pk);
+        exp_pack<32>(v, rm, nmb2, pk);
         tmem_st_32x32b_x16(trow + kColP + c / 2u, pk);
       }
       if (tail) {
@@ -411,23 +418,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t rm = row_mask(c_tail) & 0xffffu;
         tmem_ld_wait();
         uint32_t pk[8];
-        exp_pack<16>(v, rm, mb, l0, l1, pk);
+        exp_pack<16>(v, rm, nmb2, pk);
         tmem_st_32x32b_x8(trow + kColP + c_tail / 2u, pk);
       }
       tmem_st_wait();
-      red_sum[s * 512u + cq * 128u + r] = l0 + l1;
 
-      // ---- the previous item's O, this warp's 16 columns ----
+      // ---- the previous item's O (this warp's 16 columns) and row sum ----
       uint32_t o[16];
       float inv = 0.0f;
       if (lt > 0) {
+        uint32_t lsum;
         tmem_ld_32x32b_x16(trow + kColO + 16u * cq, o);
-        // p_full of the previous item has completed (its P.V ran), so every
-        // part's row sum for it is in red_sum
-        if (!wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag)) { ok = false; break; }
-        const float* ps = red_sum + (s ^ 1u) * 512u + r;
-        inv = __fdiv_rn(1.0f, ((ps[0] + ps[128]) + ps[256]) + ps[384] + prev_sink_term);
+        tmem_ld_32x32b_x1(trow + kColL, lsum);
         tmem_ld_wait();
+        inv = __fdiv_rn(1.0f, __uint_as_float(lsum) + prev_sink_term);
       }
       tc_fence_before();
       mbar_arrive(p_full);
@@ -437,14 +441,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       prev_out = a.out + (size_t)(row_ok ? t : 0) * out_ld + (size_t)(hk * group + (row_ok ? hl : 0u)) * 64u +
                  16u * cq;
     }
-    if (ok && lt > 0 && wait_or_abort(o_full, (lt - 1u) & 1u, a.err, abort_flag) &&
-        wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag)) {
+    if (ok && lt > 0 && wait_or_abort(o_full, (lt - 1u) & 1u, a.err, abort_flag)) {
       tc_fence_after();
-      uint32_t o[16];
+      uint32_t o[16], lsum;
       tmem_ld_32x32b_x16(trow + kColO + 16u * cq, o);
-      const float* ps = red_sum + ((lt - 1u) & 1u) * 512u + r;
-      const float inv = __fdiv_rn(1.0f, ((ps[0] + ps[128]) + ps[256]) + ps[384] + prev_sink_term);
+      tmem_ld_32x32b_x1(trow + kColL, lsum);
       tmem_ld_wait();
+      const float inv = __fdiv_rn(1.0f, __uint_as_float(lsum) + prev_sink_term);
       if (prev_ok) store_quarter_row(prev_out, o, inv);
     }
   }
