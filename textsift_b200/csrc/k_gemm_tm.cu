@@ -17,14 +17,18 @@
 // never touch shared memory.
 //
 // Persistent, warp-specialized: one CTA per SM walks (token tile, 128-wide
-// output tile) pairs, 20 warps:
-//   warp 0       producer: TMA box of x + bulk copy of the blob per chunk
+// output tile) pairs, 20 warps, over three rings with their own barriers
+// (activation tiles and weight blobs in smem, dequantised chunks in TMEM),
+// so a TMEM slot is handed back by its MMAs' commit, not by the next copy:
+//   warp 0       producer of the x tiles (TMA box per chunk)
+//   warp 3       producer of the packed weight blobs (bulk copy per chunk)
 //   warp 1       MMA issuer: 4 x tcgen05.mma (A from TMEM) per chunk, from
 //                one elected lane of a warp that runs the loop in lockstep
-//   warp 2       TMEM allocator: 2 accumulators x 192 columns + 4 A stages
+//   warp 2       TMEM allocator: 2 accumulators x 192 columns + 4 A slots
 //                x 32 columns = 512
 //   warps 4..11  dequantise: warp w owns TMEM lanes 32(w%4).. (output rows);
-//                warps 4..7 take the even chunks, 8..11 the odd ones
+//                warps 4..7 take the even chunks, 8..11 the odd ones; each
+//                reads its blob into registers and releases it at once
 //   warps 12..19 epilogue of the previous tile: warp w reads lanes 32(w%4)..
 //                (one output column per thread) for tokens 96((w-12)/4)..;
 //                lane pairs exchange values so each store is 32 bits
@@ -39,21 +43,26 @@
 namespace ts {
 
 namespace tm {
-constexpr int S = 4;                      // stages: smem (x tile + blob) and TMEM A
+// Three rings, each with its own full/empty barriers, so that the latency of
+// one (a copy from L2, a wake-up) is covered by the depth of the others:
+constexpr uint32_t SX = 4;                // activation tiles in smem (TMA)
+constexpr uint32_t SR = 4;                // packed weight blobs in smem (bulk copy)
+constexpr uint32_t SA = 4;                // dequantised weight chunks in TMEM (MMA A operand)
 constexpr uint32_t TOK = 192;             // tokens per tile = MMA N
 constexpr uint32_t X_BYTES = TOK * 128;   // 192 rows x 64 fp16
 constexpr uint32_t RAW_BYTES = 128 * 37;  // packed blob of a 128-row x 64-K chunk (w4_blob_bytes(128))
 constexpr uint32_t RAW_STRIDE = 5120;
-constexpr uint32_t OFF_RAW = S * X_BYTES;
-constexpr uint32_t OFF_BAR = OFF_RAW + S * RAW_STRIDE;
-constexpr uint32_t NUM_BARS = 3 * S + 4;
+constexpr uint32_t OFF_RAW = SX * X_BYTES;
+constexpr uint32_t OFF_BAR = OFF_RAW + SR * RAW_STRIDE;
+constexpr uint32_t NUM_BARS = 2 * SX + 2 * SR + 2 * SA + 4 + 1;
 constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_A = 2 * TOK;  // first A stage column, after the two accumulators
 constexpr int THREADS = 640;
 static_assert(X_BYTES % 1024 == 0, "swizzle atoms");
-static_assert(COL_A + S * 32 <= TMEM_COLS, "TMEM budget");
+static_assert(COL_A + SA * 32 <= TMEM_COLS, "TMEM budget");
+static_assert(SA % 2 == 0, "the two dequantising groups own alternate A slots");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 }  // namespace tm
 
@@ -178,11 +187,15 @@ __global__ void __launch_bounds__(640, 1)
   uint8_t* sX = smem;
   uint8_t* sR = smem + OFF_RAW;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + S;
-  uint64_t* aready = bars + 2 * S;
-  uint64_t* acc_full = bars + 3 * S;       // [2]
-  uint64_t* acc_empty = bars + 3 * S + 2;  // [2]
+  uint64_t* x_full = bars;                 // [SX] activation tile landed
+  uint64_t* x_empty = x_full + SX;         // [SX] its MMAs completed
+  uint64_t* r_full = x_empty + SX;         // [SR] weight blob landed
+  uint64_t* r_empty = r_full + SR;         // [SR] the dequantising group has read it
+  uint64_t* a_ready = r_empty + SR;        // [SA] dequantised chunk stored in TMEM
+  uint64_t* a_free = a_ready + SA;         // [SA] its MMAs completed
+  uint64_t* acc_full = a_free + SA;        // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint64_t* drain = acc_empty + 2;         // every MMA issued has completed (teardown)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
 
@@ -192,15 +205,23 @@ __global__ void __launch_bounds__(640, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-      mbar_init(&aready[s], 128);
+    for (uint32_t i = 0; i < SX; i++) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (uint32_t i = 0; i < SR; i++) {
+      mbar_init(&r_full[i], 1);
+      mbar_init(&r_empty[i], 128);
+    }
+    for (uint32_t i = 0; i < SA; i++) {
+      mbar_init(&a_ready[i], 128);
+      mbar_init(&a_free[i], 1);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 32u * kEpiWarps);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     mbar_fence_init();
     fence_proxy_async_smem();
@@ -215,28 +236,40 @@ __global__ void __launch_bounds__(640, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t n_kc = args.n_kc;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 3) {
+    // ---- producers, one lane each: warp 0 the activation tiles (TMA box),
+    // warp 3 the weight blobs (bulk copy); each runs as far ahead as its ring
+    // allows.  After an abort each waits (bounded) for its copies in flight.
     if (lane == 0) {
+      const bool is_x = warp == 0;
+      const uint32_t R = is_x ? SX : SR;
+      uint64_t* fullb = is_x ? x_full : r_full;
+      uint64_t* emptyb = is_x ? x_empty : r_empty;
       uint32_t it = 0;
       bool ok = true;
       for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const TmTile ti = tm_tile(args, tile, n_ntiles);
         const uint8_t* wb = args.wblob + (size_t)ti.expert * args.expert_stride + (size_t)ti.n_tile * n_kc * RAW_BYTES;
         for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1u;
-          if (!wait_or_abort(&empty[s], ph ^ 1u, args.err, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], X_BYTES + RAW_BYTES);
-          tma_load_2d(sX + s * X_BYTES, &tmap_x, (int32_t)(kc * kChunkK), (int32_t)ti.row0, &full[s]);
-          bulk_g2s(sR + s * RAW_STRIDE, wb + (size_t)kc * RAW_BYTES, RAW_BYTES, &full[s]);
+          const uint32_t s = it % R, u = it / R;
+          if (!wait_or_abort(&emptyb[s], (u & 1u) ^ 1u, args.err, abort_flag)) { ok = false; break; }
+          if (is_x) {
+            mbar_arrive_expect_tx(&fullb[s], X_BYTES);
+            tma_load_2d(sX + s * X_BYTES, &tmap_x, (int32_t)(kc * kChunkK), (int32_t)ti.row0, &fullb[s]);
+          } else {
+            mbar_arrive_expect_tx(&fullb[s], RAW_BYTES);
+            bulk_g2s(sR + s * RAW_STRIDE, wb + (size_t)kc * RAW_BYTES, RAW_BYTES, &fullb[s]);
+          }
         }
       }
+      if (!ok)
+        for (uint32_t j = it > R ? it - R : 0u; j < it; j++) mbar_wait(&fullb[j % R], (j / R) & 1u, args.err);
     }
   } else if (warp == 1) {
     // The whole warp runs the loop (warp-uniform state, cheap to issue next to
     // the busy dequantising/epilogue warps of this scheduler); one elected
-    // lane issues the MMAs and commits.  Descriptors: stage s's x tile starts
-    // s * X_BYTES / 16 descriptor units after stage 0's, K step k 2 units.
+    // lane issues the MMAs and commits.  Descriptors: x slot s starts
+    // s * X_BYTES / 16 descriptor units after slot 0's, K step k 2 units.
     constexpr uint32_t idesc = umma_idesc_f16_f32(128, TOK);
     const uint64_t xdesc0 = umma_desc_sw128(smem_u32(sX));
     uint32_t it = 0, lt = 0;
@@ -248,29 +281,34 @@ __global__ void __launch_bounds__(640, 1)
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + b * TOK;
       for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1u;
-        ok = __all_sync(0xffffffffu, wait_or_abort(&full[s], ph, args.err, abort_flag) &&
-                                         wait_or_abort(&aready[s], ph, args.err, abort_flag));
+        const uint32_t sx = it % SX, sa = it % SA;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&x_full[sx], (it / SX) & 1u, args.err, abort_flag) &&
+                                         wait_or_abort(&a_ready[sa], (it / SA) & 1u, args.err, abort_flag));
         if (!ok) break;
         tc_fence_after();
         if (elect_one()) {
-          const uint64_t xd = xdesc0 + (uint64_t)((uint32_t)s * (X_BYTES >> 4));
-          const uint32_t a_tmem = tmem_base + COL_A + (uint32_t)s * 32u;
+          const uint64_t xd = xdesc0 + (uint64_t)(sx * (X_BYTES >> 4));
+          const uint32_t a_tmem = tmem_base + COL_A + sa * 32u;
 #pragma unroll
           for (int k = 0; k < 4; k++)
             tc_mma_f16_ts(d_tmem, a_tmem + 8u * k, xd + 2u * k, idesc, (kc | (uint32_t)k) != 0u);
-          tc_commit(&empty[s]);
+          tc_commit(&x_empty[sx]);
+          tc_commit(&a_free[sa]);
         }
         __syncwarp();
       }
       if (ok && elect_one()) tc_commit(&acc_full[b]);
       __syncwarp();
     }
+    // every MMA issued above has completed before TMEM is freed
+    if (elect_one()) tc_commit(drain);
+    __syncwarp();
+    if (lane == 0) mbar_wait(drain, 0, args.err);
   } else if (warp >= 4 && warp < 4 + kDqWarps) {
     // ---- dequantise; thread = one output row, both K halves.  With 8 warps,
-    // 4..7 take the even chunks and 8..11 the odd ones (two chunks in flight);
-    // with 4 warps each takes every chunk. ----
+    // 4..7 take the even chunks and 8..11 the odd ones (two chunks in flight;
+    // each group owns alternate A slots); with 4 warps each takes every chunk.
+    // The blob is read into registers and released before the A slot's wait. ----
     const uint32_t q = (uint32_t)(warp & 3), grp = (uint32_t)(warp - 4) >> 2;
     const uint32_t r = q * 32u + (uint32_t)lane;
     const uint32_t tcol = tmem_base + ((q * 32u) << 16) + COL_A;
@@ -279,17 +317,14 @@ __global__ void __launch_bounds__(640, 1)
     for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
       for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
         if (kDqWarps == 8 && (it & 1u) != grp) continue;
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1u;
-        // full[s] of this use follows the MMAs of the stage's previous use
-        // (the producer waited for their commit), so its TMEM A stage is free
-        if (!wait_or_abort(&full[s], ph, args.err, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint8_t* raw = sR + s * RAW_STRIDE;
+        const uint32_t sr = it % SR, sa = it % SA;
+        if (!wait_or_abort(&r_full[sr], (it / SR) & 1u, args.err, abort_flag)) { ok = false; break; }
+        const uint8_t* raw = sR + sr * RAW_STRIDE;
         const uint4 h0 = *reinterpret_cast<const uint4*>(raw + r * 16u);
         const uint4 h1 = *reinterpret_cast<const uint4*>(raw + 128u * 16u + r * 16u);
         const uint32_t sc2 = *reinterpret_cast<const uint32_t*>(raw + 128u * 32u + r * 4u);
         const uint32_t zb = raw[128u * 36u + r];
+        mbar_arrive(&r_empty[sr]);  // release: the loads above are ordered before it
         uint32_t o[32];
 #pragma unroll
         for (int hf = 0; hf < 2; hf++) {
@@ -309,10 +344,13 @@ __global__ void __launch_bounds__(640, 1)
             }
           }
         }
-        tmem_st_32x32b_x32(tcol + (uint32_t)s * 32u, o);
+        // the A slot's previous chunk has been consumed by its MMAs
+        if (!wait_or_abort(&a_free[sa], ((it / SA) & 1u) ^ 1u, args.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        tmem_st_32x32b_x32(tcol + sa * 32u, o);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&aready[s]);
+        mbar_arrive(&a_ready[sa]);
       }
     }
   } else if (warp >= 4 + kDqWarps) {
