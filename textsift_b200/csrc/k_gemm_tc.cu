@@ -162,7 +162,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
 // router_topk_kernel (wasm_exports.zig:367-426 + 919-958, block.ts:201-206):
 // the top 4 logits in descending order, equal logits in ascending expert
 // order, softmax over them with the exact exponential, each weight scaled by
-// 1/4.  Expert counts go to hist[row / 128] (the permutation's chunks).
+// 1/4.  Expert counts go to hist[row / kPermChunk] (the permutation's chunks).
 __device__ __forceinline__ void router_topk_epilogue(const GemmArgs& a, uint32_t acc, uint32_t grow, bool row_ok,
                                                      const float* sbias, uint64_t* acc_empty) {
   float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f, t3 = 0.0f;
@@ -204,7 +204,7 @@ __device__ __forceinline__ void router_topk_epilogue(const GemmArgs& a, uint32_t
   reinterpret_cast<float4*>(a.out1)[grow] =
       make_float4((float)((double)__fmul_rn(e0, inv) * inv_k), (float)((double)__fmul_rn(e1, inv) * inv_k),
                   (float)((double)__fmul_rn(e2, inv) * inv_k), (float)((double)__fmul_rn(e3, inv) * inv_k));
-  int* h = a.hist + (size_t)(grow >> 7) * a.N;
+  int* h = a.hist + (size_t)(grow / kPermChunk) * a.N;
   atomicAdd(h + i0, 1);
   atomicAdd(h + i1, 1);
   atomicAdd(h + i2, 1);

@@ -308,10 +308,11 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
 // and order the reference's strict-'>' insertion sort produces -- then softmax
 // over the k values in that order and x (1/k) in double like the JS caller.
 // One warp per token (lane l holds logits l, l+32, ...), 128 tokens per block;
-// each block also counts its routes per expert (hist[block][e]) for the
-// permutation.
+// each block also adds its routes per expert into the permutation chunk's
+// row hist[token / kPermChunk][e].
 // ---------------------------------------------------------------------------
-constexpr uint32_t kRouteChunk = 128;  // tokens per top-k block / permutation chunk
+constexpr uint32_t kRouteChunk = 128;  // tokens per top-k block
+static_assert(kPermChunk % kRouteChunk == 0 && kPermChunk == 1024, "permutation chunk = 32 words of 32 tokens");
 constexpr uint32_t kMaxExperts = 256;
 
 // One warp per token: K rounds of a warp arg-max (value desc, index asc: the
@@ -389,44 +390,25 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     }
   }
   __syncthreads();
-  if (hist)
-    for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) hist[(size_t)blockIdx.x * E + i] = h[i];
+  if (hist) {
+    int* row = hist + (size_t)(blockIdx.x / (kPermChunk / kRouteChunk)) * E;
+    for (uint32_t i = threadIdx.x; i < E; i += blockDim.x)
+      if (h[i]) atomicAdd(row + i, h[i]);
+  }
 }
 
 // ---------------------------------------------------------------------------
 // MoE permutation, stable (ascending token within each expert, the order
-// expert.ts:137-145 builds).  scan: one block; thread e walks the chunk
-// histograms to give each (chunk, expert) its base position, then the expert
-// segments, their 128-row GEMM tiles and the tile count.  place: one block per
-// chunk; a route's rank inside its chunk is the number of earlier tokens of
-// the chunk that chose the same expert (a 128-bit token mask per expert).
+// expert.ts:137-145 builds), over chunks of kPermChunk tokens whose expert
+// counts the router's top-k left in hist[chunk][e].  scan: one block turns
+// hist into each (chunk, expert)'s base position inside the expert's segment,
+// then the expert segments, their GEMM tiles and the tile counts.  place: one
+// block per chunk; a route's rank inside its chunk is the number of earlier
+// tokens of the chunk that chose the same expert (a 1024-bit token mask per
+// expert with per-word prefix counts).
 // ---------------------------------------------------------------------------
-// Exclusive scan of hist[c][e] over chunks c, one warp per expert; total[e].
-__global__ void __launch_bounds__(256) moe_chunk_scan_kernel(int* __restrict__ hist, uint32_t n_chunks, uint32_t E,
-                                                             int* __restrict__ counts) {
-  pdl_trigger();
-  pdl_wait();
-  const uint32_t e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (e >= E) return;
-  int run = 0;
-  for (uint32_t c0 = 0; c0 < n_chunks; c0 += 32) {
-    const uint32_t c = c0 + lane;
-    const int v = c < n_chunks ? hist[(size_t)c * E + e] : 0;
-    int incl = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    if (c < n_chunks) hist[(size_t)c * E + e] = run + incl - v;
-    run += __shfl_sync(0xffffffffu, incl, 31);
-  }
-  if (lane == 0) counts[e] = run;
-}
-
-// Exclusive prefix sum of one int per thread over a block of up to
-// kMaxExperts threads (warp shuffles, then the warp totals).
+// Exclusive prefix sum of one int per thread over the block (warp shuffles,
+// then the warp totals in warp_tot[blockDim.x / 32]).
 __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int incl = v;
@@ -443,24 +425,51 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
   return base + incl - v;
 }
 
-// Expert segments, their 128-row GEMM tiles (exact path) and rows_tc-row
-// GEMM tiles (tensor-core path), and both tile counts, from counts.
-__global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __restrict__ counts, uint32_t E,
-                                                                   int4* __restrict__ tiles, int* __restrict__ n_tiles,
-                                                                   int4* __restrict__ tiles_tc,
-                                                                   int* __restrict__ n_tiles_tc, int rows_tc,
-                                                                   int* __restrict__ seg_start,
-                                                                   int* __restrict__ seg_end) {
+// One block of 1024 threads: G = 1024 / E threads per expert each sum a run
+// of chunks, then rewrite hist[c][e] as the exclusive prefix over chunks; the
+// expert totals (counts) give the segments, the 128-row GEMM tiles (exact
+// path), the rows_tc-row tiles (tensor-core path) and both tile counts.
+__global__ void __launch_bounds__(1024) moe_scan_segments_kernel(int* __restrict__ hist, uint32_t n_chunks, uint32_t E,
+                                                                 int* __restrict__ counts, int4* __restrict__ tiles,
+                                                                 int* __restrict__ n_tiles, int4* __restrict__ tiles_tc,
+                                                                 int* __restrict__ n_tiles_tc, int rows_tc,
+                                                                 int* __restrict__ seg_start,
+                                                                 int* __restrict__ seg_end) {
   pdl_trigger();
   pdl_wait();
-  __shared__ int wt[kMaxExperts / 32];
-  const uint32_t e = threadIdx.x;
-  const int cnt = e < E ? counts[e] : 0;
+  __shared__ int part[1024];
+  __shared__ int wt[32];
+  const uint32_t G = 1024u / E, tid = threadIdx.x;
+  const uint32_t e = tid % E, g = tid / E;
+  const bool act = g < G;
+  const uint32_t L = (n_chunks + G - 1) / G;
+  const uint32_t c0 = min(n_chunks, g * L), c1 = min(n_chunks, c0 + L);
+  int s = 0;
+  if (act)
+    for (uint32_t c = c0; c < c1; c++) s += hist[(size_t)c * E + e];
+  part[tid] = s;
+  __syncthreads();
+  int run = 0, total = 0;
+  if (act) {
+    for (uint32_t gg = 0; gg < G; gg++) {
+      const int v = part[gg * E + e];
+      if (gg < g) run += v;
+      total += v;
+    }
+    for (uint32_t c = c0; c < c1; c++) {
+      const int v = hist[(size_t)c * E + e];
+      hist[(size_t)c * E + e] = run;
+      run += v;
+    }
+  }
+  // expert e's total sits with thread e (g == 0)
+  const int cnt = tid < E ? total : 0;
+  if (tid < E) counts[e] = cnt;
   const int t1 = (cnt + 127) / 128, t2 = (cnt + rows_tc - 1) / rows_tc;
   const int base = block_exclusive_scan(cnt, wt);
   const int tb1 = block_exclusive_scan(t1, wt);
   const int tb2 = block_exclusive_scan(t2, wt);
-  if (e < E) {
+  if (tid < E) {
     seg_start[e] = base;
     seg_end[e] = base + cnt;
     for (int tt = 0; tt < t1; tt++)
@@ -469,22 +478,25 @@ __global__ void __launch_bounds__(kMaxExperts) moe_segments_kernel(const int* __
       for (int tt = 0; tt < t2; tt++)
         tiles_tc[tb2 + tt] = make_int4((int)e, base + tt * rows_tc, base + min(cnt, (tt + 1) * rows_tc), base);
   }
-  if (e == E - 1) {
+  if (tid == E - 1) {
     *n_tiles = tb1 + t1;
     if (n_tiles_tc) *n_tiles_tc = tb2 + t2;
   }
 }
 
-__global__ void __launch_bounds__(kRouteChunk) moe_place_kernel(const int32_t* __restrict__ idx,
-                                                                int* __restrict__ hist,
-                                                                const int* __restrict__ seg_start, uint32_t T,
-                                                                uint32_t K, uint32_t E, int* __restrict__ perm_tok,
-                                                                int* __restrict__ route_pos) {
-  __shared__ uint32_t mask[kMaxExperts][kRouteChunk / 32];
+__global__ void __launch_bounds__(kPermChunk) moe_place_kernel(const int32_t* __restrict__ idx,
+                                                               int* __restrict__ hist,
+                                                               const int* __restrict__ seg_start, uint32_t T,
+                                                               uint32_t K, uint32_t E, int* __restrict__ perm_tok,
+                                                               int* __restrict__ route_pos) {
+  constexpr uint32_t kWords = kPermChunk / 32;
+  __shared__ uint32_t mask[kMaxExperts][kWords];  // bit b of word w: token 32 w + b chose the expert
+  __shared__ uint16_t pref[kMaxExperts][kWords];  // the expert's tokens in words < w
   pdl_trigger();
   pdl_wait();
-  const uint32_t tl = threadIdx.x, t = blockIdx.x * kRouteChunk + tl;
-  for (uint32_t i = threadIdx.x; i < E * (kRouteChunk / 32); i += blockDim.x) mask[i / 4][i % 4] = 0;
+  const uint32_t tl = threadIdx.x, t = blockIdx.x * kPermChunk + tl;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (uint32_t i = threadIdx.x; i < E * kWords; i += blockDim.x) mask[i / kWords][i % kWords] = 0;
   __syncthreads();
   int ek[8];
   const bool ok = t < T;
@@ -493,17 +505,28 @@ __global__ void __launch_bounds__(kRouteChunk) moe_place_kernel(const int32_t* _
     if (ek[k] >= 0 && (uint32_t)ek[k] < E) atomicOr(&mask[ek[k]][tl >> 5], 1u << (tl & 31));
   }
   __syncthreads();
+  // per expert, one warp scans the popcounts of its 32 words (lane = word)
+  for (uint32_t x = (uint32_t)warp; x < E; x += blockDim.x >> 5) {
+    const int c = __popc(mask[x][lane]);
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    pref[x][lane] = (uint16_t)(incl - c);
+  }
+  __syncthreads();
   for (uint32_t k = 0; k < K && ok; k++) {
     const int e = ek[k];
     if (e < 0 || (uint32_t)e >= E) { route_pos[(size_t)t * K + k] = -1; continue; }
-    int rank = __popc(mask[e][tl >> 5] & ((1u << (tl & 31)) - 1u));
-    for (uint32_t wdx = 0; wdx < (tl >> 5); wdx++) rank += __popc(mask[e][wdx]);
+    const int rank = (int)pref[e][tl >> 5] + __popc(mask[e][tl >> 5] & ((1u << (tl & 31)) - 1u));
     const int p = seg_start[e] + hist[(size_t)blockIdx.x * E + e] + rank;
     perm_tok[p] = (int)t;
     route_pos[(size_t)t * K + k] = p;
   }
-  // this chunk's row is consumed: leave it zero for the next fused top-k,
-  // which accumulates expert counts into it
+  // this chunk's row is consumed: leave it zero for the next top-k, which
+  // accumulates expert counts into it
   __syncthreads();
   for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) hist[(size_t)blockIdx.x * E + i] = 0;
 }
@@ -921,17 +944,17 @@ cudaError_t launch_matmul_exact(const ExactArgs& a_in, bool x_f32, int out_mode,
   return cudaGetLastError();
 }
 
-uint32_t route_chunks(uint32_t T) { return (T + kRouteChunk - 1) / kRouteChunk; }
+uint32_t route_chunks(uint32_t T) { return (T + kPermChunk - 1) / kPermChunk; }
 
 cudaError_t launch_router_topk(const float* logits, int32_t* idx, float* w, int* hist, uint32_t T, uint32_t E,
                                uint32_t K, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (K > 8 || K > E || E > kMaxExperts) return cudaErrorInvalidValue;
+  const uint32_t blocks = (T + kRouteChunk - 1) / kRouteChunk;
   if (E <= 128)
-    router_topk_kernel<4><<<route_chunks(T), 256, 0, st>>>(logits, idx, w, hist, T, E, K, 1.0 / (double)K);
+    router_topk_kernel<4><<<blocks, 256, 0, st>>>(logits, idx, w, hist, T, E, K, 1.0 / (double)K);
   else
-    router_topk_kernel<kMaxExperts / 32><<<route_chunks(T), 256, 0, st>>>(logits, idx, w, hist, T, E, K,
-                                                                           1.0 / (double)K);
+    router_topk_kernel<kMaxExperts / 32><<<blocks, 256, 0, st>>>(logits, idx, w, hist, T, E, K, 1.0 / (double)K);
   return cudaGetLastError();
 }
 
@@ -939,13 +962,12 @@ cudaError_t launch_moe_permute(const int32_t* idx, int* hist, uint32_t T, uint32
                                int* perm_tok, int* route_pos, int4* tiles, int* n_tiles, int4* tiles_tc,
                                int* n_tiles_tc, uint32_t rows_tc, int* seg_start, int* seg_end, cudaStream_t st) {
   if (E > kMaxExperts || K > 8 || (tiles_tc && rows_tc == 0)) return cudaErrorInvalidValue;
+  if (T == 0 || E == 0) return cudaSuccess;
   const uint32_t nc = route_chunks(T);
-  cudaError_t e = launch_pdl(moe_chunk_scan_kernel, dim3((E + 7) / 8), dim3(256), 0, st, hist, nc, E, counts);
+  cudaError_t e = launch_pdl(moe_scan_segments_kernel, dim3(1), dim3(1024), 0, st, hist, nc, E, counts, tiles, n_tiles,
+                             tiles_tc, n_tiles_tc, (int)rows_tc, seg_start, seg_end);
   if (e != cudaSuccess) return e;
-  e = launch_pdl(moe_segments_kernel, dim3(1), dim3(kMaxExperts), 0, st, counts, E, tiles, n_tiles, tiles_tc, n_tiles_tc,
-                 (int)rows_tc, seg_start, seg_end);
-  if (e != cudaSuccess) return e;
-  return launch_pdl(moe_place_kernel, dim3(nc), dim3(kRouteChunk), 0, st, idx, hist, seg_start, T, K, E, perm_tok,
+  return launch_pdl(moe_place_kernel, dim3(nc), dim3(kPermChunk), 0, st, idx, hist, seg_start, T, K, E, perm_tok,
                     route_pos);
 }
 

@@ -444,8 +444,8 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
   ts::ExactArgs ra = L.router.exact();
   ra.x = n32; ra.ldx = D; ra.M = T; ra.rloc = rloc; ra.rlen = rlen; ra.out = w.rlogits.p; ra.ldo = E;
   {
-    // kernels: logits GEMM (+ top-k kernel unless fused) + 3 permutation kernels
-    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, (!exact && K == 4 && E <= 128) ? 4 : 5);
+    // kernels: logits GEMM (+ top-k kernel unless fused) + 2 permutation kernels
+    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, (!exact && K == 4 && E <= 128) ? 3 : 4);
     if (exact) {
       TS_K(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
     } else {
@@ -1215,10 +1215,9 @@ int ts_cuda_op_moe(ts_cuda_t* h, uint32_t layer, const float* d_x, uint16_t* d_o
   int rc = ensure_workspace(h, exact);
   if (rc) return rc;
   const ts_cuda_cfg& c = h->cfg;
-  if (!exact) {
-    TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, h->ws.xn16.p, (size_t)T * c.d_model, st));
-    TS_CUDA_TRY(cudaMemsetAsync(h->ws.hist.p, 0, (size_t)ts::route_chunks(T) * c.n_experts * sizeof(int), st));
-  }
+  if (!exact) TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, h->ws.xn16.p, (size_t)T * c.d_model, st));
+  // both top-k paths add expert counts into zeroed permutation rows
+  TS_CUDA_TRY(cudaMemsetAsync(h->ws.hist.p, 0, (size_t)ts::route_chunks(T) * c.n_experts * sizeof(int), st));
   rc = moe_half(h, *h->layers[layer], d_x, h->ws.xn16.p, nullptr, d_out, T, nullptr, nullptr, exact, st, -1);
   if (rc) return rc;
   if (d_idx) TS_CUDA_TRY(cudaMemcpyAsync(d_idx, h->ws.ridx.p, (size_t)T * c.top_k * 4, cudaMemcpyDeviceToDevice, st));

@@ -27,6 +27,9 @@ namespace ts {
 // Padding rows/columns carry nibble 8, zero point 8 and scale 0.
 // ----------------------------------------------------------------------------
 constexpr uint32_t kChunkK = 64;
+// Tokens per MoE permutation chunk: the router's top-k adds each token's
+// expert counts into hist[token / kPermChunk][expert].
+constexpr uint32_t kPermChunk = 1024;
 __host__ __device__ constexpr uint32_t w4_blob_bytes(uint32_t bn) { return bn * 37u; }
 
 struct W4Tiles {
