@@ -153,13 +153,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* full = bars;       // [2] Q/K/V of a stage landed
   uint64_t* empty = bars + 2;  // [2] the stage's last MMA finished
-  uint64_t* s_full = bars + 4;
-  uint64_t* p_full = bars + 5;
-  uint64_t* o_full = bars + 6;
+  uint64_t* s_full = bars + 4;  // S of the item is in TMEM
+  uint64_t* s_free = bars + 5;  // the softmax has read S and written P
+  uint64_t* o_full = bars + 6;  // P.V (and the row sums) of the item completed
   uint64_t* drain = bars + 7;
   uint64_t* pair_bar = bars + 8;  // [4] the four softmax warps of a lane quarter exchanged row maxima
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 12) + 1;
+  uint64_t* o_read = bars + 12;   // the softmax has read O and the row sums of the item
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13) + 1;
   float* red_max = reinterpret_cast<float*>(smem + kOffRed);
   ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + kOffMeta);
 
@@ -173,7 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 512);
+    mbar_init(s_free, 512);
+    mbar_init(o_read, 512);
     for (int q = 0; q < 4; q++) mbar_init(&pair_bar[q], 128);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
@@ -278,6 +280,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_mma_f16_ts(tmem + kColL, tmem + kColP + 8u * j, ones_d, idesc_l, j > 0u);
       }
     };
+    // P.V of item j overwrites O: it waits until the softmax has read O of
+    // item j - 1 (o_read phase j - 1), which it does after releasing S.
+    auto pv_of = [&](uint32_t j, uint32_t sj) -> bool {
+      if (j >= 1u && !__all_sync(0xffffffffu, wait_or_abort(o_read, (j - 1u) & 1u, a.err, abort_flag))) return false;
+      tc_fence_after();
+      if (elect_one()) {
+        issue_pv(sj);
+        tc_commit(o_full);
+        tc_commit(&empty[sj]);
+      }
+      __syncwarp();
+      return true;
+    };
     uint32_t lt = 0, prev_s = 0;
     bool ok = true;
     for (uint32_t item = blockIdx.x; item < items; item += gridDim.x, lt++) {
@@ -285,12 +300,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the stage has landed, and the softmax of the previous item is done
       // with S (and has written P)
       ok = __all_sync(0xffffffffu, wait_or_abort(&full[s], (lt >> 1) & 1u, a.err, abort_flag) &&
-                                       (lt == 0 || wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag)));
+                                       (lt == 0 || wait_or_abort(s_free, (lt - 1u) & 1u, a.err, abort_flag)));
       if (!ok) break;
       tc_fence_after();
       if (elect_one()) {
-        // S of this item first, so its softmax starts while P.V of the
-        // previous item runs behind it on the tensor core
+        // S of this item first: its softmax starts while the softmax warps
+        // finish the previous item's output and P.V runs behind it
         const uint64_t qd = qd0 + (uint64_t)(s * kStageUnits), kd = kd0 + (uint64_t)(s * kStageUnits);
 #pragma unroll
         for (uint32_t k = 0; k < 4; k++) tc_mma_f16(tmem + kColS, qd + 2u * k, kd + 2u * k, idesc1, k > 0u);
@@ -300,24 +315,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_mma_f16(tmem + kColS + n1, qd + 2u * k, kd + n1 * 8u + 2u * k, idesc2, k > 0u);
         }
         tc_commit(s_full);
-        if (lt > 0) {
-          issue_pv(prev_s);
-          tc_commit(o_full);
-          tc_commit(&empty[prev_s]);
-        }
       }
       __syncwarp();
+      if (lt > 0 && !(ok = pv_of(lt - 1u, prev_s))) break;
       prev_s = s;
     }
-    if (ok && lt > 0 && __all_sync(0xffffffffu, wait_or_abort(p_full, (lt - 1u) & 1u, a.err, abort_flag))) {
-      tc_fence_after();
-      if (elect_one()) {
-        issue_pv(prev_s);
-        tc_commit(o_full);
-        tc_commit(&empty[prev_s]);
-      }
-      __syncwarp();
-    }
+    if (ok && lt > 0 && __all_sync(0xffffffffu, wait_or_abort(s_free, (lt - 1u) & 1u, a.err, abort_flag)))
+      pv_of(lt - 1u, prev_s);
     // every MMA issued above has completed before TMEM is freed
     if (elect_one()) tc_commit(drain);
     __syncwarp();
@@ -422,20 +426,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_32x32b_x8(trow + kColP + c_tail / 2u, pk);
       }
       tmem_st_wait();
+      // S is read and P written: the next item's S may go ahead
+      tc_fence_before();
+      mbar_arrive(s_free);
 
       // ---- the previous item's O (this warp's 16 columns) and row sum ----
-      uint32_t o[16];
-      float inv = 0.0f;
       if (lt > 0) {
-        uint32_t lsum;
+        uint32_t o[16], lsum;
         tmem_ld_32x32b_x16(trow + kColO + 16u * cq, o);
         tmem_ld_32x32b_x1(trow + kColL, lsum);
         tmem_ld_wait();
-        inv = __fdiv_rn(1.0f, __uint_as_float(lsum) + prev_sink_term);
+        tc_fence_before();
+        mbar_arrive(o_read);
+        if (prev_ok) store_quarter_row(prev_out, o, __fdiv_rn(1.0f, __uint_as_float(lsum) + prev_sink_term));
       }
-      tc_fence_before();
-      mbar_arrive(p_full);
-      if (lt > 0 && prev_ok) store_quarter_row(prev_out, o, inv);
       prev_ok = row_ok;
       prev_sink_term = ex2_approx(fmaf(sink, kL2E, -mb));
       prev_out = a.out + (size_t)(row_ok ? t : 0) * out_ld + (size_t)(hk * group + (row_ok ? hl : 0u)) * 64u +
