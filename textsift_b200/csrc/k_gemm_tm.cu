@@ -17,7 +17,7 @@
 // never touch shared memory.
 //
 // Persistent, warp-specialized: one CTA per SM walks (token tile, 128-wide
-// output tile) pairs, 20 warps, over three rings with their own barriers
+// output tile) pairs, 24 warps (20 for QKV), over three rings with their own barriers
 // (activation tiles and weight blobs in smem, dequantised chunks in TMEM),
 // so a TMEM slot is handed back by its MMAs' commit, not by the next copy:
 //   warp 0       producer of the x tiles (TMA box per chunk)
@@ -29,8 +29,8 @@
 //   warps 4..11  dequantise: warp w owns TMEM lanes 32(w%4).. (output rows);
 //                warps 4..7 take the even chunks, 8..11 the odd ones; each
 //                reads its blob into registers and releases it at once
-//   warps 12..19 epilogue of the previous tile: warp w reads lanes 32(w%4)..
-//                (one output column per thread) for tokens 96((w-12)/4)..;
+//   warps 12..23 epilogue of the previous tile: warp w reads lanes 32(w%4)..
+//                (one output column per thread) for tokens 64((w-12)/4)..;
 //                lane pairs exchange values so each store is 32 bits
 // With the RoPE epilogue (QKV) warps 4..7 dequantise every chunk and warps
 // 8..19 run the epilogue, 64 tokens each.
@@ -59,7 +59,15 @@ constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_A = 2 * TOK;  // first A stage column, after the two accumulators
-constexpr int THREADS = 640;
+// Role warps per epilogue kind: dequantising and epilogue warps (multiples
+// of 4, one per TMEM lane quarter); 4 more warps run the producers, the MMA
+// issue and the TMEM allocation.  Every kind has 12 epilogue warps (three
+// per scheduler: 64 tokens each); the RoPE epilogue's GEMM (QKV, K = 640
+// chunks of one weight tile) is fed by 4 dequantising warps, the others by 8
+// in two groups (20 or 24 warps, at most 80 registers a thread).
+__host__ __device__ constexpr uint32_t dq_warps(int epi) { return epi == kEpiQkvRope ? 4u : 8u; }
+__host__ __device__ constexpr uint32_t epi_warps(int) { return 12u; }
+__host__ __device__ constexpr uint32_t threads(int epi) { return 32u * (4u + dq_warps(epi) + epi_warps(epi)); }
 static_assert(X_BYTES % 1024 == 0, "swizzle atoms");
 static_assert(COL_A + SA * 32 <= TMEM_COLS, "TMEM budget");
 static_assert(SA % 2 == 0, "the two dequantising groups own alternate A slots");
@@ -170,13 +178,11 @@ __device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTil
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(640, 1)
+__global__ void __launch_bounds__(tm::threads(EPI), 1)
     gemm_w4_tm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args, uint32_t n_ntiles) {
   using namespace tm;
-  // the 16 role warps: the RoPE epilogue (loads of the rotation table) gets
-  // 12 warps and dequantisation 4; the other epilogues 8 and 8
-  constexpr uint32_t kDqWarps = EPI == kEpiQkvRope ? 4 : 8;
-  constexpr uint32_t kEpiWarps = 16 - kDqWarps;
+  constexpr uint32_t kDqWarps = dq_warps(EPI);
+  constexpr uint32_t kEpiWarps = epi_warps(EPI);
   constexpr uint32_t kPartTok = TOK / (kEpiWarps / 4);  // tokens per epilogue warp
   static_assert(kPartTok % 32 == 0, "32-token slices");
   extern __shared__ uint8_t smem_dyn[];
@@ -400,7 +406,7 @@ static cudaError_t launch_tm(const CUtensorMap& tmap, const GemmArgs& args, uint
   }
   const uint64_t max_tiles = (uint64_t)grid_m * n_tiles;
   const uint32_t grid = (uint32_t)std::min<uint64_t>(max_tiles, (uint64_t)num_sms());
-  return launch_pdl(gemm_w4_tm_kernel<EPI>, dim3(grid), dim3(tm::THREADS), tm::SMEM_BYTES, st, tmap, args, n_tiles);
+  return launch_pdl(gemm_w4_tm_kernel<EPI>, dim3(grid), dim3(tm::threads(EPI)), tm::SMEM_BYTES, st, tmap, args, n_tiles);
 }
 
 uint32_t gemm_tm_rows() { return tm::TOK; }
