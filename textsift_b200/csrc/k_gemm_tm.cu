@@ -17,7 +17,7 @@
 // never touch shared memory.
 //
 // Persistent, warp-specialized: one CTA per SM walks (token tile, 128-wide
-// output tile) pairs, 24 warps (20 for QKV), over three rings with their own barriers
+// output tile) pairs, 24 warps, over three rings with their own barriers
 // (activation tiles and weight blobs in smem, dequantised chunks in TMEM),
 // so a TMEM slot is handed back by its MMAs' commit, not by the next copy:
 //   warp 0       producer of the x tiles (TMA box per chunk)
@@ -32,8 +32,6 @@
 //   warps 12..23 epilogue of the previous tile: warp w reads lanes 32(w%4)..
 //                (one output column per thread) for tokens 64((w-12)/4)..;
 //                lane pairs exchange values so each store is 32 bits
-// With the RoPE epilogue (QKV) warps 4..7 dequantise every chunk and warps
-// 8..19 run the epilogue, 64 tokens each.
 // All waits are bounded (ts_common.cuh) and set the device error flag.
 #include "ts_common.cuh"
 #include "ts_kernels.h"
@@ -62,10 +60,9 @@ constexpr uint32_t COL_A = 2 * TOK;  // first A stage column, after the two accu
 // Role warps per epilogue kind: dequantising and epilogue warps (multiples
 // of 4, one per TMEM lane quarter); 4 more warps run the producers, the MMA
 // issue and the TMEM allocation.  Every kind has 12 epilogue warps (three
-// per scheduler: 64 tokens each); the RoPE epilogue's GEMM (QKV, K = 640
-// chunks of one weight tile) is fed by 4 dequantising warps, the others by 8
-// in two groups (20 or 24 warps, at most 80 registers a thread).
-__host__ __device__ constexpr uint32_t dq_warps(int epi) { return epi == kEpiQkvRope ? 4u : 8u; }
+// per scheduler: 64 tokens each) and 8 dequantising warps in two groups
+// that take alternate chunks: 24 warps, at most 80 registers a thread.
+__host__ __device__ constexpr uint32_t dq_warps(int) { return 8u; }
 __host__ __device__ constexpr uint32_t epi_warps(int) { return 12u; }
 __host__ __device__ constexpr uint32_t threads(int epi) { return 32u * (4u + dq_warps(epi) + epi_warps(epi)); }
 static_assert(X_BYTES % 1024 == 0, "swizzle atoms");
