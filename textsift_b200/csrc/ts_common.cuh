@@ -390,7 +390,7 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
       : "memory");
 }
 
-// 2-D tiled tensor copy global -> shared (no multicast).
+// 2-D tiled tensor copy global -> shared of this CTA.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int32_t c0, int32_t c1,
                                             uint64_t* bar) {
   asm volatile(
