@@ -97,7 +97,7 @@ __device__ __forceinline__ TmTile tm_tile(const GemmArgs& a, uint32_t tile, uint
 // even lane both outputs of token m0+2jj and the odd lane those of m0+2jj+1.
 template <int EPI>
 __device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTile& ti, uint32_t m0, uint32_t n,
-                                                  float bv, const uint32_t (&v)[32], int lane) {
+                                                  float bv, const uint32_t (&v)[32], int lane, int mypos) {
   const uint32_t odd = (uint32_t)lane & 1u;
   const uint32_t ncol = n & ~1u;
   const bool col_ok = ncol < a.N;
@@ -152,8 +152,7 @@ __device__ __forceinline__ void tm_epilogue_slice(const GemmArgs& a, const TmTil
     uint32_t csn[16];  // cos | sin << 16
     if (rope) {
       // position of token m0 + lane, then each lane's (cos, sin) of pair (n % 64) / 2
-      const uint32_t ml = m0 + (uint32_t)lane;
-      const int mypos = ml < ti.row_end ? a.pos[ml] : 0;
+      // mypos: the position of token m0 + lane, loaded before the accumulator wait
       const uint32_t p = (n & 63u) >> 1;
 #pragma unroll
       for (int jj = 0; jj < 16; jj++) {
@@ -366,20 +365,27 @@ __global__ void __launch_bounds__(tm::threads(EPI), 1)
       const TmTile ti = tm_tile(args, tile, n_ntiles);
       const uint32_t n = ti.n_tile * 128u + nl;
       const float bv = n < args.N ? f16_ref_to_f32(args.bias[(size_t)ti.expert * args.N + n]) : 0.0f;
+      // RoPE: each lane's token position for both slices, in flight during the wait
+      int pos_s[kPartTok / 32];
+#pragma unroll
+      for (uint32_t j = 0; j < kPartTok / 32; j++) {
+        const uint32_t ml = ti.row0 + g * kPartTok + 32u * j + (uint32_t)lane;
+        pos_s[j] = EPI == kEpiQkvRope && ml < ti.row_end ? args.pos[ml] : 0;
+      }
       if (!wait_or_abort(&acc_full[b], bph, args.err, abort_flag)) break;
       tc_fence_after();
       const uint32_t acc = tmem_base + ((q * 32u) << 16) + b * TOK + g * kPartTok;
-#pragma unroll 1
-      for (uint32_t c0 = 0; c0 < kPartTok; c0 += 32) {
+#pragma unroll
+      for (uint32_t j = 0; j < kPartTok / 32; j++) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(acc + c0, v);
+        tmem_ld_32x32b_x32(acc + 32u * j, v);
         tmem_ld_wait();
-        if (c0 + 32 >= kPartTok) {
+        if (j + 1 == kPartTok / 32) {
           // every TMEM read of this buffer by this thread is complete: release it
           tc_fence_before();
           mbar_arrive(&acc_empty[b]);
         }
-        tm_epilogue_slice<EPI>(args, ti, ti.row0 + g * kPartTok + c0, n, bv, v, lane);
+        tm_epilogue_slice<EPI>(args, ti, ti.row0 + g * kPartTok + 32u * j, n, bv, v, lane, pos_s[j]);
       }
     }
   }
