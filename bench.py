@@ -34,6 +34,19 @@ sys.path.insert(0, ROOT)
 METRIC = "classified tokens/sec, int4 MoE forward, 1/2/4/8 B200; expert-GEMM % TC peak"
 SEED = 0
 
+# stdout carries exactly one JSON line.  main() keeps the process's original
+# stdout descriptor here and points descriptor 1 at stderr, so whatever a
+# library prints (NCCL's version and debug lines, for instance) lands on
+# stderr and only emit() writes to the original stdout.
+_OUT_FD = None
+
+
+def emit(line: dict) -> None:
+    data = (json.dumps(line) + "\n").encode()
+    fd = _OUT_FD if _OUT_FD is not None else 1
+    while data:
+        data = data[os.write(fd, data):]
+
 
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -132,7 +145,7 @@ def run_reference(args):
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": f"{args.steps} x one {tok}-token chunk, all {cores} host threads"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_ours(args):
@@ -144,9 +157,6 @@ def run_ours(args):
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
-        # stdout carries exactly one JSON line: NCCL's own messages (printed
-        # when NCCL_DEBUG is set, e.g. its version line) go to stderr
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     L = abi.lib()
@@ -287,7 +297,7 @@ def run_ours(args):
                 "gpu_launches": int(n_launch.value),
                 "clocks": clk.summary(),
                 "device": be.device_name()}
-        print(json.dumps(line), flush=True)
+        emit(line)
     be.dispose()
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -305,6 +315,10 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    global _OUT_FD
+    sys.stdout.flush()
+    _OUT_FD = os.dup(1)
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
     else:
