@@ -6,7 +6,7 @@ teamchong/textsift (dumped from browser WebGPU by
 tests/conformance/dump-fixtures.spec.ts).  The reference checkout is only
 present where the fixtures are generated; the GPU hosts read the npz.
 
-Run: python tests/golden/make_golden.py [path/to/textsift]
+Run: python tests/golden/make_golden.py path/to/textsift
 """
 from __future__ import annotations
 
@@ -38,4 +38,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py path/to/textsift")
+    main(sys.argv[1])
