@@ -59,14 +59,14 @@ class Tokenizer:
         ptrs = (ctypes.c_char_p * max(1, k))(*enc)
         lens = (ctypes.c_size_t * max(1, k))(*[len(e) for e in enc])
         begin = np.zeros(k + 1, np.uint64)
-        abi.check(self._lib.ts_tok_encode_batch(self._h, ptrs, lens, k, threads, None, None, None, 0,
-                                                begin.ctypes.data))
-        total = int(begin[-1])
-        ids = np.empty(total, np.int32)
-        st = np.empty(total, np.uint32)
-        en = np.empty(total, np.uint32)
+        # every token covers at least one byte of its text: one call with room
+        # for as many tokens as there are bytes tokenizes each text once
+        cap = max(1, sum(len(e) for e in enc))
+        ids = np.empty(cap, np.int32)
+        st = np.empty(cap, np.uint32)
+        en = np.empty(cap, np.uint32)
         abi.check(self._lib.ts_tok_encode_batch(self._h, ptrs, lens, k, threads, ids.ctypes.data, st.ctypes.data,
-                                                en.ctypes.data, total, begin.ctypes.data))
+                                                en.ctypes.data, cap, begin.ctypes.data))
         return [(ids[begin[i]:begin[i + 1]], st[begin[i]:begin[i + 1]], en[begin[i]:begin[i + 1]]) for i in range(k)]
 
     def decode(self, ids) -> str:
