@@ -290,7 +290,9 @@ int ts_tok_encode(ts_tok_t* t, const char* utf8, size_t len, int32_t* ids, uint3
  * token_begin [n_texts + 1]: text i's tokens are [token_begin[i],
  * token_begin[i + 1]) of ids, starts and ends (UTF-16 start and end of
  * each token within its text), written when non-NULL if the total <= cap.
- * All three NULL: size query. */
+ * All three NULL: size query.  Every token covers at least one input byte,
+ * so cap = the texts' total byte length always suffices and tokenizes each
+ * text once (a size query followed by a filling call tokenizes twice). */
 int ts_tok_encode_batch(ts_tok_t* t, const char* const* texts, const size_t* lens, uint32_t n_texts,
                         uint32_t n_threads, int32_t* ids, uint32_t* starts, uint32_t* ends, size_t cap,
                         uint64_t* token_begin);
