@@ -366,12 +366,8 @@ cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st) {
   if (a.hd != kHD || a.Hq % a.Hkv != 0 || a.Hq / a.Hkv > 7) return cudaErrorInvalidValue;
   const uint32_t band = (kAttnRows + 2 * a.window + 15) & ~15u;
   const size_t sm = (size_t)band * 256 + band + 16;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};
+  if (cudaError_t e = smem_attr_per_device(attn_tc_kernel, 200 * 1024, attr_done); e != cudaSuccess) return e;
   if (sm > 200 * 1024) return cudaErrorInvalidValue;
   if (a.n_tiles == 0) return cudaSuccess;
   dim3 grid(a.n_tiles, a.Hkv);

@@ -516,12 +516,8 @@ cudaError_t launch_attention_umma(const AttnArgs& a, cudaStream_t st) {
       !make_tmap_2d(&tk, a.k, (uint64_t)a.Hkv * 64u, a.T, kld, 64, band / 2u) ||
       !make_tmap_2d(&tv, a.v, (uint64_t)a.Hkv * 64u, a.T, vld, 64, band / 2u))
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};
+  if (cudaError_t e = smem_attr_per_device(attn_umma_kernel, (int)kSmemBytes, attr_done); e != cudaSuccess) return e;
   const uint64_t items = (uint64_t)a.n_tiles * a.Hkv;
   const uint32_t grid = (uint32_t)std::min<uint64_t>(items, (uint64_t)num_sms());
   return launch_pdl(attn_umma_kernel, dim3(grid), dim3(kThreads), kSmemBytes, st, tq, tk, tv, a, band);

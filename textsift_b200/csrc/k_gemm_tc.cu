@@ -574,13 +574,10 @@ template <int BN, int BM, int EPI>
 static cudaError_t launch_one(const CUtensorMap& tmap, const GemmArgs& args, uint32_t n_tiles, uint32_t grid_m,
                               cudaStream_t st) {
   using C = GemmCfg<BN, BM>;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_w4_tc_kernel<BN, BM, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_done = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};
+  if (cudaError_t e = smem_attr_per_device(gemm_w4_tc_kernel<BN, BM, EPI>, (int)C::SMEM_BYTES, attr_done);
+      e != cudaSuccess)
+    return e;
   // persistent: at most one CTA per SM, never more CTAs than tiles can exist
   const uint64_t max_tiles = (uint64_t)grid_m * n_tiles;
   const uint32_t grid = (uint32_t)std::min<uint64_t>(max_tiles, (uint64_t)num_sms());

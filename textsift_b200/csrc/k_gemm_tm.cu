@@ -400,13 +400,9 @@ __global__ void __launch_bounds__(tm::threads(EPI), 1)
 template <int EPI>
 static cudaError_t launch_tm(const CUtensorMap& tmap, const GemmArgs& args, uint32_t n_tiles, uint32_t grid_m,
                              cudaStream_t st) {
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_w4_tm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)tm::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_done = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};
+  if (cudaError_t e = smem_attr_per_device(gemm_w4_tm_kernel<EPI>, (int)tm::SMEM_BYTES, attr_done); e != cudaSuccess)
+    return e;
   const uint64_t max_tiles = (uint64_t)grid_m * n_tiles;
   const uint32_t grid = (uint32_t)std::min<uint64_t>(max_tiles, (uint64_t)num_sms());
   return launch_pdl(gemm_w4_tm_kernel<EPI>, dim3(grid), dim3(tm::threads(EPI)), tm::SMEM_BYTES, st, tmap, args, n_tiles);

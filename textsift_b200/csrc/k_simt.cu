@@ -920,8 +920,12 @@ cudaError_t launch_matmul_exact(const ExactArgs& a_in, bool x_f32, int out_mode,
   dim3 grid(nblk(a.N, 128), grid_m);
   const size_t sm = exact_smem_bytes(a.K);
   if (sm > 227 * 1024) return cudaErrorInvalidValue;
-  static size_t attr_bytes = 0;
-  if (sm > 48 * 1024 && sm > attr_bytes) {
+  // the largest limit set so far on each device (function attributes belong
+  // to a device's context); devices past 63 set it on every call
+  static std::atomic<size_t> attr_bytes[64];
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
+  if (sm > 48 * 1024 && (dev < 0 || dev >= 64 || sm > attr_bytes[dev].load(std::memory_order_relaxed))) {
     const int v = (int)sm;
     cudaError_t e;
     if ((e = cudaFuncSetAttribute(matmul_w4_exact_kernel<true, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, v)) ||
@@ -930,7 +934,7 @@ cudaError_t launch_matmul_exact(const ExactArgs& a_in, bool x_f32, int out_mode,
         (e = cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, v)) ||
         (e = cudaFuncSetAttribute(matmul_w4_exact_kernel<false, kOutF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, v)))
       return e;
-    attr_bytes = sm;
+    if (dev >= 0 && dev < 64) attr_bytes[dev].store(sm, std::memory_order_relaxed);
   }
   if (x_f32) {
     if (out_mode == kOutF16) matmul_w4_exact_kernel<true, kOutF16><<<grid, 256, sm, st>>>(a);

@@ -183,12 +183,8 @@ cudaError_t launch_viterbi(const float* logits, const int* offs_dev, uint32_t n_
   if (n_seqs == 0 || max_len == 0) return cudaSuccess;
   if (max_len > viterbi_max_len()) return cudaErrorInvalidValue;
   const size_t sm = (size_t)max_len * kTags;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(viterbi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};
+  if (cudaError_t e = smem_attr_per_device(viterbi_kernel, 227 * 1024, attr_done); e != cudaSuccess) return e;
   viterbi_kernel<<<n_seqs, 32, sm, st>>>(logits, offs_dev, cal[0], cal[1], cal[2], cal[3], cal[4], cal[5], tags);
   return cudaGetLastError();
 }

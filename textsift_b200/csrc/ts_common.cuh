@@ -10,6 +10,7 @@
 //   programming error can never hang the GPU.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -249,6 +250,22 @@ __device__ __forceinline__ void swiglu_fast2(float g0, float u0, float g1, float
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Raise a kernel's dynamic shared-memory limit once per device: function
+// attributes belong to a device's context, so a process that drives several
+// GPUs sets them on each.  Bit d of `done` records device d (devices past 63
+// set the attribute on every call).
+template <typename... KArgs>
+inline cudaError_t smem_attr_per_device(void (*kernel)(KArgs...), int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+  if (bit && (done.load(std::memory_order_relaxed) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_relaxed);
+  return e;
+}
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
