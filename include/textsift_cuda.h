@@ -241,13 +241,16 @@ int ts_cuda_op_viterbi(const float* d_logits, const uint32_t* seq_offsets, uint3
  * runtime, a serving loop) or that cannot afford cudaMalloc/cudaFree's
  * implicit device-wide synchronisation between their kernels cannot allow.
  * This variant keeps that scratch in one static device array of ~221 KB per
- * GPU (held until the process exits) and calls no allocator.
+ * GPU (held until the process exits) and calls no allocator; the sequence
+ * offsets reach the GPU as a kernel parameter and the tile list is built
+ * there, so no host memory is copied either.
  * Limits: T <= 16384 tokens, n_seqs <= 1024 sequences per call, otherwise
  * TS_ERR_UNSUPPORTED.  Every call on a GPU shares the array: calls that
  * overlap on the GPU (e.g. on two streams at once) race and must be
- * serialized by the caller.  The first call on each device looks up the
- * array's device address (cudaGetSymbolAddress); make that first call before
- * any stream capture.  Same arguments and results as
+ * serialized by the caller.  Every call looks up the array's address for the
+ * current device (cudaGetSymbolAddress, which allocates nothing); the first
+ * call on a device may load the library's device code there, so make that
+ * first call before any stream capture.  Same arguments and results as
  * ts_cuda_op_banded_attention, except that it returns once the work is
  * queued on `stream` (no synchronize): synchronize the stream before reading
  * d_out. */
@@ -255,6 +258,49 @@ int ts_cuda_op_banded_attention_noalloc(const uint16_t* d_q, const uint16_t* d_k
                                         const float* d_sinks, const uint8_t* d_mask, uint16_t* d_out, uint32_t T,
                                         uint32_t Hq, uint32_t Hkv, uint32_t head_dim, uint32_t window,
                                         const uint32_t* seq_offsets, uint32_t n_seqs, int32_t mode, void* stream);
+
+/* The banded attention of the forward on the handle (its Hq, Hkv, head_dim,
+ * window and mode; zig/wasm_exports.zig:1286-1432 as in
+ * ts_cuda_op_banded_attention) over packed sequences (seq_offsets host,
+ * n_seqs + 1 entries, at most max_tokens tokens): d_q fp16 [T, Hq*hd],
+ * d_k/d_v fp16 [T, Hkv*hd], d_sinks f32 [Hq], d_mask u8 [T] or NULL ->
+ * d_out fp16 [T, Hq*hd].  Scratch comes from the handle's workspace, so it
+ * allocates nothing and returns once the work is queued on `stream`. */
+int ts_cuda_op_attention(ts_cuda_t* h, const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v,
+                         const float* d_sinks, const uint8_t* d_mask, uint16_t* d_out, const uint32_t* seq_offsets,
+                         uint32_t n_seqs, void* stream);
+
+/* RoPE alone, the reference routine rope_apply (zig/wasm_exports.zig:
+ * 1460-1502; three fp16 roundings per output, its fp16 decode): d_x fp16
+ * [T, H * head_dim] (interleaved pairs per head) -> d_out (may equal d_x);
+ * token t uses row d_pos[t] (device i32 [T]) of the fp16 tables d_cos/d_sin
+ * [rows, head_dim / 2] -- the reference indexes them by t, i.e. d_pos = 0..T-1.
+ * The kernel of the exact-mode forward. */
+int ts_cuda_op_rope(const uint16_t* d_x, uint16_t* d_out, const uint16_t* d_cos, const uint16_t* d_sin,
+                    const int32_t* d_pos, uint32_t T, uint32_t H, uint32_t head_dim, void* stream);
+
+/* The fast-mode Q/K/V projection of block `layer` with RoPE fused into its
+ * epilogue, exactly as the forward runs it (the three matmuls and two
+ * rope_apply calls of browser/inference/attention.ts:124-145): d_x fp16
+ * [T, d_model] (the normed input) over packed sequences (seq_offsets host,
+ * n_seqs + 1 entries; positions restart at each sequence) -> d_q fp16
+ * [T, Hq*hd], d_k / d_v fp16 [T, Hkv*hd], q and k rotated with the
+ * handle's YaRN tables. */
+int ts_cuda_op_qkv_rope(ts_cuda_t* h, uint32_t layer, const uint16_t* d_x, const uint32_t* seq_offsets,
+                        uint32_t n_seqs, uint16_t* d_q, uint16_t* d_k, uint16_t* d_v, void* stream);
+
+/* Self-test of the bounded device waits (no counterpart in the reference,
+ * whose GPU work is waited for by a host fence, native/vulkan/bridge.h:95-97).
+ * Enqueues on `stream` one CTA that holds TMEM while one warp waits on an
+ * mbarrier nothing arrives at, with a limit of limit_us microseconds
+ * (1..1000000; the kernels' own waits use 4 s), and another warp waits on a
+ * second such barrier until the first one's abort releases it; the timeout
+ * is recorded in the handle's device error flag and the TMEM is freed before
+ * the CTA exits.  The next ts_cuda_check on `stream` then returns
+ * TS_ERR_DEVICE ("bounded wait timed out") and clears the flag; the handle
+ * stays usable.  d_result (device, 2 x i32, may be NULL) receives 1 for each
+ * of the two waits that completed normally, 0 for each that gave up. */
+int ts_cuda_selftest_wait_timeout(ts_cuda_t* h, uint32_t limit_us, int32_t* d_result, void* stream);
 
 /* YaRN RoPE tables of the handle (browser/inference/rope.ts:348-356), fp16
  * [rows, head_dim/2] each, copied to host. */

@@ -1,0 +1,160 @@
+"""RoPE on the GPU against the reference, op by op, through the C ABI.
+
+Three pieces of the forward rotate Q and K (reference: rope_apply,
+zig/wasm_exports.zig:1460-1502, and the YaRN tables of
+browser/inference/rope.ts:239-356, restated in oracle/):
+
+* the handle's YaRN cos/sin tables (built on the host at finalize) --
+  bit-exact against the oracle's tables;
+* split_rope_kernel, the exact-mode RoPE (ts_cuda_op_rope) -- bit-exact
+  against the oracle's rope_apply, including fp16 inputs chosen to hit the
+  reference's subnormal decode quirk;
+* the fast-mode QKV GEMM with RoPE fused into its epilogue
+  (ts_cuda_op_qkv_rope) -- against rope_apply applied to the same GEMM's
+  un-rotated fp16 output: identical except where an fp16 subnormal appears
+  (an input, a product or a result), where the reference decodes subnormals
+  as if normal and rounds subnormal results half-up; those are counted.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import dev, empty, host, ptr, stream, w4_handle
+
+pytestmark = pytest.mark.gpu
+
+F16 = np.uint16
+HQ, HKV, HD = 14, 2, 64
+SUB = 2.0 ** -14  # smallest normal fp16
+
+
+def rng(seed):
+    return np.random.Generator(np.random.PCG64(seed))
+
+
+@pytest.fixture(scope="module")
+def model(cuda_lib):
+    from textsift_b200 import CudaBackend, make_weights, small_config
+    cfg = small_config(n_layers=1, vocab=1024)
+    w = make_weights(cfg, seed=17, bias_std=0.05)
+    b = CudaBackend(w, cfg, max_tokens=8192, max_seq_len=4096)
+    b.warmup()
+    yield cfg, w, b
+    b.dispose()
+
+
+def test_rope_tables_bit_exact(cuda_lib, oracle, model):
+    _, _, b = model
+    rows = 2048
+    c = np.empty((rows, HD // 2), F16)
+    s = np.empty((rows, HD // 2), F16)
+    assert cuda_lib.ts_cuda_rope_tables(b.handle, rows, c.ctypes.data, s.ctypes.data) == 0, cuda_lib.ts_cuda_last_error()
+    rc, rs = oracle.rope_tables(rows)
+    assert np.array_equal(c, rc) and np.array_equal(s, rs)
+
+
+def _f16_random(r, shape):
+    x = r.normal(0, 1.5, size=shape).astype(np.float16).view(F16)
+    # sprinkle the reference's awkward values: subnormals (decoded as if
+    # normal by math.zig:45-52), zeros of both signs, tiny normals
+    flat = x.reshape(-1)
+    n = flat.size
+    pick = r.choice(n, size=n // 50, replace=False)
+    flat[pick[0::4]] = r.integers(1, 0x400, size=flat[pick[0::4]].size).astype(F16)          # +subnormal
+    flat[pick[1::4]] = (r.integers(1, 0x400, size=flat[pick[1::4]].size) | 0x8000).astype(F16)  # -subnormal
+    flat[pick[2::4]] = 0x8000
+    flat[pick[3::4]] = r.integers(0x0400, 0x0800, size=flat[pick[3::4]].size).astype(F16)    # tiny normals
+    return x
+
+
+@pytest.mark.parametrize("T,H", [(257, 14), (1000, 2), (4, 4)])
+def test_op_rope_bit_exact(cuda_lib, oracle, T, H):
+    r = rng(T + H)
+    x = _f16_random(r, (T, H * HD))
+    tc, ts_ = oracle.rope_tables(T)
+    pos = np.arange(T, dtype=np.int32)
+    out = empty((T, H * HD), np.uint16)
+    assert cuda_lib.ts_cuda_op_rope(ptr(dev(x)), ptr(out), ptr(dev(tc)), ptr(dev(ts_)), ptr(dev(pos)), T, H, HD,
+                                    stream()) == 0, cuda_lib.ts_cuda_last_error()
+    ref = oracle.rope_apply(x, tc, ts_, T, H, HD)
+    assert np.array_equal(host(out, F16), ref)
+
+
+def test_op_rope_positions(cuda_lib, oracle):
+    # token t reads table row pos[t]: scattered positions equal the reference
+    # applied to the gathered table rows
+    r = rng(5)
+    T, H = 300, 2
+    x = _f16_random(r, (T, H * HD))
+    tc, ts_ = oracle.rope_tables(4096)
+    pos = r.integers(0, 4096, size=T).astype(np.int32)
+    out = empty((T, H * HD), np.uint16)
+    assert cuda_lib.ts_cuda_op_rope(ptr(dev(x)), ptr(out), ptr(dev(tc)), ptr(dev(ts_)), ptr(dev(pos)), T, H, HD,
+                                    stream()) == 0
+    ref = oracle.rope_apply(x, tc[pos], ts_[pos], T, H, HD)
+    assert np.array_equal(host(out, F16), ref)
+
+
+def _fused_qkv(w):
+    p = "layers.0.attn."
+    cat = lambda f: np.concatenate([w[p + n + "." + f] for n in ("q_proj", "k_proj", "v_proj")], axis=0)
+    return cat("int4")[None], cat("scales")[None], cat("zp")[None], cat("bias")[None]
+
+
+def _subnormal_involved(a, b, c, s, out):
+    """Per output: does any input, product or result of the RoPE pair that
+    produced it lie strictly between 0 and the smallest normal fp16?"""
+    f = lambda u: np.asarray(u, F16).view(np.float16).astype(np.float64)
+    tiny = lambda v: (v != 0) & (np.abs(v) < SUB)
+    A, B, C, S = f(a), f(b), f(c), f(s)
+    hit = tiny(A) | tiny(B) | tiny(C) | tiny(S) | tiny(A * C) | tiny(B * S) | tiny(B * C) | tiny(A * S)
+    return hit | tiny(f(out))
+
+
+def test_qkv_rope_epilogue_matches_reference_rope(cuda_lib, oracle, model):
+    cfg, w, b = model
+    L = cuda_lib
+    r = rng(9)
+    lens = [300, 1, 2048, 77, 1000]
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+    T = int(offs[-1])
+    x = r.normal(0, 1, size=(T, cfg["d_model"])).astype(np.float16).view(F16)
+    dx = dev(x)
+    q = empty((T, HQ * HD), np.uint16)
+    k = empty((T, HKV * HD), np.uint16)
+    v = empty((T, HKV * HD), np.uint16)
+    assert L.ts_cuda_op_qkv_rope(b.handle, 0, ptr(dx), offs.ctypes.data, len(lens), ptr(q), ptr(k), ptr(v),
+                                 stream()) == 0, L.ts_cuda_last_error()
+    # the same GEMM with the plain fp16 epilogue: un-rotated q | k | v
+    i4, sc, zp, bias = _fused_qkv(w)
+    hw = w4_handle(L, i4, sc, zp, bias)
+    try:
+        N = i4.shape[1]
+        raw = empty((T, N), np.uint16)
+        assert L.ts_cuda_op_matmul_nbits(hw, 0, ptr(dx), 1, ptr(raw), 1, T, 0, stream()) == 0, L.ts_cuda_last_error()
+        raw = host(raw, F16)
+    finally:
+        L.ts_cuda_w4_destroy(hw)
+    pos = np.concatenate([np.arange(n) for n in lens])
+    tc, ts_ = oracle.rope_tables(4096)
+    cpos, spos = tc[pos], ts_[pos]
+    Q, KV = HQ * HD, HKV * HD
+    assert np.array_equal(host(v, F16), raw[:, Q + KV:])
+    total = mism = 0
+    for got, raw_part, H in ((host(q, F16), raw[:, :Q], HQ), (host(k, F16), raw[:, Q:Q + KV], HKV)):
+        ref = oracle.rope_apply(raw_part, cpos, spos, T, H, HD)
+        diff = got != ref
+        total += got.size
+        if diff.any():
+            # the pair each output comes from, with its table entries
+            a = raw_part.reshape(T, H, HD // 2, 2)[..., 0]
+            bb = raw_part.reshape(T, H, HD // 2, 2)[..., 1]
+            cc = np.broadcast_to(cpos[:, None, :], a.shape)
+            ss = np.broadcast_to(spos[:, None, :], a.shape)
+            hit = _subnormal_involved(a, bb, cc, ss, ref.reshape(T, H, HD // 2, 2)[..., 0])
+            hit |= _subnormal_involved(a, bb, cc, ss, ref.reshape(T, H, HD // 2, 2)[..., 1])
+            d = diff.reshape(T, H, HD // 2, 2).any(axis=-1)
+            assert not (d & ~hit).any(), f"{int((d & ~hit).sum())} RoPE pairs differ without an fp16 subnormal"
+            mism += int(diff.sum())
+    # subnormals are rare for N(0,1) activations: the differences stay a tiny share
+    assert mism <= total * 1e-3, f"{mism} of {total} outputs differ"
+    print(f"fused QKV RoPE: {mism} of {total} outputs differ from rope_apply, all at fp16 subnormals")

@@ -2,8 +2,11 @@
 against the allocating entry point (ts_cuda_op_banded_attention), through the
 C ABI.  Both run the same kernels on the same inputs, so the outputs must be
 bit-identical; two calls in a row with different shapes check that nothing
-left in the shared scratch array by one call leaks into the next.  This file
-is collected last so it also runs after every other GPU test."""
+left in the shared scratch array by one call leaks into the next.  The
+sequence offsets reach the GPU as a kernel parameter and the tile list is
+built there, so these comparisons also check that device-side tile list
+against the host-built one of the allocating entry point.  This file is
+collected last so it also runs after every other GPU test."""
 import ctypes
 
 import numpy as np
@@ -57,14 +60,18 @@ def test_noalloc_matches_allocating_op_twice(L, mode):
         assert np.array_equal(host(out, F16), host(ref, F16))
 
 
-def test_noalloc_max_size(L):
-    lens = [16] * 1023 + [16384 - 16 * 1023]  # 16384 tokens in 1024 sequences
-    T, bufs, offs = _inputs(13, lens)
+@pytest.mark.parametrize("mode", [0, 1])
+def test_noalloc_max_size(L, mode):
+    # 16384 tokens in 1024 sequences whose lengths are not multiples of the
+    # 16-query tile: 1023 x 15 tokens + one of 1039, so the tensor-core tile
+    # list built on the GPU has 1023 + 65 = 1088 entries, near T/16 + n_seqs
+    lens = [15] * 1023 + [16384 - 15 * 1023]
+    T, bufs, offs = _inputs(13 + mode, lens)
     assert T == 16384 and len(offs) == 1025
     out = empty((T, HQ * HD), np.uint16)
     ref = empty((T, HQ * HD), np.uint16)
-    assert _call(L.ts_cuda_op_banded_attention_noalloc, T, bufs, offs, out, 0) == 0, L.ts_cuda_last_error()
-    assert _call(L.ts_cuda_op_banded_attention, T, bufs, offs, ref, 0) == 0, L.ts_cuda_last_error()
+    assert _call(L.ts_cuda_op_banded_attention_noalloc, T, bufs, offs, out, mode) == 0, L.ts_cuda_last_error()
+    assert _call(L.ts_cuda_op_banded_attention, T, bufs, offs, ref, mode) == 0, L.ts_cuda_last_error()
     assert np.array_equal(host(out, F16), host(ref, F16))
 
 

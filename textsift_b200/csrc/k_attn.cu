@@ -377,6 +377,8 @@ cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st) {
 
 uint32_t attention_max_tiles(uint32_t T, uint32_t n_seqs) { return T / kAttnRows + n_seqs + 1; }
 
+uint32_t attention_tile_rows() { return kAttnRows; }
+
 void attention_tiles(const uint32_t* offs, uint32_t n_seqs, int2* out, uint32_t* n_out) {
   uint32_t n = 0;
   for (uint32_t s = 0; s < n_seqs; s++)

@@ -560,13 +560,20 @@ bool make_act_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K
   return r == CUDA_SUCCESS;
 }
 
+// SM count of the current device (persistent grid size), cached per device
+// ordinal; devices past the cache are queried on every call.
 int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  const bool cached = dev >= 0 && dev < 64;
+  if (cached) {
+    const int n = cache[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
   }
+  int n = 0;
+  if (dev < 0 || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (cached) cache[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 

@@ -7,7 +7,10 @@
 // fixed budget, or a latency-sensitive loop that cannot afford the implicit
 // device-wide synchronisation cudaMalloc/cudaFree may perform between its
 // kernels.  This variant runs the same kernels with its scratch in one
-// file-scope device array instead, so it allocates nothing.
+// file-scope device array instead, so it allocates nothing, and it copies
+// nothing from host memory either: the sequence offsets travel to the GPU as
+// a kernel parameter, and the tile list is built on the GPU from them, so a
+// call only enqueues kernels and returns.
 //
 // Limits: at most kNoAllocMaxTokens tokens and kNoAllocMaxSeqs sequences per
 // call (larger calls are rejected with TS_ERR_UNSUPPORTED).  The array lives
@@ -19,8 +22,6 @@
 #include "textsift_cuda.h"
 #include "ts_common.cuh"
 #include "ts_simt.h"
-
-#include <mutex>
 
 namespace {
 
@@ -39,12 +40,37 @@ constexpr size_t kScratchBytes = align256(kOffTiles + 8 * kNoAllocMaxTiles);   /
 
 static __device__ __align__(256) unsigned char g_attn_scratch[kScratchBytes];
 
-// Device address of g_attn_scratch, looked up once per device.  In host code
-// the symbol's name only stands in for the device array; the address a kernel
-// can use comes from cudaGetSymbolAddress with that device current.
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-unsigned char* g_scratch_dev[kMaxDevices] = {nullptr};
+// The sequence offsets by value: 4,100 bytes of kernel parameters (the
+// parameter space of sm_70 and later holds up to 32,764 bytes).
+struct SeqOffsets {
+  uint32_t v[kNoAllocMaxSeqs + 1];
+};
+
+// One block of 1024 threads: copies the offsets into the scratch array and,
+// for the tensor-core path, writes the tile list that attention_tiles() builds
+// on the host for the allocating entry point -- sequence s contributes
+// ceil(len_s / rows) tiles {first query, sequence end} in order, placed after
+// the tiles of sequences 0..s-1 (an exclusive scan over one count per thread).
+__global__ void __launch_bounds__(1024) noalloc_prep_kernel(const SeqOffsets offs, uint32_t ns, uint32_t rows,
+                                                            int build_tiles, uint32_t* __restrict__ d_offs,
+                                                            int2* __restrict__ d_tiles) {
+  __shared__ uint32_t warp_total[32];
+  const uint32_t s = threadIdx.x, lane = s & 31u, warp = s >> 5;
+  for (uint32_t i = s; i <= ns; i += blockDim.x) d_offs[i] = offs.v[i];
+  if (!build_tiles) return;
+  const uint32_t lo = s < ns ? offs.v[s] : 0u, hi = s < ns ? offs.v[s + 1] : 0u;
+  const uint32_t cnt = (hi - lo + rows - 1) / rows;
+  uint32_t incl = cnt;  // inclusive scan within the warp
+  for (uint32_t d = 1; d < 32; d <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) warp_total[warp] = incl;
+  __syncthreads();
+  uint32_t base = incl - cnt;
+  for (uint32_t w = 0; w < warp; w++) base += warp_total[w];
+  for (uint32_t j = 0; j < cnt; j++) d_tiles[base + j] = make_int2((int)(lo + j * rows), (int)hi);
+}
 
 // Errors go to the library's per-thread message (ts_cuda_last_error).
 int noalloc_fail(int code, const char* msg) {
@@ -73,26 +99,22 @@ extern "C" int ts_cuda_op_banded_attention_noalloc(const uint16_t* d_q, const ui
   if (ns == 0 || ho[0] != 0 || ho[ns] != T) return noalloc_fail(TS_ERR_ARG, "seq_offsets must run from 0 to T");
   for (uint32_t s = 0; s < ns; s++)
     if (ho[s + 1] <= ho[s]) return noalloc_fail(TS_ERR_ARG, "empty sequence");
-  if (ts::attention_max_tiles(T, ns) > kNoAllocMaxTiles)
+  const uint32_t rows = ts::attention_tile_rows();
+  uint32_t ntl = 0;
+  for (uint32_t s = 0; s < ns; s++) ntl += (ho[s + 1] - ho[s] + rows - 1) / rows;
+  if (ntl > kNoAllocMaxTiles)
     return noalloc_fail(TS_ERR_UNSUPPORTED, "ts_cuda_op_banded_attention_noalloc: tile list exceeds scratch");
   if (mode == TS_MODE_FAST && (head_dim != 64 || Hq / Hkv > 7))
     return noalloc_fail(TS_ERR_UNSUPPORTED, "tensor-core attention needs head_dim 64, group <= 7");
 
-  // once per device: the scratch array's device address
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return noalloc_fail(TS_ERR_CUDA, "cudaGetDevice failed");
-  unsigned char* scratch;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_scratch_dev[dev]) {
-      void* p = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
-      if (e != cudaSuccess || !p) return noalloc_fail(TS_ERR_CUDA, cudaGetErrorString(e));
-      g_scratch_dev[dev] = static_cast<unsigned char*>(p);
-    }
-    scratch = g_scratch_dev[dev];
-  }
+  // The scratch array's device address for the current device and context,
+  // looked up on every call (no allocation, a table lookup once the module is
+  // loaded): a cached address would go stale after cudaDeviceReset or under a
+  // different context made current by the caller.
+  void* sym = nullptr;
+  const cudaError_t se = cudaGetSymbolAddress(&sym, g_attn_scratch);
+  if (se != cudaSuccess || !sym) return noalloc_fail(TS_ERR_CUDA, cudaGetErrorString(se));
+  unsigned char* scratch = static_cast<unsigned char*>(sym);
   uint32_t* d_offs = reinterpret_cast<uint32_t*>(scratch + kOffOffs);
   int* d_pos = reinterpret_cast<int*>(scratch + kOffPos);
   int* d_start = reinterpret_cast<int*>(scratch + kOffStart);
@@ -100,22 +122,20 @@ extern "C" int ts_cuda_op_banded_attention_noalloc(const uint16_t* d_q, const ui
   int2* d_tiles = reinterpret_cast<int2*>(scratch + kOffTiles);
 
   cudaStream_t st = (cudaStream_t)stream;
-  // A copy from pageable host memory is staged before cudaMemcpyAsync returns,
-  // so the host arrays below may go out of scope afterwards.
-  cudaError_t e = cudaMemcpyAsync(d_offs, ho, (size_t)(ns + 1) * 4, cudaMemcpyHostToDevice, st);
+  SeqOffsets po;
+  for (uint32_t s = 0; s <= ns; s++) po.v[s] = ho[s];
+  const bool fast = mode == TS_MODE_FAST;
+  noalloc_prep_kernel<<<1, 1024, 0, st>>>(po, ns, rows, fast ? 1 : 0, d_offs, d_tiles);
+  cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = ts::launch_seq_info(d_offs, ns, T, d_pos, d_start, d_len, st);
   if (e != cudaSuccess) return noalloc_fail(TS_ERR_CUDA, cudaGetErrorString(e));
   ts::AttnArgs a;
   a.q = d_q; a.k = d_k; a.v = d_v; a.sinks = d_sinks; a.mask = d_mask; a.out = d_out;
   a.sstart = d_start; a.slen = d_len; a.T = T; a.Hq = Hq; a.Hkv = Hkv; a.hd = head_dim; a.window = window;
-  if (mode == TS_MODE_FAST) {
-    int2 th[kNoAllocMaxTiles];
-    uint32_t ntl = 0;
-    ts::attention_tiles(ho, ns, th, &ntl);
-    e = cudaMemcpyAsync(d_tiles, th, (size_t)ntl * sizeof(int2), cudaMemcpyHostToDevice, st);
+  if (fast) {
     a.tiles = d_tiles;
     a.n_tiles = ntl;
-    if (e == cudaSuccess) e = ts::launch_attention_tc(a, st);
+    e = ts::launch_attention_tc(a, st);
   } else {
     e = ts::launch_attention_exact(a, st);
   }

@@ -1287,6 +1287,106 @@ int ts_cuda_op_viterbi(const float* d_logits, const uint32_t* seq_offsets, uint3
   return TS_OK;
 }
 
+int ts_cuda_op_rope(const uint16_t* d_x, uint16_t* d_out, const uint16_t* d_cos, const uint16_t* d_sin,
+                    const int32_t* d_pos, uint32_t T, uint32_t H, uint32_t head_dim, void* stream) {
+  if (!d_x || !d_out || !d_cos || !d_sin || !d_pos) return fail(TS_ERR_ARG, "ts_cuda_op_rope: null pointer");
+  if (head_dim == 0 || head_dim % 2 || H == 0) return fail(TS_ERR_ARG, "head_dim must be even and H > 0");
+  if (T == 0) return TS_OK;
+  // the exact-mode RoPE: the rotation half of split_rope_kernel over one
+  // [T, H * head_dim] block (no K or V part)
+  TS_CUDA_TRY(ts::launch_split_rope(d_x, d_out, nullptr, nullptr, d_pos, d_cos, d_sin, T, H * head_dim, 0, 0, head_dim,
+                                    (cudaStream_t)stream));
+  return TS_OK;
+}
+
+int ts_cuda_op_qkv_rope(ts_cuda_t* h, uint32_t layer, const uint16_t* d_x, const uint32_t* seq_offsets,
+                        uint32_t n_seqs, uint16_t* d_q, uint16_t* d_k, uint16_t* d_v, void* stream) {
+  if (!h || !d_x || !d_q || !d_k || !d_v || !seq_offsets || n_seqs == 0)
+    return fail(TS_ERR_ARG, "ts_cuda_op_qkv_rope: null argument");
+  if (!h->finalized || layer >= h->cfg.n_layers) return fail(TS_ERR_STATE, "handle not finalized or bad layer");
+  const ts_cuda_cfg& c = h->cfg;
+  if (seq_offsets[0] != 0) return fail(TS_ERR_ARG, "seq_offsets[0] must be 0");
+  for (uint32_t s = 0; s < n_seqs; s++) {
+    if (seq_offsets[s + 1] <= seq_offsets[s]) return fail(TS_ERR_ARG, "sequence %u is empty", s);
+    if (seq_offsets[s + 1] - seq_offsets[s] > c.max_seq_len) return fail(TS_ERR_UNSUPPORTED, "sequence > max_seq_len");
+  }
+  const uint32_t T = seq_offsets[n_seqs];
+  if (T > c.max_tokens) return fail(TS_ERR_UNSUPPORTED, "%u tokens > max_tokens %u", T, c.max_tokens);
+  DevGuard g(c.device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+  int rc = ensure_workspace(h, false);
+  if (rc) return rc;
+  Workspace& w = h->ws;
+  ts_cuda::Stage* sg = nullptr;
+  if ((rc = next_stage(h, (size_t)(n_seqs + 1) * 4, &sg))) return rc;
+  memcpy(sg->p, seq_offsets, (size_t)(n_seqs + 1) * 4);
+  TS_CUDA_TRY(cudaMemcpyAsync(w.offs.p, sg->p, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st));
+  TS_CUDA_TRY(cudaEventRecord(sg->done, st));
+  TS_CUDA_TRY(ts::launch_seq_info(w.offs.p, n_seqs, T, w.pos.p, w.sstart.p, w.slen.p, st));
+  const uint32_t Q = c.n_heads * c.head_dim, KV = c.n_kv_heads * c.head_dim;
+  ts::GemmArgs ga;
+  ga.M = T; ga.err = h->err.p;
+  ga.out0 = d_q; ga.ld0 = Q; ga.out1 = d_k; ga.ld1 = KV; ga.out2 = d_v; ga.ld2 = KV;
+  ga.q_cols = Q; ga.k_cols = KV; ga.pos = w.pos.p; ga.rope_cos = h->rope_cos.p; ga.rope_sin = h->rope_sin.p;
+  ga.rope_cs = h->rope_cs.p;
+  const uint32_t mt_tc = (T + ts::gemm_tm_rows() - 1) / ts::gemm_tm_rows();
+  TS_CUDA_TRY(ts::launch_gemm_w4_tm(h->layers[layer]->qkv.tiles(), d_x, T, ga, ts::kEpiQkvRope, mt_tc, st));
+  return TS_OK;
+}
+
+int ts_cuda_op_attention(ts_cuda_t* h, const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v,
+                         const float* d_sinks, const uint8_t* d_mask, uint16_t* d_out, const uint32_t* seq_offsets,
+                         uint32_t n_seqs, void* stream) {
+  if (!h || !d_q || !d_k || !d_v || !d_sinks || !d_out || !seq_offsets || n_seqs == 0)
+    return fail(TS_ERR_ARG, "ts_cuda_op_attention: null argument");
+  if (!h->finalized) return fail(TS_ERR_STATE, "ts_cuda_finalize has not succeeded");
+  const ts_cuda_cfg& c = h->cfg;
+  if (seq_offsets[0] != 0) return fail(TS_ERR_ARG, "seq_offsets[0] must be 0");
+  for (uint32_t s = 0; s < n_seqs; s++)
+    if (seq_offsets[s + 1] <= seq_offsets[s]) return fail(TS_ERR_ARG, "sequence %u is empty", s);
+  const uint32_t T = seq_offsets[n_seqs];
+  if (T > c.max_tokens) return fail(TS_ERR_UNSUPPORTED, "%u tokens > max_tokens %u", T, c.max_tokens);
+  DevGuard g(c.device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+  const bool exact = c.mode == TS_MODE_EXACT;
+  int rc = ensure_workspace(h, false);
+  if (rc) return rc;
+  Workspace& w = h->ws;
+  // offsets and the tile list through the pinned ring, as in the forward
+  const size_t offs_bytes = ((size_t)(n_seqs + 1) * 4 + 15) & ~size_t(15);
+  ts_cuda::Stage* sg = nullptr;
+  if ((rc = next_stage(h, offs_bytes + (size_t)ts::attention_max_tiles(T, n_seqs) * sizeof(int2), &sg))) return rc;
+  memcpy(sg->p, seq_offsets, (size_t)(n_seqs + 1) * 4);
+  TS_CUDA_TRY(cudaMemcpyAsync(w.offs.p, sg->p, (size_t)(n_seqs + 1) * 4, cudaMemcpyHostToDevice, st));
+  ts::AttnArgs aa;
+  aa.q = d_q; aa.k = d_k; aa.v = d_v; aa.sinks = d_sinks; aa.mask = d_mask; aa.out = d_out;
+  aa.sstart = w.sstart.p; aa.slen = w.slen.p; aa.T = T; aa.Hq = c.n_heads; aa.Hkv = c.n_kv_heads;
+  aa.hd = c.head_dim; aa.window = c.window; aa.err = h->err.p;
+  if (!exact) {
+    uint32_t nt = 0;
+    int2* th = reinterpret_cast<int2*>(sg->p + offs_bytes);
+    ts::attention_tiles(seq_offsets, n_seqs, th, &nt);
+    TS_CUDA_TRY(cudaMemcpyAsync(w.atiles.p, th, (size_t)nt * sizeof(int2), cudaMemcpyHostToDevice, st));
+    aa.tiles = w.atiles.p;
+    aa.n_tiles = nt;
+  }
+  TS_CUDA_TRY(cudaEventRecord(sg->done, st));
+  TS_CUDA_TRY(ts::launch_seq_info(w.offs.p, n_seqs, T, w.pos.p, w.sstart.p, w.slen.p, st));
+  h->n_launch += 2;
+  if (exact) TS_CUDA_TRY(ts::launch_attention_exact(aa, st));
+  else TS_CUDA_TRY(ts::launch_attention_tc(aa, st));
+  return TS_OK;
+}
+
+int ts_cuda_selftest_wait_timeout(ts_cuda_t* h, uint32_t limit_us, int32_t* d_result, void* stream) {
+  if (!h) return fail(TS_ERR_ARG, "ts_cuda_selftest_wait_timeout: null handle");
+  if (limit_us == 0 || limit_us > 1000000u) return fail(TS_ERR_ARG, "limit_us must be in [1, 1000000]");
+  DevGuard g(h->cfg.device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+  TS_CUDA_TRY(ts::launch_wait_selftest(h->err.p, 1000ull * limit_us, d_result, st));
+  return TS_OK;
+}
+
 int ts_cuda_rope_tables(ts_cuda_t* h, uint32_t rows, uint16_t* cos_out, uint16_t* sin_out) {
   if (!h || !cos_out || !sin_out) return fail(TS_ERR_ARG, "ts_cuda_rope_tables: null argument");
   if (!h->finalized) return fail(TS_ERR_STATE, "handle not finalized");

@@ -361,14 +361,16 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Bounded wait.  Returns false (and records kDevErrWaitTimeout) if the phase
-// did not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// did not complete within limit_ns (kWaitLimitNs in every kernel; a shorter
+// limit only in the wait self-test, k_selftest.cu).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   uint32_t it = 0;
   while (true) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
-    if ((++it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((++it & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       set_dev_err(err, kDevErrWaitTimeout);
       return false;
     }
@@ -376,7 +378,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // Bounded wait that also gives up as soon as another role aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag,
+                                              unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   uint32_t it = 0;
@@ -384,7 +387,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
     if (mbar_try_wait_sleep(bar, parity)) return true;
     if ((++it & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         set_dev_err(err, kDevErrWaitTimeout);
         *abort_flag = 1;
         return false;

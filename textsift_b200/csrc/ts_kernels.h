@@ -102,4 +102,9 @@ uint32_t gemm_tm_rows();
 cudaError_t launch_gemm_w4_tm(const W4Tiles& w, const void* x, uint64_t x_rows, GemmArgs args, int epi,
                               uint32_t grid_m, cudaStream_t st);
 
+// Bounded-wait self-test (k_selftest.cu): one CTA whose wait runs out after
+// limit_ns; result (device, 2 ints, may be null) = {1 if the timed wait
+// completed, 1 if the aborted one did}.
+cudaError_t launch_wait_selftest(int* err, unsigned long long limit_ns, int* result, cudaStream_t st);
+
 }  // namespace ts

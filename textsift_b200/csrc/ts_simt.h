@@ -113,6 +113,8 @@ cudaError_t launch_attention_umma(const AttnArgs& a, cudaStream_t st);
 // Host: the tensor-core tile list for packed sequences (offs has n_seqs + 1 entries).
 void attention_tiles(const uint32_t* offs, uint32_t n_seqs, int2* out, uint32_t* n_out);
 uint32_t attention_max_tiles(uint32_t T, uint32_t n_seqs);
+// Queries per tile of that list (a tile never crosses a sequence end).
+uint32_t attention_tile_rows();
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st);     // mma.sync tensor-core path
 cudaError_t launch_attention_exact(const AttnArgs& a, cudaStream_t st);  // reference-order CUDA-core path
 
