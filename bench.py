@@ -1,16 +1,25 @@
 #!/usr/bin/env python
-"""Whole-model privacy-filter throughput on B200 (classified tokens/s).
+"""Privacy-filter forward throughput on B200 (classified tokens/s) and the
+per-configuration measurements of BASELINE.json.
 
-Workload: documents with lengths uniform in
-[256, 4096] tokens, uniform random ids, chunked like textsift's chunkInput
-(2048 tokens, 128 overlap) and forwarded through the full config[0]
-architecture (8 blocks, 128 experts top-4, vocab 200064) with seeded q4f16
-weights.  Document-parallel: each rank gets its own documents (LPT-balanced),
-no collective on the data path; one step = one packed launch of at most
---max-tokens tokens per rank.  "Classified tokens" counts each document token
-once (chunk overlap excluded).
+Default (--config 4, the headline): BASELINE.json config[4] -- documents with
+lengths uniform in [256, 4096] tokens, uniform random ids, chunked like
+textsift's chunkInput (2048 tokens, 128 overlap) and forwarded through the
+full config[0] architecture (8 blocks, 128 experts top-4, vocab 200064) with
+seeded q4f16 weights.  Document-parallel: each rank gets its own documents
+(LPT-balanced), no collective on the data path; one step = one packed launch
+of at most --max-tokens tokens per rank.  "Classified tokens" counts each
+document token once (chunk overlap excluded).  --full-set runs all 8192
+documents of config[4] split across the ranks (strong scaling) instead of K
+steps per rank.
+
+--config 0..3 print one line each for the other configurations (1 x 512
+forward latency; MatMulNBits tensor-core table; one MoE layer under uniform
+and Zipf routing; banded attention 64 x 8192), each with its roofline and a
+bounded CPU baseline.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config 0|1|2|3|4] [--full-set]
 
 Under torchrun (N > 1) every rank runs its share; timing is the max over
 ranks of CUDA-event time around K steps bracketed by barriers.
@@ -24,6 +33,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 import numpy as np
@@ -33,6 +43,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "classified tokens/sec, int4 MoE forward, 1/2/4/8 B200; expert-GEMM % TC peak"
 SEED = 0
+N_DOCS_FULL = 8192
 
 # stdout carries exactly one JSON line.  main() keeps the process's original
 # stdout descriptor here and points descriptor 1 at stderr, so whatever a
@@ -46,6 +57,10 @@ def emit(line: dict) -> None:
     fd = _OUT_FD if _OUT_FD is not None else 1
     while data:
         data = data[os.write(fd, data):]
+
+
+def log(msg: str) -> None:
+    print(msg, file=sys.stderr, flush=True)
 
 
 def peaks():
@@ -101,51 +116,199 @@ class ClockSampler:
         sm = [int(r[1]) for r in rows]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+                "samples": len(rows), "power_w_max": max(pw) if pw else None}
 
 
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
-def cpu_sample_forward(weights, tokens: int, n_threads: int):
-    """Time the CPU restatement of textsift's WASM forward on one chunk."""
+# ---------------------------------------------------------------------------
+# Workload: config[4] documents as chunks (the unit both arms process)
+# ---------------------------------------------------------------------------
+def batch_chunks(batch, lengths):
+    """The chunks of a packed batch as (ids, unique document tokens): a
+    document's first chunk counts all its tokens, each later chunk only the
+    tokens past the previous chunk's end (the 128-token overlap once)."""
+    from textsift_b200.shard import chunk_spans
+    uniq = []
+    for d in batch.doc_ids:
+        spans = chunk_spans(int(lengths[d]))
+        prev = 0
+        for s, e in spans:
+            uniq.append(e - max(s, prev))
+            prev = e
+    offs = batch.offsets
+    assert len(uniq) == len(offs) - 1
+    return [(batch.ids[offs[i]:offs[i + 1]], uniq[i]) for i in range(len(uniq))]
+
+
+def config4_chunks(rank: int, world: int, n_docs: int, vocab: int, max_tokens: int, n_chunks: int):
+    """The first n_chunks chunks, in order, of the documents rank `rank` owns in
+    a config[4] job of n_docs documents over `world` ranks."""
+    from textsift_b200.shard import config4_lengths, rank_batches
+    lengths = config4_lengths(n_docs, SEED)
+    out = []
+    for b in rank_batches(rank, world, n_docs, vocab, max_tokens, SEED):
+        out += batch_chunks(b, lengths)
+        if len(out) >= n_chunks:
+            break
+    return out[:n_chunks]
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the C restatement of textsift's WASM forward (oracle/) with
+# the reference's MtPool partitioning, on this host's cores
+# ---------------------------------------------------------------------------
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def ref_default_threads(cores: int) -> int:
+    """The WASM backend's worker count, max(2, min(6, cores - 1))
+    (packages/textsift/src/browser/backends/wasm.ts:660-661)."""
+    return max(2, min(6, cores - 1))
+
+
+_ORACLE_MODELS = {}
+
+
+def oracle_model(weights, cfg):
     from oracle import oracle
-    from textsift_b200 import PF_CONFIG
     oracle.build()
-    m = oracle.OracleModel(PF_CONFIG, weights)
-    ids = np.random.Generator(np.random.PCG64(123)).integers(0, PF_CONFIG["vocab"], size=tokens).astype(np.int32)
-    t0 = time.perf_counter()
-    m.forward(ids, n_threads=n_threads)
-    return time.perf_counter() - t0
+    key = id(weights)
+    if key not in _ORACLE_MODELS:
+        _ORACLE_MODELS[key] = oracle.OracleModel(cfg, weights)
+    return _ORACLE_MODELS[key]
+
+
+def cpu_forward_rate(model, ids, n_threads: int, repeats: int = 1) -> float:
+    """Median seconds of `repeats` oracle forwards of one chunk."""
+    ts = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        model.forward(ids, n_threads=n_threads)
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts)
+
+
+def cpu_modes(model, ids, unique: int, budget: dict | None = None) -> dict:
+    """tokens/s of one chunk in the three modes BASELINE.md plans: single
+    thread (the canonical order), the reference's default worker count, and
+    every host core.  `budget` = forwards per mode."""
+    cores = host_cores()
+    budget = budget or {}
+    out = {}
+    for label, n in (("single_thread", 1), ("reference_default_threads", ref_default_threads(cores)),
+                     ("all_cores", cores)):
+        sec = cpu_forward_rate(model, ids, n, budget.get(label, 1))
+        out[label] = {"threads": n, "tokens_per_s": unique / sec, "s_per_chunk": sec}
+    return out
 
 
 def run_reference(args):
-    """The reference arm: textsift's WASM CPU forward cannot run here (no JS/WASM
-    runtime); its C restatement (oracle/, same kernels and order) runs on all
-    host cores with the reference's token-range / head partitioning."""
+    """The reference arm: textsift's WASM CPU forward cannot run here (no
+    JS/WASM runtime); its C restatement (oracle/, same kernels and summation
+    order) runs with every host thread and the reference's token-range / head
+    partitioning, one config[4] chunk (up to 2048 tokens) per step -- the
+    chunks rank 0 of the GPU arm owns, in order."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
     from textsift_b200 import PF_CONFIG, make_weights
-    cores = os.cpu_count() or 1
+    cores = host_cores()
     w = make_weights(PF_CONFIG, seed=SEED)
-    tok = args.ref_tokens
-    for _ in range(args.warmup):
-        cpu_sample_forward(w, tok, cores)
-    times = [cpu_sample_forward(w, tok, cores) for _ in range(args.steps)]
-    total = sum(times)
-    v = tok * args.steps / total
+    m = oracle_model(w, PF_CONFIG)
+    chunks = config4_chunks(0, world, N_DOCS_FULL if args.full_set else weak_n_docs(args, world), PF_CONFIG["vocab"],
+                            args.max_tokens, args.warmup + args.steps)
+    for ids, _ in chunks[:args.warmup]:
+        m.forward(ids, n_threads=cores)
+    t0 = time.perf_counter()
+    uniq = proc = 0
+    for ids, u in chunks[args.warmup:]:
+        m.forward(ids, n_threads=cores)
+        uniq += u
+        proc += ids.size
+    total = time.perf_counter() - t0
+    v = uniq / total
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"config[4] documents, {tok}-token chunk per step (bounded CPU sample)",
-                       "model": "privacy-filter (8 blocks, 128 experts top-4, vocab 200064), seeded q4f16"},
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded q4f16 weights, uniform ids)",
+            "config": config4_desc(world),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": f"{args.steps} x one {tok}-token chunk, all {cores} host threads"},
+                             "sample": f"{args.steps} config[4] chunks ({proc} tokens, {uniq} unique document "
+                                       f"tokens) of rank 0's documents, one chunk per step, all {cores} host "
+                                       f"threads"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
+
+
+def weak_n_docs(args, world: int) -> int:
+    """Documents of the weak-scaling job: enough for warmup + steps packed
+    launches on every rank (documents average ~2300 chunked tokens)."""
+    return max(8, int((args.warmup + args.steps) * args.max_tokens / 2300) + 8) * world
+
+
+def config4_desc(world: int, full_set: bool = False) -> dict:
+    return {"workload": "config[4]: documents U[256,4096] tokens, chunked 2048/128, full config[0] architecture, "
+                        "document-parallel" + (f", all {N_DOCS_FULL} documents split over the ranks" if full_set
+                                               else ""),
+            "model": "privacy-filter (8 blocks, 128 experts top-4, vocab 200064)",
+            "parallelism": f"dp{world} (documents, no collective)",
+            "l2": "no flush: each step streams 0.8 GB of weights and GBs of activations (> 126 MB L2)"}
+
+
+# ---------------------------------------------------------------------------
+# Our arm, config[4]
+# ---------------------------------------------------------------------------
+class Forwarder:
+    """Packed forwards of config[4] batches through the C ABI on one stream."""
+
+    def __init__(self, be, batches, max_tokens, n_classes):
+        import torch
+        from textsift_b200 import abi
+        self.L = abi.lib()
+        self.abi = abi
+        self.h = be.handle
+        self.batches = batches
+        self.dev_ids = [torch.from_numpy(b.ids).cuda() for b in batches]
+        self.offs = [np.ascontiguousarray(b.offsets) for b in batches]
+        self.logits = torch.empty((max_tokens, n_classes), dtype=torch.float32, device="cuda")
+        self.st = torch.cuda.Stream()
+        self.sp = ctypes.c_void_p(self.st.cuda_stream)
+
+    def step(self, i):
+        rc = self.L.ts_cuda_forward_packed_device(self.h, self.dev_ids[i].data_ptr(), None, self.offs[i].ctypes.data,
+                                                  len(self.offs[i]) - 1, self.logits.data_ptr(), self.sp)
+        if rc != 0:
+            raise self.abi.TextsiftCudaError(rc, self.abi.last_error())
+
+    def check(self):
+        self.abi.check(self.L.ts_cuda_check(self.h, self.sp))
+
+    def timed(self, idx, barrier=None):
+        """Device milliseconds of the steps in idx (CUDA events on the stream)."""
+        import torch
+        self.check()
+        if barrier:
+            barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.st)
+        for i in idx:
+            self.step(i)
+        e1.record(self.st)
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        self.check()
+        return e0.elapsed_time(e1)
 
 
 def run_ours(args):
@@ -159,148 +322,569 @@ def run_ours(args):
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
-    L = abi.lib()
-    weights = make_weights(PF_CONFIG, seed=SEED)
-    be = CudaBackend(weights, PF_CONFIG, device=local, max_tokens=args.max_tokens, max_seq_len=2048)
-    be.warmup()
-    h = be.handle
-    need = args.warmup + args.steps
-    docs_per_rank = max(8, int(need * args.max_tokens / 2300) + 8)
-    batches = rank_batches(rank, world, docs_per_rank * world, PF_CONFIG["vocab"], args.max_tokens, SEED)
-    batches = [b for b in batches if b.tokens > args.max_tokens // 2] or batches  # drop the short tail batch
-    seq = [batches[i % len(batches)] for i in range(need)]
-    dev_ids = [torch.from_numpy(b.ids).cuda() for b in seq]
-    offs = [np.ascontiguousarray(b.offsets) for b in seq]
-    logits = torch.empty((args.max_tokens, PF_CONFIG["n_classes"]), dtype=torch.float32, device="cuda")
-    st = torch.cuda.Stream()
-    sp = ctypes.c_void_p(st.cuda_stream)
-
-    def step(i):
-        rc = L.ts_cuda_forward_packed_device(h, dev_ids[i].data_ptr(), None, offs[i].ctypes.data,
-                                             len(offs[i]) - 1, logits.data_ptr(), sp)
-        if rc != 0:
-            raise abi.TextsiftCudaError(rc, abi.last_error())
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
 
-    for i in range(args.warmup):
-        step(i)
-    abi.check(L.ts_cuda_check(h, sp))
-    barrier()
-    torch.cuda.synchronize()
+    L = abi.lib()
+    weights = make_weights(PF_CONFIG, seed=SEED)
+    be = CudaBackend(weights, PF_CONFIG, device=local, max_tokens=args.max_tokens, max_seq_len=2048)
+    be.warmup()
+    h = be.handle
+    if args.full_set:
+        batches = rank_batches(rank, world, N_DOCS_FULL, PF_CONFIG["vocab"], args.max_tokens, SEED)
+        seq = batches[:args.warmup] + batches  # warm-up on the first batches, then every batch once, timed
+        timed_idx = list(range(min(args.warmup, len(batches)), len(seq)))
+        warm_idx = list(range(min(args.warmup, len(batches))))
+    else:
+        need = args.warmup + args.steps
+        batches = rank_batches(rank, world, weak_n_docs(args, world), PF_CONFIG["vocab"], args.max_tokens, SEED)
+        batches = [b for b in batches if b.tokens > args.max_tokens // 2] or batches  # drop the short tail batch
+        seq = [batches[i % len(batches)] for i in range(need)]
+        warm_idx, timed_idx = list(range(args.warmup)), list(range(args.warmup, need))
+    fw = Forwarder(be, seq, args.max_tokens, PF_CONFIG["n_classes"])
+    for i in warm_idx:
+        fw.step(i)
     # Headline pass: no per-phase events inside the steps (an event recorded
     # between two kernels serialises their programmatic launch).
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    abi.check(L.ts_cuda_profile(h, 0))
     with ClockSampler(local) as clk:
-        e0.record(st)
-        for i in range(args.warmup, need):
-            step(i)
-        e1.record(st)
-        torch.cuda.synchronize()
-    barrier()
-    abi.check(L.ts_cuda_check(h, sp))
-    ms = e0.elapsed_time(e1)
-    # Second timed pass of the same steps with CUDA events around each phase:
-    # per-kernel durations for the phase table and the roofline.
+        ms = fw.timed(timed_idx, barrier)
+    n_launch = ctypes.c_uint64()
+    abi.check(L.ts_cuda_profile_read(h, None, None, None, ctypes.byref(n_launch)))
+    n_steps = len(timed_idx)
+    # Second timed pass of (up to 20 of) the same steps with CUDA events
+    # around each phase: per-kernel durations for the phase table and the
+    # roofline.
+    prof_idx = timed_idx[:20]
     abi.check(L.ts_cuda_profile(h, 1))
-    barrier()
-    torch.cuda.synchronize()
-    for i in range(args.warmup, need):
-        step(i)
-    torch.cuda.synchronize()
-    barrier()
-    abi.check(L.ts_cuda_check(h, sp))
+    fw.timed(prof_idx, barrier)
     ph_ms = (ctypes.c_double * 7)()
     ph_n = (ctypes.c_uint64 * 7)()
     ph_fl = (ctypes.c_uint64 * 7)()
-    n_launch = ctypes.c_uint64()
-    abi.check(L.ts_cuda_profile_read(h, ph_ms, ph_n, ph_fl, ctypes.byref(n_launch)))
+    abi.check(L.ts_cuda_profile_read(h, ph_ms, ph_n, ph_fl, None))
     abi.check(L.ts_cuda_profile(h, 0))
-    toks = sum(b.unique_tokens for b in seq[args.warmup:])
-    processed = sum(b.tokens for b in seq[args.warmup:])
+    toks = sum(seq[i].unique_tokens for i in timed_idx)
+    processed = sum(seq[i].tokens for i in timed_idx)
 
     # ---- end to end through the public C ABI with host buffers ----
-    host_ids = [b.ids for b in seq]
+    e2e_idx = timed_idx[:args.steps] if args.full_set else timed_idx
     out = np.empty((args.max_tokens * PF_CONFIG["n_classes"],), np.float32)
-    for i in range(min(2, args.warmup)):
-        abi.check(L.ts_cuda_forward_packed(h, host_ids[i].ctypes.data, None, offs[i].ctypes.data,
-                                           len(offs[i]) - 1, out.ctypes.data))
+    for i in warm_idx[:2]:
+        abi.check(L.ts_cuda_forward_packed(h, seq[i].ids.ctypes.data, None, fw.offs[i].ctypes.data,
+                                           len(fw.offs[i]) - 1, out.ctypes.data))
     barrier()
     t0 = time.perf_counter()
-    for i in range(args.warmup, need):
-        abi.check(L.ts_cuda_forward_packed(h, host_ids[i].ctypes.data, None, offs[i].ctypes.data,
-                                           len(offs[i]) - 1, out.ctypes.data))
+    for i in e2e_idx:
+        abi.check(L.ts_cuda_forward_packed(h, seq[i].ids.ctypes.data, None, fw.offs[i].ctypes.data,
+                                           len(fw.offs[i]) - 1, out.ctypes.data))
     e2e_s = time.perf_counter() - t0
     barrier()
-    h2d = sum(b.tokens * 4 + b.offsets.nbytes for b in seq[args.warmup:]) / args.steps
-    d2h = sum(b.tokens * PF_CONFIG["n_classes"] * 4 for b in seq[args.warmup:]) / args.steps
+    e2e_toks = sum(seq[i].unique_tokens for i in e2e_idx)
+    h2d = sum(seq[i].tokens * 4 + seq[i].offsets.nbytes for i in e2e_idx) / len(e2e_idx)
+    d2h = sum(seq[i].tokens * PF_CONFIG["n_classes"] * 4 for i in e2e_idx) / len(e2e_idx)
 
-    vals = torch.tensor([ms, e2e_s, float(toks)], dtype=torch.float64, device="cuda")
+    # ---- the parity-green path: the same steps in exact mode (reference
+    # summation order on CUDA cores), a few of them ----
+    exact = None
+    if not args.no_exact:
+        abi.check(L.ts_cuda_set_mode(h, abi.TS_MODE_EXACT))
+        fw.step(warm_idx[0])
+        ex_idx = timed_idx[:3]
+        ex_ms = fw.timed(ex_idx, barrier)
+        abi.check(L.ts_cuda_set_mode(h, abi.TS_MODE_FAST))
+        exact = (ex_ms, float(sum(seq[i].unique_tokens for i in ex_idx)), len(ex_idx))
+
+    vals = torch.tensor([ms, e2e_s, float(toks), float(e2e_toks), exact[0] if exact else 0.0,
+                         exact[1] if exact else 0.0], dtype=torch.float64, device="cuda")
     if world > 1:
         mx = vals.clone()
         torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
         sm = vals.clone()
         torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
-        ms_max, e2e_max, toks_all = mx[0].item(), mx[1].item(), sm[2].item()
+        ms_max, e2e_max, toks_all, e2e_toks_all = mx[0].item(), mx[1].item(), sm[2].item(), sm[3].item()
+        ex_ms_max, ex_toks_all = mx[4].item(), sm[5].item()
     else:
-        ms_max, e2e_max, toks_all = ms, e2e_s, float(toks)
+        ms_max, e2e_max, toks_all, e2e_toks_all = ms, e2e_s, float(toks), float(e2e_toks)
+        ex_ms_max, ex_toks_all = (exact[0], exact[1]) if exact else (0.0, 0.0)
+
+    full = None
+    if rank == 0 and world == 1 and not args.full_set and not args.no_full_set:
+        full = full_set_n1(be, PF_CONFIG, args)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cores = os.cpu_count() or 1
-        t = cpu_sample_forward(weights, args.ref_tokens, cores)
-        cpu = {"value": args.ref_tokens / t, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"one {args.ref_tokens}-token config[4] chunk through the C restatement of the WASM "
-                         f"forward, {cores} host threads"}
+        cpu = config4_cpu_baseline(weights, PF_CONFIG, args.max_tokens)
 
     if rank == 0:
-        pk = peaks()
-        gu = abi.PHASES.index("expert_gate_up")
-        dn = abi.PHASES.index("expert_down")
-        n_launch_e = ph_n[gu] + ph_n[dn]
-        dur_ms = (ph_ms[gu] + ph_ms[dn]) / max(1, n_launch_e)
-        fl = (ph_fl[gu] + ph_fl[dn]) / max(1, n_launch_e)
-        achieved = fl / (dur_ms * 1e-3) / 1e12 if dur_ms > 0 else 0.0
-        traffic = None
-        tpath = os.path.join(ROOT, "profiles", "expert_gemm_traffic.json")
-        if os.path.exists(tpath):
-            traffic = json.load(open(tpath)).get("bytes_per_launch")
-        phases = {abi.PHASES[i]: {"ms": round(ph_ms[i], 3), "launches": int(ph_n[i]),
-                                  "tflops": round(ph_fl[i] / (ph_ms[i] * 1e-3) / 1e12, 1) if ph_ms[i] > 0 else None}
-                  for i in range(7)}
-        value = toks_all / (ms_max * 1e-3)
-        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-                "data": "synthetic (seeded q4f16 weights, uniform ids)",
-                "config": {"workload": "config[4]: documents U[256,4096] tokens, chunked 2048/128, full config[0] "
-                                       "architecture, document-parallel",
-                           "model": "privacy-filter (8 blocks, 128 experts top-4, vocab 200064)",
-                           "tokens_per_step_per_gpu": processed / args.steps,
-                           "unique_tokens_per_step_per_gpu": toks / args.steps,
-                           "global_batch_tokens": processed / args.steps * world,
-                           "parallelism": f"dp{world} (documents, no collective)",
-                           "l2": "no flush: each step streams 0.8 GB of weights and GBs of activations (> 126 MB L2)"},
-                "roofline": {"bound": "tensor", "kernel": "expert GEMMs (gate_up + down, tcgen05 int4 dequant)",
-                             "achieved": achieved, "peak": pk["tflops_sustained"], "unit": "TFLOP/s",
-                             "frac": achieved / pk["tflops_sustained"], "peak_source":
-                                 f"{pk['source']} bf16 sustained", "traffic": traffic,
-                             "avg_launch_ms": dur_ms, "flops_per_launch": fl,
-                             "timing": "CUDA events around each expert-GEMM launch on a second timed pass of the "
-                                       "same steps (per-phase events kept out of the headline pass)"},
-                "phases": phases,
-                "cpu_baseline": cpu,
-                "e2e": {"value": toks_all / e2e_max, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
-                        "d2h_bytes_per_step": int(d2h)},
-                "gpu_launches": int(n_launch.value),
-                "clocks": clk.summary(),
-                "device": be.device_name()}
+        line = config4_line(args, world, ms_max, n_steps, toks_all, processed, toks, ph_ms, ph_n, ph_fl,
+                            e2e_toks_all / e2e_max, h2d, d2h, int(n_launch.value), clk.summary(), be.device_name())
+        if exact:
+            line["exact_mode"] = {"value": ex_toks_all / (ex_ms_max * 1e-3), "unit": "tokens/s",
+                                  "ms_per_step": ex_ms_max / exact[2], "steps": exact[2],
+                                  "what": "TS_MODE_EXACT: every GEMM and the attention in the reference's f32 "
+                                          "summation order on CUDA cores (the mode whose routing, argmax and "
+                                          "logits match the reference on config[0]); same steps as the headline"}
+        if full:
+            line["full_set"] = full
+        line["cpu_baseline"] = cpu
         emit(line)
+    fw = None
     be.dispose()
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def full_set_n1(be, cfg, args) -> dict:
+    """All 8192 config[4] documents through one GPU (the literal config[4]
+    job at N = 1): every packed launch once, CUDA events around all of them."""
+    from textsift_b200.shard import rank_batches
+    batches = rank_batches(0, 1, N_DOCS_FULL, cfg["vocab"], args.max_tokens, SEED)
+    fw = Forwarder(be, batches, args.max_tokens, cfg["n_classes"])
+    for i in range(min(2, len(batches))):
+        fw.step(i)
+    ms = fw.timed(range(len(batches)))
+    toks = sum(b.unique_tokens for b in batches)
+    return {"value": toks / (ms * 1e-3), "unit": "tokens/s", "documents": N_DOCS_FULL, "unique_tokens": toks,
+            "processed_tokens": sum(b.tokens for b in batches), "launches": len(batches), "ms": ms}
+
+
+def config4_cpu_baseline(weights, cfg, max_tokens) -> dict:
+    """One full 2048-token config[4] chunk (the workload's chunk size) through
+    the oracle in the three thread modes; `value` = all host cores."""
+    cores = host_cores()
+    chunks = config4_chunks(0, 1, 64, cfg["vocab"], max_tokens, 64)
+    ids, uniq = next((c for c in chunks if c[0].size == 2048), chunks[0])
+    m = oracle_model(weights, cfg)
+    modes = cpu_modes(m, ids, uniq, {"all_cores": 2})
+    return {"value": modes["all_cores"]["tokens_per_s"], "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"one {ids.size}-token config[4] chunk through the C restatement of the WASM forward "
+                      f"(reference summation order, MtPool partitioning); value = all {cores} host threads",
+            "modes": modes}
+
+
+def config4_line(args, world, ms_max, n_steps, toks_all, processed, toks, ph_ms, ph_n, ph_fl, e2e_value, h2d, d2h,
+                 n_launch, clocks, device) -> dict:
+    from textsift_b200 import abi
+    pk = peaks()
+    gu = abi.PHASES.index("expert_gate_up")
+    dn = abi.PHASES.index("expert_down")
+    n_launch_e = ph_n[gu] + ph_n[dn]
+    dur_ms = (ph_ms[gu] + ph_ms[dn]) / max(1, n_launch_e)
+    fl = (ph_fl[gu] + ph_fl[dn]) / max(1, n_launch_e)
+    achieved = fl / (dur_ms * 1e-3) / 1e12 if dur_ms > 0 else 0.0
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "expert_gemm_traffic.json")
+    if os.path.exists(tpath):
+        traffic = json.load(open(tpath)).get("bytes_per_launch")
+    phases = {abi.PHASES[i]: {"ms": round(ph_ms[i], 3), "launches": int(ph_n[i]),
+                              "tflops": round(ph_fl[i] / (ph_ms[i] * 1e-3) / 1e12, 1) if ph_ms[i] > 0 else None}
+              for i in range(7)}
+    cfgd = config4_desc(world, args.full_set)
+    cfgd.update({"tokens_per_step_per_gpu": processed / n_steps, "unique_tokens_per_step_per_gpu": toks / n_steps,
+                 "global_batch_tokens": processed / n_steps * world})
+    return {"metric": METRIC, "value": toks_all / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": n_steps, "warmup": args.warmup, "ms_per_step": ms_max / n_steps, "higher_is_better": True,
+            "scaling": "strong" if args.full_set else "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded q4f16 weights, uniform ids)", "config": cfgd,
+            "roofline": {"bound": "tensor", "kernel": "expert GEMMs (gate_up + down, tcgen05 int4 dequant)",
+                         "achieved": achieved, "peak": pk["tflops_sustained"], "unit": "TFLOP/s",
+                         "frac": achieved / pk["tflops_sustained"],
+                         "peak_source": f"{pk['source']} bf16 sustained", "traffic": traffic,
+                         "avg_launch_ms": dur_ms, "flops_per_launch": fl,
+                         "timing": "CUDA events around each expert-GEMM launch on a second timed pass of the "
+                                   "same steps (per-phase events kept out of the headline pass)"},
+            "phases": phases,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": n_launch, "clocks": clocks, "device": device}
+
+
+# ---------------------------------------------------------------------------
+# Configs [0]-[3]: one line each
+# ---------------------------------------------------------------------------
+class Timer:
+    """Per-launch CUDA-event timing on one stream, optionally with an L2
+    flush (a 256 MB write, twice the L2) between launches, outside the
+    events."""
+
+    def __init__(self, flush: bool):
+        import torch
+        self.torch = torch
+        self.st = torch.cuda.Stream()
+        self.sp = ctypes.c_void_p(self.st.cuda_stream)
+        self.buf = torch.empty(64 << 20, dtype=torch.int32, device="cuda") if flush else None
+
+    def run(self, fn, reps: int, warmup: int = 3):
+        torch = self.torch
+        for _ in range(warmup):
+            fn(self.sp)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        with torch.cuda.stream(self.st):
+            for a, b in ev:
+                if self.buf is not None:
+                    self.buf.fill_(1)
+                a.record(self.st)
+                fn(self.sp)
+                b.record(self.st)
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in ev]
+
+
+def base_line(cfg_name: str, value, unit, args, higher=True, **kw) -> dict:
+    d = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+         "higher_is_better": higher, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+         "data": "synthetic (seeded q4f16 weights, BASELINE.json distributions)", "config": {"workload": cfg_name}}
+    d.update(kw)
+    return d
+
+
+def weight_blob_bytes(cfg) -> int:
+    """Bytes of the tensor-core weight tiles one forward streams: 37 bytes per
+    output row per 64-wide K chunk (32 B nibbles, 4 B scales, 1 B zero
+    points), for every layer's Q/K/V, O, router and all experts, plus the
+    classifier's one 128-row tile."""
+    D, F, E, Q = cfg["d_model"], cfg["d_ff"], cfg["n_experts"], cfg["n_heads"] * cfg["head_dim"]
+    KV = cfg["n_kv_heads"] * cfg["head_dim"]
+    rows_k = [(Q + 2 * KV, D), (D, Q), (E, D), (E * 2 * F, D), (E * D, F)]
+    per_layer = sum(r * (k // 64) * 37 for r, k in rows_k)
+    return cfg["n_layers"] * per_layer + 128 * (D // 64) * 37
+
+
+def run_config0(args):
+    """[0] one 512-token sequence through the full model: forward latency on
+    the device and end to end through ts_cuda_forward (host ids in, host
+    logits out)."""
+    import torch
+    from textsift_b200 import PF_CONFIG, CudaBackend, abi, make_weights
+    torch.cuda.set_device(0)
+    T = 512
+    w = make_weights(PF_CONFIG, seed=SEED)
+    be = CudaBackend(w, PF_CONFIG, max_tokens=T, max_seq_len=T)
+    be.warmup()
+    L, h = abi.lib(), be.handle
+    ids = np.random.Generator(np.random.PCG64(SEED + 1)).integers(0, PF_CONFIG["vocab"], size=T).astype(np.int32)
+    d_ids = torch.from_numpy(ids).cuda()
+    logits = torch.empty((T, PF_CONFIG["n_classes"]), dtype=torch.float32, device="cuda")
+    offs = np.array([0, T], np.uint32)
+    tm = Timer(flush=False)  # each forward streams 0.73 GB of weights (> L2)
+
+    def fwd(sp):
+        abi.check(L.ts_cuda_forward_packed_device(h, d_ids.data_ptr(), None, offs.ctypes.data, 1,
+                                                  logits.data_ptr(), sp))
+    reps = max(args.steps, 20)
+    abi.check(L.ts_cuda_profile(h, 0))
+    with ClockSampler(0) as clk:
+        dev_ms = tm.run(fwd, reps, args.warmup)
+    n_launch = ctypes.c_uint64()
+    abi.check(L.ts_cuda_profile_read(h, None, None, None, ctypes.byref(n_launch)))
+    abi.check(L.ts_cuda_check(h, tm.sp))
+    out = np.empty((T, PF_CONFIG["n_classes"]), np.float32)
+    for _ in range(args.warmup):
+        abi.check(L.ts_cuda_forward(h, ids.ctypes.data, None, T, out.ctypes.data))
+    e2e = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        abi.check(L.ts_cuda_forward(h, ids.ctypes.data, None, T, out.ctypes.data))
+        e2e.append(time.perf_counter() - t0)
+    lat = statistics.median(dev_ms)
+    pk = peaks()
+    nbytes = weight_blob_bytes(PF_CONFIG) + T * 370
+    cpu = None
+    if not args.no_cpu_baseline:
+        m = oracle_model(w, PF_CONFIG)
+        m.forward(ids, n_threads=host_cores())
+        modes = cpu_modes(m, ids, T, {"all_cores": 3})
+        cpu = {"value": modes["all_cores"]["tokens_per_s"], "unit": "tokens/s", "cores": host_cores(),
+               "kind": "port", "sample": "the same 1 x 512 forward through the oracle (median of 3 on all cores, "
+                                         "one forward per other mode)", "modes": modes,
+               "latency_ms_all_cores": 1000 * modes["all_cores"]["s_per_chunk"]}
+    line = base_line("config[0]: one sequence of 512 tokens, full model (8 blocks, 128 experts top-4, vocab 200064)",
+                     T / (lat * 1e-3), "tokens/s", args, steps=reps, ms_per_step=lat,
+                     latency_ms={"device_median": lat, "device_min": min(dev_ms), "e2e_median":
+                                 1000 * statistics.median(e2e)},
+                     roofline={"bound": "hbm", "kernel": "whole forward (weight streaming)", "achieved":
+                               nbytes / (lat * 1e-3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                               "frac": nbytes / (lat * 1e-3) / 1e9 / pk["hbm_gbs"], "traffic": None,
+                               "algorithmic_bytes": nbytes,
+                               "note": "every expert is routed to at 1 x 512 (2048 routes over 128 experts), so "
+                                       "one forward reads all weight tiles once: 37 B per row per 64-wide K chunk"},
+                     e2e={"value": T / statistics.median(e2e), "unit": "tokens/s", "h2d_bytes_per_step": T * 4,
+                          "d2h_bytes_per_step": T * PF_CONFIG["n_classes"] * 4},
+                     gpu_launches=int(n_launch.value) // (reps + args.warmup) * reps, clocks=clk.summary(),
+                     cpu_baseline=cpu)
+    emit(line)
+    be.dispose()
+
+
+def run_config1(args):
+    """[1] MatMulNBits alone on the tensor cores (tcgen05, int4 weights
+    dequantised into TMEM, fp16 in and out): M in {128, 1024, 4096, 16384} x
+    N in {640, 1280}, K = 640.  L2 flushed between launches."""
+    import torch
+    from textsift_b200 import abi
+    torch.cuda.set_device(0)
+    L = abi.lib()
+    pk = peaks()
+    K = 640
+    r = np.random.Generator(np.random.PCG64(SEED + 11))
+    tm = Timer(flush=True)
+    rows = []
+    reps = max(args.steps, 20)
+    with ClockSampler(0) as clk:
+        for N in (640, 1280):
+            int4 = r.integers(0, 256, size=(1, N, K // 2), dtype=np.uint8)
+            sc = r.uniform(1e-3, 1e-2, size=(1, N, K // 32)).astype(np.float16).view(np.uint16)
+            zp = np.full((1, N, (K // 32 + 1) // 2), 0x88, np.uint8)
+            bias = np.zeros((1, N), np.uint16)
+            err = ctypes.create_string_buffer(512)
+            h = L.ts_cuda_w4_create(0, int4.ctypes.data, sc.ctypes.data, zp.ctypes.data, bias.ctypes.data, 1, N, K,
+                                    err, 512)
+            if not h:
+                raise RuntimeError(err.value.decode())
+            try:
+                for M in (128, 1024, 4096, 16384):
+                    x = torch.from_numpy(r.normal(0, 1, size=(M, K)).astype(np.float16)).cuda()
+                    y = torch.empty((M, N), dtype=torch.float16, device="cuda")
+
+                    def mm(sp, x=x, y=y, M=M):
+                        abi.check(L.ts_cuda_op_matmul_nbits(h, 0, x.data_ptr(), abi.TS_DTYPE_F16, y.data_ptr(),
+                                                            abi.TS_DTYPE_F16, M, abi.TS_MODE_FAST, sp))
+                    ms = statistics.mean(tm.run(mm, reps, args.warmup))
+                    fl = 2.0 * M * N * K
+                    nbytes = 2 * M * K + N * K // 2 + 2 * N * (K // 32) + N * ((K // 32 + 1) // 2) + 2 * M * N
+                    rows.append({"M": M, "N": N, "ms": ms, "tflops": fl / (ms * 1e-3) / 1e12,
+                                 "tc_frac": fl / (ms * 1e-3) / 1e12 / pk["tflops"],
+                                 "gbs": nbytes / (ms * 1e-3) / 1e9,
+                                 "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]})
+            finally:
+                L.ts_cuda_w4_destroy(h)
+    head = next(x for x in rows if x["M"] == 4096 and x["N"] == 640)
+    big = max(rows, key=lambda x: x["tflops"])
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle
+        oracle.build()
+        M, N = 128, 640
+        int4 = r.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
+        sc = r.uniform(1e-3, 1e-2, size=(N, K // 32)).astype(np.float16).view(np.uint16)
+        zp = np.full((N, (K // 32 + 1) // 2), 0x88, np.uint8)
+        x = r.normal(0, 1, size=(M, K)).astype(np.float16).view(np.uint16)
+        oracle.matmul_int4(x, int4, sc, zp, np.zeros(N, np.uint16), False)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 2.0:
+            oracle.matmul_int4(x, int4, sc, zp, np.zeros(N, np.uint16), False)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        cpu = {"value": 2.0 * M * N * K / dt / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+               "sample": f"M={M}, N={N}, K={K} through the oracle's matmul_int4 (the WASM kernel's tile/tail "
+                         f"order), one thread, {n} calls"}
+    line = base_line("config[1]: MatMulNBits, A fp16 N(0,1) [M, 640], int4 W [N, 640] block 32, fp16 scales "
+                     "U[1e-3,1e-2], zero point 8; headline M=4096, N=640", head["tflops"], "TFLOP/s", args,
+                     steps=reps, ms_per_step=head["ms"], table=rows,
+                     roofline={"bound": "tensor", "kernel": "gemm_w4_tm_kernel (fp16 epilogue)", "achieved":
+                               head["tflops"], "peak": pk["tflops"], "unit": "TFLOP/s", "frac": head["tc_frac"],
+                               "peak_source": f"{pk['source']} bf16 burst (a kernel timed alone)", "traffic": None,
+                               "best": {"M": big["M"], "N": big["N"], "tflops": big["tflops"],
+                                        "frac": big["tc_frac"]}},
+                     l2="flushed between launches (256 MB write outside the timed events)",
+                     clocks=clk.summary(), cpu_baseline=cpu, gpu_launches=reps * len(rows))
+    emit(line)
+
+
+def moe_config_weights(regime: str):
+    """config[2]'s one-layer model: router fp16 N(0, 0.02) stored as the model
+    stores it (int4 MatMulNBits, block 32), uniform or Zipf(1.2) expert
+    popularity through the router bias; experts as config[0]."""
+    from textsift_b200 import make_weights, small_config
+    from textsift_b200.synth import quantize_int4, zipf_router_bias
+    cfg = small_config(n_layers=1, vocab=256)
+    bias = zipf_router_bias(cfg["n_experts"], 1.2, seed=5) if regime == "zipf" else None
+    w = make_weights(cfg, seed=SEED + 21, router_bias=bias)
+    rr = np.random.Generator(np.random.PCG64(SEED + 22))
+    i4, sc, zp = quantize_int4(rr.normal(0, 0.02, size=(cfg["n_experts"], cfg["d_model"])).astype(np.float32))
+    w["layers.0.router.int4"], w["layers.0.router.scales"], w["layers.0.router.zp"] = i4, sc, zp
+    return cfg, w
+
+
+def run_config2(args):
+    """[2] one MoE layer (router + top-4 + permutation + SwiGLU experts +
+    combine) on 16384 tokens, uniform and Zipf(1.2) routing, through
+    ts_cuda_op_moe; L2 flushed between calls."""
+    import torch
+    from textsift_b200 import CudaBackend, abi
+    torch.cuda.set_device(0)
+    L = abi.lib()
+    pk = peaks()
+    T = 16384
+    x = np.random.Generator(np.random.PCG64(SEED + 23)).normal(0, 1, size=(T, 640)).astype(np.float32)
+    dx = torch.from_numpy(x).cuda()
+    out = torch.empty((T, 640), dtype=torch.int16, device="cuda")
+    idx = torch.empty((T, 4), dtype=torch.int32, device="cuda")
+    tm = Timer(flush=True)
+    reps = max(args.steps, 20)
+    res = {}
+    cpu = None
+    with ClockSampler(0) as clk:
+        for regime in ("uniform", "zipf"):
+            cfg, w = moe_config_weights(regime)
+            be = CudaBackend(w, cfg, max_tokens=T, max_seq_len=2048)
+            be.warmup()
+            h = be.handle
+
+            def moe(sp):
+                abi.check(L.ts_cuda_op_moe(h, 0, dx.data_ptr(), out.data_ptr(), idx.data_ptr(), None, T, sp))
+            abi.check(L.ts_cuda_profile(h, 0))
+            ms = statistics.mean(tm.run(moe, reps, args.warmup))
+            abi.check(L.ts_cuda_profile(h, 1))
+            tm.run(moe, reps, 0)
+            ph_ms = (ctypes.c_double * 7)()
+            ph_n = (ctypes.c_uint64 * 7)()
+            ph_fl = (ctypes.c_uint64 * 7)()
+            abi.check(L.ts_cuda_profile_read(h, ph_ms, ph_n, ph_fl, None))
+            abi.check(L.ts_cuda_profile(h, 0))
+            abi.check(L.ts_cuda_check(h, tm.sp))
+            gu, dn = abi.PHASES.index("expert_gate_up"), abi.PHASES.index("expert_down")
+            ro = abi.PHASES.index("router")
+            e_ms = (ph_ms[gu] + ph_ms[dn]) / reps
+            e_fl = (ph_fl[gu] + ph_fl[dn]) / reps
+            hist = np.bincount(idx.cpu().numpy().reshape(-1), minlength=cfg["n_experts"])
+            fl = 2.0 * T * 4 * (2 * 640 * 640 + 640 * 640) + 2.0 * T * 128 * 640
+            res[regime] = {"ms": ms, "tokens_per_s": T / (ms * 1e-3), "tflops": fl / (ms * 1e-3) / 1e12,
+                           "expert_gemm_ms": e_ms, "expert_gemm_tflops": e_fl / (e_ms * 1e-3) / 1e12,
+                           "expert_gemm_frac": e_fl / (e_ms * 1e-3) / 1e12 / pk["tflops"],
+                           "router_ms": ph_ms[ro] / reps,
+                           "routes_per_expert": {"max": int(hist.max()), "min": int(hist.min()),
+                                                 "mean": float(hist.mean()),
+                                                 "top8_share": float(np.sort(hist)[-8:].sum() / hist.sum())}}
+            if regime == "uniform" and not args.no_cpu_baseline:
+                from oracle import oracle
+                oracle.build()
+                om = oracle.OracleModel(cfg, w)
+                n = 2048
+                t0 = time.perf_counter()
+                om.moe(0, x[:n], n_threads=host_cores())
+                dt = time.perf_counter() - t0
+                cpu = {"value": n / dt, "unit": "tokens/s", "cores": host_cores(), "kind": "port",
+                       "sample": f"the first {n} of the 16384 tokens through the oracle's MoE half (router, "
+                                 f"top-4, experts, combine in the WASM order), all {host_cores()} host threads"}
+            be.dispose()
+    u = res["uniform"]
+    line = base_line("config[2]: one MoE layer on 16384 tokens, hidden N(0,1), router N(0,0.02) as int4, "
+                     "128 experts top-4, SwiGLU 640-640-640 int4; uniform and Zipf(1.2) routing",
+                     u["tokens_per_s"], "tokens/s", args, steps=reps, ms_per_step=u["ms"], regimes=res,
+                     roofline={"bound": "tensor", "kernel": "expert GEMMs (gate_up + down), uniform routing",
+                               "achieved": u["expert_gemm_tflops"], "peak": pk["tflops"], "unit": "TFLOP/s",
+                               "frac": u["expert_gemm_frac"], "peak_source": f"{pk['source']} bf16 burst",
+                               "traffic": None,
+                               "zipf": {"achieved": res["zipf"]["expert_gemm_tflops"],
+                                        "frac": res["zipf"]["expert_gemm_frac"]}},
+                     l2="flushed between calls (256 MB write outside the timed events)", clocks=clk.summary(),
+                     cpu_baseline=cpu, e2e=None)
+    emit(line)
+
+
+def run_config3(args):
+    """[3] banded GQA attention alone, 64 sequences x 8192 tokens, 14/2 heads,
+    head_dim 64, window +-128, q/k rotated with the reference's YaRN RoPE
+    (theta 150000), keys masked on the last 10% of every sequence; the
+    tensor-core kernel through ts_cuda_op_attention (no allocation, no
+    synchronize inside).  Inputs 1.2 GB (> L2)."""
+    import torch
+    from textsift_b200 import CudaBackend, abi, make_weights, small_config
+    torch.cuda.set_device(0)
+    L = abi.lib()
+    pk = peaks()
+    B, S, Hq, Hkv, hd, W = 64, 8192, 14, 2, 64, 128
+    T = B * S
+    cfg = small_config(n_layers=1, vocab=256)
+    be = CudaBackend(make_weights(cfg, seed=SEED), cfg, max_tokens=T, max_seq_len=S)
+    be.warmup()
+    h = be.handle
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 3)
+    q0 = torch.randn((T, Hq * hd), generator=g, device="cuda").half()
+    k0 = torch.randn((T, Hkv * hd), generator=g, device="cuda").half()
+    v = torch.randn((T, Hkv * hd), generator=g, device="cuda").half()
+    cs = np.empty((S, hd // 2), np.uint16)
+    sn = np.empty((S, hd // 2), np.uint16)
+    abi.check(L.ts_cuda_rope_tables(h, S, cs.ctypes.data, sn.ctypes.data))
+    dcs, dsn = torch.from_numpy(cs.view(np.int16)).cuda(), torch.from_numpy(sn.view(np.int16)).cuda()
+    pos = torch.arange(S, dtype=torch.int32, device="cuda").repeat(B)
+    q, k = torch.empty_like(q0), torch.empty_like(k0)
+    sp0 = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    abi.check(L.ts_cuda_op_rope(q0.data_ptr(), q.data_ptr(), dcs.data_ptr(), dsn.data_ptr(), pos.data_ptr(), T, Hq, hd,
+                                sp0))
+    abi.check(L.ts_cuda_op_rope(k0.data_ptr(), k.data_ptr(), dcs.data_ptr(), dsn.data_ptr(), pos.data_ptr(), T, Hkv,
+                                hd, sp0))
+    del q0, k0
+    mask = torch.ones((B, S), dtype=torch.uint8, device="cuda")
+    mask[:, int(S * 0.9):] = 0
+    mask = mask.reshape(-1)
+    sinks = torch.zeros(Hq, dtype=torch.float32, device="cuda")
+    out = torch.empty_like(q)
+    offs = (np.arange(B + 1) * S).astype(np.uint32)
+    torch.cuda.synchronize()
+
+    def attn(sp):
+        abi.check(L.ts_cuda_op_attention(h, q.data_ptr(), k.data_ptr(), v.data_ptr(), sinks.data_ptr(),
+                                          mask.data_ptr(), out.data_ptr(), offs.ctypes.data, B, sp))
+    tm = Timer(flush=False)
+    reps = max(args.steps, 20)
+    with ClockSampler(0) as clk:
+        ms_all = tm.run(attn, reps, args.warmup)
+    abi.check(L.ts_cuda_check(h, tm.sp))
+    ms = statistics.mean(ms_all)
+    nk = sum(min(S, t + W + 1) - max(0, t - W) for t in range(S))  # keys per query, summed over a sequence
+    fl = 4.0 * B * Hq * hd * nk
+    nbytes = B * S * (2 * Hq * hd * 2 + 2 * Hkv * hd * 2 + 1)
+    n_exp = B * Hq * (nk + S)  # one exponential per score plus the sink
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle
+        oracle.build()
+        Ts = 2048
+        r = np.random.Generator(np.random.PCG64(SEED + 4))
+        qh = r.normal(0, 1, size=(Ts, Hq * hd)).astype(np.float16).view(np.uint16)
+        kh = r.normal(0, 1, size=(Ts, Hkv * hd)).astype(np.float16).view(np.uint16)
+        vh = r.normal(0, 1, size=(Ts, Hkv * hd)).astype(np.float16).view(np.uint16)
+        mh = np.ones(Ts, np.uint8)
+        sk = np.zeros(Hq, np.float32)
+        cores = host_cores()
+        nth = min(cores, Hq)
+        outs = [None] * nth
+
+        def part(i):
+            h0, h1 = i * Hq // nth, (i + 1) * Hq // nth
+            outs[i] = oracle.banded_attention(qh, kh, vh, sk, mh, Ts, Hq, Hkv, hd, W, h0, h1)
+        t0 = time.perf_counter()
+        ths = [threading.Thread(target=part, args=(i,)) for i in range(nth)]
+        for t_ in ths:
+            t_.start()
+        for t_ in ths:
+            t_.join()
+        dt = time.perf_counter() - t0
+        cpu = {"value": Ts / dt, "unit": "tokens/s", "cores": nth, "kind": "port",
+               "sample": f"one {Ts}-token sequence through the oracle's banded attention (the WASM order), query "
+                         f"heads split over {nth} threads as the reference's MtPool does"}
+    line = base_line(f"config[3]: banded GQA attention, {B} x {S} tokens, {Hq}/{Hkv} heads, head_dim {hd}, window "
+                     f"+-{W}, YaRN RoPE on q/k, keys masked on the last 10% of each sequence", T / (ms * 1e-3),
+                     "tokens/s", args, steps=reps, ms_per_step=ms,
+                     roofline={"bound": "hbm", "kernel": "attn_umma_kernel", "achieved": gbs, "peak": pk["hbm_gbs"],
+                               "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "traffic": None,
+                               "algorithmic_bytes": nbytes,
+                               "tensor": {"achieved": fl / (ms * 1e-3) / 1e12, "peak": pk["tflops"],
+                                          "frac": fl / (ms * 1e-3) / 1e12 / pk["tflops"]},
+                               "exponentials_per_launch": n_exp,
+                               "peak_source": f"{pk['source']} (HBM copy; bf16 burst for the tensor share)"},
+                     l2="inputs 1.2 GB > L2, no flush", clocks=clk.summary(), cpu_baseline=cpu,
+                     gpu_launches=2 * reps)
+    emit(line)
+    be.dispose()
 
 
 def main():
@@ -309,8 +893,11 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=4, choices=[0, 1, 2, 3, 4])
     ap.add_argument("--max-tokens", type=int, default=65536)
-    ap.add_argument("--ref-tokens", type=int, default=128, help="tokens per CPU baseline sample")
+    ap.add_argument("--full-set", action="store_true", help="config[4]: all 8192 documents split over the ranks")
+    ap.add_argument("--no-full-set", action="store_true", help="skip the N=1 all-documents extra measurement")
+    ap.add_argument("--no-exact", action="store_true", help="skip the exact-mode extra measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -320,9 +907,15 @@ def main():
     _OUT_FD = os.dup(1)
     os.dup2(2, 1)
     if args.impl == "reference":
+        if args.config != 4:
+            rank, _, _ = dist_env()
+            if rank == 0:
+                emit({"impl": "reference", "unavailable": "the reference arm is timed on config[4]; configs 0-3 "
+                                                          "carry their CPU baselines in their own lines"})
+            return
         run_reference(args)
     else:
-        run_ours(args)
+        {0: run_config0, 1: run_config1, 2: run_config2, 3: run_config3, 4: run_ours}[args.config](args)
 
 
 if __name__ == "__main__":

