@@ -214,14 +214,14 @@ def cpu_modes(model, ids, unique: int, budget: dict | None = None) -> dict:
 def run_reference(args):
     """The reference arm: textsift's WASM CPU forward cannot run here (no
     JS/WASM runtime); its C restatement (oracle/, same kernels and summation
-    order) runs with every host thread and the reference's token-range / head
-    partitioning, one config[4] chunk (up to 2048 tokens) per step -- the
-    chunks rank 0 of the GPU arm owns, in order."""
+    order) runs with the reference's default worker count and its token-range
+    / head partitioning, one config[4] chunk (up to 2048 tokens) per step --
+    the chunks rank 0 of the GPU arm owns, in order."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
     from textsift_b200 import PF_CONFIG, make_weights
-    cores = host_cores()
+    cores = ref_default_threads(host_cores())
     w = make_weights(PF_CONFIG, seed=SEED)
     m = oracle_model(w, PF_CONFIG)
     chunks = config4_chunks(0, world, N_DOCS_FULL if args.full_set else weak_n_docs(args, world), PF_CONFIG["vocab"],
@@ -243,8 +243,10 @@ def run_reference(args):
             "config": config4_desc(world),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": f"{args.steps} config[4] chunks ({proc} tokens, {uniq} unique document "
-                                       f"tokens) of rank 0's documents, one chunk per step, all {cores} host "
-                                       f"threads"},
+                                       f"tokens) of rank 0's documents, one chunk per step, {cores} threads: the "
+                                       f"reference's default worker count max(2, min(6, cores - 1)) on this "
+                                       f"{host_cores()}-core host, its fastest mode (every worker streams all "
+                                       f"expert weights, so more workers run slower)"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
 
@@ -457,11 +459,13 @@ def config4_cpu_baseline(weights, cfg, max_tokens) -> dict:
     chunks = config4_chunks(0, 1, 64, cfg["vocab"], max_tokens, 64)
     ids, uniq = next((c for c in chunks if c[0].size == 2048), chunks[0])
     m = oracle_model(weights, cfg)
-    modes = cpu_modes(m, ids, uniq, {"all_cores": 2})
-    return {"value": modes["all_cores"]["tokens_per_s"], "unit": "tokens/s", "cores": cores, "kind": "port",
+    modes = cpu_modes(m, ids, uniq, {"reference_default_threads": 2})
+    best = max(modes, key=lambda k: modes[k]["tokens_per_s"])
+    return {"value": modes[best]["tokens_per_s"], "unit": "tokens/s", "cores": modes[best]["threads"],
+            "kind": "port",
             "sample": f"one {ids.size}-token config[4] chunk through the C restatement of the WASM forward "
-                      f"(reference summation order, MtPool partitioning); value = all {cores} host threads",
-            "modes": modes}
+                      f"(reference summation order, MtPool partitioning) in three thread modes on this "
+                      f"{cores}-core host; value = the fastest ({best})", "modes": modes}
 
 
 def config4_line(args, world, ms_max, n_steps, toks_all, processed, toks, ph_ms, ph_n, ph_fl, e2e_value, h2d, d2h,
@@ -595,12 +599,14 @@ def run_config0(args):
     cpu = None
     if not args.no_cpu_baseline:
         m = oracle_model(w, PF_CONFIG)
-        m.forward(ids, n_threads=host_cores())
-        modes = cpu_modes(m, ids, T, {"all_cores": 3})
-        cpu = {"value": modes["all_cores"]["tokens_per_s"], "unit": "tokens/s", "cores": host_cores(),
-               "kind": "port", "sample": "the same 1 x 512 forward through the oracle (median of 3 on all cores, "
-                                         "one forward per other mode)", "modes": modes,
-               "latency_ms_all_cores": 1000 * modes["all_cores"]["s_per_chunk"]}
+        m.forward(ids, n_threads=ref_default_threads(host_cores()))
+        modes = cpu_modes(m, ids, T, {"reference_default_threads": 3})
+        best = max(modes, key=lambda k: modes[k]["tokens_per_s"])
+        cpu = {"value": modes[best]["tokens_per_s"], "unit": "tokens/s", "cores": modes[best]["threads"],
+               "kind": "port", "sample": f"the same 1 x 512 forward through the oracle in three thread modes "
+                                         f"(median of 3 with the reference's default workers, one forward per "
+                                         f"other mode); value = the fastest ({best})", "modes": modes,
+               "latency_ms": 1000 * modes[best]["s_per_chunk"]}
     line = base_line("config[0]: one sequence of 512 tokens, full model (8 blocks, 128 experts top-4, vocab 200064)",
                      T / (lat * 1e-3), "tokens/s", args, steps=reps, ms_per_step=lat,
                      latency_ms={"device_median": lat, "device_min": min(dev_ms), "e2e_median":

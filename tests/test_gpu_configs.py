@@ -5,7 +5,8 @@ launch), with the same tolerances as the per-op tests.
 
   [1] MatMulNBits, A fp16 N(0,1) [M=16384, K=640], N in {640, 1280}
   [2] one MoE layer on 16384 tokens, router N(0, 0.02) quantised to int4,
-      uniform and Zipf(s=1.2)-skewed expert popularity
+      uniform and Zipf(s=1.2)-skewed expert popularity (top-k bit-exact in
+      both modes)
   [3] banded attention, batch 64 x 8192, 14/2 heads, head_dim 64, window
       +-128, RoPE (theta 150000, the reference's YaRN tables) applied to q/k,
       keys masked on the last 10% of every sequence
@@ -92,15 +93,14 @@ def test_config2_moe_layer_16384(moe_case, cuda_lib, mode):
           f"top-8 share {np.sort(hist)[-8:].sum() / hist.sum():.3f}")
     if regime == "zipf":
         assert np.sort(hist)[-8:].sum() / hist.sum() > 0.2  # the skew is real
+    # the router is the reference's on the same f32 input in both modes
+    assert np.array_equal(gidx, ridx)
     if mode == abi.TS_MODE_EXACT:
-        assert np.array_equal(gidx, ridx)
         assert ulp_diff(got, ref).max() <= 1 and (got == ref).mean() > 0.99
     else:
-        same = np.array([set(a) == set(c) for a, c in zip(gidx, ridx)])
-        assert same.mean() >= 0.98, same.mean()
-        e = np.abs(f16(got) - f16(ref))[same]
+        e = np.abs(f16(got) - f16(ref))
         assert e.max() <= 1e-2 * np.abs(f16(ref)).max(), e.max()
-        assert np.sqrt((e ** 2).mean() / (f16(ref)[same] ** 2).mean()) < 3e-3
+        assert np.sqrt((e ** 2).mean() / (f16(ref) ** 2).mean()) < 3e-3
 
 
 # ------------------------------------------------------------------ config[3]

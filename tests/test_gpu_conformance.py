@@ -92,7 +92,7 @@ def test_matmul_int4_fp16_f16(L, golden, mode):
         else:
             # tensor cores (fp16 dequantised operand, f32 accumulation):
             # |err| <= 2e-3 max|y| + 1e-3, as in test_gpu_ops.py
-            e = f16(exp)
+            e = f16(exp).reshape(T, N)
             assert np.abs(f16(got) - e).max() <= 2e-3 * np.abs(e).max() + 1e-3
     finally:
         L.ts_cuda_w4_destroy(h)

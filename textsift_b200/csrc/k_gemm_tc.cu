@@ -52,7 +52,9 @@ struct GemmCfg {
   // f32 [2][BN], decoded bias of the tile; read as float4, so 16-byte aligned
   static constexpr uint32_t OFF_BIAS = (OFF_BAR + NUM_BARS * 8 + 127u) & ~127u;
   static constexpr uint32_t OFF_MISC = OFF_BIAS + 2 * BN * 4;
-  static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+  // f32 [2][kMaxRouterExperts]: the router bound table (kEpiRouterCert)
+  static constexpr uint32_t OFF_RB = OFF_MISC + 16;
+  static constexpr uint32_t SMEM_BYTES = OFF_RB + 2 * kMaxRouterExperts * 4 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;                    // two accumulators
   static constexpr uint32_t ACC_STRIDE = 256;                   // column offset of tile buffer 1
   static constexpr uint32_t ACC_ROWS = BM / 128;                // 128-row accumulators per tile buffer
@@ -157,31 +159,48 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
   }
 }
 
-// Router top-k on the accumulator row of one token (BM = 256: the thread owns
-// all BN = 128 expert columns of its row).  The same selection and weights as
-// router_topk_kernel (wasm_exports.zig:367-426 + 919-958, block.ts:201-206):
-// the top 4 logits in descending order, equal logits in ascending expert
-// order, softmax over them with the exact exponential, each weight scaled by
-// 1/4.  Expert counts go to hist[row / kPermChunk] (the permutation's chunks).
-__device__ __forceinline__ void router_topk_epilogue(const GemmArgs& a, uint32_t acc, uint32_t grow, bool row_ok,
-                                                     const float* sbias, uint64_t* acc_empty) {
+// Router candidates on the accumulator row of one token (BM = 256: the thread
+// owns all BN = 128 expert columns of its row).  The tensor-core logits
+// v_e = acc + bias come from fp16(x) and fp16((q - zp) * s); the reference
+// computes the same dot from f32 x and exact int4 values in its own f32
+// order.  Their difference is at most
+//   B_e = kRouterCertRel * wmax_e * S + add_e + S * 2^-24 + |v_e| * 2^-22,
+// with S = sum |x| of the token (a.absum), wmax_e = max_i |w_ei| and add_e
+// covering the subnormal and bias-decode terms (the per-expert table
+// a.rbound = [wmax_0..wmax_{E-1}, add_0..add_{E-1}], built with the weights).
+// kRouterCertRel = 1.5e-3 bounds 2 * 2^-11 (the two fp16 roundings) plus
+// 2e-4 for the tensor core's f32 accumulation and 2e-6 for the reference's.
+// With tau = min over the approximate top 4 of (v_a - B_a), the exact 4th
+// largest logit is >= tau, so every expert of the exact top 4 satisfies
+// v_e + B_e >= tau: those experts are the candidates written to a.out0 (one
+// uint4 per token: .x = count, .y/.z = up to 8 expert ids as bytes; count
+// 0xFF = more than 8, recompute every expert).  router_cert_kernel then
+// evaluates the candidates in the reference's order and selects exactly.
+constexpr float kRouterCertRel = 1.5e-3f;
+
+__device__ __forceinline__ float router_bound(float cS, float addS, const float* srb, uint32_t e, float v) {
+  return fmaf(cS, srb[e], srb[kMaxRouterExperts + e] + addS + 2.384185791015625e-7f * fabsf(v));
+}
+
+__device__ __forceinline__ void router_cert_epilogue(const GemmArgs& a, uint32_t acc, uint32_t grow, bool row_ok,
+                                                     const float* sbias, const float* srb, uint64_t* acc_empty) {
+  const float S = row_ok ? a.absum[grow] : 0.0f;
+  const float cS = kRouterCertRel * S, addS = 5.9604644775390625e-8f * S;
   float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f, t3 = 0.0f;
   int i0 = -1, i1 = -1, i2 = -1, i3 = -1;
+  bool finite = isfinite(S);
+  // pass 1: the approximate top 4 (value descending, ties to the lower expert)
 #pragma unroll 1
   for (uint32_t c0 = 0; c0 < 128; c0 += 32) {
     uint32_t v[32];
     tmem_ld_32x32b_x32(acc + c0, v);
     tmem_ld_wait();
-    if (c0 == 96) {
-      tc_fence_before();
-      mbar_arrive(acc_empty);
-    }
 #pragma unroll
     for (int j = 0; j < 32; j++) {
       const int c = (int)c0 + j;
       if ((uint32_t)c >= a.N) break;
       const float x = __fadd_rn(__uint_as_float(v[j]), sbias[c]);
-      // strict '>' in ascending column order: equal logits keep the lower expert first
+      finite = finite && isfinite(x);
       if (i3 < 0 || x > t3) {
         if (i2 < 0 || x > t2) {
           t3 = t2; i3 = i2;
@@ -194,21 +213,37 @@ __device__ __forceinline__ void router_topk_epilogue(const GemmArgs& a, uint32_t
       }
     }
   }
+  float tau = t0 - router_bound(cS, addS, srb, (uint32_t)i0, t0);
+  tau = fminf(tau, t1 - router_bound(cS, addS, srb, (uint32_t)i1, t1));
+  tau = fminf(tau, t2 - router_bound(cS, addS, srb, (uint32_t)i2, t2));
+  tau = fminf(tau, t3 - router_bound(cS, addS, srb, (uint32_t)i3, t3));
+  // pass 2: every expert whose logit may reach tau
+  uint32_t n = 0, ids0 = 0, ids1 = 0;
+#pragma unroll 1
+  for (uint32_t c0 = 0; c0 < 128; c0 += 32) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(acc + c0, v);
+    tmem_ld_wait();
+    if (c0 == 96) {
+      // every TMEM read of this buffer by this thread is complete: release it
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const uint32_t c = c0 + (uint32_t)j;
+      if (c >= a.N) break;
+      const float x = __fadd_rn(__uint_as_float(v[j]), sbias[c]);
+      if (x + router_bound(cS, addS, srb, c, x) >= tau) {
+        if (n < 4) ids0 |= c << (8 * n);
+        else if (n < 8) ids1 |= c << (8 * (n - 4));
+        n++;
+      }
+    }
+  }
   if (!row_ok) return;
-  const float e0 = expf_ref(__fsub_rn(t0, t0)), e1 = expf_ref(__fsub_rn(t1, t0));
-  const float e2 = expf_ref(__fsub_rn(t2, t0)), e3 = expf_ref(__fsub_rn(t3, t0));
-  const float sum = __fadd_rn(__fadd_rn(__fadd_rn(e0, e1), e2), e3);
-  const float inv = sum > 0.0f ? __fdiv_rn(1.0f, sum) : __fdiv_rn(1.0f, 4.0f);
-  const double inv_k = 0.25;
-  reinterpret_cast<int4*>(a.out0)[grow] = make_int4(i0, i1, i2, i3);
-  reinterpret_cast<float4*>(a.out1)[grow] =
-      make_float4((float)((double)__fmul_rn(e0, inv) * inv_k), (float)((double)__fmul_rn(e1, inv) * inv_k),
-                  (float)((double)__fmul_rn(e2, inv) * inv_k), (float)((double)__fmul_rn(e3, inv) * inv_k));
-  int* h = a.hist + (size_t)(grow / kPermChunk) * a.N;
-  atomicAdd(h + i0, 1);
-  atomicAdd(h + i1, 1);
-  atomicAdd(h + i2, 1);
-  atomicAdd(h + i3, 1);
+  if (!finite || n > 8) n = 0xFFu;
+  reinterpret_cast<uint4*>(a.out0)[grow] = make_uint4(n, ids0, ids1, 0u);
 }
 
 struct TileInfo {
@@ -392,6 +427,10 @@ __global__ void __launch_bounds__(640, 1)
     const uint32_t r = rh * 128u + quarter * 32u + (uint32_t)lane;
     const uint32_t et = threadIdx.x - 384;  // 0..255 across the 8 epilogue warps
     float* sbias_all = reinterpret_cast<float*>(smem + C::OFF_BIAS);
+    float* srb = reinterpret_cast<float*>(smem + C::OFF_RB);
+    // the router bound table, visible to all epilogue warps once the first
+    // tile's bias barrier below has completed
+    if constexpr (EPI == kEpiRouterCert) srb[et] = args.rbound[et];
     uint32_t lt = 0;
     for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x, lt++) {
       const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;
@@ -412,8 +451,8 @@ __global__ void __launch_bounds__(640, 1)
       const bool row_ok = grow < ti.row_end;
       const uint32_t col_lo = chalf * (BN / 2);
       const uint32_t acc = tmem_base + b * C::ACC_STRIDE + rh * BN + ((quarter * 32u) << 16);
-      if constexpr (EPI == kEpiRouterTopk) {
-        router_topk_epilogue(args, acc, grow, row_ok, sbias, &acc_empty[b]);
+      if constexpr (EPI == kEpiRouterCert) {
+        router_cert_epilogue(args, acc, grow, row_ok, sbias, srb, &acc_empty[b]);
       } else {
 #pragma unroll 1
         for (uint32_t c0 = col_lo; c0 < col_lo + kCols; c0 += 32) {
@@ -608,9 +647,9 @@ cudaError_t launch_gemm_w4_tc(const W4Tiles& w, const CUtensorMap& tmap_a, GemmA
       case kEpiQkvRope: return launch_one<128, 256, kEpiQkvRope>(tmap_a, args, w.n_tiles, grid_m, st);
       case kEpiSwiglu: return launch_one<128, 256, kEpiSwiglu>(tmap_a, args, w.n_tiles, grid_m, st);
       case kEpiF16Widen: return launch_one<128, 256, kEpiF16Widen>(tmap_a, args, w.n_tiles, grid_m, st);
-      case kEpiRouterTopk:
-        if (w.N > 128 || w.n_tiles != 1 || !args.hist) return cudaErrorInvalidValue;
-        return launch_one<128, 256, kEpiRouterTopk>(tmap_a, args, w.n_tiles, grid_m, st);
+      case kEpiRouterCert:
+        if (w.N > kMaxRouterExperts || w.n_tiles != 1 || !args.absum || !args.rbound) return cudaErrorInvalidValue;
+        return launch_one<128, 256, kEpiRouterCert>(tmap_a, args, w.n_tiles, grid_m, st);
     }
   }
   return cudaErrorInvalidValue;

@@ -1,0 +1,323 @@
+// k_router.cu — the fast-mode router, exact on identical inputs.
+//
+// The router logits of the tensor-core GEMM (fp16 operands, f32
+// accumulation) pick, per token, the experts that may belong to the exact top
+// 4 (the kEpiRouterCert epilogue of k_gemm_tc.cu, with a proven bound on the
+// difference to the reference's f32 logits).  router_cert_kernel evaluates
+// exactly those candidates in the reference's order -- matmulInt4BlockImpl's
+// tile or tail path (zig/wasm_exports.zig:560-708) on the f32 router input --
+// and selects the top k from their exact logits with the reference's tie rule
+// (wasm_exports.zig:367-426), then the softmax over k with the exact
+// exponential and x 1/k (wasm_exports.zig:919-958, browser/inference/
+// block.ts:201-206).  Indices and weights are therefore those of the
+// reference on the same f32 input, bit for bit.
+//
+// One thread per token.  The f32 router input is either given (the per-op
+// entry) or rebuilt from the residual and attention output exactly as the
+// fast add+RMSNorm computed it (rmsnorm_fast_kernel<true>): the same lane
+// partial sums of squares, combined in the same butterfly order, the same
+// rsqrtf and the same products.
+#include "ts_common.cuh"
+#include "ts_kernels.h"
+#include "ts_simt.h"
+
+#include <cmath>
+
+namespace ts {
+
+namespace {
+
+constexpr uint32_t kCertThreads = 256;  // tokens per block, inside one permutation chunk
+static_assert(kPermChunk % kCertThreads == 0, "a block's tokens share one permutation chunk");
+constexpr uint32_t kCertMax = 8;         // candidates per token held in registers
+
+// The reference's value of one 32-block: the tile path's four lane chains of
+// eight fused multiply-adds (wasm_exports.zig:615-646) or the tail path's even
+// / odd chunk accumulators (689-697), exactly as matmul_w4_exact_kernel.
+__device__ __forceinline__ float block_dot_ref(const float (&x)[32], const float (&q)[32], bool tile_path) {
+  if (tile_path) {
+    float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      v0 = __fmaf_rn(x[4 * c + 0], q[4 * c + 0], v0);
+      v1 = __fmaf_rn(x[4 * c + 1], q[4 * c + 1], v1);
+      v2 = __fmaf_rn(x[4 * c + 2], q[4 * c + 2], v2);
+      v3 = __fmaf_rn(x[4 * c + 3], q[4 * c + 3], v3);
+    }
+    return __fadd_rn(__fadd_rn(v0, v1), __fadd_rn(v2, v3));
+  }
+  float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int k = 0; k < 4; k++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      a0[j] = __fmaf_rn(x[8 * k + j], q[8 * k + j], a0[j]);
+      a1[j] = __fmaf_rn(x[8 * k + 4 + j], q[8 * k + 4 + j], a1[j]);
+    }
+  const float c0 = __fadd_rn(a0[0], a1[0]), c1 = __fadd_rn(a0[1], a1[1]);
+  const float c2 = __fadd_rn(a0[2], a1[2]), c3 = __fadd_rn(a0[3], a1[3]);
+  return __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
+}
+
+// 32 int4 values of one block minus its zero point, as exact floats: the
+// nibble goes into the mantissa of 2^23 (prmt), then 2^23 + zp is subtracted.
+__device__ __forceinline__ void block_q(uint4 pk, float zp, float (&q)[32]) {
+  const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
+  const float off = 8388608.0f + zp;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const uint32_t lo = wd[i] & 0x0F0F0F0Fu, hi = (wd[i] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      // byte j of the word holds elements 8i + 2j (low nibble) and 8i + 2j + 1
+      q[8 * i + 2 * j] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | (uint32_t)j)) - off;
+      q[8 * i + 2 * j + 1] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | (uint32_t)j)) - off;
+    }
+  }
+}
+
+// (value descending, index ascending) -- the order the reference's strict '>'
+// insertion produces (the rule router_topk_kernel uses).
+__device__ __forceinline__ bool better(float v, int e, float bv, int be) {
+  return be < 0 || v > bv || (v == bv && e < be);
+}
+
+}  // namespace
+
+template <int SRC>
+__global__ void __launch_bounds__(kCertThreads) router_cert_kernel(const RouterCertArgs a) {
+  __shared__ int h[kMaxRouterExperts];
+  pdl_trigger();
+  for (uint32_t i = threadIdx.x; i < a.E; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  pdl_wait();
+  const uint32_t t = blockIdx.x * kCertThreads + threadIdx.x;
+  const uint32_t D = a.D, nb = D / 32, zs = (nb + 1) / 2, K = a.K;
+  if (t < a.T) {
+    const uint4 cd = reinterpret_cast<const uint4*>(a.cand)[t];
+    const bool all = cd.x > kCertMax;
+    const uint32_t n_c = all ? kCertMax : cd.x;
+    uint32_t loc, len;
+    if (a.rloc) { loc = (uint32_t)a.rloc[t]; len = (uint32_t)a.rlen[t]; }
+    else { loc = t; len = a.T; }
+    const bool tile_path = loc < (len & ~7u);
+
+    // the f32 router input: rebuilt with rmsnorm_fast_kernel<true>'s arithmetic
+    float inv_rms = 0.0f;
+    const size_t base = (size_t)t * D;
+    if constexpr (SRC == kRouterSrcAddNorm) {
+      const uint32_t nc = D / 8;
+      float p[32];  // lane l's sum of squares over chunks l, l + 32, l + 64, l + 96
+#pragma unroll
+      for (int l = 0; l < 32; l++) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          const uint32_t c = (uint32_t)l + 32u * r;
+          if (c >= nc) break;
+          const uint4 av = *reinterpret_cast<const uint4*>(a.a + base + 8 * c);
+          const uint4 bv = *reinterpret_cast<const uint4*>(a.b + base + 8 * c);
+          const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
+            const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
+            const float s0 = fa.x + fb.x, s1 = fa.y + fb.y;
+            ss = fmaf(s0, s0, ss);
+            ss = fmaf(s1, s1, ss);
+          }
+        }
+        p[l] = ss;
+      }
+      // the shuffle butterfly: lane l adds lane l ^ o's value to its own
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int l = 0; l < o; l++) p[l] = p[l] + p[l + o];
+      inv_rms = rsqrtf(p[0] / (float)D + a.eps);
+    }
+
+    float ov[kCertMax], sum[kCertMax];
+    int oi[kCertMax];
+#pragma unroll
+    for (uint32_t k = 0; k < kCertMax; k++) { ov[k] = 0.0f; oi[k] = -1; }
+    // candidates in groups of up to 8 (a single group unless every expert is a candidate)
+    for (uint32_t g0 = 0; g0 < (all ? a.E : 1u); g0 += kCertMax) {
+      int ids[kCertMax];
+      uint32_t n = n_c;
+      if (all) {
+        n = min(kCertMax, a.E - g0);
+#pragma unroll
+        for (uint32_t k = 0; k < kCertMax; k++) ids[k] = (int)(g0 + k);
+      } else {
+#pragma unroll
+        for (uint32_t k = 0; k < kCertMax; k++) ids[k] = (int)(((k < 4 ? cd.y : cd.z) >> (8 * (k & 3))) & 0xffu);
+      }
+#pragma unroll
+      for (uint32_t k = 0; k < kCertMax; k++) sum[k] = 0.0f;
+      for (uint32_t b = 0; b < nb; b++) {
+        float x[32];
+        if constexpr (SRC == kRouterSrcAddNorm) {
+#pragma unroll
+          for (int cc = 0; cc < 4; cc++) {
+            const size_t o = base + 32 * b + 8 * cc;
+            const uint4 av = *reinterpret_cast<const uint4*>(a.a + o);
+            const uint4 bv = *reinterpret_cast<const uint4*>(a.b + o);
+            const uint4 gv = *reinterpret_cast<const uint4*>(a.gamma + 32 * b + 8 * cc);
+            const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
+              const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
+              const uint32_t sw = f32x2_to_h2(fa.x + fb.x, fa.y + fb.y);
+              const float2 xs = __half22float2(*reinterpret_cast<const __half2*>(&sw));
+              const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
+              x[8 * cc + 2 * j] = xs.x * inv_rms * g.x;
+              x[8 * cc + 2 * j + 1] = xs.y * inv_rms * g.y;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c4 = 0; c4 < 8; c4++) {
+            const float4 v = *reinterpret_cast<const float4*>(a.x32 + base + 32 * b + 4 * c4);
+            x[4 * c4] = v.x; x[4 * c4 + 1] = v.y; x[4 * c4 + 2] = v.z; x[4 * c4 + 3] = v.w;
+          }
+        }
+#pragma unroll
+        for (uint32_t k = 0; k < kCertMax; k++) {
+          if (k >= n) break;
+          const uint32_t e = (uint32_t)ids[k];
+          const float scale = f16_ref_to_f32(a.w_scales[(size_t)e * nb + b]);
+          int zp = 0;
+          if (a.w_zp) {
+            const uint8_t zb = a.w_zp[(size_t)e * zs + (b >> 1)];
+            zp = (b & 1) ? (zb >> 4) & 15 : zb & 15;
+          }
+          float q[32];
+          block_q(*reinterpret_cast<const uint4*>(a.w_int4 + (size_t)e * (D / 2) + 16 * b), (float)zp, q);
+          sum[k] = __fadd_rn(sum[k], __fmul_rn(block_dot_ref(x, q, tile_path), scale));
+        }
+      }
+      // merge this group into the top k (insertion, kept sorted)
+#pragma unroll
+      for (uint32_t k = 0; k < kCertMax; k++) {
+        if (k >= n) break;
+        const int e = ids[k];
+        float v = __fadd_rn(sum[k], f16_ref_to_f32(a.bias[e]));
+        int ve = e;
+#pragma unroll
+        for (uint32_t s = 0; s < kCertMax; s++) {
+          if (s >= K) break;
+          if (better(v, ve, ov[s], oi[s])) {
+            const float tv = ov[s];
+            const int ti = oi[s];
+            ov[s] = v; oi[s] = ve;
+            v = tv; ve = ti;
+            if (ve < 0) break;
+          }
+        }
+      }
+    }
+    // softmax over the k values in order (wasm_exports.zig:919-958), x 1/k in double
+    float m = ov[0];
+#pragma unroll
+    for (uint32_t c = 1; c < kCertMax; c++)
+      if (c < K && ov[c] > m) m = ov[c];
+    float ex[kCertMax], s = 0.0f;
+#pragma unroll
+    for (uint32_t c = 0; c < kCertMax; c++) {
+      ex[c] = c < K ? expf_ref(__fsub_rn(ov[c], m)) : 0.0f;
+      if (c < K) s = __fadd_rn(s, ex[c]);
+    }
+    const float inv = s > 0.0f ? __fdiv_rn(1.0f, s) : __fdiv_rn(1.0f, (float)K);
+    const double inv_k = 1.0 / (double)K;
+#pragma unroll
+    for (uint32_t c = 0; c < kCertMax; c++) {
+      if (c >= K) break;
+      a.idx[(size_t)t * K + c] = oi[c];
+      a.w[(size_t)t * K + c] = (float)((double)__fmul_rn(ex[c], inv) * inv_k);
+      if (oi[c] >= 0) atomicAdd(&h[oi[c]], 1);
+    }
+  }
+  __syncthreads();
+  if (a.hist) {
+    int* row = a.hist + (size_t)(blockIdx.x * kCertThreads / kPermChunk) * a.E;
+    for (uint32_t i = threadIdx.x; i < a.E; i += blockDim.x)
+      if (h[i]) atomicAdd(row + i, h[i]);
+  }
+}
+
+// One warp per row: fp16 round-to-nearest copy of an f32 row and the sum of
+// its absolute values (the bound's S for the router candidates).
+__global__ void __launch_bounds__(256) f32_to_f16_absum_kernel(const float* __restrict__ x, uint16_t* __restrict__ y,
+                                                               float* __restrict__ absum, uint32_t T, uint32_t D) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  float s = 0.0f;
+  for (uint32_t i = (uint32_t)lane * 2; i < D; i += 64) {
+    const float2 v = *reinterpret_cast<const float2*>(x + (size_t)row * D + i);
+    s += fabsf(v.x) + fabsf(v.y);
+    *reinterpret_cast<uint32_t*>(y + (size_t)row * D + i) = f32x2_to_h2(v.x, v.y);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) absum[row] = s;
+}
+
+cudaError_t launch_router_cert(const RouterCertArgs& a, int src, cudaStream_t st) {
+  if (a.T == 0) return cudaSuccess;
+  if (a.E > kMaxRouterExperts || a.K == 0 || a.K > kCertMax || a.D % 32 || a.D > 1024) return cudaErrorInvalidValue;
+  const dim3 grid((a.T + kCertThreads - 1) / kCertThreads);
+  if (src == kRouterSrcAddNorm) return launch_pdl(router_cert_kernel<kRouterSrcAddNorm>, grid, dim3(kCertThreads), 0, st, a);
+  return launch_pdl(router_cert_kernel<kRouterSrcF32>, grid, dim3(kCertThreads), 0, st, a);
+}
+
+cudaError_t launch_f32_to_f16_absum(const float* x, uint16_t* y, float* absum, uint32_t T, uint32_t D,
+                                    cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (D % 2) return cudaErrorInvalidValue;
+  return launch_pdl(f32_to_f16_absum_kernel, dim3((T + 7) / 8), dim3(256), 0, st, x, y, absum, T, D);
+}
+
+// Host: the bound table of a router weight in reference layout (int4 [E][D/2],
+// fp16 scales [E][D/32], zero points [E][ceil(D/64)] or none, fp16 bias [E]):
+// out[e] = max_i |w_ei| and out[kMaxRouterExperts + e] = sum_i |w_ei| * 2^-24
+// + 1e-6, with |w_ei| = |q - zp| * |scale| and the scale decoded both ways
+// (IEEE and the reference's subnormal quirk), taking the larger.
+void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8_t* zp, uint32_t E, uint32_t D,
+                        float* out) {
+  const uint32_t nb = D / 32, zs = (nb + 1) / 2;
+  for (uint32_t i = 0; i < 2 * kMaxRouterExperts; i++) out[i] = 0.0f;
+  for (uint32_t e = 0; e < E && e < kMaxRouterExperts; e++) {
+    double wmax = 0.0, wsum = 0.0;
+    for (uint32_t b = 0; b < nb; b++) {
+      const uint16_t s16 = scales[(size_t)e * nb + b];
+      const uint32_t mant = s16 & 0x3ffu, ex = (s16 >> 10) & 0x1fu;
+      double ieee = ex == 0 ? std::ldexp((double)mant, -24) : std::ldexp(1.0 + mant / 1024.0, (int)ex - 15);
+      if (ex == 31) ieee = INFINITY;
+      // the reference's decode (math.zig:45-52): a subnormal is read as if normal
+      const double quirk = ex == 0 && mant ? std::ldexp(1.0 + mant / 1024.0, -15) : ieee;
+      const double sc = std::fmax(ieee, quirk);
+      int z = 0;
+      if (zp) {
+        const uint8_t zb = zp[(size_t)e * zs + (b >> 1)];
+        z = (b & 1) ? (zb >> 4) & 15 : zb & 15;
+      }
+      for (uint32_t i = 0; i < 32; i++) {
+        const uint8_t byte = int4[(size_t)e * (D / 2) + 16 * b + i / 2];
+        const int qv = (i & 1) ? (byte >> 4) & 15 : byte & 15;
+        const double w = std::fabs((double)(qv - z)) * sc;
+        wmax = std::fmax(wmax, w);
+        wsum += w;
+      }
+    }
+    out[e] = (float)(wmax * (1.0 + 1e-6));
+    out[kMaxRouterExperts + e] = (float)(wsum * std::ldexp(1.0, -24) + 1e-6);
+  }
+}
+
+}  // namespace ts

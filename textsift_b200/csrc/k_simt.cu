@@ -611,7 +611,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
                                                            const uint16_t* __restrict__ gamma,
                                                            uint16_t* __restrict__ sum_out,
                                                            uint16_t* __restrict__ out16, uint32_t T, uint32_t D,
-                                                           float eps) {
+                                                           float eps, float* __restrict__ absum) {
   pdl_trigger();
   pdl_wait();
   const int lane = threadIdx.x & 31;
@@ -655,6 +655,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float inv_rms = rsqrtf(ss / (float)D + eps);
+  float as = 0.0f;  // sum of |normalised value| (the router's error bound, k_router.cu)
 #pragma unroll
   for (int r = 0; r < 4; r++) {
     const uint32_t c = (uint32_t)lane + 32u * r;
@@ -666,9 +667,16 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
     for (int j = 0; j < 4; j++) {
       const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&xw[j]));
       const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
-      ow[j] = f32x2_to_h2(x.x * inv_rms * g.x, x.y * inv_rms * g.y);
+      const float n0 = x.x * inv_rms * g.x, n1 = x.y * inv_rms * g.y;
+      as += fabsf(n0) + fabsf(n1);
+      ow[j] = f32x2_to_h2(n0, n1);
     }
     *reinterpret_cast<uint4*>(out16 + base + 8 * c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  }
+  if (absum) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) as += __shfl_xor_sync(0xffffffffu, as, o);
+    if (lane == 0) absum[row] = as;
   }
 }
 
@@ -1008,13 +1016,15 @@ cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uin
 }
 
 cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
-                                uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st) {
+                                uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st, float* absum) {
   if (T == 0) return cudaSuccess;
   if (D % 8 || D > 1024 || !out16 || (b && !sum_out)) return cudaErrorInvalidValue;
   const uint32_t blocks = (T + 7) / 8;
-  if (b) return launch_pdl(rmsnorm_fast_kernel<true>, dim3(blocks), dim3(256), 0, st, a, b, gamma, sum_out, out16, T, D, eps);
+  if (b)
+    return launch_pdl(rmsnorm_fast_kernel<true>, dim3(blocks), dim3(256), 0, st, a, b, gamma, sum_out, out16, T, D, eps,
+                      absum);
   return launch_pdl(rmsnorm_fast_kernel<false>, dim3(blocks), dim3(256), 0, st, a, (const uint16_t*)nullptr, gamma,
-                    (uint16_t*)nullptr, out16, T, D, eps);
+                    (uint16_t*)nullptr, out16, T, D, eps, absum);
 }
 
 cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,

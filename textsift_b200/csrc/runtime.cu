@@ -195,6 +195,7 @@ struct LayerDev {
   DevArr<uint16_t> ln1, ln2;
   DevArr<float> sinks;
   W4Dev qkv, o, router, gate_up, down;
+  DevArr<float> rbound;  // the router's bound table (ts::router_bound_table), E <= kMaxRouterExperts
 };
 
 struct Workspace {
@@ -208,6 +209,8 @@ struct Workspace {
   DevArr<int32_t> ridx;
   DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, n_tiles_tc, hist;
   DevArr<int4> tiles, tiles_tc;  // 128-row tiles (exact path), gemm_tm_rows()-row tiles (tensor cores)
+  DevArr<int4> rcand;            // router candidates per token (kEpiRouterCert)
+  DevArr<float> absum;           // sum |x| of each token's router input
   DevArr<int2> atiles;
   DevArr<uint16_t> aperm16, glu16;
   DevArr<float> aperm32, gu32, glu32, down32;
@@ -356,6 +359,8 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.n32.alloc(T * D));
     TS_CUDA_TRY(w.rlogits.alloc(T * E));
     TS_CUDA_TRY(w.ridx.alloc(R));
+    TS_CUDA_TRY(w.rcand.alloc(T));
+    TS_CUDA_TRY(w.absum.alloc(T));
     TS_CUDA_TRY(w.rw.alloc(R));
     TS_CUDA_TRY(w.counts.alloc(E));
     TS_CUDA_TRY(w.hist.alloc((size_t)ts::route_chunks((uint32_t)T) * E));
@@ -432,8 +437,31 @@ struct Phase {
 // combine.  res == nullptr writes the bare MoE output fp16(K * sum w e(x)).
 // next_gamma (fast mode) fuses the next RMSNorm into the combine: xn16 then
 // holds RMSNorm(out) * next_gamma on return.
+// Where the fast router's exact candidate pass reads its f32 input: given
+// (x32) or rebuilt from the block's residual a, attention output b and norm
+// weight gamma; absum = each token's sum |x| from the kernel that made xn16.
+struct RouterIn {
+  int src = ts::kRouterSrcF32;
+  const float* x32 = nullptr;
+  const uint16_t *a = nullptr, *b = nullptr, *gamma = nullptr;
+  const float* absum = nullptr;
+};
+
+ts::RouterCertArgs router_cert_args(ts_cuda* h, const LayerDev& L, const RouterIn& rin, const int* rloc,
+                                    const int* rlen, int32_t* idx, float* wt, int* hist, uint32_t T) {
+  const ts_cuda_cfg& c = h->cfg;
+  ts::RouterCertArgs a;
+  a.cand = reinterpret_cast<const uint8_t*>(h->ws.rcand.p);
+  a.x32 = rin.x32; a.a = rin.a; a.b = rin.b; a.gamma = rin.gamma; a.eps = c.eps;
+  a.w_int4 = L.router.int4.p; a.w_scales = L.router.scales.p; a.w_zp = L.router.has_zp ? L.router.zp.p : nullptr;
+  a.bias = L.router.bias.p;
+  a.rloc = rloc; a.rlen = rlen; a.idx = idx; a.w = wt; a.hist = hist;
+  a.T = T; a.D = c.d_model; a.E = c.n_experts; a.K = c.top_k;
+  return a;
+}
+
 int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, const uint16_t* res, uint16_t* out,
-             uint32_t T, const int* rloc, const int* rlen, bool exact, cudaStream_t st, int layer,
+             uint32_t T, const int* rloc, const int* rlen, bool exact, cudaStream_t st, int layer, const RouterIn& rin,
              const uint16_t* next_gamma = nullptr) {
   Workspace& w = h->ws;
   const ts_cuda_cfg& c = h->cfg;
@@ -444,8 +472,8 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
   ts::ExactArgs ra = L.router.exact();
   ra.x = n32; ra.ldx = D; ra.M = T; ra.rloc = rloc; ra.rlen = rlen; ra.out = w.rlogits.p; ra.ldo = E;
   {
-    // kernels: logits GEMM (+ top-k kernel unless fused) + 2 permutation kernels
-    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, (!exact && K == 4 && E <= 128) ? 3 : 4);
+    // kernels: logits GEMM, top-k (or the exact candidate pass), 2 permutation kernels
+    Phase p(h, st, TS_PHASE_ROUTER, 2ull * T * E * D, 4);
     if (exact) {
       TS_K(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
     } else {
@@ -454,12 +482,16 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
       if (!ts::make_act_tmap(&tx, xn16, T, D)) return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed (router)");
       ts::GemmArgs gr;
       gr.M = T; gr.err = h->err.p;
-      if (K == 4 && E <= 128) {
-        // top-k and the permutation's expert counts in the GEMM epilogue; the
-        // counts start from zero (the forward or the op zeroes them once, and
+      if (K == 4 && E <= ts::kMaxRouterExperts && rin.absum) {
+        // candidates of the exact top 4 from the tensor-core logits, then the
+        // candidates in the reference's order: the reference's top-k and
+        // weights on the same f32 input.  The permutation's expert counts
+        // start from zero (the forward or the op zeroes them once, and
         // moe_place zeroes each chunk's row after consuming it)
-        gr.out0 = w.ridx.p; gr.out1 = w.rw.p; gr.hist = w.hist.p;
-        TS_K(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiRouterTopk, (T + 127) / 128, st));
+        gr.out0 = w.rcand.p; gr.absum = rin.absum; gr.rbound = L.rbound.p;
+        TS_K(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiRouterCert, (T + 127) / 128, st));
+        TS_K(ts::launch_router_cert(router_cert_args(h, L, rin, rloc, rlen, w.ridx.p, w.rw.p, w.hist.p, T), rin.src,
+                                    st));
       } else {
         gr.out0 = w.rlogits.p; gr.ld0 = E;
         TS_K(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiF32, (T + 127) / 128, st));
@@ -628,7 +660,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
       }
       {
         Phase p(h, st, TS_PHASE_OTHER, 0, 1);
-        TS_K(ts::launch_rmsnorm_fast(src, w.o16.p, L.ln2.p, w.res2.p, w.xn16.p, T, D, c.eps, st));
+        TS_K(ts::launch_rmsnorm_fast(src, w.o16.p, L.ln2.p, w.res2.p, w.xn16.p, T, D, c.eps, st, w.absum.p));
       }
     } else {
       Phase p(h, st, TS_PHASE_OTHER, fl_qkv + fl_o + fl_attn, 6);
@@ -646,7 +678,9 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
       TS_K(ts::launch_add_rmsnorm(src, w.o16.p, L.ln2.p, w.res2.p, w.n32.p, nullptr, T, D, c.eps, st));
     }
     const uint16_t* next_gamma = exact ? nullptr : li + 1 < c.n_layers ? h->layers[li + 1]->ln1.p : h->final_norm.p;
-    rc = moe_half(h, L, w.n32.p, w.xn16.p, w.res2.p, dst, T, w.pos.p, w.slen.p, exact, st, (int)li, next_gamma);
+    RouterIn rin;  // fast mode: the router input rebuilt from the block's add + RMSNorm
+    rin.src = ts::kRouterSrcAddNorm; rin.a = src; rin.b = w.o16.p; rin.gamma = L.ln2.p; rin.absum = w.absum.p;
+    rc = moe_half(h, L, w.n32.p, w.xn16.p, w.res2.p, dst, T, w.pos.p, w.slen.p, exact, st, (int)li, rin, next_gamma);
     if (rc) return rc;
     std::swap(src, dst);
   }
@@ -837,6 +871,12 @@ int ts_cuda_finalize(ts_cuda_t* h) {
         (rc = w4_upload(L->down, p8(p + "experts.down.int4"), p16(p + "experts.down.scales"),
                         p8(p + "experts.down.zp"), p16(p + "experts.down.bias"), E, D, F, 128, true, bad.p, st)))
       return rc;
+    if (E <= ts::kMaxRouterExperts) {
+      std::vector<float> tb(2 * ts::kMaxRouterExperts);
+      ts::router_bound_table(p8(p + "router.int4"), p16(p + "router.scales"), p8(p + "router.zp"), E, D, tb.data());
+      TS_CUDA_TRY(L->rbound.alloc(tb.size()));
+      TS_CUDA_TRY(cudaMemcpy(L->rbound.p, tb.data(), tb.size() * 4, cudaMemcpyHostToDevice));
+    }
     h->layers.push_back(std::move(L));
   }
   std::vector<uint16_t> cs, sn;
@@ -1181,19 +1221,21 @@ int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32
   if (rc) return rc;
   const ts_cuda_cfg& c = h->cfg;
   if (T == 0) return TS_OK;
-  if (c.mode != TS_MODE_EXACT && c.top_k == 4 && c.n_experts <= 128) {
-    // fast mode, as the forward runs it: fp16 operand, tensor-core logits,
-    // top-k in the GEMM epilogue
+  if (c.mode != TS_MODE_EXACT && c.top_k == 4 && c.n_experts <= ts::kMaxRouterExperts) {
+    // fast mode, as the forward runs it: tensor-core logits from fp16(x)
+    // name the candidates, which are then evaluated in the reference's order
     Workspace& w = h->ws;
-    TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, w.xn16.p, (size_t)T * c.d_model, st));
+    TS_CUDA_TRY(ts::launch_f32_to_f16_absum(d_x, w.xn16.p, w.absum.p, T, c.d_model, st));
     CUtensorMap tx;
     if (!ts::make_act_tmap(&tx, w.xn16.p, T, c.d_model)) return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed (router)");
-    TS_CUDA_TRY(cudaMemsetAsync(w.hist.p, 0, (size_t)ts::route_chunks(T) * c.n_experts * sizeof(int), st));
+    const LayerDev& L = *h->layers[layer];
     ts::GemmArgs gr;
-    gr.M = T; gr.err = h->err.p; gr.out0 = w.ridx.p; gr.out1 = w.rw.p; gr.hist = w.hist.p;
-    TS_CUDA_TRY(ts::launch_gemm_w4_tc(h->layers[layer]->router.tiles(), tx, gr, ts::kEpiRouterTopk, (T + 127) / 128, st));
-    TS_CUDA_TRY(cudaMemcpyAsync(d_idx, w.ridx.p, (size_t)T * 4 * 4, cudaMemcpyDeviceToDevice, st));
-    TS_CUDA_TRY(cudaMemcpyAsync(d_w, w.rw.p, (size_t)T * 4 * 4, cudaMemcpyDeviceToDevice, st));
+    gr.M = T; gr.err = h->err.p; gr.out0 = w.rcand.p; gr.absum = w.absum.p; gr.rbound = L.rbound.p;
+    TS_CUDA_TRY(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiRouterCert, (T + 127) / 128, st));
+    RouterIn rin;
+    rin.x32 = d_x; rin.absum = w.absum.p;
+    TS_CUDA_TRY(ts::launch_router_cert(router_cert_args(h, L, rin, nullptr, nullptr, d_idx, d_w, nullptr, T),
+                                       ts::kRouterSrcF32, st));
     return TS_OK;
   }
   ts::ExactArgs ra = h->layers[layer]->router.exact();
@@ -1215,10 +1257,12 @@ int ts_cuda_op_moe(ts_cuda_t* h, uint32_t layer, const float* d_x, uint16_t* d_o
   int rc = ensure_workspace(h, exact);
   if (rc) return rc;
   const ts_cuda_cfg& c = h->cfg;
-  if (!exact) TS_CUDA_TRY(ts::launch_f32_to_f16(d_x, h->ws.xn16.p, (size_t)T * c.d_model, st));
+  if (!exact) TS_CUDA_TRY(ts::launch_f32_to_f16_absum(d_x, h->ws.xn16.p, h->ws.absum.p, T, c.d_model, st));
   // both top-k paths add expert counts into zeroed permutation rows
   TS_CUDA_TRY(cudaMemsetAsync(h->ws.hist.p, 0, (size_t)ts::route_chunks(T) * c.n_experts * sizeof(int), st));
-  rc = moe_half(h, *h->layers[layer], d_x, h->ws.xn16.p, nullptr, d_out, T, nullptr, nullptr, exact, st, -1);
+  RouterIn rin;  // the router input is the given f32 x
+  rin.x32 = d_x; rin.absum = h->ws.absum.p;
+  rc = moe_half(h, *h->layers[layer], d_x, h->ws.xn16.p, nullptr, d_out, T, nullptr, nullptr, exact, st, -1, rin);
   if (rc) return rc;
   if (d_idx) TS_CUDA_TRY(cudaMemcpyAsync(d_idx, h->ws.ridx.p, (size_t)T * c.top_k * 4, cudaMemcpyDeviceToDevice, st));
   if (d_w) TS_CUDA_TRY(cudaMemcpyAsync(d_w, h->ws.rw.p, (size_t)T * c.top_k * 4, cudaMemcpyDeviceToDevice, st));

@@ -54,9 +54,12 @@ enum GemmEpi : int {
   kEpiQkvRope = 2, // q/k with the reference's 3-rounding RoPE, v plain (fp16)
   kEpiSwiglu = 3,  // out0 fp16 [row][N/2] = f16(swiglu(gate, up))
   kEpiF16Widen = 4,  // out0 f32 [row][ld0] = f32(f16(acc + bias)) (logits, wasm.ts:776-797)
-  kEpiRouterTopk = 5,  // router logits -> top-4 experts: out0 int32 [row][4] ids, out1 f32 [row][4]
-                       // weights, hist [row / 128][N] += 1 per route (block.ts:201-206)
+  kEpiRouterCert = 5,  // router logits -> candidate experts of the exact top 4: out0 uint4 [row]
+                       // {count, ids 0-3, ids 4-7, 0} (count 0xFF: all experts); needs absum, rbound
 };
+
+// Largest expert count of the certified router path (one 128-column tile).
+constexpr uint32_t kMaxRouterExperts = 128;
 
 struct GemmArgs {
   const uint8_t* wblob = nullptr;
@@ -75,7 +78,8 @@ struct GemmArgs {
   const uint16_t* rope_cos = nullptr;
   const uint16_t* rope_sin = nullptr;
   const uint32_t* rope_cs = nullptr;  // kEpiQkvRope (launch_gemm_w4_tm): cos | sin << 16, [pos][32]
-  int* hist = nullptr;               // kEpiRouterTopk: per 128-row chunk expert counts (zeroed)
+  const float* absum = nullptr;      // kEpiRouterCert: sum |x| of each row's f32 input
+  const float* rbound = nullptr;     // kEpiRouterCert: f32 [2][kMaxRouterExperts] wmax_e, add_e
   int* err = nullptr;
 };
 

@@ -69,7 +69,8 @@ cudaError_t launch_viterbi(const float* logits, const int* offs_dev, uint32_t n_
 // Fast mode: RMSNorm (b != nullptr: of a + b, the sum written to sum_out)
 // to fp16, any summation order; MoE combine from fp16 expert outputs.
 cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
-                                uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st);
+                                uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st,
+                                float* absum = nullptr);
 // With norm_gamma set it also writes norm_out = RMSNorm(out) * norm_gamma, the
 // same bits as launch_rmsnorm_fast on out (D <= 1024).
 cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,
@@ -117,6 +118,40 @@ uint32_t attention_max_tiles(uint32_t T, uint32_t n_seqs);
 uint32_t attention_tile_rows();
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t st);     // mma.sync tensor-core path
 cudaError_t launch_attention_exact(const AttnArgs& a, cudaStream_t st);  // reference-order CUDA-core path
+
+// The certified fast-mode router (k_router.cu): exact top-k over the
+// candidates the kEpiRouterCert GEMM epilogue leaves.
+enum RouterSrc : int {
+  kRouterSrcF32 = 0,      // the f32 router input is given (x32)
+  kRouterSrcAddNorm = 1,  // rebuilt as rmsnorm_fast_kernel<true>(a + b) * gamma computes it
+};
+struct RouterCertArgs {
+  const uint8_t* cand = nullptr;   // uint4 per token from the kEpiRouterCert epilogue
+  const float* x32 = nullptr;      // kRouterSrcF32: [T, D]
+  const uint16_t* a = nullptr;     // kRouterSrcAddNorm: residual fp16 [T, D]
+  const uint16_t* b = nullptr;     //   attention output fp16 [T, D]
+  const uint16_t* gamma = nullptr; //   norm weight fp16 [D]
+  float eps = 0.0f;
+  // the router weight in reference layout: int4 [E][D/2], fp16 scales
+  // [E][D/32], zero points [E][ceil(D/64)] (or null), fp16 bias [E]
+  const uint8_t* w_int4 = nullptr;
+  const uint16_t* w_scales = nullptr;
+  const uint8_t* w_zp = nullptr;
+  const uint16_t* bias = nullptr;
+  const int* rloc = nullptr;  // token position / sequence length (tile or tail path); null: row t of T
+  const int* rlen = nullptr;
+  int32_t* idx = nullptr;     // [T, K]
+  float* w = nullptr;         // [T, K]
+  int* hist = nullptr;        // per-permutation-chunk expert counts (or null)
+  uint32_t T = 0, D = 0, E = 0, K = 0;
+};
+cudaError_t launch_router_cert(const RouterCertArgs& a, int src, cudaStream_t st);
+// fp16 copy of f32 rows and each row's sum of |x| (the router bound's S).
+cudaError_t launch_f32_to_f16_absum(const float* x, uint16_t* y, float* absum, uint32_t T, uint32_t D, cudaStream_t st);
+// Host: the router's bound table, f32 [2][kMaxRouterExperts] (max |w| per
+// expert, then the additive term per expert).
+void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8_t* zp, uint32_t E, uint32_t D,
+                        float* out);
 
 // Sets the calling thread's message returned by ts_cuda_last_error().
 void set_last_error(const char* msg);
