@@ -84,8 +84,9 @@ def test_router_topk_bit_exact(small_backend, small_oracle, cuda_lib, mode, T):
             _, ridx, rw = small_oracle.moe(layer, x)
             assert np.array_equal(host(idx, np.int32), ridx)
             # weights: softmax over 4 with exp -> the kernel's correctly
-            # rounded exp vs the C library's expf may differ by an ulp
-            assert f32_ulps(host(w, np.float32), rw).max() <= 1
+            # rounded exp vs the C library's expf differ by an ulp at most,
+            # which the normalisation can carry to 2 ulps of a weight
+            assert f32_ulps(host(w, np.float32), rw).max() <= 2
     finally:
         small_backend.set_mode(abi.TS_MODE_FAST)
 

@@ -172,10 +172,9 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
 // 2e-4 for the tensor core's f32 accumulation and 2e-6 for the reference's.
 // With tau = min over the approximate top 4 of (v_a - B_a), the exact 4th
 // largest logit is >= tau, so every expert of the exact top 4 satisfies
-// v_e + B_e >= tau: those experts are the candidates written to a.out0 (one
-// uint4 per token: .x = count, .y/.z = up to 8 expert ids as bytes; count
-// 0xFF = more than 8, recompute every expert).  router_cert_kernel then
-// evaluates the candidates in the reference's order and selects exactly.
+// v_e + B_e >= tau: those experts are the candidates written to a.out0 (a
+// 32-byte record per token).  router_cert_kernel then evaluates the
+// candidates in the reference's order and selects exactly.
 constexpr float kRouterCertRel = 1.5e-3f;
 
 __device__ __forceinline__ float router_bound(float cS, float addS, const float* srb, uint32_t e, float v) {
@@ -217,8 +216,10 @@ __device__ __forceinline__ void router_cert_epilogue(const GemmArgs& a, uint32_t
   tau = fminf(tau, t1 - router_bound(cS, addS, srb, (uint32_t)i1, t1));
   tau = fminf(tau, t2 - router_bound(cS, addS, srb, (uint32_t)i2, t2));
   tau = fminf(tau, t3 - router_bound(cS, addS, srb, (uint32_t)i3, t3));
-  // pass 2: every expert whose logit may reach tau
-  uint32_t n = 0, ids0 = 0, ids1 = 0;
+  // pass 2: every expert whose logit may reach tau, as a 32-byte record:
+  // byte 0 = the count, bytes 1..31 = expert ids (count 0xFF: more than 31,
+  // or a value that is not finite -- every expert is then a candidate)
+  uint32_t n = 0, rec[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll 1
   for (uint32_t c0 = 0; c0 < 128; c0 += 32) {
     uint32_t v[32];
@@ -235,15 +236,20 @@ __device__ __forceinline__ void router_cert_epilogue(const GemmArgs& a, uint32_t
       if (c >= a.N) break;
       const float x = __fadd_rn(__uint_as_float(v[j]), sbias[c]);
       if (x + router_bound(cS, addS, srb, c, x) >= tau) {
-        if (n < 4) ids0 |= c << (8 * n);
-        else if (n < 8) ids1 |= c << (8 * (n - 4));
         n++;
+        if (n < 32) {
+#pragma unroll
+          for (uint32_t q = 0; q < 8; q++)
+            if (q == (n >> 2)) rec[q] |= c << (8 * (n & 3u));
+        }
       }
     }
   }
   if (!row_ok) return;
-  if (!finite || n > 8) n = 0xFFu;
-  reinterpret_cast<uint4*>(a.out0)[grow] = make_uint4(n, ids0, ids1, 0u);
+  rec[0] |= (!finite || n > 31) ? 0xFFu : n;
+  uint4* o = reinterpret_cast<uint4*>(a.out0) + 2 * (size_t)grow;
+  o[0] = make_uint4(rec[0], rec[1], rec[2], rec[3]);
+  o[1] = make_uint4(rec[4], rec[5], rec[6], rec[7]);
 }
 
 struct TileInfo {

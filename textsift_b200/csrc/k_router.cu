@@ -12,11 +12,13 @@
 // block.ts:201-206).  Indices and weights are therefore those of the
 // reference on the same f32 input, bit for bit.
 //
-// One thread per token.  The f32 router input is either given (the per-op
+// One warp per token.  The f32 router input is either given (the per-op
 // entry) or rebuilt from the residual and attention output exactly as the
-// fast add+RMSNorm computed it (rmsnorm_fast_kernel<true>): the same lane
-// partial sums of squares, combined in the same butterfly order, the same
-// rsqrtf and the same products.
+// fast add+RMSNorm computed it (rmsnorm_fast_kernel<true>, also one warp per
+// row): the same lane chunks and sum-of-squares chains, the same shuffle
+// tree, rsqrtf and products.  The lanes then split the candidates' 32-blocks
+// between them, and each candidate's blocks are added in the reference's
+// order.
 #include "ts_common.cuh"
 #include "ts_kernels.h"
 #include "ts_simt.h"
@@ -29,7 +31,6 @@ namespace {
 
 constexpr uint32_t kCertThreads = 256;  // tokens per block, inside one permutation chunk
 static_assert(kPermChunk % kCertThreads == 0, "a block's tokens share one permutation chunk");
-constexpr uint32_t kCertMax = 8;         // candidates per token held in registers
 
 // The reference's value of one 32-block: the tile path's four lane chains of
 // eight fused multiply-adds (wasm_exports.zig:615-646) or the tail path's even
@@ -76,174 +77,202 @@ __device__ __forceinline__ void block_q(uint4 pk, float zp, float (&q)[32]) {
   }
 }
 
-// (value descending, index ascending) -- the order the reference's strict '>'
-// insertion produces (the rule router_topk_kernel uses).
-__device__ __forceinline__ bool better(float v, int e, float bv, int be) {
-  return be < 0 || v > bv || (v == bv && e < be);
-}
-
 }  // namespace
+
+// Shared memory of one warp: the token's f32 router input (each 32-block
+// padded to 36 floats so that lanes reading different blocks hit different
+// banks), the per-(candidate, block) products of one batch of 32 candidates
+// (rows padded to nb + 1), and every candidate's exact logit and expert id.
+__host__ __device__ constexpr uint32_t cert_x_floats(uint32_t D) { return D / 32 * 36; }
+__host__ __device__ constexpr uint32_t cert_warp_floats(uint32_t D) {
+  return cert_x_floats(D) + 32 * (D / 32 + 1) + 2 * kMaxRouterExperts;
+}
 
 template <int SRC>
 __global__ void __launch_bounds__(kCertThreads) router_cert_kernel(const RouterCertArgs a) {
+  extern __shared__ __align__(16) float cert_smem[];
   __shared__ int h[kMaxRouterExperts];
   pdl_trigger();
   for (uint32_t i = threadIdx.x; i < a.E; i += blockDim.x) h[i] = 0;
   __syncthreads();
   pdl_wait();
-  const uint32_t t = blockIdx.x * kCertThreads + threadIdx.x;
-  const uint32_t D = a.D, nb = D / 32, zs = (nb + 1) / 2, K = a.K;
-  if (t < a.T) {
-    const uint4 cd = reinterpret_cast<const uint4*>(a.cand)[t];
-    const bool all = cd.x > kCertMax;
-    const uint32_t n_c = all ? kCertMax : cd.x;
+  const uint32_t D = a.D, nb = D / 32, zs = (nb + 1) / 2, K = a.K, E = a.E;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* xs = cert_smem + (size_t)warp * cert_warp_floats(D);
+  float* pb = xs + cert_x_floats(D);     // [32][nb + 1]
+  float* cv = pb + 32 * (nb + 1);        // [kMaxRouterExperts] exact logits
+  int* ci = reinterpret_cast<int*>(cv + kMaxRouterExperts);  // their expert ids
+  const uint32_t t_begin = blockIdx.x * kCertThreads;
+  for (uint32_t tl = (uint32_t)warp; tl < kCertThreads; tl += kCertThreads / 32) {
+    const uint32_t t = t_begin + tl;
+    if (t >= a.T) break;
+    // the candidate record: byte 0 = count, byte k + 1 = expert id k
+    const uint32_t cnt = a.cand[(size_t)t * 32];
+    const bool all = cnt > 31u;
+    const uint32_t n_c = all ? E : cnt;
     uint32_t loc, len;
     if (a.rloc) { loc = (uint32_t)a.rloc[t]; len = (uint32_t)a.rlen[t]; }
     else { loc = t; len = a.T; }
     const bool tile_path = loc < (len & ~7u);
 
-    // the f32 router input: rebuilt with rmsnorm_fast_kernel<true>'s arithmetic
-    float inv_rms = 0.0f;
+    // ---- the f32 router input into xs ----
     const size_t base = (size_t)t * D;
     if constexpr (SRC == kRouterSrcAddNorm) {
+      // rmsnorm_fast_kernel<true>'s arithmetic: lane l owns chunks l, l + 32,
+      // l + 64, l + 96 of 8 values, the same sum-of-squares chain, the same
+      // shuffle tree and rsqrtf, the same products
       const uint32_t nc = D / 8;
-      float p[32];  // lane l's sum of squares over chunks l, l + 32, l + 64, l + 96
+      uint32_t sw[4][4];  // the fp16-rounded sums of this lane's chunks
+      float ss = 0.0f;
 #pragma unroll
-      for (int l = 0; l < 32; l++) {
-        float ss = 0.0f;
+      for (int r = 0; r < 4; r++) {
+        const uint32_t c = (uint32_t)lane + 32u * r;
+        if (c >= nc) break;
+        const uint4 av = *reinterpret_cast<const uint4*>(a.a + base + 8 * c);
+        const uint4 bv = *reinterpret_cast<const uint4*>(a.b + base + 8 * c);
+        const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
-          const uint32_t c = (uint32_t)l + 32u * r;
-          if (c >= nc) break;
-          const uint4 av = *reinterpret_cast<const uint4*>(a.a + base + 8 * c);
-          const uint4 bv = *reinterpret_cast<const uint4*>(a.b + base + 8 * c);
-          const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-          for (int j = 0; j < 4; j++) {
-            const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
-            const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
-            const float s0 = fa.x + fb.x, s1 = fa.y + fb.y;
-            ss = fmaf(s0, s0, ss);
-            ss = fmaf(s1, s1, ss);
-          }
+        for (int j = 0; j < 4; j++) {
+          const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
+          const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
+          const float s0 = fa.x + fb.x, s1 = fa.y + fb.y;
+          ss = fmaf(s0, s0, ss);
+          ss = fmaf(s1, s1, ss);
+          sw[r][j] = f32x2_to_h2(s0, s1);
         }
-        p[l] = ss;
       }
-      // the shuffle butterfly: lane l adds lane l ^ o's value to its own
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv_rms = rsqrtf(ss / (float)D + a.eps);
 #pragma unroll
-        for (int l = 0; l < o; l++) p[l] = p[l] + p[l + o];
-      inv_rms = rsqrtf(p[0] / (float)D + a.eps);
+      for (int r = 0; r < 4; r++) {
+        const uint32_t c = (uint32_t)lane + 32u * r;
+        if (c >= nc) break;
+        const uint4 gv = *reinterpret_cast<const uint4*>(a.gamma + 8 * c);
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+        float o8[8];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&sw[r][j]));
+          const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
+          o8[2 * j] = x.x * inv_rms * g.x;
+          o8[2 * j + 1] = x.y * inv_rms * g.y;
+        }
+        float* dst = xs + (c >> 2) * 36u + (c & 3u) * 8u;
+        *reinterpret_cast<float4*>(dst) = make_float4(o8[0], o8[1], o8[2], o8[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(o8[4], o8[5], o8[6], o8[7]);
+      }
+    } else {
+      for (uint32_t i = (uint32_t)lane * 4u; i < D; i += 128u) {
+        const float4 v = *reinterpret_cast<const float4*>(a.x32 + base + i);
+        *reinterpret_cast<float4*>(xs + (i >> 5) * 36u + (i & 31u)) = v;
+      }
+    }
+    __syncwarp();
+
+    // ---- exact logits of the candidates, 32 at a time: lanes take
+    // (candidate, block) pairs, then lane c adds candidate c's blocks in order ----
+    for (uint32_t cb = 0; cb < n_c; cb += 32u) {
+      const uint32_t nbt = min(32u, n_c - cb);
+      for (uint32_t p = (uint32_t)lane; p < nbt * nb; p += 32u) {
+        const uint32_t c = p / nb, b = p - c * nb;
+        const uint32_t k = cb + c;
+        const uint32_t e = all ? k : (uint32_t)a.cand[(size_t)t * 32 + k + 1];
+        const float scale = f16_ref_to_f32(a.w_scales[(size_t)e * nb + b]);
+        int zp = 0;
+        if (a.w_zp) {
+          const uint8_t zb = a.w_zp[(size_t)e * zs + (b >> 1)];
+          zp = (b & 1) ? (zb >> 4) & 15 : zb & 15;
+        }
+        float q[32], x[32];
+        block_q(*reinterpret_cast<const uint4*>(a.w_int4 + (size_t)e * (D / 2) + 16 * b), (float)zp, q);
+        const float* xb = xs + b * 36u;
+#pragma unroll
+        for (int c4 = 0; c4 < 8; c4++) {
+          const float4 v = *reinterpret_cast<const float4*>(xb + 4 * c4);
+          x[4 * c4] = v.x; x[4 * c4 + 1] = v.y; x[4 * c4 + 2] = v.z; x[4 * c4 + 3] = v.w;
+        }
+        pb[c * (nb + 1) + b] = __fmul_rn(block_dot_ref(x, q, tile_path), scale);
+      }
+      __syncwarp();
+      if ((uint32_t)lane < nbt) {
+        const uint32_t k = cb + (uint32_t)lane;
+        const uint32_t e = all ? k : (uint32_t)a.cand[(size_t)t * 32 + k + 1];
+        float sum = 0.0f;
+        for (uint32_t b = 0; b < nb; b++) sum = __fadd_rn(sum, pb[lane * (nb + 1) + b]);
+        cv[k] = __fadd_rn(sum, f16_ref_to_f32(a.bias[e]));
+        ci[k] = (int)e;
+      }
+      __syncwarp();
     }
 
-    float ov[kCertMax], sum[kCertMax];
-    int oi[kCertMax];
+    // ---- top K among the candidates: K rounds of a warp arg-max, (value
+    // descending, index ascending) as router_topk_kernel ----
+    float ov[8];
+    int oi[8];
+    uint32_t taken = 0u;  // bit j: this lane's entry lane + 32 j is selected
 #pragma unroll
-    for (uint32_t k = 0; k < kCertMax; k++) { ov[k] = 0.0f; oi[k] = -1; }
-    // candidates in groups of up to 8 (a single group unless every expert is a candidate)
-    for (uint32_t g0 = 0; g0 < (all ? a.E : 1u); g0 += kCertMax) {
-      int ids[kCertMax];
-      uint32_t n = n_c;
-      if (all) {
-        n = min(kCertMax, a.E - g0);
-#pragma unroll
-        for (uint32_t k = 0; k < kCertMax; k++) ids[k] = (int)(g0 + k);
-      } else {
-#pragma unroll
-        for (uint32_t k = 0; k < kCertMax; k++) ids[k] = (int)(((k < 4 ? cd.y : cd.z) >> (8 * (k & 3))) & 0xffu);
+    for (uint32_t r = 0; r < 8; r++) {
+      ov[r] = 0.0f;
+      oi[r] = 0;
+      if (r >= K) continue;
+      float bv = 0.0f;
+      int bi = 0x7fffffff, bj = -1;
+      for (uint32_t j = 0; (uint32_t)lane + 32u * j < n_c; j++) {
+        if ((taken >> j) & 1u) continue;
+        const uint32_t k = (uint32_t)lane + 32u * j;
+        const float v = cv[k];
+        const int e = ci[k];
+        if (bi == 0x7fffffff || v > bv || (v == bv && e < bi)) { bv = v; bi = e; bj = (int)j; }
       }
+      int best_lane = lane;
 #pragma unroll
-      for (uint32_t k = 0; k < kCertMax; k++) sum[k] = 0.0f;
-      for (uint32_t b = 0; b < nb; b++) {
-        float x[32];
-        if constexpr (SRC == kRouterSrcAddNorm) {
-#pragma unroll
-          for (int cc = 0; cc < 4; cc++) {
-            const size_t o = base + 32 * b + 8 * cc;
-            const uint4 av = *reinterpret_cast<const uint4*>(a.a + o);
-            const uint4 bv = *reinterpret_cast<const uint4*>(a.b + o);
-            const uint4 gv = *reinterpret_cast<const uint4*>(a.gamma + 32 * b + 8 * cc);
-            const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
-            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-              const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
-              const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
-              const uint32_t sw = f32x2_to_h2(fa.x + fb.x, fa.y + fb.y);
-              const float2 xs = __half22float2(*reinterpret_cast<const __half2*>(&sw));
-              const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
-              x[8 * cc + 2 * j] = xs.x * inv_rms * g.x;
-              x[8 * cc + 2 * j + 1] = xs.y * inv_rms * g.y;
-            }
-          }
-        } else {
-#pragma unroll
-          for (int c4 = 0; c4 < 8; c4++) {
-            const float4 v = *reinterpret_cast<const float4*>(a.x32 + base + 32 * b + 4 * c4);
-            x[4 * c4] = v.x; x[4 * c4 + 1] = v.y; x[4 * c4 + 2] = v.z; x[4 * c4 + 3] = v.w;
-          }
-        }
-#pragma unroll
-        for (uint32_t k = 0; k < kCertMax; k++) {
-          if (k >= n) break;
-          const uint32_t e = (uint32_t)ids[k];
-          const float scale = f16_ref_to_f32(a.w_scales[(size_t)e * nb + b]);
-          int zp = 0;
-          if (a.w_zp) {
-            const uint8_t zb = a.w_zp[(size_t)e * zs + (b >> 1)];
-            zp = (b & 1) ? (zb >> 4) & 15 : zb & 15;
-          }
-          float q[32];
-          block_q(*reinterpret_cast<const uint4*>(a.w_int4 + (size_t)e * (D / 2) + 16 * b), (float)zp, q);
-          sum[k] = __fadd_rn(sum[k], __fmul_rn(block_dot_ref(x, q, tile_path), scale));
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ovv = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oii = __shfl_xor_sync(0xffffffffu, bi, o);
+        const int ol = __shfl_xor_sync(0xffffffffu, best_lane, o);
+        if (oii != 0x7fffffff && (bi == 0x7fffffff || ovv > bv || (ovv == bv && oii < bi))) {
+          bv = ovv; bi = oii; best_lane = ol;
         }
       }
-      // merge this group into the top k (insertion, kept sorted)
-#pragma unroll
-      for (uint32_t k = 0; k < kCertMax; k++) {
-        if (k >= n) break;
-        const int e = ids[k];
-        float v = __fadd_rn(sum[k], f16_ref_to_f32(a.bias[e]));
-        int ve = e;
-#pragma unroll
-        for (uint32_t s = 0; s < kCertMax; s++) {
-          if (s >= K) break;
-          if (better(v, ve, ov[s], oi[s])) {
-            const float tv = ov[s];
-            const int ti = oi[s];
-            ov[s] = v; oi[s] = ve;
-            v = tv; ve = ti;
-            if (ve < 0) break;
-          }
-        }
-      }
+      ov[r] = bv;
+      oi[r] = bi;
+      if (lane == best_lane && bj >= 0) taken |= 1u << bj;
     }
-    // softmax over the k values in order (wasm_exports.zig:919-958), x 1/k in double
+    // softmax over the K values in order (wasm_exports.zig:919-958), x 1/K in double
     float m = ov[0];
 #pragma unroll
-    for (uint32_t c = 1; c < kCertMax; c++)
+    for (uint32_t c = 1; c < 8; c++)
       if (c < K && ov[c] > m) m = ov[c];
-    float ex[kCertMax], s = 0.0f;
+    float mine = ov[0];
 #pragma unroll
-    for (uint32_t c = 0; c < kCertMax; c++) {
-      ex[c] = c < K ? expf_ref(__fsub_rn(ov[c], m)) : 0.0f;
-      if (c < K) s = __fadd_rn(s, ex[c]);
-    }
-    const float inv = s > 0.0f ? __fdiv_rn(1.0f, s) : __fdiv_rn(1.0f, (float)K);
-    const double inv_k = 1.0 / (double)K;
+    for (int c = 1; c < 8; c++)
+      if (lane == c) mine = ov[c];
+    const float my_e = expf_ref(__fsub_rn(mine, m));
+    float ex[8];
 #pragma unroll
-    for (uint32_t c = 0; c < kCertMax; c++) {
-      if (c >= K) break;
-      a.idx[(size_t)t * K + c] = oi[c];
-      a.w[(size_t)t * K + c] = (float)((double)__fmul_rn(ex[c], inv) * inv_k);
-      if (oi[c] >= 0) atomicAdd(&h[oi[c]], 1);
+    for (uint32_t c = 0; c < 8; c++) ex[c] = __shfl_sync(0xffffffffu, my_e, c);
+    if (lane == 0) {
+      float s = 0.0f;
+#pragma unroll
+      for (uint32_t c = 0; c < 8; c++)
+        if (c < K) s = __fadd_rn(s, ex[c]);
+      const float inv = s > 0.0f ? __fdiv_rn(1.0f, s) : __fdiv_rn(1.0f, (float)K);
+      const double inv_k = 1.0 / (double)K;
+#pragma unroll
+      for (uint32_t c = 0; c < 8; c++) {
+        if (c >= K) break;
+        a.idx[(size_t)t * K + c] = oi[c];
+        a.w[(size_t)t * K + c] = (float)((double)__fmul_rn(ex[c], inv) * inv_k);
+        atomicAdd(&h[oi[c]], 1);
+      }
     }
+    __syncwarp();
   }
   __syncthreads();
   if (a.hist) {
-    int* row = a.hist + (size_t)(blockIdx.x * kCertThreads / kPermChunk) * a.E;
-    for (uint32_t i = threadIdx.x; i < a.E; i += blockDim.x)
+    int* row = a.hist + (size_t)(blockIdx.x * kCertThreads / kPermChunk) * E;
+    for (uint32_t i = threadIdx.x; i < E; i += blockDim.x)
       if (h[i]) atomicAdd(row + i, h[i]);
   }
 }
@@ -270,10 +299,20 @@ __global__ void __launch_bounds__(256) f32_to_f16_absum_kernel(const float* __re
 
 cudaError_t launch_router_cert(const RouterCertArgs& a, int src, cudaStream_t st) {
   if (a.T == 0) return cudaSuccess;
-  if (a.E > kMaxRouterExperts || a.K == 0 || a.K > kCertMax || a.D % 32 || a.D > 1024) return cudaErrorInvalidValue;
+  if (a.E > kMaxRouterExperts || a.K == 0 || a.K > 8 || a.K > a.E || a.D % 32 || a.D > 1024)
+    return cudaErrorInvalidValue;
   const dim3 grid((a.T + kCertThreads - 1) / kCertThreads);
-  if (src == kRouterSrcAddNorm) return launch_pdl(router_cert_kernel<kRouterSrcAddNorm>, grid, dim3(kCertThreads), 0, st, a);
-  return launch_pdl(router_cert_kernel<kRouterSrcF32>, grid, dim3(kCertThreads), 0, st, a);
+  const size_t smem = (size_t)(kCertThreads / 32) * cert_warp_floats(a.D) * sizeof(float);
+  constexpr int kMaxSmem = (int)((kCertThreads / 32) * cert_warp_floats(1024) * sizeof(float));
+  static std::atomic<uint64_t> done_f32{0}, done_add{0};
+  if (src == kRouterSrcAddNorm) {
+    if (cudaError_t e = smem_attr_per_device(router_cert_kernel<kRouterSrcAddNorm>, kMaxSmem, done_add); e != cudaSuccess)
+      return e;
+    return launch_pdl(router_cert_kernel<kRouterSrcAddNorm>, grid, dim3(kCertThreads), smem, st, a);
+  }
+  if (cudaError_t e = smem_attr_per_device(router_cert_kernel<kRouterSrcF32>, kMaxSmem, done_f32); e != cudaSuccess)
+    return e;
+  return launch_pdl(router_cert_kernel<kRouterSrcF32>, grid, dim3(kCertThreads), smem, st, a);
 }
 
 cudaError_t launch_f32_to_f16_absum(const float* x, uint16_t* y, float* absum, uint32_t T, uint32_t D,

@@ -209,7 +209,7 @@ struct Workspace {
   DevArr<int32_t> ridx;
   DevArr<int> counts, seg_start, seg_end, perm_tok, route_pos, n_tiles, n_tiles_tc, hist;
   DevArr<int4> tiles, tiles_tc;  // 128-row tiles (exact path), gemm_tm_rows()-row tiles (tensor cores)
-  DevArr<int4> rcand;            // router candidates per token (kEpiRouterCert)
+  DevArr<int4> rcand;            // router candidates, 32 bytes per token (kEpiRouterCert)
   DevArr<float> absum;           // sum |x| of each token's router input
   DevArr<int2> atiles;
   DevArr<uint16_t> aperm16, glu16;
@@ -359,7 +359,7 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.n32.alloc(T * D));
     TS_CUDA_TRY(w.rlogits.alloc(T * E));
     TS_CUDA_TRY(w.ridx.alloc(R));
-    TS_CUDA_TRY(w.rcand.alloc(T));
+    TS_CUDA_TRY(w.rcand.alloc(2 * T));
     TS_CUDA_TRY(w.absum.alloc(T));
     TS_CUDA_TRY(w.rw.alloc(R));
     TS_CUDA_TRY(w.counts.alloc(E));

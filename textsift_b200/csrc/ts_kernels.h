@@ -54,8 +54,8 @@ enum GemmEpi : int {
   kEpiQkvRope = 2, // q/k with the reference's 3-rounding RoPE, v plain (fp16)
   kEpiSwiglu = 3,  // out0 fp16 [row][N/2] = f16(swiglu(gate, up))
   kEpiF16Widen = 4,  // out0 f32 [row][ld0] = f32(f16(acc + bias)) (logits, wasm.ts:776-797)
-  kEpiRouterCert = 5,  // router logits -> candidate experts of the exact top 4: out0 uint4 [row]
-                       // {count, ids 0-3, ids 4-7, 0} (count 0xFF: all experts); needs absum, rbound
+  kEpiRouterCert = 5,  // router logits -> candidate experts of the exact top 4: out0 32 bytes per row
+                       // {count, 31 ids} (count 0xFF: all experts); needs absum, rbound
 };
 
 // Largest expert count of the certified router path (one 128-column tile).
