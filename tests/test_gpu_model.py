@@ -95,7 +95,7 @@ def test_router_fast_equals_exact_mode(small_backend, cuda_lib):
     """The two modes return the same bits: both are the reference's top-k and
     softmax of the same f32 logits."""
     from textsift_b200 import abi
-    T = 16384
+    T = 8192
     x = rng(8).normal(0, 1, size=(T, 640)).astype(np.float32)
     out = {}
     try:

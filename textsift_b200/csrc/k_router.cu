@@ -29,52 +29,59 @@ namespace ts {
 
 namespace {
 
-constexpr uint32_t kCertThreads = 256;  // tokens per block, inside one permutation chunk
-static_assert(kPermChunk % kCertThreads == 0, "a block's tokens share one permutation chunk");
+constexpr uint32_t kCertThreads = 256;  // 8 warps, one token at a time each
+constexpr uint32_t kCertTokens = 64;    // tokens per block, inside one permutation chunk
+static_assert(kPermChunk % kCertTokens == 0, "a block's tokens share one permutation chunk");
 
-// The reference's value of one 32-block: the tile path's four lane chains of
-// eight fused multiply-adds (wasm_exports.zig:615-646) or the tail path's even
-// / odd chunk accumulators (689-697), exactly as matmul_w4_exact_kernel.
-__device__ __forceinline__ float block_dot_ref(const float (&x)[32], const float (&q)[32], bool tile_path) {
+// Nibble j (0..3 = byte j) of w, as the exact float (nibble - zp): the
+// nibble goes into the mantissa of 2^23 (prmt), then 2^23 + zp is
+// subtracted (zpo).  lo = w & 0x0F0F0F0F, hi = (w >> 4) & 0x0F0F0F0F.
+__device__ __forceinline__ float nib(uint32_t lohi, uint32_t j, float zpo) {
+  return __uint_as_float(__byte_perm(lohi, 0x4B000000u, 0x7650u | j)) - zpo;
+}
+
+// The reference's value of one 32-block of int4 weights (16 bytes pk, low
+// nibble = even element) against 32 f32 inputs xb (16-byte aligned, in
+// shared memory): the tile path's four lane chains of eight fused
+// multiply-adds (zig/wasm_exports.zig:615-646) or the tail path's even / odd
+// chunk accumulators (689-697), exactly as matmul_w4_exact_kernel, with the
+// values streamed eight at a time.
+__device__ __forceinline__ float block_dot_ref(const float* xb, uint4 pk, float zpo, bool tile_path) {
+  const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
   if (tile_path) {
     float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
 #pragma unroll
     for (int c = 0; c < 8; c++) {
-      v0 = __fmaf_rn(x[4 * c + 0], q[4 * c + 0], v0);
-      v1 = __fmaf_rn(x[4 * c + 1], q[4 * c + 1], v1);
-      v2 = __fmaf_rn(x[4 * c + 2], q[4 * c + 2], v2);
-      v3 = __fmaf_rn(x[4 * c + 3], q[4 * c + 3], v3);
+      // elements 4c .. 4c + 3: bytes 2 (c & 1) and 2 (c & 1) + 1 of word c / 2
+      const float4 x = *reinterpret_cast<const float4*>(xb + 4 * c);
+      const uint32_t w = wd[c >> 1], lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+      const uint32_t j0 = 2u * (uint32_t)(c & 1);
+      v0 = __fmaf_rn(x.x, nib(lo, j0, zpo), v0);
+      v1 = __fmaf_rn(x.y, nib(hi, j0, zpo), v1);
+      v2 = __fmaf_rn(x.z, nib(lo, j0 + 1u, zpo), v2);
+      v3 = __fmaf_rn(x.w, nib(hi, j0 + 1u, zpo), v3);
     }
     return __fadd_rn(__fadd_rn(v0, v1), __fadd_rn(v2, v3));
   }
   float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int k = 0; k < 4; k++)
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      a0[j] = __fmaf_rn(x[8 * k + j], q[8 * k + j], a0[j]);
-      a1[j] = __fmaf_rn(x[8 * k + 4 + j], q[8 * k + 4 + j], a1[j]);
-    }
+  for (int k = 0; k < 4; k++) {
+    // elements 8k .. 8k + 7: word k (byte j holds 8k + 2j and 8k + 2j + 1)
+    const float4 x0 = *reinterpret_cast<const float4*>(xb + 8 * k);
+    const float4 x1 = *reinterpret_cast<const float4*>(xb + 8 * k + 4);
+    const uint32_t lo = wd[k] & 0x0F0F0F0Fu, hi = (wd[k] >> 4) & 0x0F0F0F0Fu;
+    a0[0] = __fmaf_rn(x0.x, nib(lo, 0, zpo), a0[0]);
+    a0[1] = __fmaf_rn(x0.y, nib(hi, 0, zpo), a0[1]);
+    a0[2] = __fmaf_rn(x0.z, nib(lo, 1, zpo), a0[2]);
+    a0[3] = __fmaf_rn(x0.w, nib(hi, 1, zpo), a0[3]);
+    a1[0] = __fmaf_rn(x1.x, nib(lo, 2, zpo), a1[0]);
+    a1[1] = __fmaf_rn(x1.y, nib(hi, 2, zpo), a1[1]);
+    a1[2] = __fmaf_rn(x1.z, nib(lo, 3, zpo), a1[2]);
+    a1[3] = __fmaf_rn(x1.w, nib(hi, 3, zpo), a1[3]);
+  }
   const float c0 = __fadd_rn(a0[0], a1[0]), c1 = __fadd_rn(a0[1], a1[1]);
   const float c2 = __fadd_rn(a0[2], a1[2]), c3 = __fadd_rn(a0[3], a1[3]);
   return __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
-}
-
-// 32 int4 values of one block minus its zero point, as exact floats: the
-// nibble goes into the mantissa of 2^23 (prmt), then 2^23 + zp is subtracted.
-__device__ __forceinline__ void block_q(uint4 pk, float zp, float (&q)[32]) {
-  const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
-  const float off = 8388608.0f + zp;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const uint32_t lo = wd[i] & 0x0F0F0F0Fu, hi = (wd[i] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      // byte j of the word holds elements 8i + 2j (low nibble) and 8i + 2j + 1
-      q[8 * i + 2 * j] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | (uint32_t)j)) - off;
-      q[8 * i + 2 * j + 1] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | (uint32_t)j)) - off;
-    }
-  }
 }
 
 }  // namespace
@@ -89,7 +96,7 @@ __host__ __device__ constexpr uint32_t cert_warp_floats(uint32_t D) {
 }
 
 template <int SRC>
-__global__ void __launch_bounds__(kCertThreads) router_cert_kernel(const RouterCertArgs a) {
+__global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const RouterCertArgs a) {
   extern __shared__ __align__(16) float cert_smem[];
   __shared__ int h[kMaxRouterExperts];
   pdl_trigger();
@@ -102,12 +109,13 @@ __global__ void __launch_bounds__(kCertThreads) router_cert_kernel(const RouterC
   float* pb = xs + cert_x_floats(D);     // [32][nb + 1]
   float* cv = pb + 32 * (nb + 1);        // [kMaxRouterExperts] exact logits
   int* ci = reinterpret_cast<int*>(cv + kMaxRouterExperts);  // their expert ids
-  const uint32_t t_begin = blockIdx.x * kCertThreads;
-  for (uint32_t tl = (uint32_t)warp; tl < kCertThreads; tl += kCertThreads / 32) {
+  const uint32_t t_begin = blockIdx.x * kCertTokens;
+  for (uint32_t tl = (uint32_t)warp; tl < kCertTokens; tl += kCertThreads / 32) {
     const uint32_t t = t_begin + tl;
     if (t >= a.T) break;
     // the candidate record: byte 0 = count, byte k + 1 = expert id k
     const uint32_t cnt = a.cand[(size_t)t * 32];
+    const uint32_t rec_id = lane < 31 ? a.cand[(size_t)t * 32 + 1 + lane] : 0u;  // candidate `lane`
     const bool all = cnt > 31u;
     const uint32_t n_c = all ? E : cnt;
     uint32_t loc, len;
@@ -173,35 +181,44 @@ __global__ void __launch_bounds__(kCertThreads) router_cert_kernel(const RouterC
     // ---- exact logits of the candidates, 32 at a time: lanes take
     // (candidate, block) pairs, then lane c adds candidate c's blocks in order ----
     for (uint32_t cb = 0; cb < n_c; cb += 32u) {
-      const uint32_t nbt = min(32u, n_c - cb);
-      for (uint32_t p = (uint32_t)lane; p < nbt * nb; p += 32u) {
-        const uint32_t c = p / nb, b = p - c * nb;
-        const uint32_t k = cb + c;
-        const uint32_t e = all ? k : (uint32_t)a.cand[(size_t)t * 32 + k + 1];
-        const float scale = f16_ref_to_f32(a.w_scales[(size_t)e * nb + b]);
-        int zp = 0;
-        if (a.w_zp) {
-          const uint8_t zb = a.w_zp[(size_t)e * zs + (b >> 1)];
-          zp = (b & 1) ? (zb >> 4) & 15 : zb & 15;
-        }
-        float q[32], x[32];
-        block_q(*reinterpret_cast<const uint4*>(a.w_int4 + (size_t)e * (D / 2) + 16 * b), (float)zp, q);
-        const float* xb = xs + b * 36u;
+      const uint32_t nbt = min(32u, n_c - cb), npairs = nbt * nb;
+      const uint32_t myid = all ? cb + (uint32_t)lane : rec_id;  // candidate cb + lane
+      for (uint32_t p0 = 0; p0 < npairs; p0 += 128u) {
+        // every load of this lane's (up to) four pairs first, then the arithmetic
+        uint4 wv[4];
+        float sc[4], zo[4];
+        uint32_t cc[4], bb[4];
 #pragma unroll
-        for (int c4 = 0; c4 < 8; c4++) {
-          const float4 v = *reinterpret_cast<const float4*>(xb + 4 * c4);
-          x[4 * c4] = v.x; x[4 * c4 + 1] = v.y; x[4 * c4 + 2] = v.z; x[4 * c4 + 3] = v.w;
+        for (int u = 0; u < 4; u++) {
+          const uint32_t p = p0 + (uint32_t)lane + 32u * u;
+          const uint32_t c = p < npairs ? p / nb : 0u, b = p < npairs ? p - c * nb : 0u;
+          const uint32_t e = __shfl_sync(0xffffffffu, myid, c);
+          cc[u] = c;
+          bb[u] = b;
+          wv[u] = make_uint4(0u, 0u, 0u, 0u);
+          sc[u] = 0.0f;
+          zo[u] = 8388608.0f;
+          if (p < npairs) {
+            wv[u] = *reinterpret_cast<const uint4*>(a.w_int4 + (size_t)e * (D / 2) + 16 * b);
+            sc[u] = f16_ref_to_f32(a.w_scales[(size_t)e * nb + b]);
+            if (a.w_zp) {
+              const uint8_t zb = a.w_zp[(size_t)e * zs + (b >> 1)];
+              zo[u] = 8388608.0f + (float)((b & 1) ? (zb >> 4) & 15 : zb & 15);
+            }
+          }
         }
-        pb[c * (nb + 1) + b] = __fmul_rn(block_dot_ref(x, q, tile_path), scale);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          if (p0 + (uint32_t)lane + 32u * u >= npairs) break;
+          pb[cc[u] * (nb + 1) + bb[u]] = __fmul_rn(block_dot_ref(xs + bb[u] * 36u, wv[u], zo[u], tile_path), sc[u]);
+        }
       }
       __syncwarp();
       if ((uint32_t)lane < nbt) {
-        const uint32_t k = cb + (uint32_t)lane;
-        const uint32_t e = all ? k : (uint32_t)a.cand[(size_t)t * 32 + k + 1];
         float sum = 0.0f;
         for (uint32_t b = 0; b < nb; b++) sum = __fadd_rn(sum, pb[lane * (nb + 1) + b]);
-        cv[k] = __fadd_rn(sum, f16_ref_to_f32(a.bias[e]));
-        ci[k] = (int)e;
+        cv[cb + lane] = __fadd_rn(sum, f16_ref_to_f32(a.bias[myid]));
+        ci[cb + lane] = (int)myid;
       }
       __syncwarp();
     }
@@ -271,7 +288,7 @@ __global__ void __launch_bounds__(kCertThreads) router_cert_kernel(const RouterC
   }
   __syncthreads();
   if (a.hist) {
-    int* row = a.hist + (size_t)(blockIdx.x * kCertThreads / kPermChunk) * E;
+    int* row = a.hist + (size_t)(blockIdx.x * kCertTokens / kPermChunk) * E;
     for (uint32_t i = threadIdx.x; i < E; i += blockDim.x)
       if (h[i]) atomicAdd(row + i, h[i]);
   }
@@ -301,7 +318,7 @@ cudaError_t launch_router_cert(const RouterCertArgs& a, int src, cudaStream_t st
   if (a.T == 0) return cudaSuccess;
   if (a.E > kMaxRouterExperts || a.K == 0 || a.K > 8 || a.K > a.E || a.D % 32 || a.D > 1024)
     return cudaErrorInvalidValue;
-  const dim3 grid((a.T + kCertThreads - 1) / kCertThreads);
+  const dim3 grid((a.T + kCertTokens - 1) / kCertTokens);
   const size_t smem = (size_t)(kCertThreads / 32) * cert_warp_floats(a.D) * sizeof(float);
   constexpr int kMaxSmem = (int)((kCertThreads / 32) * cert_warp_floats(1024) * sizeof(float));
   static std::atomic<uint64_t> done_f32{0}, done_add{0};
