@@ -33,55 +33,70 @@ constexpr uint32_t kCertThreads = 256;  // 8 warps, one token at a time each
 constexpr uint32_t kCertTokens = 64;    // tokens per block, inside one permutation chunk
 static_assert(kPermChunk % kCertTokens == 0, "a block's tokens share one permutation chunk");
 
-// Nibble j (0..3 = byte j) of w, as the exact float (nibble - zp): the
-// nibble goes into the mantissa of 2^23 (prmt), then 2^23 + zp is
-// subtracted (zpo).  lo = w & 0x0F0F0F0F, hi = (w >> 4) & 0x0F0F0F0F.
-__device__ __forceinline__ float nib(uint32_t lohi, uint32_t j, float zpo) {
-  return __uint_as_float(__byte_perm(lohi, 0x4B000000u, 0x7650u | j)) - zpo;
+// Nibble j (0..3 = byte j) of lohi (lo = w & 0x0F0F0F0F or hi = (w >> 4) &
+// 0x0F0F0F0F) placed in the mantissa of 2^23: the float 2^23 + nibble.
+__device__ __forceinline__ float nib_raw(uint32_t lohi, uint32_t j) {
+  return __uint_as_float(__byte_perm(lohi, 0x4B000000u, 0x7650u | j));
 }
 
 // The reference's value of one 32-block of int4 weights (16 bytes pk, low
 // nibble = even element) against 32 f32 inputs xb (16-byte aligned, in
 // shared memory): the tile path's four lane chains of eight fused
 // multiply-adds (zig/wasm_exports.zig:615-646) or the tail path's even / odd
-// chunk accumulators (689-697), exactly as matmul_w4_exact_kernel, with the
-// values streamed eight at a time.
-__device__ __forceinline__ float block_dot_ref(const float* xb, uint4 pk, float zpo, bool tile_path) {
+// chunk accumulators (689-697), exactly as matmul_w4_exact_kernel.  Two
+// chains at a time run as one packed f32x2 instruction (each half an IEEE
+// fused multiply-add or add, so the same bits as the scalar chains); the
+// weight values are nibble - zp, exact (nzz = -(2^23 + zp) twice).
+__device__ __forceinline__ float block_dot_ref(const float* xb, uint4 pk, uint64_t nzz, bool tile_path) {
   const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
   if (tile_path) {
-    float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
+    uint64_t v01 = 0u, v23 = 0u;  // (v0, v1), (v2, v3)
 #pragma unroll
     for (int c = 0; c < 8; c++) {
       // elements 4c .. 4c + 3: bytes 2 (c & 1) and 2 (c & 1) + 1 of word c / 2
       const float4 x = *reinterpret_cast<const float4*>(xb + 4 * c);
       const uint32_t w = wd[c >> 1], lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
       const uint32_t j0 = 2u * (uint32_t)(c & 1);
-      v0 = __fmaf_rn(x.x, nib(lo, j0, zpo), v0);
-      v1 = __fmaf_rn(x.y, nib(hi, j0, zpo), v1);
-      v2 = __fmaf_rn(x.z, nib(lo, j0 + 1u, zpo), v2);
-      v3 = __fmaf_rn(x.w, nib(hi, j0 + 1u, zpo), v3);
+      const uint64_t q01 = add_f32x2(f2pack(nib_raw(lo, j0), nib_raw(hi, j0)), nzz);
+      const uint64_t q23 = add_f32x2(f2pack(nib_raw(lo, j0 + 1u), nib_raw(hi, j0 + 1u)), nzz);
+      v01 = fma_f32x2(f2pack(x.x, x.y), q01, v01);
+      v23 = fma_f32x2(f2pack(x.z, x.w), q23, v23);
     }
+    float v0, v1, v2, v3;
+    f2unpack(v01, v0, v1);
+    f2unpack(v23, v2, v3);
     return __fadd_rn(__fadd_rn(v0, v1), __fadd_rn(v2, v3));
   }
-  float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+  uint64_t a01 = 0u, a23 = 0u, b01 = 0u, b23 = 0u;  // (a0[0], a0[1]), (a0[2], a0[3]), the same of a1
 #pragma unroll
   for (int k = 0; k < 4; k++) {
     // elements 8k .. 8k + 7: word k (byte j holds 8k + 2j and 8k + 2j + 1)
     const float4 x0 = *reinterpret_cast<const float4*>(xb + 8 * k);
     const float4 x1 = *reinterpret_cast<const float4*>(xb + 8 * k + 4);
     const uint32_t lo = wd[k] & 0x0F0F0F0Fu, hi = (wd[k] >> 4) & 0x0F0F0F0Fu;
-    a0[0] = __fmaf_rn(x0.x, nib(lo, 0, zpo), a0[0]);
-    a0[1] = __fmaf_rn(x0.y, nib(hi, 0, zpo), a0[1]);
-    a0[2] = __fmaf_rn(x0.z, nib(lo, 1, zpo), a0[2]);
-    a0[3] = __fmaf_rn(x0.w, nib(hi, 1, zpo), a0[3]);
-    a1[0] = __fmaf_rn(x1.x, nib(lo, 2, zpo), a1[0]);
-    a1[1] = __fmaf_rn(x1.y, nib(hi, 2, zpo), a1[1]);
-    a1[2] = __fmaf_rn(x1.z, nib(lo, 3, zpo), a1[2]);
-    a1[3] = __fmaf_rn(x1.w, nib(hi, 3, zpo), a1[3]);
+    a01 = fma_f32x2(f2pack(x0.x, x0.y), add_f32x2(f2pack(nib_raw(lo, 0), nib_raw(hi, 0)), nzz), a01);
+    a23 = fma_f32x2(f2pack(x0.z, x0.w), add_f32x2(f2pack(nib_raw(lo, 1), nib_raw(hi, 1)), nzz), a23);
+    b01 = fma_f32x2(f2pack(x1.x, x1.y), add_f32x2(f2pack(nib_raw(lo, 2), nib_raw(hi, 2)), nzz), b01);
+    b23 = fma_f32x2(f2pack(x1.z, x1.w), add_f32x2(f2pack(nib_raw(lo, 3), nib_raw(hi, 3)), nzz), b23);
   }
-  const float c0 = __fadd_rn(a0[0], a1[0]), c1 = __fadd_rn(a0[1], a1[1]);
-  const float c2 = __fadd_rn(a0[2], a1[2]), c3 = __fadd_rn(a0[3], a1[3]);
+  // c_j = a0[j] + a1[j], then (c0 + c1) + (c2 + c3)
+  float c0, c1, c2, c3;
+  f2unpack(add_f32x2(a01, b01), c0, c1);
+  f2unpack(add_f32x2(a23, b23), c2, c3);
   return __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
+}
+
+// A candidate as one 64-bit key whose unsigned maximum is the reference's
+// first choice (value descending, then expert id ascending): the float's
+// bits made monotonic in the high word, the complemented id in the low word.
+__device__ __forceinline__ uint64_t cand_key(float v, uint32_t e) {
+  uint32_t u = __float_as_uint(v + 0.0f);  // -0 as +0: equal values tie on the id
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((uint64_t)u << 32) | (uint64_t)(~e);
+}
+__device__ __forceinline__ float key_value(uint64_t k) {
+  const uint32_t u = (uint32_t)(k >> 32);
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
 }
 
 }  // namespace
@@ -183,34 +198,41 @@ __global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const Rout
     for (uint32_t cb = 0; cb < n_c; cb += 32u) {
       const uint32_t nbt = min(32u, n_c - cb), npairs = nbt * nb;
       const uint32_t myid = all ? cb + (uint32_t)lane : rec_id;  // candidate cb + lane
+      // pair p = c * nb + b; this lane's pairs are lane, lane + 32, ..., their
+      // (c, b) stepped by subtraction instead of a division per pair
+      uint32_t c_n = (uint32_t)lane / nb, b_n = (uint32_t)lane - c_n * nb;
       for (uint32_t p0 = 0; p0 < npairs; p0 += 128u) {
         // every load of this lane's (up to) four pairs first, then the arithmetic
         uint4 wv[4];
-        float sc[4], zo[4];
+        float sc[4], zf[4];
         uint32_t cc[4], bb[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-          const uint32_t p = p0 + (uint32_t)lane + 32u * u;
-          const uint32_t c = p < npairs ? p / nb : 0u, b = p < npairs ? p - c * nb : 0u;
+          const bool ok = p0 + (uint32_t)lane + 32u * u < npairs;
+          const uint32_t c = ok ? c_n : 0u, b = ok ? b_n : 0u;
           const uint32_t e = __shfl_sync(0xffffffffu, myid, c);
           cc[u] = c;
           bb[u] = b;
           wv[u] = make_uint4(0u, 0u, 0u, 0u);
           sc[u] = 0.0f;
-          zo[u] = 8388608.0f;
-          if (p < npairs) {
+          zf[u] = 0.0f;
+          if (ok) {
             wv[u] = *reinterpret_cast<const uint4*>(a.w_int4 + (size_t)e * (D / 2) + 16 * b);
             sc[u] = f16_ref_to_f32(a.w_scales[(size_t)e * nb + b]);
             if (a.w_zp) {
               const uint8_t zb = a.w_zp[(size_t)e * zs + (b >> 1)];
-              zo[u] = 8388608.0f + (float)((b & 1) ? (zb >> 4) & 15 : zb & 15);
+              zf[u] = (float)((b & 1) ? (zb >> 4) & 15 : zb & 15);
             }
           }
+          b_n += 32u;
+          while (b_n >= nb) { b_n -= nb; c_n++; }
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
           if (p0 + (uint32_t)lane + 32u * u >= npairs) break;
-          pb[cc[u] * (nb + 1) + bb[u]] = __fmul_rn(block_dot_ref(xs + bb[u] * 36u, wv[u], zo[u], tile_path), sc[u]);
+          const float nz = -(8388608.0f + zf[u]);
+          pb[cc[u] * (nb + 1) + bb[u]] =
+              __fmul_rn(block_dot_ref(xs + bb[u] * 36u, wv[u], f2pack(nz, nz), tile_path), sc[u]);
         }
       }
       __syncwarp();
@@ -223,38 +245,35 @@ __global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const Rout
       __syncwarp();
     }
 
-    // ---- top K among the candidates: K rounds of a warp arg-max, (value
-    // descending, index ascending) as router_topk_kernel ----
+    // ---- top K among the candidates: K rounds of a warp-wide maximum of
+    // cand_key (value descending, then expert id ascending, the order of
+    // router_topk_kernel and the reference's insertion) ----
+    uint64_t kr[4];  // this lane's entries lane + 32 j (0 = none or taken)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const uint32_t k = (uint32_t)lane + 32u * j;
+      kr[j] = k < n_c ? cand_key(cv[k], (uint32_t)ci[k]) : 0u;
+    }
     float ov[8];
     int oi[8];
-    uint32_t taken = 0u;  // bit j: this lane's entry lane + 32 j is selected
 #pragma unroll
     for (uint32_t r = 0; r < 8; r++) {
       ov[r] = 0.0f;
       oi[r] = 0;
       if (r >= K) continue;
-      float bv = 0.0f;
-      int bi = 0x7fffffff, bj = -1;
-      for (uint32_t j = 0; (uint32_t)lane + 32u * j < n_c; j++) {
-        if ((taken >> j) & 1u) continue;
-        const uint32_t k = (uint32_t)lane + 32u * j;
-        const float v = cv[k];
-        const int e = ci[k];
-        if (bi == 0x7fffffff || v > bv || (v == bv && e < bi)) { bv = v; bi = e; bj = (int)j; }
-      }
-      int best_lane = lane;
+      uint64_t best = kr[0];
+#pragma unroll
+      for (int j = 1; j < 4; j++) best = kr[j] > best ? kr[j] : best;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        const float ovv = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oii = __shfl_xor_sync(0xffffffffu, bi, o);
-        const int ol = __shfl_xor_sync(0xffffffffu, best_lane, o);
-        if (oii != 0x7fffffff && (bi == 0x7fffffff || ovv > bv || (ovv == bv && oii < bi))) {
-          bv = ovv; bi = oii; best_lane = ol;
-        }
+        const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
       }
-      ov[r] = bv;
-      oi[r] = bi;
-      if (lane == best_lane && bj >= 0) taken |= 1u << bj;
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        if (kr[j] == best) kr[j] = 0u;
+      ov[r] = key_value(best);
+      oi[r] = (int)(~(uint32_t)best);
     }
     // softmax over the K values in order (wasm_exports.zig:919-958), x 1/K in double
     float m = ov[0];
