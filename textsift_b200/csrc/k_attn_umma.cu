@@ -55,7 +55,7 @@ constexpr uint32_t kSmemBytes = kOffRed + 4u * 128u * 4u + 1024u;  // + alignmen
 constexpr uint32_t kTmemCols = 512;
 // S: band columns; P: band / 2 (fp16 pairs); O: 64; row sums: 16 (equal) columns
 constexpr uint32_t kColS = 0, kColP = 272, kColO = 416, kColL = 480;
-constexpr int kThreads = 608;  // producer, MMA, TMEM allocator, 16 softmax warps (warps 3..18); 96 registers (5 warps per scheduler)
+constexpr int kThreads = 608;  // producer, MMA, TMEM allocator, 16 softmax warps (warps 3..18)
 static_assert(kColP >= kColS + kMaxBand && kColO >= kColP + kMaxBand / 2 && kColL >= kColO + 64 &&
                   kColL + 16 <= kTmemCols, "TMEM map");
 static_assert(kOffOnes % 1024u == 0, "SW128 alignment");
@@ -170,7 +170,7 @@ __device__ __forceinline__ void store_quarter_row(uint16_t* dst, const uint32_t 
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(104)
     attn_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv, const AttnArgs a, uint32_t band) {
   extern __shared__ uint8_t smem_raw[];
