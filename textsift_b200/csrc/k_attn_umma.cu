@@ -20,9 +20,7 @@
 //     and, behind the next item's S, O = P V with P read from TMEM and V
 //     from smem (an MN-major operand);
 //   * sixteen softmax warps, four per TMEM lane quarter (one thread per row,
-//     each warp a quarter of the band's columns), load their S columns into
-//     registers with one wait and release S at once (the next item's S MMA
-//     runs during this item's exponent pass), find the row max over the
+//     each warp a quarter of the band's columns), find the row max over the
 //     usable keys (the four partial maxima meet in smem) and write
 //     P = 2^((s - max) log2 e) into TMEM (kColP..), two exponentials per
 //     fp16x2 SFU instruction; one item later each reads 16 columns of O and
@@ -55,7 +53,7 @@ constexpr uint32_t kSmemBytes = kOffRed + 4u * 128u * 4u + 1024u;  // + alignmen
 constexpr uint32_t kTmemCols = 512;
 // S: band columns; P: band / 2 (fp16 pairs); O: 64; row sums: 16 (equal) columns
 constexpr uint32_t kColS = 0, kColP = 272, kColO = 416, kColL = 480;
-constexpr int kThreads = 608;  // producer, MMA, TMEM allocator, 16 softmax warps (warps 3..18)
+constexpr int kThreads = 640;  // producer, MMA, TMEM allocator, idle, 16 softmax warps
 static_assert(kColP >= kColS + kMaxBand && kColO >= kColP + kMaxBand / 2 && kColL >= kColO + 64 &&
                   kColL + 16 <= kTmemCols, "TMEM map");
 static_assert(kOffOnes % 1024u == 0, "SW128 alignment");
@@ -170,7 +168,7 @@ __device__ __forceinline__ void store_quarter_row(uint16_t* dst, const uint32_t 
   }
 }
 
-__global__ void __maxnreg__(104)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv, const AttnArgs a, uint32_t band) {
   extern __shared__ uint8_t smem_raw[];
@@ -182,14 +180,13 @@ __global__ void __maxnreg__(104)
   uint64_t* full = bars;       // [2] Q/K/V of a stage landed
   uint64_t* empty = bars + 2;  // [2] the stage's last MMA finished
   uint64_t* s_full = bars + 4;  // S of the item is in TMEM
-  uint64_t* s_free = bars + 5;  // the softmax warps hold S in registers: the next S may overwrite it
+  uint64_t* s_free = bars + 5;  // the softmax has read S and written P
   uint64_t* o_full = bars + 6;  // P.V (and the row sums) of the item completed
   uint64_t* drain = bars + 7;
   uint64_t* pair_bar = bars + 8;  // [4] the four softmax warps of a lane quarter exchanged row maxima
   uint64_t* o_read = bars + 12;   // the softmax has read O and the row sums of the item
-  uint64_t* p_full = bars + 13;   // the softmax has written P of the item
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 14) + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13) + 1;
   float* red_max = reinterpret_cast<float*>(smem + kOffRed);
   ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + kOffMeta);
 
@@ -204,7 +201,6 @@ __global__ void __maxnreg__(104)
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 512);
-    mbar_init(p_full, 512);
     mbar_init(o_read, 512);
     for (int q = 0; q < 4; q++) mbar_init(&pair_bar[q], 128);
     mbar_init(o_full, 1);
@@ -313,7 +309,6 @@ __global__ void __maxnreg__(104)
     // P.V of item j overwrites O: it waits until the softmax has read O of
     // item j - 1 (o_read phase j - 1), which it does after releasing S.
     auto pv_of = [&](uint32_t j, uint32_t sj) -> bool {
-      if (!__all_sync(0xffffffffu, wait_or_abort(p_full, j & 1u, a.err, abort_flag))) return false;
       if (j >= 1u && !__all_sync(0xffffffffu, wait_or_abort(o_read, (j - 1u) & 1u, a.err, abort_flag))) return false;
       tc_fence_after();
       if (elect_one()) {
@@ -328,8 +323,8 @@ __global__ void __maxnreg__(104)
     bool ok = true;
     for (uint32_t item = blockIdx.x; item < items; item += gridDim.x, lt++) {
       const uint32_t s = lt & 1u;
-      // the stage has landed, and the softmax warps hold the previous item's
-      // S in registers
+      // the stage has landed, and the softmax of the previous item is done
+      // with S (and has written P)
       ok = __all_sync(0xffffffffu, wait_or_abort(&full[s], (lt >> 1) & 1u, a.err, abort_flag) &&
                                        (lt == 0 || wait_or_abort(s_free, (lt - 1u) & 1u, a.err, abort_flag)));
       if (!ok) break;
@@ -357,12 +352,12 @@ __global__ void __maxnreg__(104)
     if (elect_one()) tc_commit(drain);
     __syncwarp();
     if (lane == 0) mbar_wait(drain, 0, a.err);
-  } else if (warp >= 3) {
+  } else if (warp >= 4) {
     // ---------------- softmax + epilogue ----------------
-    // Four warps per TMEM lane quarter: warp 3 + j (quad = warp % 4, part cq = j / 4) owns rows
+    // Four warps per TMEM lane quarter: warp (4 + quad + 4 * cq) owns rows
     // quad * 32 .. +31, column part cq of the band (its 16-column groups split
     // in four) and columns 16 cq .. +15 of O.
-    const uint32_t quad = (uint32_t)warp & 3u, cq = ((uint32_t)warp - 3u) >> 2;
+    const uint32_t quad = (uint32_t)warp & 3u, cq = ((uint32_t)warp - 4u) >> 2;
     const uint32_t r = quad * 32u + (uint32_t)lane;
     const uint32_t hl = r >> 4, i = r & 15u;
     const uint32_t trow = tmem + ((quad * 32u) << 16);
@@ -402,26 +397,24 @@ __global__ void __maxnreg__(104)
         return w & range_bits(c_lo - (int)c, c_hi - (int)c);
       };
 
-      // ---- S of this warp's columns into registers (one wait), then S is
-      // free for the next item's MMA ----
-      uint32_t v0[32], v1[32], vt[16];
-      if (n32 > 0u) tmem_ld_32x32b_x32(trow + kColS + col_begin, v0);
-      if (n32 > 1u) tmem_ld_32x32b_x32(trow + kColS + col_begin + 32u, v1);
-      if (tail) tmem_ld_32x32b_x16(trow + kColS + c_tail, vt);
-      const uint32_t rm0 = n32 > 0u ? row_mask(col_begin) : 0u;
-      const uint32_t rm1 = n32 > 1u ? row_mask(col_begin + 32u) : 0u;
-      const uint32_t rmt = tail ? row_mask(c_tail) & 0xffffu : 0u;
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(s_free);
-
-      // ---- max over this part's usable keys, then over the four parts ----
+      // ---- pass 1: max over this half's usable keys, then over the pair ----
       float m0 = sink, m1 = sink, m2 = sink, m3 = sink;
-      if (n32 > 0u) max32(v0, rm0, m0, m1, m2, m3);
-      if (n32 > 1u) max32(v1, rm1, m0, m1, m2, m3);
+#pragma unroll 1
+      for (uint32_t j = 0; j < n32; j++) {
+        const uint32_t c = col_begin + 32u * j;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(trow + kColS + c, v);
+        const uint32_t rm = row_mask(c);
+        tmem_ld_wait();
+        max32(v, rm, m0, m1, m2, m3);
+      }
       if (tail) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(trow + kColS + c_tail, v);
+        const uint32_t rm = row_mask(c_tail) & 0xffffu;
+        tmem_ld_wait();
 #pragma unroll
-        for (int b = 0; b < 16; b++) m0 = fmaxf(m0, ((rmt >> b) & 1u) ? __uint_as_float(vt[b]) : -INFINITY);
+        for (int b = 0; b < 16; b++) m0 = fmaxf(m0, ((rm >> b) & 1u) ? __uint_as_float(v[b]) : -INFINITY);
       }
       const float mh = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
       red_max[cq * 128u + r] = mh;
@@ -431,32 +424,37 @@ __global__ void __maxnreg__(104)
       const float mb = m * kL2E;
       const uint64_t nmb2 = f2pack(-mb, -mb);
 
-      // ---- P = exp(s - max) as fp16 into TMEM ----
+      // ---- pass 2: P = exp(s - max) as fp16 into TMEM ----
       // (P of the previous item must have been consumed by its P.V first; that
       // also completes the previous item's O and row sums)
       if (lt > 0) {
         if (!wait_or_abort(o_full, (lt - 1u) & 1u, a.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
       }
-      if (n32 > 0u) {
+#pragma unroll 1
+      for (uint32_t j = 0; j < n32; j++) {
+        const uint32_t c = col_begin + 32u * j;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(trow + kColS + c, v);
+        const uint32_t rm = row_mask(c);
+        tmem_ld_wait();
         uint32_t pk[16];
-        exp_pack<32>(v0, rm0, nmb2, pk);
-        tmem_st_32x32b_x16(trow + kColP + col_begin / 2u, pk);
-      }
-      if (n32 > 1u) {
-        uint32_t pk[16];
-        exp_pack<32>(v1, rm1, nmb2, pk);
-        tmem_st_32x32b_x16(trow + kColP + (col_begin + 32u) / 2u, pk);
+        exp_pack<32>(v, rm, nmb2, pk);
+        tmem_st_32x32b_x16(trow + kColP + c / 2u, pk);
       }
       if (tail) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(trow + kColS + c_tail, v);
+        const uint32_t rm = row_mask(c_tail) & 0xffffu;
+        tmem_ld_wait();
         uint32_t pk[8];
-        exp_pack<16>(vt, rmt, nmb2, pk);
+        exp_pack<16>(v, rm, nmb2, pk);
         tmem_st_32x32b_x8(trow + kColP + c_tail / 2u, pk);
       }
       tmem_st_wait();
-      // P is written: this item's P.V may go ahead
+      // S is read and P written: the next item's S may go ahead
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(s_free);
 
       // ---- the previous item's O (this warp's 16 columns) and row sum ----
       if (lt > 0) {
