@@ -24,6 +24,7 @@
 #include "ts_simt.h"
 
 #include <cmath>
+#include <cstring>
 
 namespace ts {
 
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const Rout
   for (uint32_t i = threadIdx.x; i < a.E; i += blockDim.x) h[i] = 0;
   __syncthreads();
   pdl_wait();
-  const uint32_t D = a.D, nb = D / 32, zs = (nb + 1) / 2, K = a.K, E = a.E;
+  const uint32_t D = a.D, nb = D / 32, K = a.K, E = a.E;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* xs = cert_smem + (size_t)warp * cert_warp_floats(D);
   float* pb = xs + cert_x_floats(D);     // [32][nb + 1]
@@ -193,18 +194,18 @@ __global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const Rout
     }
     __syncwarp();
 
-    // ---- exact logits of the candidates, 32 at a time: lanes take
-    // (candidate, block) pairs, then lane c adds candidate c's blocks in order ----
-    for (uint32_t cb = 0; cb < n_c; cb += 32u) {
-      const uint32_t nbt = min(32u, n_c - cb), npairs = nbt * nb;
-      const uint32_t myid = all ? cb + (uint32_t)lane : rec_id;  // candidate cb + lane
+    // ---- exact logits of up to 32 candidates (candidate c = cb + lane has
+    // id myid): lanes take (candidate, block) pairs, then lane c adds
+    // candidate c's blocks in order and the bias ----
+    auto batch_logits = [&](uint32_t cb, uint32_t nbt, uint32_t myid) -> float {
+      const uint32_t npairs = nbt * nb;
       // pair p = c * nb + b; this lane's pairs are lane, lane + 32, ..., their
       // (c, b) stepped by subtraction instead of a division per pair
       uint32_t c_n = (uint32_t)lane / nb, b_n = (uint32_t)lane - c_n * nb;
       for (uint32_t p0 = 0; p0 < npairs; p0 += 128u) {
         // every load of this lane's (up to) four pairs first, then the arithmetic
         uint4 wv[4];
-        float sc[4], zf[4];
+        float2 sz[4];
         uint32_t cc[4], bb[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
@@ -214,15 +215,10 @@ __global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const Rout
           cc[u] = c;
           bb[u] = b;
           wv[u] = make_uint4(0u, 0u, 0u, 0u);
-          sc[u] = 0.0f;
-          zf[u] = 0.0f;
+          sz[u] = make_float2(0.0f, 0.0f);
           if (ok) {
             wv[u] = *reinterpret_cast<const uint4*>(a.w_int4 + (size_t)e * (D / 2) + 16 * b);
-            sc[u] = f16_ref_to_f32(a.w_scales[(size_t)e * nb + b]);
-            if (a.w_zp) {
-              const uint8_t zb = a.w_zp[(size_t)e * zs + (b >> 1)];
-              zf[u] = (float)((b & 1) ? (zb >> 4) & 15 : zb & 15);
-            }
+            sz[u] = *reinterpret_cast<const float2*>(a.w_sz + 2 * ((size_t)e * nb + b));
           }
           b_n += 32u;
           while (b_n >= nb) { b_n -= nb; c_n++; }
@@ -230,78 +226,94 @@ __global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const Rout
 #pragma unroll
         for (int u = 0; u < 4; u++) {
           if (p0 + (uint32_t)lane + 32u * u >= npairs) break;
-          const float nz = -(8388608.0f + zf[u]);
           pb[cc[u] * (nb + 1) + bb[u]] =
-              __fmul_rn(block_dot_ref(xs + bb[u] * 36u, wv[u], f2pack(nz, nz), tile_path), sc[u]);
+              __fmul_rn(block_dot_ref(xs + bb[u] * 36u, wv[u], f2pack(sz[u].y, sz[u].y), tile_path), sz[u].x);
         }
       }
       __syncwarp();
+      float v = 0.0f;
       if ((uint32_t)lane < nbt) {
         float sum = 0.0f;
         for (uint32_t b = 0; b < nb; b++) sum = __fadd_rn(sum, pb[lane * (nb + 1) + b]);
-        cv[cb + lane] = __fadd_rn(sum, f16_ref_to_f32(a.bias[myid]));
-        ci[cb + lane] = (int)myid;
+        v = __fadd_rn(sum, f16_ref_to_f32(a.bias[myid]));
       }
       __syncwarp();
-    }
+      return v;
+    };
 
-    // ---- top K among the candidates: K rounds of a warp-wide maximum of
-    // cand_key (value descending, then expert id ascending, the order of
-    // router_topk_kernel and the reference's insertion) ----
-    uint64_t kr[4];  // this lane's entries lane + 32 j (0 = none or taken)
+    // ---- the top K, (value descending, then expert id ascending: the order of
+    // router_topk_kernel and the reference's insertion); lane r < K ends up
+    // holding choice r in sel_v / sel_e ----
+    float sel_v = 0.0f;
+    uint32_t sel_e = 0u;
+    if (!all) {
+      // one candidate per lane: its rank is the number of better candidates
+      const float v = batch_logits(0u, n_c, rec_id);
+      const bool valid = (uint32_t)lane < n_c;
+      const uint64_t key = valid ? cand_key(v, rec_id) : 0u;
+      uint32_t rank = 0;
+      for (uint32_t j = 0; j < n_c; j++) rank += __shfl_sync(0xffffffffu, key, j) > key ? 1u : 0u;
+      uint32_t src = 0;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const uint32_t k = (uint32_t)lane + 32u * j;
-      kr[j] = k < n_c ? cand_key(cv[k], (uint32_t)ci[k]) : 0u;
+      for (uint32_t r = 0; r < 8; r++) {
+        const uint32_t bal = __ballot_sync(0xffffffffu, valid && rank == r);
+        if ((uint32_t)lane == r && bal) src = (uint32_t)(__ffs(bal) - 1);
+      }
+      sel_v = __shfl_sync(0xffffffffu, v, src);
+      sel_e = __shfl_sync(0xffffffffu, rec_id, src);
+    } else {
+      // every expert: batches of 32 into shared memory, then K rounds of a
+      // warp-wide maximum of the keys
+      for (uint32_t cb = 0; cb < E; cb += 32u) {
+        const uint32_t nbt = min(32u, E - cb);
+        const float v = batch_logits(cb, nbt, cb + (uint32_t)lane);
+        if ((uint32_t)lane < nbt) {
+          cv[cb + lane] = v;
+          ci[cb + lane] = (int)(cb + lane);
+        }
+      }
+      __syncwarp();
+      uint64_t kr[4];  // this lane's entries lane + 32 j (0 = none or taken)
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint32_t k = (uint32_t)lane + 32u * j;
+        kr[j] = k < E ? cand_key(cv[k], (uint32_t)ci[k]) : 0u;
+      }
+#pragma unroll
+      for (uint32_t r = 0; r < 8; r++) {
+        if (r >= K) break;
+        uint64_t best = kr[0];
+#pragma unroll
+        for (int j = 1; j < 4; j++) best = kr[j] > best ? kr[j] : best;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+          best = other > best ? other : best;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          if (kr[j] == best) kr[j] = 0u;
+        if ((uint32_t)lane == r) {
+          sel_v = key_value(best);
+          sel_e = ~(uint32_t)best;
+        }
+      }
     }
-    float ov[8];
-    int oi[8];
+    // softmax over the K values in order (wasm_exports.zig:919-958), x 1/K in
+    // double; the first choice holds the maximum
+    const float m = __shfl_sync(0xffffffffu, sel_v, 0);
+    const float ex = (uint32_t)lane < K ? expf_ref(__fsub_rn(sel_v, m)) : 0.0f;
+    float ssum = 0.0f;
 #pragma unroll
     for (uint32_t r = 0; r < 8; r++) {
-      ov[r] = 0.0f;
-      oi[r] = 0;
-      if (r >= K) continue;
-      uint64_t best = kr[0];
-#pragma unroll
-      for (int j = 1; j < 4; j++) best = kr[j] > best ? kr[j] : best;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
-        best = other > best ? other : best;
-      }
-#pragma unroll
-      for (int j = 0; j < 4; j++)
-        if (kr[j] == best) kr[j] = 0u;
-      ov[r] = key_value(best);
-      oi[r] = (int)(~(uint32_t)best);
+      const float er = __shfl_sync(0xffffffffu, ex, r);
+      if (r < K) ssum = __fadd_rn(ssum, er);
     }
-    // softmax over the K values in order (wasm_exports.zig:919-958), x 1/K in double
-    float m = ov[0];
-#pragma unroll
-    for (uint32_t c = 1; c < 8; c++)
-      if (c < K && ov[c] > m) m = ov[c];
-    float mine = ov[0];
-#pragma unroll
-    for (int c = 1; c < 8; c++)
-      if (lane == c) mine = ov[c];
-    const float my_e = expf_ref(__fsub_rn(mine, m));
-    float ex[8];
-#pragma unroll
-    for (uint32_t c = 0; c < 8; c++) ex[c] = __shfl_sync(0xffffffffu, my_e, c);
-    if (lane == 0) {
-      float s = 0.0f;
-#pragma unroll
-      for (uint32_t c = 0; c < 8; c++)
-        if (c < K) s = __fadd_rn(s, ex[c]);
-      const float inv = s > 0.0f ? __fdiv_rn(1.0f, s) : __fdiv_rn(1.0f, (float)K);
-      const double inv_k = 1.0 / (double)K;
-#pragma unroll
-      for (uint32_t c = 0; c < 8; c++) {
-        if (c >= K) break;
-        a.idx[(size_t)t * K + c] = oi[c];
-        a.w[(size_t)t * K + c] = (float)((double)__fmul_rn(ex[c], inv) * inv_k);
-        atomicAdd(&h[oi[c]], 1);
-      }
+    const float inv = ssum > 0.0f ? __fdiv_rn(1.0f, ssum) : __fdiv_rn(1.0f, (float)K);
+    if ((uint32_t)lane < K) {
+      a.idx[(size_t)t * K + lane] = (int32_t)sel_e;
+      a.w[(size_t)t * K + lane] = (float)((double)__fmul_rn(ex, inv) * (1.0 / (double)K));
+      atomicAdd(&h[sel_e], 1);
     }
     __syncwarp();
   }
@@ -358,15 +370,17 @@ cudaError_t launch_f32_to_f16_absum(const float* x, uint16_t* y, float* absum, u
   return launch_pdl(f32_to_f16_absum_kernel, dim3((T + 7) / 8), dim3(256), 0, st, x, y, absum, T, D);
 }
 
-// Host: the bound table of a router weight in reference layout (int4 [E][D/2],
-// fp16 scales [E][D/32], zero points [E][ceil(D/64)] or none, fp16 bias [E]):
-// out[e] = max_i |w_ei| and out[kMaxRouterExperts + e] = sum_i |w_ei| * 2^-24
-// + 1e-6, with |w_ei| = |q - zp| * |scale| and the scale decoded both ways
-// (IEEE and the reference's subnormal quirk), taking the larger.
+// Host: the tables of a router weight in reference layout (int4 [E][D/2],
+// fp16 scales [E][D/32], zero points [E][ceil(D/64)] or none):
+//   bound[e] = max_i |w_ei|, bound[kMaxRouterExperts + e] = sum_i |w_ei| *
+//   2^-24 + 1e-6, with |w_ei| = |q - zp| * |scale| and the scale decoded both
+//   ways (IEEE and the reference's subnormal quirk), taking the larger;
+//   sz[2 (e nb + b)] = the block's scale as the reference decodes it,
+//   sz[2 (e nb + b) + 1] = -(2^23 + zp) (router_cert_kernel's nibble offset).
 void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8_t* zp, uint32_t E, uint32_t D,
-                        float* out) {
+                        float* bound, float* sz) {
   const uint32_t nb = D / 32, zs = (nb + 1) / 2;
-  for (uint32_t i = 0; i < 2 * kMaxRouterExperts; i++) out[i] = 0.0f;
+  for (uint32_t i = 0; i < 2 * kMaxRouterExperts; i++) bound[i] = 0.0f;
   for (uint32_t e = 0; e < E && e < kMaxRouterExperts; e++) {
     double wmax = 0.0, wsum = 0.0;
     for (uint32_t b = 0; b < nb; b++) {
@@ -376,12 +390,19 @@ void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8
       if (ex == 31) ieee = INFINITY;
       // the reference's decode (math.zig:45-52): a subnormal is read as if normal
       const double quirk = ex == 0 && mant ? std::ldexp(1.0 + mant / 1024.0, -15) : ieee;
-      const double sc = std::fmax(ieee, quirk);
+      const double sc = std::fmax(ieee, quirk);  // both decodes are bounded
       int z = 0;
       if (zp) {
         const uint8_t zb = zp[(size_t)e * zs + (b >> 1)];
         z = (b & 1) ? (zb >> 4) & 15 : zb & 15;
       }
+      // the scale exactly as f16_ref_to_f32 reads it on the device
+      const uint32_t rest = s16 & 0x7fffu;
+      const uint32_t bits = ((uint32_t)(s16 & 0x8000u) << 16) | (rest ? (rest << 13) + (112u << 23) : 0u);
+      float ref;
+      std::memcpy(&ref, &bits, 4);
+      sz[2 * ((size_t)e * nb + b)] = ref;
+      sz[2 * ((size_t)e * nb + b) + 1] = -(8388608.0f + (float)z);
       for (uint32_t i = 0; i < 32; i++) {
         const uint8_t byte = int4[(size_t)e * (D / 2) + 16 * b + i / 2];
         const int qv = (i & 1) ? (byte >> 4) & 15 : byte & 15;
@@ -390,8 +411,8 @@ void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8
         wsum += w;
       }
     }
-    out[e] = (float)(wmax * (1.0 + 1e-6));
-    out[kMaxRouterExperts + e] = (float)(wsum * std::ldexp(1.0, -24) + 1e-6);
+    bound[e] = (float)(wmax * (1.0 + 1e-6));
+    bound[kMaxRouterExperts + e] = (float)(wsum * std::ldexp(1.0, -24) + 1e-6);
   }
 }
 

@@ -196,6 +196,7 @@ struct LayerDev {
   DevArr<float> sinks;
   W4Dev qkv, o, router, gate_up, down;
   DevArr<float> rbound;  // the router's bound table (ts::router_bound_table), E <= kMaxRouterExperts
+  DevArr<float> rsz;     // the router's per-block scale and zero-point table
 };
 
 struct Workspace {
@@ -453,7 +454,7 @@ ts::RouterCertArgs router_cert_args(ts_cuda* h, const LayerDev& L, const RouterI
   ts::RouterCertArgs a;
   a.cand = reinterpret_cast<const uint8_t*>(h->ws.rcand.p);
   a.x32 = rin.x32; a.a = rin.a; a.b = rin.b; a.gamma = rin.gamma; a.eps = c.eps;
-  a.w_int4 = L.router.int4.p; a.w_scales = L.router.scales.p; a.w_zp = L.router.has_zp ? L.router.zp.p : nullptr;
+  a.w_int4 = L.router.int4.p; a.w_sz = L.rsz.p;
   a.bias = L.router.bias.p;
   a.rloc = rloc; a.rlen = rlen; a.idx = idx; a.w = wt; a.hist = hist;
   a.T = T; a.D = c.d_model; a.E = c.n_experts; a.K = c.top_k;
@@ -872,10 +873,13 @@ int ts_cuda_finalize(ts_cuda_t* h) {
                         p8(p + "experts.down.zp"), p16(p + "experts.down.bias"), E, D, F, 128, true, bad.p, st)))
       return rc;
     if (E <= ts::kMaxRouterExperts) {
-      std::vector<float> tb(2 * ts::kMaxRouterExperts);
-      ts::router_bound_table(p8(p + "router.int4"), p16(p + "router.scales"), p8(p + "router.zp"), E, D, tb.data());
+      std::vector<float> tb(2 * ts::kMaxRouterExperts), tsz(2 * (size_t)E * (D / 32));
+      ts::router_bound_table(p8(p + "router.int4"), p16(p + "router.scales"), p8(p + "router.zp"), E, D, tb.data(),
+                             tsz.data());
       TS_CUDA_TRY(L->rbound.alloc(tb.size()));
       TS_CUDA_TRY(cudaMemcpy(L->rbound.p, tb.data(), tb.size() * 4, cudaMemcpyHostToDevice));
+      TS_CUDA_TRY(L->rsz.alloc(tsz.size()));
+      TS_CUDA_TRY(cudaMemcpy(L->rsz.p, tsz.data(), tsz.size() * 4, cudaMemcpyHostToDevice));
     }
     h->layers.push_back(std::move(L));
   }

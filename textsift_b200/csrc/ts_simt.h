@@ -132,11 +132,10 @@ struct RouterCertArgs {
   const uint16_t* b = nullptr;     //   attention output fp16 [T, D]
   const uint16_t* gamma = nullptr; //   norm weight fp16 [D]
   float eps = 0.0f;
-  // the router weight in reference layout: int4 [E][D/2], fp16 scales
-  // [E][D/32], zero points [E][ceil(D/64)] (or null), fp16 bias [E]
+  // the router weight: int4 [E][D/2] in reference layout, the table of
+  // router_bound_table (scale, -(2^23 + zp) per block), fp16 bias [E]
   const uint8_t* w_int4 = nullptr;
-  const uint16_t* w_scales = nullptr;
-  const uint8_t* w_zp = nullptr;
+  const float* w_sz = nullptr;  // per (expert, block): scale (reference decode), -(2^23 + zp)
   const uint16_t* bias = nullptr;
   const int* rloc = nullptr;  // token position / sequence length (tile or tail path); null: row t of T
   const int* rlen = nullptr;
@@ -149,9 +148,10 @@ cudaError_t launch_router_cert(const RouterCertArgs& a, int src, cudaStream_t st
 // fp16 copy of f32 rows and each row's sum of |x| (the router bound's S).
 cudaError_t launch_f32_to_f16_absum(const float* x, uint16_t* y, float* absum, uint32_t T, uint32_t D, cudaStream_t st);
 // Host: the router's bound table, f32 [2][kMaxRouterExperts] (max |w| per
-// expert, then the additive term per expert).
+// expert, then the additive term per expert), and the per-block scale /
+// zero-point table, f32 [E][D/32][2].
 void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8_t* zp, uint32_t E, uint32_t D,
-                        float* out);
+                        float* bound, float* sz);
 
 // Sets the calling thread's message returned by ts_cuda_last_error().
 void set_last_error(const char* msg);
