@@ -54,7 +54,7 @@ struct GemmCfg {
   static constexpr uint32_t OFF_MISC = OFF_BIAS + 2 * BN * 4;
   // f32 [2][kMaxRouterExperts]: the router bound table (kEpiRouterCert)
   static constexpr uint32_t OFF_RB = OFF_MISC + 16;
-  static constexpr uint32_t SMEM_BYTES = OFF_RB + 2 * kMaxRouterExperts * 4 + 1024;  // + alignment slack
+  static constexpr uint32_t SMEM_BYTES = OFF_RB + (2 * kMaxRouterExperts + 4) * 4 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;                    // two accumulators
   static constexpr uint32_t ACC_STRIDE = 256;                   // column offset of tile buffer 1
   static constexpr uint32_t ACC_ROWS = BM / 128;                // 128-row accumulators per tile buffer
@@ -167,7 +167,8 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, uint32_t 
 //   B_e = kRouterCertRel * wmax_e * S + add_e + S * 2^-24 + |v_e| * 2^-22,
 // with S = sum |x| of the token (a.absum), wmax_e = max_i |w_ei| and add_e
 // covering the subnormal and bias-decode terms (the per-expert table
-// a.rbound = [wmax_0..wmax_{E-1}, add_0..add_{E-1}], built with the weights).
+// a.rbound = [wmax_0..wmax_127, add_0..add_127, max wmax, max add], built
+// with the weights).
 // kRouterCertRel = 1.5e-3 bounds 2 * 2^-11 (the two fp16 roundings) plus
 // 2e-4 for the tensor core's f32 accumulation and 2e-6 for the reference's.
 // With tau = min over the approximate top 4 of (v_a - B_a), the exact 4th
@@ -218,8 +219,12 @@ __device__ __forceinline__ void router_cert_epilogue(const GemmArgs& a, uint32_t
   tau = fminf(tau, t3 - router_bound(cS, addS, srb, (uint32_t)i3, t3));
   // pass 2: every expert whose logit may reach tau, as a 32-byte record:
   // byte 0 = the count, bytes 1..31 = expert ids (count 0xFF: more than 31,
-  // or a value that is not finite -- every expert is then a candidate)
-  uint32_t n = 0, rec[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+  // or a value that is not finite -- every expert is then a candidate).  A
+  // column below tau by more than the largest bound of the table is no
+  // candidate without its own bound.
+  const float reach = tau - 1.0001f * fmaf(cS, srb[2 * kMaxRouterExperts], srb[2 * kMaxRouterExperts + 1] + addS);
+  uint8_t* rec = reinterpret_cast<uint8_t*>(a.out0) + 32 * (size_t)grow;
+  uint32_t n = 0;
 #pragma unroll 1
   for (uint32_t c0 = 0; c0 < 128; c0 += 32) {
     uint32_t v[32];
@@ -235,21 +240,14 @@ __device__ __forceinline__ void router_cert_epilogue(const GemmArgs& a, uint32_t
       const uint32_t c = c0 + (uint32_t)j;
       if (c >= a.N) break;
       const float x = __fadd_rn(__uint_as_float(v[j]), sbias[c]);
-      if (x + router_bound(cS, addS, srb, c, x) >= tau) {
+      if (x + 2.384185791015625e-7f * fabsf(x) >= reach && x + router_bound(cS, addS, srb, c, x) >= tau) {
         n++;
-        if (n < 32) {
-#pragma unroll
-          for (uint32_t q = 0; q < 8; q++)
-            if (q == (n >> 2)) rec[q] |= c << (8 * (n & 3u));
-        }
+        if (row_ok && n < 32) rec[n] = (uint8_t)c;
       }
     }
   }
   if (!row_ok) return;
-  rec[0] |= (!finite || n > 31) ? 0xFFu : n;
-  uint4* o = reinterpret_cast<uint4*>(a.out0) + 2 * (size_t)grow;
-  o[0] = make_uint4(rec[0], rec[1], rec[2], rec[3]);
-  o[1] = make_uint4(rec[4], rec[5], rec[6], rec[7]);
+  rec[0] = (uint8_t)((!finite || n > 31) ? 0xFFu : n);
 }
 
 struct TileInfo {
@@ -436,7 +434,10 @@ __global__ void __launch_bounds__(640, 1)
     float* srb = reinterpret_cast<float*>(smem + C::OFF_RB);
     // the router bound table, visible to all epilogue warps once the first
     // tile's bias barrier below has completed
-    if constexpr (EPI == kEpiRouterCert) srb[et] = args.rbound[et];
+    if constexpr (EPI == kEpiRouterCert) {
+      srb[et] = args.rbound[et];
+      if (et < 2) srb[2 * kMaxRouterExperts + et] = args.rbound[2 * kMaxRouterExperts + et];
+    }
     uint32_t lt = 0;
     for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x, lt++) {
       const uint32_t b = lt & 1u, bph = (lt >> 1) & 1u;

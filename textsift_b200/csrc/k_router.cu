@@ -31,7 +31,7 @@ namespace ts {
 namespace {
 
 constexpr uint32_t kCertThreads = 256;  // 8 warps, one token at a time each
-constexpr uint32_t kCertTokens = 64;    // tokens per block, inside one permutation chunk
+constexpr uint32_t kCertTokens = 32;    // tokens per block, inside one permutation chunk
 static_assert(kPermChunk % kCertTokens == 0, "a block's tokens share one permutation chunk");
 
 // Nibble j (0..3 = byte j) of lohi (lo = w & 0x0F0F0F0F or hi = (w >> 4) &
@@ -374,13 +374,14 @@ cudaError_t launch_f32_to_f16_absum(const float* x, uint16_t* y, float* absum, u
 // fp16 scales [E][D/32], zero points [E][ceil(D/64)] or none):
 //   bound[e] = max_i |w_ei|, bound[kMaxRouterExperts + e] = sum_i |w_ei| *
 //   2^-24 + 1e-6, with |w_ei| = |q - zp| * |scale| and the scale decoded both
-//   ways (IEEE and the reference's subnormal quirk), taking the larger;
+//   ways (IEEE and the reference's subnormal quirk), taking the larger; then
+//   the largest of each (bound[2 kMaxRouterExperts], [.. + 1]);
 //   sz[2 (e nb + b)] = the block's scale as the reference decodes it,
 //   sz[2 (e nb + b) + 1] = -(2^23 + zp) (router_cert_kernel's nibble offset).
 void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8_t* zp, uint32_t E, uint32_t D,
                         float* bound, float* sz) {
   const uint32_t nb = D / 32, zs = (nb + 1) / 2;
-  for (uint32_t i = 0; i < 2 * kMaxRouterExperts; i++) bound[i] = 0.0f;
+  for (uint32_t i = 0; i < 2 * kMaxRouterExperts + 2; i++) bound[i] = 0.0f;
   for (uint32_t e = 0; e < E && e < kMaxRouterExperts; e++) {
     double wmax = 0.0, wsum = 0.0;
     for (uint32_t b = 0; b < nb; b++) {
@@ -413,6 +414,8 @@ void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8
     }
     bound[e] = (float)(wmax * (1.0 + 1e-6));
     bound[kMaxRouterExperts + e] = (float)(wsum * std::ldexp(1.0, -24) + 1e-6);
+    bound[2 * kMaxRouterExperts] = std::fmax(bound[2 * kMaxRouterExperts], bound[e]);
+    bound[2 * kMaxRouterExperts + 1] = std::fmax(bound[2 * kMaxRouterExperts + 1], bound[kMaxRouterExperts + e]);
   }
 }
 

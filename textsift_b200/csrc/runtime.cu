@@ -873,7 +873,7 @@ int ts_cuda_finalize(ts_cuda_t* h) {
                         p8(p + "experts.down.zp"), p16(p + "experts.down.bias"), E, D, F, 128, true, bad.p, st)))
       return rc;
     if (E <= ts::kMaxRouterExperts) {
-      std::vector<float> tb(2 * ts::kMaxRouterExperts), tsz(2 * (size_t)E * (D / 32));
+      std::vector<float> tb(2 * ts::kMaxRouterExperts + 2), tsz(2 * (size_t)E * (D / 32));
       ts::router_bound_table(p8(p + "router.int4"), p16(p + "router.scales"), p8(p + "router.zp"), E, D, tb.data(),
                              tsz.data());
       TS_CUDA_TRY(L->rbound.alloc(tb.size()));

@@ -79,7 +79,7 @@ struct GemmArgs {
   const uint16_t* rope_sin = nullptr;
   const uint32_t* rope_cs = nullptr;  // kEpiQkvRope (launch_gemm_w4_tm): cos | sin << 16, [pos][32]
   const float* absum = nullptr;      // kEpiRouterCert: sum |x| of each row's f32 input
-  const float* rbound = nullptr;     // kEpiRouterCert: f32 [2][kMaxRouterExperts] wmax_e, add_e
+  const float* rbound = nullptr;     // kEpiRouterCert: f32 wmax_e [128], add_e [128], their maxima [2]
   int* err = nullptr;
 };
 

@@ -147,8 +147,8 @@ struct RouterCertArgs {
 cudaError_t launch_router_cert(const RouterCertArgs& a, int src, cudaStream_t st);
 // fp16 copy of f32 rows and each row's sum of |x| (the router bound's S).
 cudaError_t launch_f32_to_f16_absum(const float* x, uint16_t* y, float* absum, uint32_t T, uint32_t D, cudaStream_t st);
-// Host: the router's bound table, f32 [2][kMaxRouterExperts] (max |w| per
-// expert, then the additive term per expert), and the per-block scale /
+// Host: the router's bound table, f32 [2 kMaxRouterExperts + 2] (max |w| per
+// expert, the additive term per expert, the largest of each), and the per-block scale /
 // zero-point table, f32 [E][D/32][2].
 void router_bound_table(const uint8_t* int4, const uint16_t* scales, const uint8_t* zp, uint32_t E, uint32_t D,
                         float* bound, float* sz);
