@@ -76,6 +76,59 @@ __global__ void embed_gather_kernel(const uint8_t* __restrict__ w, const uint16_
   }
 }
 
+// The same gather from the forward's packed table: vocabulary row id holds
+// its D/2 nibble bytes, then its D/32 fp16 scales, then its zero-point bytes,
+// padded to row_bytes (a multiple of 128), so one token's gather reads whole
+// 128-byte lines of one region instead of parts of three tables.
+__global__ void embed_rows_kernel(const uint8_t* __restrict__ rows, uint32_t row_bytes, const int32_t* __restrict__ ids,
+                                  uint16_t* __restrict__ out, uint32_t T, uint32_t V, uint32_t D) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t nb = D / 32;
+  uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= T * nb) return;
+  uint32_t t = gid / nb, b = gid % nb;
+  int32_t id = ids[t];
+  uint4* o = reinterpret_cast<uint4*>(out + (size_t)t * D + b * 32);
+  if (id < 0 || (uint32_t)id >= V) {
+    for (int i = 0; i < 4; i++) o[i] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint8_t* row = rows + (size_t)id * row_bytes;
+  const uint4 pk = *reinterpret_cast<const uint4*>(row + b * 16);
+  const float s = f16_ref_to_f32(*reinterpret_cast<const uint16_t*>(row + D / 2 + 2 * b));
+  const uint8_t zb = row[D / 2 + 2 * nb + (b >> 1)];
+  const int z = (b & 1) ? (zb >> 4) & 15 : zb & 15;
+  const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {  // byte j of word q holds elements 8q+2j (lo) and 8q+2j+1 (hi)
+      uint32_t byte = (wd[q] >> (8 * j)) & 0xffu;
+      float lo = __fmul_rn((float)((int)(byte & 15u) - z), s);
+      float hi = __fmul_rn((float)((int)(byte >> 4) - z), s);
+      r[j] = (uint32_t)f32_to_f16_ref(lo) | ((uint32_t)f32_to_f16_ref(hi) << 16);
+    }
+    o[q] = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+// Builds the packed table: one thread per (row, byte) of the packed row.
+__global__ void embed_pack_kernel(const uint8_t* __restrict__ w, const uint16_t* __restrict__ sc,
+                                  const uint8_t* __restrict__ zp, uint8_t* __restrict__ rows, uint32_t row_bytes,
+                                  uint32_t V, uint32_t D) {
+  const uint32_t nb = D / 32, zs = (nb + 1) / 2;
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)V * row_bytes) return;
+  const uint32_t r = (uint32_t)(i / row_bytes), c = (uint32_t)(i % row_bytes);
+  uint8_t v = 0;
+  if (c < D / 2) v = w[(size_t)r * (D / 2) + c];
+  else if (c < D / 2 + 2 * nb) v = reinterpret_cast<const uint8_t*>(sc + (size_t)r * nb)[c - D / 2];
+  else if (c < D / 2 + 2 * nb + zs) v = zp[(size_t)r * zs + (c - D / 2 - 2 * nb)];
+  rows[i] = v;
+}
+
 // ---------------------------------------------------------------------------
 // RMSNorm fp16 -> f32 (and/or the fp16 tensor-core operand), one warp per row.
 // Lanes 0..3 accumulate the four 4-lane partial sums of squares in order.
@@ -890,6 +943,23 @@ cudaError_t launch_seq_info(const uint32_t* offs, uint32_t n_seqs, uint32_t T, i
                             cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   return launch_pdl(seq_info_kernel, dim3(nblk(T, 256)), dim3(256), 0, st, offs, n_seqs, T, pos, sstart, slen);
+}
+
+uint32_t embed_row_bytes(uint32_t D) { return (D / 2 + 2 * (D / 32) + (D / 32 + 1) / 2 + 127) & ~127u; }
+
+cudaError_t launch_embed_pack(const uint8_t* w, const uint16_t* sc, const uint8_t* zp, uint8_t* rows, uint32_t V,
+                              uint32_t D, cudaStream_t st) {
+  const size_t n = (size_t)V * embed_row_bytes(D);
+  if (n == 0) return cudaSuccess;
+  embed_pack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, sc, zp, rows, embed_row_bytes(D), V, D);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed_rows(const uint8_t* rows, const int32_t* ids, uint16_t* out, uint32_t T, uint32_t V,
+                              uint32_t D, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  return launch_pdl(embed_rows_kernel, dim3(nblk((size_t)T * (D / 32), 128)), dim3(128), 0, st, rows,
+                    embed_row_bytes(D), ids, out, T, V, D);
 }
 
 cudaError_t launch_embed(const uint8_t* w, const uint16_t* sc, const uint8_t* zp, const int32_t* ids, uint16_t* out,

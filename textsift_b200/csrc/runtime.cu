@@ -229,6 +229,7 @@ struct ts_cuda {
   bool finalized = false;
   // device weights
   DevArr<uint8_t> embed_int4, embed_zp;
+  DevArr<uint8_t> embed_rows;  // the packed table the forward gathers from (ts::embed_row_bytes per row)
   DevArr<uint16_t> embed_scales, final_norm;
   W4Dev score;
   std::vector<std::unique_ptr<LayerDev>> layers;
@@ -598,7 +599,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   {
     Phase p(h, st, TS_PHASE_OTHER, 0, 2);
     TS_K(ts::launch_seq_info(w.offs.p, n_seqs, T, w.pos.p, w.sstart.p, w.slen.p, st));
-    TS_K(ts::launch_embed(h->embed_int4.p, h->embed_scales.p, h->embed_zp.p, d_ids, w.x0.p, T, c.vocab, D, st));
+    TS_K(ts::launch_embed_rows(h->embed_rows.p, d_ids, w.x0.p, T, c.vocab, D, st));
   }
   uint64_t band_pairs = 0;  // sum over tokens of the keys each query attends (attention flops)
   for (uint32_t s = 0; s < n_seqs; s++) {
@@ -829,6 +830,8 @@ int ts_cuda_finalize(ts_cuda_t* h) {
   if ((rc = up(h->embed_int4, "embed.int4")) || (rc = up(h->embed_scales, "embed.scales")) ||
       (rc = up(h->embed_zp, "embed.zp")) || (rc = up(h->final_norm, "final_norm")))
     return rc;
+  TS_CUDA_TRY(h->embed_rows.alloc((size_t)c.vocab * ts::embed_row_bytes(D)));
+  TS_CUDA_TRY(ts::launch_embed_pack(h->embed_int4.p, h->embed_scales.p, h->embed_zp.p, h->embed_rows.p, c.vocab, D, st));
   auto p8 = [&](const std::string& n) { return staged_ptr(h, n); };
   auto p16 = [&](const std::string& n) { return reinterpret_cast<const uint16_t*>(staged_ptr(h, n)); };
   DevArr<int> bad;
@@ -896,6 +899,10 @@ int ts_cuda_finalize(ts_cuda_t* h) {
   int nbad = 0;
   TS_CUDA_TRY(cudaMemcpyAsync(&nbad, bad.p, 4, cudaMemcpyDeviceToHost, st));
   TS_CUDA_TRY(cudaStreamSynchronize(st));
+  // the forward gathers from the packed table only
+  h->embed_int4.release();
+  h->embed_scales.release();
+  h->embed_zp.release();
   if (nbad)
     return fail(TS_ERR_UNSUPPORTED,
                 "%d fp16 weight scales are subnormal, inf or NaN; the tensor-core path reproduces the reference "

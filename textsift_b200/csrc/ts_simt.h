@@ -33,6 +33,13 @@ struct ExactArgs {
 
 cudaError_t launch_seq_info(const uint32_t* offs, uint32_t n_seqs, uint32_t T, int* pos, int* sstart, int* slen,
                             cudaStream_t st);
+// The forward's packed embedding table: per vocabulary row its nibbles,
+// scales and zero points in one row of embed_row_bytes(D) bytes.
+uint32_t embed_row_bytes(uint32_t D);
+cudaError_t launch_embed_pack(const uint8_t* w, const uint16_t* sc, const uint8_t* zp, uint8_t* rows, uint32_t V,
+                              uint32_t D, cudaStream_t st);
+cudaError_t launch_embed_rows(const uint8_t* rows, const int32_t* ids, uint16_t* out, uint32_t T, uint32_t V,
+                              uint32_t D, cudaStream_t st);
 cudaError_t launch_embed(const uint8_t* w, const uint16_t* sc, const uint8_t* zp, const int32_t* ids, uint16_t* out,
                          uint32_t T, uint32_t V, uint32_t D, cudaStream_t st);
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* gamma, float* out32, uint16_t* out16, uint32_t T,
