@@ -112,7 +112,7 @@ __host__ __device__ constexpr uint32_t cert_warp_floats(uint32_t D) {
 }
 
 template <int SRC>
-__global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const RouterCertArgs a) {
+__global__ void __launch_bounds__(kCertThreads, 4) router_cert_kernel(const RouterCertArgs a) {
   extern __shared__ __align__(16) float cert_smem[];
   __shared__ int h[kMaxRouterExperts];
   pdl_trigger();
@@ -146,7 +146,6 @@ __global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const Rout
       // l + 64, l + 96 of 8 values, the same sum-of-squares chain, the same
       // shuffle tree and rsqrtf, the same products
       const uint32_t nc = D / 8;
-      uint32_t sw[4][4];  // the fp16-rounded sums of this lane's chunks
       float ss = 0.0f;
 #pragma unroll
       for (int r = 0; r < 4; r++) {
@@ -162,22 +161,28 @@ __global__ void __launch_bounds__(kCertThreads, 3) router_cert_kernel(const Rout
           const float s0 = fa.x + fb.x, s1 = fa.y + fb.y;
           ss = fmaf(s0, s0, ss);
           ss = fmaf(s1, s1, ss);
-          sw[r][j] = f32x2_to_h2(s0, s1);
         }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float inv_rms = rsqrtf(ss / (float)D + a.eps);
+      // the same chunks again (cache hits): the fp16-rounded sums, normalised
 #pragma unroll
       for (int r = 0; r < 4; r++) {
         const uint32_t c = (uint32_t)lane + 32u * r;
         if (c >= nc) break;
+        const uint4 av = *reinterpret_cast<const uint4*>(a.a + base + 8 * c);
+        const uint4 bv = *reinterpret_cast<const uint4*>(a.b + base + 8 * c);
         const uint4 gv = *reinterpret_cast<const uint4*>(a.gamma + 8 * c);
+        const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
         const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
         float o8[8];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&sw[r][j]));
+          const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
+          const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
+          const uint32_t sw = f32x2_to_h2(fa.x + fb.x, fa.y + fb.y);
+          const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&sw));
           const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
           o8[2 * j] = x.x * inv_rms * g.x;
           o8[2 * j + 1] = x.y * inv_rms * g.y;
