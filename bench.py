@@ -11,7 +11,10 @@ seeded q4f16 weights.  Document-parallel: each rank gets its own documents
 of at most --max-tokens tokens per rank.  "Classified tokens" counts each
 document token once (chunk overlap excluded).  --full-set runs all 8192
 documents of config[4] split across the ranks (strong scaling) instead of K
-steps per rank.
+steps per rank.  --ep (N > 1) keeps the document split but shards the
+experts: each GPU holds 128 / N experts of every layer and the routed rows
+cross NVLink (NCCL grouped send/recv) to the GPU that holds their expert and
+back, twice per layer.
 
 --config 0..3 print one line each for the other configurations (1 x 512
 forward latency; MatMulNBits tensor-core table; one MoE layer under uniform
@@ -19,7 +22,7 @@ and Zipf routing; banded attention 64 x 8192), each with its roofline and a
 bounded CPU baseline.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config 0|1|2|3|4] [--full-set]
+                  [--config 0|1|2|3|4] [--full-set] [--ep]
 
 Under torchrun (N > 1) every rank runs its share; timing is the max over
 ranks of CUDA-event time around K steps bracketed by barriers.
@@ -257,12 +260,15 @@ def weak_n_docs(args, world: int) -> int:
     return max(8, int((args.warmup + args.steps) * args.max_tokens / 2300) + 8) * world
 
 
-def config4_desc(world: int, full_set: bool = False) -> dict:
+def config4_desc(world: int, full_set: bool = False, ep: bool = False) -> dict:
+    par = (f"ep{world} (documents split over the ranks; each GPU holds {128 // world} experts per layer, routed "
+           f"rows exchanged by NCCL grouped send/recv twice per layer)" if ep
+           else f"dp{world} (documents, no collective)")
     return {"workload": "config[4]: documents U[256,4096] tokens, chunked 2048/128, full config[0] architecture, "
                         "document-parallel" + (f", all {N_DOCS_FULL} documents split over the ranks" if full_set
                                                else ""),
             "model": "privacy-filter (8 blocks, 128 experts top-4, vocab 200064)",
-            "parallelism": f"dp{world} (documents, no collective)",
+            "parallelism": par,
             "l2": "no flush: each step streams 0.8 GB of weights and GBs of activations (> 126 MB L2)"}
 
 
@@ -332,6 +338,13 @@ def run_ours(args):
     L = abi.lib()
     weights = make_weights(PF_CONFIG, seed=SEED)
     be = CudaBackend(weights, PF_CONFIG, device=local, max_tokens=args.max_tokens, max_seq_len=2048)
+    ep = args.ep and world > 1
+    if ep:
+        # expert parallelism: rank 0's NCCL id to every rank, then each rank
+        # keeps its 128 / world experts (the communicator forms here)
+        ident = [CudaBackend.ep_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(ident, src=0)
+        be.ep_init(rank, world, ident[0])
     be.warmup()
     h = be.handle
     if args.full_set:
@@ -390,7 +403,7 @@ def run_ours(args):
     # ---- the parity-green path: the same steps in exact mode (reference
     # summation order on CUDA cores), a few of them ----
     exact = None
-    if not args.no_exact:
+    if not args.no_exact and not ep:
         abi.check(L.ts_cuda_set_mode(h, abi.TS_MODE_EXACT))
         fw.step(warm_idx[0])
         ex_idx = timed_idx[:3]
@@ -421,7 +434,8 @@ def run_ours(args):
 
     if rank == 0:
         line = config4_line(args, world, ms_max, n_steps, toks_all, processed, toks, ph_ms, ph_n, ph_fl,
-                            e2e_toks_all / e2e_max, h2d, d2h, int(n_launch.value), clk.summary(), be.device_name())
+                            e2e_toks_all / e2e_max, h2d, d2h, int(n_launch.value), clk.summary(), be.device_name(),
+                            ep)
         if exact:
             line["exact_mode"] = {"value": ex_toks_all / (ex_ms_max * 1e-3), "unit": "tokens/s",
                                   "ms_per_step": ex_ms_max / exact[2], "steps": exact[2],
@@ -469,7 +483,7 @@ def config4_cpu_baseline(weights, cfg, max_tokens) -> dict:
 
 
 def config4_line(args, world, ms_max, n_steps, toks_all, processed, toks, ph_ms, ph_n, ph_fl, e2e_value, h2d, d2h,
-                 n_launch, clocks, device) -> dict:
+                 n_launch, clocks, device, ep=False) -> dict:
     from textsift_b200 import abi
     pk = peaks()
     gu = abi.PHASES.index("expert_gate_up")
@@ -485,7 +499,7 @@ def config4_line(args, world, ms_max, n_steps, toks_all, processed, toks, ph_ms,
     phases = {abi.PHASES[i]: {"ms": round(ph_ms[i], 3), "launches": int(ph_n[i]),
                               "tflops": round(ph_fl[i] / (ph_ms[i] * 1e-3) / 1e12, 1) if ph_ms[i] > 0 else None}
               for i in range(7)}
-    cfgd = config4_desc(world, args.full_set)
+    cfgd = config4_desc(world, args.full_set, ep)
     cfgd.update({"tokens_per_step_per_gpu": processed / n_steps, "unique_tokens_per_step_per_gpu": toks / n_steps,
                  "global_batch_tokens": processed / n_steps * world})
     return {"metric": METRIC, "value": toks_all / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
@@ -905,6 +919,8 @@ def main():
     ap.add_argument("--no-full-set", action="store_true", help="skip the N=1 all-documents extra measurement")
     ap.add_argument("--no-exact", action="store_true", help="skip the exact-mode extra measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep", action="store_true", help="config[4] at N > 1: expert parallelism (128 / N experts "
+                                                      "per GPU) instead of replicated weights")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

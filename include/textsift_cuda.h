@@ -289,6 +289,40 @@ int ts_cuda_op_rope(const uint16_t* d_x, uint16_t* d_out, const uint16_t* d_cos,
 int ts_cuda_op_qkv_rope(ts_cuda_t* h, uint32_t layer, const uint16_t* d_x, const uint32_t* seq_offsets,
                         uint32_t n_seqs, uint16_t* d_q, uint16_t* d_k, uint16_t* d_v, void* stream);
 
+/* ---- expert parallelism (BASELINE config[4]'s expert-parallel variant; the
+ * reference runs one process on one device and has no counterpart) ----
+ * With R ranks, each GPU holds n_experts / R consecutive experts of every
+ * layer and every rank forwards its own sequences; per layer the routed rows
+ * go to the ranks that hold their experts and the outputs come back (NCCL
+ * grouped send/recv on the forward's stream; libnccl.so.2 is opened at run
+ * time), and each token's combine is the single-GPU one (ascending expert
+ * id, the reference's order).  Fast mode only; ts_cuda_op_moe is refused on
+ * such a handle.  Every rank must run its forwards in the same order, each
+ * layer exchanging with every other rank; each layer waits once on the host
+ * for the route counts (so ts_cuda_forward_packed_device synchronizes its
+ * stream per layer on such a handle). */
+
+/* The NCCL unique id (rank 0 makes it and hands the bytes to every rank):
+ * writes it to out when out is non-NULL and cap is large enough; returns its
+ * size in bytes, 0 on failure. */
+size_t ts_cuda_ep_unique_id(uint8_t* out, size_t cap);
+
+/* Before ts_cuda_finalize: join the ranks' NCCL communicator (blocks until
+ * all `world` ranks have called it) and keep only experts
+ * [rank * n_experts / world, (rank + 1) * n_experts / world) at finalize. */
+int ts_cuda_ep_init(ts_cuda_t* h, int32_t rank, int32_t world, const uint8_t* nccl_id, size_t id_len);
+
+/* Host-only: the exchange plan of one layer on one rank.  counts: this rank's
+ * routes per global expert [world * e_local]; recv_counts: routes each source
+ * sends to each local expert [world][e_local].  Writes rows to send to /
+ * receive from each peer (send_n, recv_n [world], may be NULL) and the local
+ * grouped-GEMM tiles {local expert, first row, end row, segment start} over
+ * the received rows (source-major, then expert-major; tiles [tiles_cap][4],
+ * may be NULL), *n_tiles = their number. */
+int ts_cuda_ep_plan(const int32_t* counts, const int32_t* recv_counts, int32_t world, int32_t e_local,
+                    int32_t tile_rows, uint64_t* send_n, uint64_t* recv_n, int32_t* tiles, uint32_t tiles_cap,
+                    uint32_t* n_tiles);
+
 /* Self-test of the bounded device waits (no counterpart in the reference,
  * whose GPU work is waited for by a host fence, native/vulkan/bridge.h:95-97).
  * Enqueues on `stream` one CTA that holds TMEM while one warp waits on an

@@ -89,10 +89,7 @@ class CudaBackend:
         return b
 
     # -- lifecycle -------------------------------------------------------
-    def warmup(self) -> None:
-        """Create the device context, upload and repack weights (idempotent)."""
-        if self._ready:
-            return
+    def _create(self) -> None:
         L = abi.lib()
         if self._h is None:
             err = ctypes.create_string_buffer(1024)
@@ -100,6 +97,30 @@ class CudaBackend:
             if not h:
                 raise abi.TextsiftCudaError(abi.TS_ERR_CUDA, err.value.decode(errors="replace"))
             self._h = h
+
+    def ep_init(self, rank: int, world: int, nccl_id: bytes) -> None:
+        """Expert parallelism over `world` ranks (call on every rank before
+        warmup, with the same id from ep_unique_id() on rank 0): this
+        backend keeps experts [rank E / world, (rank + 1) E / world)."""
+        self._create()
+        ident = np.frombuffer(nccl_id, dtype=np.uint8)
+        abi.check(abi.lib().ts_cuda_ep_init(self._h, rank, world, _ptr(ident), ident.size))
+
+    @staticmethod
+    def ep_unique_id() -> bytes:
+        L = abi.lib()
+        n = L.ts_cuda_ep_unique_id(None, 0)
+        buf = (ctypes.c_uint8 * n)()
+        if L.ts_cuda_ep_unique_id(buf, n) != n:
+            raise abi.TextsiftCudaError(abi.TS_ERR_CUDA, abi.last_error())
+        return bytes(buf)
+
+    def warmup(self) -> None:
+        """Create the device context, upload and repack weights (idempotent)."""
+        if self._ready:
+            return
+        L = abi.lib()
+        self._create()
         if self._onnx is not None:
             graph, ext = self._onnx
             g = np.frombuffer(graph, dtype=np.uint8)

@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB = os.path.join(HERE, "libtextsift_cuda.so")
-SOURCES = ["k_gemm_tc.cu", "k_gemm_tm.cu", "k_simt.cu", "k_router.cu", "k_attn.cu", "k_attn_umma.cu", "k_viterbi.cu", "k_selftest.cu", "runtime.cu", "noalloc.cu", "onnx_load.cu", "tokenizer.cu"]
+SOURCES = ["k_gemm_tc.cu", "k_gemm_tm.cu", "k_simt.cu", "k_router.cu", "k_attn.cu", "k_attn_umma.cu", "k_viterbi.cu", "k_selftest.cu", "runtime.cu", "ep.cu", "noalloc.cu", "onnx_load.cu", "tokenizer.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
@@ -41,7 +41,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    subprocess.run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs], check=True)
+    subprocess.run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-ldl"], check=True)
     os.replace(tmp, LIB)
     return LIB
 

@@ -11,6 +11,7 @@
 #include "ts_common.cuh"
 #include "ts_kernels.h"
 #include "ts_simt.h"
+#include "ts_ep.h"
 
 #include <cmath>
 #include <cstdarg>
@@ -248,6 +249,17 @@ struct ts_cuda {
   uint32_t stage_next = 0;
   // when set, each layer's top-k experts are copied here ([n_layers][T][top_k])
   int32_t* trace_topk = nullptr;
+  // expert parallelism (ts_cuda_ep_init): this rank holds experts
+  // [e_first, e_first + e_local) of every layer; ep_world = 0 when off
+  int ep_world = 0, ep_rank = 0;
+  uint32_t e_first = 0, e_local = 0;
+  void* ep_comm = nullptr;
+  int* ep_hcounts = nullptr;  // pinned: E route counts of this rank, then [world][e_local] received
+  uint64_t ep_cap = 0;        // rows the receive buffers hold
+  DevArr<int> ep_rc;          // [world][e_local] route counts received
+  DevArr<uint16_t> ep_recv, ep_glu, ep_out;  // received rows, their SwiGLU, their expert outputs
+  DevArr<int4> ep_tiles;
+  DevArr<int> ep_ntiles;
   // kernel launches issued by forwards / MoE ops (ts_cuda_profile_read)
   uint64_t n_launch = 0;
   // optional per-phase CUDA-event timing (ts_cuda_profile)
@@ -449,6 +461,73 @@ struct RouterIn {
   const float* absum = nullptr;
 };
 
+int next_stage(ts_cuda* h, size_t bytes, ts_cuda::Stage** out);
+
+// Expert parallelism: the experts of one layer for the routes in
+// w.aperm16 (this rank's permuted operand, expert-major = destination-major),
+// with their outputs left in w.down16 at the same positions, as the
+// single-GPU grouped GEMMs leave them (ep.cu describes the exchange).
+int ep_experts(ts_cuda* h, LayerDev& L, cudaStream_t st) {
+  Workspace& w = h->ws;
+  const ts_cuda_cfg& c = h->cfg;
+  const int world = h->ep_world;
+  const uint32_t D = c.d_model, F = c.d_ff, E = c.n_experts, El = h->e_local;
+  std::string err;
+  std::vector<uint64_t> co(world), cn(world, El);
+  for (int p = 0; p < world; p++) co[p] = (uint64_t)p * El;
+  {
+    Phase p(h, st, TS_PHASE_OTHER, 0, 0);
+    // routes per expert: this rank's to each peer's experts, each source's to ours
+    if (!ts::ep_exchange(h->ep_comm, world, w.counts.p, co.data(), cn.data(), h->ep_rc.p, co.data(), cn.data(), 4, st,
+                         &err))
+      return fail(TS_ERR_CUDA, "%s", err.c_str());
+    TS_K(cudaMemcpyAsync(h->ep_hcounts, w.counts.p, (size_t)E * 4, cudaMemcpyDeviceToHost, st));
+    TS_K(cudaMemcpyAsync(h->ep_hcounts + E, h->ep_rc.p, (size_t)world * El * 4, cudaMemcpyDeviceToHost, st));
+    TS_K(cudaStreamSynchronize(st));
+  }
+  ts::EpPlan plan;
+  ts::ep_plan(h->ep_hcounts, h->ep_hcounts + E, world, h->ep_rank, (int)El, (int)ts::gemm_tm_rows(), &plan);
+  if (plan.recv_total > h->ep_cap)
+    return fail(TS_ERR_UNSUPPORTED, "expert parallelism: %llu routed rows for this rank > capacity %llu",
+                (unsigned long long)plan.recv_total, (unsigned long long)h->ep_cap);
+  const uint32_t nt = (uint32_t)plan.tiles.size();
+  ts_cuda::Stage* sg = nullptr;
+  int rc = next_stage(h, 16 + (size_t)nt * sizeof(int4), &sg);
+  if (rc) return rc;
+  std::memcpy(sg->p, &nt, 4);
+  if (nt) std::memcpy(sg->p + 16, plan.tiles.data(), (size_t)nt * sizeof(int4));
+  TS_K(cudaMemcpyAsync(h->ep_ntiles.p, sg->p, 4, cudaMemcpyHostToDevice, st));
+  if (nt) TS_K(cudaMemcpyAsync(h->ep_tiles.p, sg->p + 16, (size_t)nt * sizeof(int4), cudaMemcpyHostToDevice, st));
+  TS_K(cudaEventRecord(sg->done, st));
+  {
+    Phase p(h, st, TS_PHASE_OTHER, 0, 0);
+    if (!ts::ep_exchange(h->ep_comm, world, w.aperm16.p, plan.send_off.data(), plan.send_n.data(), h->ep_recv.p,
+                         plan.recv_off.data(), plan.recv_n.data(), (size_t)D * 2, st, &err))
+      return fail(TS_ERR_CUDA, "%s", err.c_str());
+  }
+  const uint64_t rows = plan.recv_total;
+  if (nt) {
+    ts::GemmArgs g;
+    g.tiles = h->ep_tiles.p; g.n_tiles = h->ep_ntiles.p; g.err = h->err.p; g.out0 = h->ep_glu.p; g.ld0 = F;
+    {
+      Phase p(h, st, TS_PHASE_EXPERT_GATE_UP, 2ull * rows * (2ull * F) * D, 1);
+      TS_K(ts::launch_gemm_w4_tm(L.gate_up.tiles(), h->ep_recv.p, rows, g, ts::kEpiSwiglu, nt, st));
+    }
+    ts::GemmArgs g2;
+    g2.tiles = h->ep_tiles.p; g2.n_tiles = h->ep_ntiles.p; g2.err = h->err.p; g2.out0 = h->ep_out.p; g2.ld0 = D;
+    {
+      Phase p(h, st, TS_PHASE_EXPERT_DOWN, 2ull * rows * D * F, 1);
+      TS_K(ts::launch_gemm_w4_tm(L.down.tiles(), h->ep_glu.p, rows, g2, ts::kEpiF16, nt, st));
+    }
+  }
+  Phase p(h, st, TS_PHASE_OTHER, 0, 0);
+  // the outputs back to the positions their rows had at their source
+  if (!ts::ep_exchange(h->ep_comm, world, h->ep_out.p, plan.recv_off.data(), plan.recv_n.data(), w.down16.p,
+                       plan.send_off.data(), plan.send_n.data(), (size_t)D * 2, st, &err))
+    return fail(TS_ERR_CUDA, "%s", err.c_str());
+  return TS_OK;
+}
+
 ts::RouterCertArgs router_cert_args(ts_cuda* h, const LayerDev& L, const RouterIn& rin, const int* rloc,
                                     const int* rlen, int32_t* idx, float* wt, int* hist, uint32_t T) {
   const ts_cuda_cfg& c = h->cfg;
@@ -513,6 +592,10 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
       Phase p(h, st, TS_PHASE_OTHER, 0, 1);
       TS_K(ts::launch_gather_rows(xn16, w.aperm16.p, w.perm_tok.p, nullptr, R, D * 2, st));
     }
+    if (h->ep_world > 0) {
+      const int rc = ep_experts(h, L, st);
+      if (rc) return rc;
+    } else {
     const uint32_t grid_tc = R / ts::gemm_tm_rows() + E + 1;
     ts::GemmArgs g;
     g.tiles = w.tiles_tc.p; g.n_tiles = w.n_tiles_tc.p; g.err = h->err.p;
@@ -527,6 +610,7 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
     {
       Phase p(h, st, TS_PHASE_EXPERT_DOWN, fl_dn, 1);
       TS_K(ts::launch_gemm_w4_tm(L.down.tiles(), w.glu16.p, R, g2, ts::kEpiF16, grid_tc, st));
+    }
     }
   } else {
     Phase p(h, st, TS_PHASE_EXPERT_GATE_UP, fl_gu + fl_dn, 4);
@@ -553,7 +637,7 @@ int moe_half(ts_cuda* h, LayerDev& L, const float* n32, const uint16_t* xn16, co
 
 // Next slot of the pinned staging ring with room for `bytes`, once the copies
 // queued from it by an earlier forward have executed.
-static int next_stage(ts_cuda* h, size_t bytes, ts_cuda::Stage** out) {
+int next_stage(ts_cuda* h, size_t bytes, ts_cuda::Stage** out) {
   ts_cuda::Stage& sg = h->stage[h->stage_next++ % 4];
   if (sg.done) TS_CUDA_TRY(cudaEventSynchronize(sg.done));
   else TS_CUDA_TRY(cudaEventCreateWithFlags(&sg.done, cudaEventDisableTiming));
@@ -582,6 +666,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   const uint32_t T = offs[n_seqs];
   if (T > c.max_tokens) return fail(TS_ERR_UNSUPPORTED, "%u tokens > max_tokens %u", T, c.max_tokens);
   const bool exact = c.mode == TS_MODE_EXACT;
+  if (exact && h->ep_world > 0) return fail(TS_ERR_UNSUPPORTED, "expert parallelism runs the fast mode only");
   int rc = ensure_workspace(h, exact);
   if (rc) return rc;
   Workspace& w = h->ws;
@@ -837,6 +922,17 @@ int ts_cuda_finalize(ts_cuda_t* h) {
   DevArr<int> bad;
   TS_CUDA_TRY(bad.alloc(1));
   TS_CUDA_TRY(cudaMemsetAsync(bad.p, 0, 4, st));
+  // the experts this handle holds: all, or [e_first, e_first + e_local) under
+  // expert parallelism (consecutive in the loader layout [E][N][...])
+  const uint32_t e0 = h->ep_world > 0 ? h->e_first : 0u, ne = h->ep_world > 0 ? h->e_local : E;
+  auto upload_experts = [&](W4Dev& wd, const std::string& pre, uint32_t N, uint32_t K) -> int {
+    const size_t nb = K / 32, zs = (nb + 1) / 2;
+    // a missing tensor stays a null pointer (no zero points: the constant 8)
+    auto at = [&](const auto* base, size_t per_expert) { return base ? base + (size_t)e0 * per_expert : base; };
+    return w4_upload(wd, at(p8(pre + "int4"), (size_t)N * (K / 2)), at(p16(pre + "scales"), (size_t)N * nb),
+                     at(p8(pre + "zp"), (size_t)N * zs), at(p16(pre + "bias"), (size_t)N), ne, N, K, 128, true, bad.p,
+                     st);
+  };
   rc = w4_upload(h->score, p8("score.int4"), p16("score.scales"), p8("score.zp"),
                  h->staged.count("score.bias") ? p16("score.bias") : nullptr, 1, c.n_classes, D, 128, true, bad.p, st);
   if (rc) return rc;
@@ -869,11 +965,8 @@ int ts_cuda_finalize(ts_cuda_t* h) {
                         p16(p + "attn.o_proj.bias"), 1, D, Q, 128, true, bad.p, st)) ||
         (rc = w4_upload(L->router, p8(p + "router.int4"), p16(p + "router.scales"), p8(p + "router.zp"),
                         p16(p + "router.bias"), 1, E, D, 128, true, bad.p, st)) ||
-        (rc = w4_upload(L->gate_up, p8(p + "experts.gate_up.int4"), p16(p + "experts.gate_up.scales"),
-                        p8(p + "experts.gate_up.zp"), p16(p + "experts.gate_up.bias"), E, 2 * F, D, 128, true, bad.p,
-                        st)) ||
-        (rc = w4_upload(L->down, p8(p + "experts.down.int4"), p16(p + "experts.down.scales"),
-                        p8(p + "experts.down.zp"), p16(p + "experts.down.bias"), E, D, F, 128, true, bad.p, st)))
+        (rc = upload_experts(L->gate_up, p + "experts.gate_up.", 2 * F, D)) ||
+        (rc = upload_experts(L->down, p + "experts.down.", D, F)))
       return rc;
     if (E <= ts::kMaxRouterExperts) {
       std::vector<float> tb(2 * ts::kMaxRouterExperts + 2), tsz(2 * (size_t)E * (D / 32));
@@ -909,6 +1002,17 @@ int ts_cuda_finalize(ts_cuda_t* h) {
                 "dequantisation only for zero or normal scales",
                 nbad);
   if ((rc = ensure_workspace(h, c.mode == TS_MODE_EXACT))) return rc;
+  if (h->ep_world > 0 && !h->ep_hcounts) {
+    // every rank may route all of its routes to this one: world * max_tokens * k rows
+    h->ep_cap = (uint64_t)h->ep_world * c.max_tokens * c.top_k;
+    TS_CUDA_TRY(h->ep_rc.alloc((size_t)h->ep_world * h->e_local));
+    TS_CUDA_TRY(h->ep_recv.alloc(h->ep_cap * D));
+    TS_CUDA_TRY(h->ep_glu.alloc(h->ep_cap * F));
+    TS_CUDA_TRY(h->ep_out.alloc(h->ep_cap * D));
+    TS_CUDA_TRY(h->ep_tiles.alloc(h->ep_cap / ts::gemm_tm_rows() + (size_t)h->ep_world * h->e_local + 1));
+    TS_CUDA_TRY(h->ep_ntiles.alloc(1));
+    TS_CUDA_TRY(cudaMallocHost(&h->ep_hcounts, ((size_t)E + (size_t)h->ep_world * h->e_local) * sizeof(int)));
+  }
   const size_t pin_need = (size_t)c.max_tokens * (4 + 1 + 4 * c.n_classes) + 64;
   if (!h->pin) {
     TS_CUDA_TRY(cudaMallocHost(&h->pin, pin_need));
@@ -1104,6 +1208,9 @@ void ts_cuda_destroy(ts_cuda_t* h) {
     }
     for (auto& m : h->marks) { cudaEventDestroy(m.a); cudaEventDestroy(m.b); }
     for (auto e : h->ev_pool) cudaEventDestroy(e);
+    if (h->ep_hcounts) cudaFreeHost(h->ep_hcounts);
+    ts::ep_comm_destroy(h->ep_comm, false);
+    h->ep_comm = nullptr;
     h->layers.clear();
     if (h->stream) cudaStreamDestroy(h->stream);
     h->stream = nullptr;
@@ -1259,6 +1366,7 @@ int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32
 int ts_cuda_op_moe(ts_cuda_t* h, uint32_t layer, const float* d_x, uint16_t* d_out, int32_t* d_idx, float* d_w,
                    uint32_t T, void* stream) {
   if (!h || !d_x || !d_out) return fail(TS_ERR_ARG, "ts_cuda_op_moe: null argument");
+  if (h->ep_world > 0) return fail(TS_ERR_UNSUPPORTED, "ts_cuda_op_moe: the handle holds a slice of the experts");
   if (!h->finalized || layer >= h->cfg.n_layers) return fail(TS_ERR_STATE, "handle not finalized or bad layer");
   if (T > h->cfg.max_tokens) return fail(TS_ERR_UNSUPPORTED, "T > max_tokens");
   if (T == 0) return TS_OK;
@@ -1430,6 +1538,59 @@ int ts_cuda_op_attention(ts_cuda_t* h, const uint16_t* d_q, const uint16_t* d_k,
   h->n_launch += 2;
   if (exact) TS_CUDA_TRY(ts::launch_attention_exact(aa, st));
   else TS_CUDA_TRY(ts::launch_attention_tc(aa, st));
+  return TS_OK;
+}
+
+size_t ts_cuda_ep_unique_id(uint8_t* out, size_t cap) {
+  if (!out) return ts::ep_unique_id_bytes();
+  std::string err;
+  if (!ts::ep_unique_id(out, cap, &err)) {
+    fail(TS_ERR_CUDA, "%s", err.c_str());
+    return 0;
+  }
+  return ts::ep_unique_id_bytes();
+}
+
+int ts_cuda_ep_init(ts_cuda_t* h, int32_t rank, int32_t world, const uint8_t* nccl_id, size_t id_len) {
+  if (!h || !nccl_id || world < 1 || rank < 0 || rank >= world) return fail(TS_ERR_ARG, "ts_cuda_ep_init: bad argument");
+  if (h->finalized || h->ep_world > 0) return fail(TS_ERR_STATE, "ts_cuda_ep_init: call it once, before ts_cuda_finalize");
+  const ts_cuda_cfg& c = h->cfg;
+  if (c.n_experts % (uint32_t)world) return fail(TS_ERR_UNSUPPORTED, "%u experts do not split over %d ranks", c.n_experts, world);
+  if (c.top_k != 4 || c.n_experts > ts::kMaxRouterExperts)
+    return fail(TS_ERR_UNSUPPORTED, "expert parallelism needs the fast router (top_k 4, at most 128 experts)");
+  DevGuard g(c.device);
+  std::string err;
+  void* comm = nullptr;
+  if (!ts::ep_comm_init(&comm, world, nccl_id, id_len, rank, &err)) return fail(TS_ERR_CUDA, "%s", err.c_str());
+  h->ep_comm = comm;
+  h->ep_world = world;
+  h->ep_rank = rank;
+  h->e_local = c.n_experts / (uint32_t)world;
+  h->e_first = (uint32_t)rank * h->e_local;
+  return TS_OK;
+}
+
+int ts_cuda_ep_plan(const int32_t* counts, const int32_t* recv_counts, int32_t world, int32_t e_local,
+                    int32_t tile_rows, uint64_t* send_n, uint64_t* recv_n, int32_t* tiles, uint32_t tiles_cap,
+                    uint32_t* n_tiles) {
+  if (!counts || !recv_counts || world < 1 || e_local < 1 || tile_rows < 1 || !n_tiles)
+    return fail(TS_ERR_ARG, "ts_cuda_ep_plan: bad argument");
+  ts::EpPlan plan;
+  ts::ep_plan(counts, recv_counts, world, 0, e_local, tile_rows, &plan);
+  for (int p = 0; p < world; p++) {
+    if (send_n) send_n[p] = plan.send_n[p];
+    if (recv_n) recv_n[p] = plan.recv_n[p];
+  }
+  *n_tiles = (uint32_t)plan.tiles.size();
+  if (tiles) {
+    if (plan.tiles.size() > tiles_cap) return fail(TS_ERR_ARG, "ts_cuda_ep_plan: %zu tiles > capacity", plan.tiles.size());
+    for (size_t i = 0; i < plan.tiles.size(); i++) {
+      tiles[4 * i] = plan.tiles[i].x;
+      tiles[4 * i + 1] = plan.tiles[i].y;
+      tiles[4 * i + 2] = plan.tiles[i].z;
+      tiles[4 * i + 3] = plan.tiles[i].w;
+    }
+  }
   return TS_OK;
 }
 
