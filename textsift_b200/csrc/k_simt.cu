@@ -42,6 +42,33 @@ __global__ void seq_info_kernel(const uint32_t* __restrict__ offs, uint32_t n_se
 // GatherBlockQuantized embedding: out[t, d] = f16((u4 - zp) * f32(scale)).
 // One thread per (token, 32-block); out-of-range ids give zero rows.
 // ---------------------------------------------------------------------------
+// One 32-block of an int4 embedding row (16 bytes pk, low nibble = even
+// element) dequantised as the reference does (zig/wasm_exports.zig:1523-1570):
+// f32 (q - zp) * scale, then its f32 -> fp16 encode.  Hardware round-to-
+// nearest-even equals that encode for zero and normal fp16 results, so a
+// pair takes one packed conversion and only pairs with a subnormal or
+// overflowing value go through the reference routine.  q - zp is formed
+// exactly as 2^23 + q (byte permute) minus 2^23 + zp.
+__device__ __forceinline__ void embed_block_ref(uint4 pk, float s, int z, uint4* dst) {
+  const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
+  const float off = 8388608.0f + (float)z;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const uint32_t lo4 = wd[q] & 0x0F0F0F0Fu, hi4 = (wd[q] >> 4) & 0x0F0F0F0Fu;
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {  // byte j of word q holds elements 8q+2j (lo) and 8q+2j+1 (hi)
+      const float lo = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(lo4, 0x4B000000u, 0x7650u | (uint32_t)j)), off), s);
+      const float hi = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(hi4, 0x4B000000u, 0x7650u | (uint32_t)j)), off), s);
+      const float alo = fabsf(lo), ahi = fabsf(hi);
+      const bool fast = (alo >= 6.103515625e-05f || alo == 0.0f) && alo < 65520.0f &&
+                        (ahi >= 6.103515625e-05f || ahi == 0.0f) && ahi < 65520.0f;
+      r[j] = fast ? f32x2_to_h2(lo, hi) : ((uint32_t)f32_to_f16_ref(lo) | ((uint32_t)f32_to_f16_ref(hi) << 16));
+    }
+    dst[q] = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+
 __global__ void embed_gather_kernel(const uint8_t* __restrict__ w, const uint16_t* __restrict__ sc,
                                     const uint8_t* __restrict__ zp, const int32_t* __restrict__ ids,
                                     uint16_t* __restrict__ out, uint32_t T, uint32_t V, uint32_t D) {
@@ -61,25 +88,9 @@ __global__ void embed_gather_kernel(const uint8_t* __restrict__ w, const uint16_
   const float s = f16_ref_to_f32(sc[(size_t)id * nb + b]);
   const uint8_t zb = zp[(size_t)id * zs + (b >> 1)];
   const int z = (b & 1) ? (zb >> 4) & 15 : zb & 15;
-  const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
-#pragma unroll
-  for (int q = 0; q < 4; q++) {
-    uint32_t r[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {  // byte j of word q holds elements 8q+2j (lo) and 8q+2j+1 (hi)
-      uint32_t byte = (wd[q] >> (8 * j)) & 0xffu;
-      float lo = __fmul_rn((float)((int)(byte & 15u) - z), s);
-      float hi = __fmul_rn((float)((int)(byte >> 4) - z), s);
-      r[j] = (uint32_t)f32_to_f16_ref(lo) | ((uint32_t)f32_to_f16_ref(hi) << 16);
-    }
-    o[q] = make_uint4(r[0], r[1], r[2], r[3]);
-  }
+  embed_block_ref(pk, s, z, o);
 }
 
-// The same gather from the forward's packed table: vocabulary row id holds
-// its D/2 nibble bytes, then its D/32 fp16 scales, then its zero-point bytes,
-// padded to row_bytes (a multiple of 128), so one token's gather reads whole
-// 128-byte lines of one region instead of parts of three tables.
 __global__ void embed_rows_kernel(const uint8_t* __restrict__ rows, uint32_t row_bytes, const int32_t* __restrict__ ids,
                                   uint16_t* __restrict__ out, uint32_t T, uint32_t V, uint32_t D) {
   pdl_trigger();
@@ -99,19 +110,7 @@ __global__ void embed_rows_kernel(const uint8_t* __restrict__ rows, uint32_t row
   const float s = f16_ref_to_f32(*reinterpret_cast<const uint16_t*>(row + D / 2 + 2 * b));
   const uint8_t zb = row[D / 2 + 2 * nb + (b >> 1)];
   const int z = (b & 1) ? (zb >> 4) & 15 : zb & 15;
-  const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
-#pragma unroll
-  for (int q = 0; q < 4; q++) {
-    uint32_t r[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {  // byte j of word q holds elements 8q+2j (lo) and 8q+2j+1 (hi)
-      uint32_t byte = (wd[q] >> (8 * j)) & 0xffu;
-      float lo = __fmul_rn((float)((int)(byte & 15u) - z), s);
-      float hi = __fmul_rn((float)((int)(byte >> 4) - z), s);
-      r[j] = (uint32_t)f32_to_f16_ref(lo) | ((uint32_t)f32_to_f16_ref(hi) << 16);
-    }
-    o[q] = make_uint4(r[0], r[1], r[2], r[3]);
-  }
+  embed_block_ref(pk, s, z, o);
 }
 
 // Builds the packed table: one thread per (row, byte) of the packed row.
