@@ -173,7 +173,7 @@ const char* ts_cuda_last_error(void);
 void ts_cuda_destroy(ts_cuda_t* h);             /* NativeApi.destroyBackend (native/backend.ts:37) */
 
 /* ---- per-op entry points: the analogue of the reference's
- * vulkanDispatchOneShot conformance path (native/vulkan_backend.zig:342-364,
+ * vulkanDispatchOneShot conformance path (native/vulkan_backend.zig:239-270,
  * tests/native/vulkan/conformance-all.js).  All device pointers. ---- */
 
 /* GatherBlockQuantized embedding (zig/wasm_exports.zig:1523-1573). */
@@ -204,12 +204,23 @@ int ts_cuda_op_matmul_nbits(const ts_cuda_w4_t* w, uint32_t expert, const void* 
                             int32_t out_dtype, uint32_t M, int32_t mode, void* stream);
 
 /* Router of layer `layer`: logits, top-k with the reference tie rule,
- * softmax over k, x 1/k (browser/inference/block.ts:154-207).  Exact mode:
+ * softmax over k, x 1/k (browser/inference/block.ts:49-103).  Exact mode:
  * f32 logits in the reference order.  Fast mode (the forward's fast path):
  * logits on the tensor cores from fp16(x), top-k in the GEMM epilogue.
  * d_x: f32 [T, d_model]; d_idx: i32 [T, k]; d_w: f32 [T, k]. */
 int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32_t* d_idx, float* d_w, uint32_t T,
                            void* stream);
+
+/* The fast forward's router step of block `layer` from the block's residual
+ * and attention output (fp16 [T, d_model] each, device): the add + RMSNorm
+ * (ln2, browser/inference/block.ts:145-176), tensor-core logits naming the
+ * candidates, and the exact candidate pass, which rebuilds its f32 input from
+ * the norm's stored fp16 sum and 1 / rms.  d_x32 (f32 [T, d_model], may be
+ * NULL) receives the norm's f32 output: the router input that d_idx / d_w
+ * are the reference's top-k and weights of (block.ts:49-103).  Fast mode
+ * only (top_k 4, at most 128 experts). */
+int ts_cuda_op_router_addnorm(ts_cuda_t* h, uint32_t layer, const uint16_t* d_res, const uint16_t* d_attn,
+                              float* d_x32, int32_t* d_idx, float* d_w, uint32_t T, void* stream);
 
 /* MoE half of block `layer` (router + experts, browser/inference/block.ts:
  * 286-299 + expert.ts:104-212): d_x f32 [T, d_model] -> d_out fp16
@@ -336,7 +347,7 @@ int ts_cuda_ep_plan(const int32_t* counts, const int32_t* recv_counts, int32_t w
  * of the two waits that completed normally, 0 for each that gave up. */
 int ts_cuda_selftest_wait_timeout(ts_cuda_t* h, uint32_t limit_us, int32_t* d_result, void* stream);
 
-/* YaRN RoPE tables of the handle (browser/inference/rope.ts:348-356), fp16
+/* YaRN RoPE tables of the handle (browser/inference/rope.ts:117-135), fp16
  * [rows, head_dim/2] each, copied to host. */
 int ts_cuda_rope_tables(ts_cuda_t* h, uint32_t rows, uint16_t* cos_out, uint16_t* sin_out);
 

@@ -116,8 +116,8 @@ int        tso_model_set(tso_model* m, const char* name, const void* data, size_
 /* Full forward of one sequence.  mask may be NULL (= all ones); an all-ones
  * mask is treated as NULL like wasm.ts:755-764.  logits_out: f32 [T, n_classes].
  * n_threads <= 1: canonical single-thread order (the bit-exact reference).
- * n_threads > 1: the reference's MtPool partitioning (block.ts:168-192,
- * attention.ts:389-478, mt-expert.ts:63-191).
+ * n_threads > 1: the reference's MtPool partitioning (block.ts:63-95,
+ * attention.ts:84-185, mt-expert.ts:63-191).
  * Optional traces (may be NULL): hidden_trace fp16 [n_layers+1, T, d_model]
  * (residual stream after embed and after each block), topk_trace i32
  * [n_layers, T, top_k], normed_trace f32 [n_layers, T, d_model] (router input). */

@@ -4,8 +4,8 @@
  * TEST INFRASTRUCTURE ONLY (parity checker + timed CPU baseline).
  * Citations are into packages/textsift/src/browser/ of teamchong/textsift:
  *   inference/model.ts:50-105      modelForward
- *   inference/block.ts:154-302     routerForward / blockForward
- *   inference/attention.ts:347-517 attentionForward
+ *   inference/block.ts:49-197     routerForward / blockForward
+ *   inference/attention.ts:45-215 attentionForward
  *   inference/expert.ts:104-212    expertDispatch (single thread)
  *   inference/mt-expert.ts:63-191  expertDispatchParallel (MtPool mode)
  *   inference/rope.ts:27-144       YaRN tables
@@ -138,7 +138,7 @@ void tso_build_rope_tables(const tso_rope_cfg* c, uint32_t T, uint16_t* cos_out,
 
 static inline uint32_t part_lo(uint32_t w, uint32_t n, uint32_t N) { return (uint32_t)(((uint64_t)w * n) / N); }
 
-/* T-partitioned int4 matmul (block.ts:168-192, attention.ts:389-424): each
+/* T-partitioned int4 matmul (block.ts:63-95, attention.ts:84-146): each
  * worker runs the kernel on its own row slice, which changes which rows
  * take the tile vs tail path exactly as the reference's MtPool does. */
 static void matmul_rows(int nt, int x_f32, int o_f32, const void* x, const i4w* w, void* out,
@@ -162,7 +162,7 @@ static void matmul_rows(int nt, int x_f32, int o_f32, const void* x, const i4w* 
   }
 }
 
-/* attention.ts:347-517 */
+/* attention.ts:45-215 */
 static void attention_forward(const tso_model* m, const layer_w* lw, const float* hf, uint16_t* out,
                               const uint16_t* cos_t, const uint16_t* sin_t, const uint8_t* mask,
                               uint32_t T, int nt) {
@@ -201,7 +201,7 @@ static void attention_forward(const tso_model* m, const layer_w* lw, const float
     tso_rope_apply(q, cos_t, sin_t, T, Hq, hd);
     tso_rope_apply(k, cos_t, sin_t, T, Hkv, hd);
   }
-  /* attention.ts:458-483: H_q partition when Hq >= 2 * threads */
+  /* attention.ts:150-185: H_q partition when Hq >= 2 * threads */
   if (nt > 1 && Hq >= (uint32_t)nt * 2) {
 #pragma omp parallel num_threads(nt)
     {
@@ -221,7 +221,7 @@ static void attention_forward(const tso_model* m, const layer_w* lw, const float
   free(q); free(k); free(v); free(ao); free(af);
 }
 
-/* block.ts:154-207: f32 router logits, top-k, softmax over k, x(1/K) in JS doubles */
+/* block.ts:49-103: f32 router logits, top-k, softmax over k, x(1/K) in JS doubles */
 static void router_forward(const tso_model* m, const layer_w* lw, const float* x, int32_t* idx,
                            float* scores, uint32_t T, int nt, const int32_t* forced) {
   const uint32_t E = m->cfg.n_experts, K = m->cfg.top_k, D = m->cfg.d_model;
@@ -334,7 +334,7 @@ int tso_moe_forward(const tso_model* m, uint32_t layer, const float* normed, uin
   return 0;
 }
 
-/* block.ts:213-302 */
+/* block.ts:108-197 */
 static void block_forward(const tso_model* m, const layer_w* lw, const uint16_t* in, uint16_t* out,
                           const uint16_t* cos_t, const uint16_t* sin_t, const uint8_t* mask,
                           uint32_t T, int nt, int32_t* topk_trace, float* normed_trace,

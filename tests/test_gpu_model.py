@@ -112,6 +112,32 @@ def test_router_fast_equals_exact_mode(small_backend, cuda_lib):
     assert np.array_equal(out[0][1].view(np.uint32), out[1][1].view(np.uint32))
 
 
+@pytest.mark.parametrize("T", [1000, 4097])
+def test_router_from_add_norm_bit_exact(small_backend, small_oracle, cuda_lib, T):
+    """The forward's own router step (ts_cuda_op_router_addnorm): the fast
+    add + RMSNorm, then the candidate pass on the f32 input it rebuilds from
+    the norm's stored fp16 sum and 1 / rms.  Indices and weights must be the
+    reference's on the norm's f32 output (returned by the op).  Ties:
+    duplicated rows and a zero row (residual + attention output = 0)."""
+    from textsift_b200 import abi
+    r = rng(40 + T)
+    res = r.normal(0, 1, size=(T, 640)).astype(np.float16)
+    att = r.normal(0, 0.5, size=(T, 640)).astype(np.float16)
+    res[9], att[9] = res[2], att[2]
+    res[13], att[13] = 0.0, 0.0
+    res[17] *= np.float16(30.0)  # a large row: wide bound, many candidates
+    idx = empty((T, 4), np.int32)
+    w = empty((T, 4), np.float32)
+    x32 = empty((T, 640), np.float32)
+    for layer in (0, 1):
+        assert cuda_lib.ts_cuda_op_router_addnorm(small_backend.handle, layer, ptr(dev(res.view(np.uint16))),
+                                                  ptr(dev(att.view(np.uint16))), ptr(x32), ptr(idx), ptr(w), T,
+                                                  stream()) == 0, abi.last_error()
+        _, ridx, rw = small_oracle.moe(layer, host(x32, np.float32))
+        assert np.array_equal(host(idx, np.int32), ridx)
+        assert f32_ulps(host(w, np.float32), rw).max() <= 2
+
+
 def router_logits(oracle, weights, layer, normed):
     p = f"layers.{layer}.router."
     return oracle.matmul_int4(normed, weights[p + "int4"], weights[p + "scales"], weights[p + "zp"],

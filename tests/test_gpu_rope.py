@@ -2,7 +2,7 @@
 
 Three pieces of the forward rotate Q and K (reference: rope_apply,
 zig/wasm_exports.zig:1460-1502, and the YaRN tables of
-browser/inference/rope.ts:239-356, restated in oracle/):
+browser/inference/rope.ts:9-144, restated in oracle/):
 
 * the handle's YaRN cos/sin tables (built on the host at finalize) --
   bit-exact against the oracle's tables;

@@ -88,7 +88,7 @@ def test_exp_approx_accuracy(oracle):
 
 
 def test_rope_tables_reference_constants(oracle):
-    # rope.ts:348-356 with the PF_CONFIG YaRN parameters (wasm.ts:474-482):
+    # rope.ts:117-135 with the PF_CONFIG YaRN parameters (wasm.ts:474-482):
     # position 0 is (cos, sin) = (mscale, 0) with mscale = 0.1 ln 32 + 1.
     c, s = oracle.rope_tables(4)
     msc = 0.1 * math.log(32.0) + 1.0

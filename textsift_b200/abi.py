@@ -86,6 +86,7 @@ SIGNATURES = [
     ("ts_cuda_op_attention", ctypes.c_int, [P, P, P, P, P, P, P, P, U32, P]),
     ("ts_cuda_op_rope", ctypes.c_int, [P, P, P, P, P, U32, U32, U32, P]),
     ("ts_cuda_op_qkv_rope", ctypes.c_int, [P, U32, P, P, U32, P, P, P, P]),
+    ("ts_cuda_op_router_addnorm", ctypes.c_int, [P, U32, P, P, P, P, P, U32, P]),
     ("ts_cuda_ep_unique_id", ctypes.c_size_t, [P, ctypes.c_size_t]),
     ("ts_cuda_ep_init", ctypes.c_int, [P, I32, I32, P, ctypes.c_size_t]),
     ("ts_cuda_ep_plan", ctypes.c_int, [P, P, I32, I32, I32, P, P, P, U32, P]),

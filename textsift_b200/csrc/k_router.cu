@@ -9,16 +9,15 @@
 // and selects the top k from their exact logits with the reference's tie rule
 // (wasm_exports.zig:367-426), then the softmax over k with the exact
 // exponential and x 1/k (wasm_exports.zig:919-958, browser/inference/
-// block.ts:201-206).  Indices and weights are therefore those of the
+// block.ts:98-102).  Indices and weights are therefore those of the
 // reference on the same f32 input, bit for bit.
 //
 // One warp per token.  The f32 router input is either given (the per-op
-// entry) or rebuilt from the residual and attention output exactly as the
-// fast add+RMSNorm computed it (rmsnorm_fast_kernel<true>, also one warp per
-// row): the same lane chunks and sum-of-squares chains, the same shuffle
-// tree, rsqrtf and products.  The lanes then split the candidates' 32-blocks
-// between them, and each candidate's blocks are added in the reference's
-// order.
+// entry) or rebuilt exactly as the fast add+RMSNorm computed it
+// (rmsnorm_fast_kernel<true>): its stored fp16 sum times its stored 1 / rms
+// times the norm weight, the same products.  The lanes then split the
+// candidates' 32-blocks between them, and each candidate's blocks are added
+// in the reference's order.
 #include "ts_common.cuh"
 #include "ts_kernels.h"
 #include "ts_simt.h"
@@ -32,6 +31,7 @@ namespace {
 
 constexpr uint32_t kCertThreads = 256;  // 8 warps, one token at a time each
 constexpr uint32_t kCertTokens = 32;    // tokens per block, inside one permutation chunk
+constexpr int kPairBatch = 2;           // (candidate, block) pairs per lane whose loads go out together
 static_assert(kPermChunk % kCertTokens == 0, "a block's tokens share one permutation chunk");
 
 // Nibble j (0..3 = byte j) of lohi (lo = w & 0x0F0F0F0F or hi = (w >> 4) &
@@ -142,50 +142,21 @@ __global__ void __launch_bounds__(kCertThreads, 4) router_cert_kernel(const Rout
     // ---- the f32 router input into xs ----
     const size_t base = (size_t)t * D;
     if constexpr (SRC == kRouterSrcAddNorm) {
-      // rmsnorm_fast_kernel<true>'s arithmetic: lane l owns chunks l, l + 32,
-      // l + 64, l + 96 of 8 values, the same sum-of-squares chain, the same
-      // shuffle tree and rsqrtf, the same products
-      const uint32_t nc = D / 8;
-      float ss = 0.0f;
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const uint32_t c = (uint32_t)lane + 32u * r;
-        if (c >= nc) break;
-        const uint4 av = *reinterpret_cast<const uint4*>(a.a + base + 8 * c);
-        const uint4 bv = *reinterpret_cast<const uint4*>(a.b + base + 8 * c);
-        const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
-          const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
-          const float s0 = fa.x + fb.x, s1 = fa.y + fb.y;
-          ss = fmaf(s0, s0, ss);
-          ss = fmaf(s1, s1, ss);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float inv_rms = rsqrtf(ss / (float)D + a.eps);
-      // the same chunks again (cache hits): the fp16-rounded sums, normalised
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const uint32_t c = (uint32_t)lane + 32u * r;
-        if (c >= nc) break;
-        const uint4 av = *reinterpret_cast<const uint4*>(a.a + base + 8 * c);
-        const uint4 bv = *reinterpret_cast<const uint4*>(a.b + base + 8 * c);
+      // rmsnorm_fast_kernel<true>'s product (x * inv_rms) * gamma on the fp16
+      // sum it stored and the 1 / rms it stored: the same f32 bits (two
+      // products per lane of an f32x2 multiply are two IEEE products)
+      const float inv = a.inv[t];
+      const uint64_t inv2 = f2pack(inv, inv);
+      for (uint32_t c = (uint32_t)lane; c < D / 8u; c += 32u) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(a.a + base + 8 * c);
         const uint4 gv = *reinterpret_cast<const uint4*>(a.gamma + 8 * c);
-        const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
-        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
         float o8[8];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[j]));
-          const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[j]));
-          const uint32_t sw = f32x2_to_h2(fa.x + fb.x, fa.y + fb.y);
-          const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&sw));
+          const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&xw[j]));
           const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[j]));
-          o8[2 * j] = x.x * inv_rms * g.x;
-          o8[2 * j + 1] = x.y * inv_rms * g.y;
+          f2unpack(mul_f32x2(mul_f32x2(f2pack(x.x, x.y), inv2), f2pack(g.x, g.y)), o8[2 * j], o8[2 * j + 1]);
         }
         float* dst = xs + (c >> 2) * 36u + (c & 3u) * 8u;
         *reinterpret_cast<float4*>(dst) = make_float4(o8[0], o8[1], o8[2], o8[3]);
@@ -205,15 +176,17 @@ __global__ void __launch_bounds__(kCertThreads, 4) router_cert_kernel(const Rout
     auto batch_logits = [&](uint32_t cb, uint32_t nbt, uint32_t myid) -> float {
       const uint32_t npairs = nbt * nb;
       // pair p = c * nb + b; this lane's pairs are lane, lane + 32, ..., their
-      // (c, b) stepped by subtraction instead of a division per pair
+      // (c, b) stepped by (32 / nb, 32 % nb) and at most one carry instead of
+      // a division per pair
       uint32_t c_n = (uint32_t)lane / nb, b_n = (uint32_t)lane - c_n * nb;
-      for (uint32_t p0 = 0; p0 < npairs; p0 += 128u) {
-        // every load of this lane's (up to) four pairs first, then the arithmetic
-        uint4 wv[4];
-        float2 sz[4];
-        uint32_t cc[4], bb[4];
+      const uint32_t step_c = 32u / nb, step_b = 32u - step_c * nb;
+      for (uint32_t p0 = 0; p0 < npairs; p0 += 32u * kPairBatch) {
+        // every load of this lane's (up to) kPairBatch pairs first, then the arithmetic
+        uint4 wv[kPairBatch];
+        float2 sz[kPairBatch];
+        uint32_t cc[kPairBatch], bb[kPairBatch];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < kPairBatch; u++) {
           const bool ok = p0 + (uint32_t)lane + 32u * u < npairs;
           const uint32_t c = ok ? c_n : 0u, b = ok ? b_n : 0u;
           const uint32_t e = __shfl_sync(0xffffffffu, myid, c);
@@ -225,11 +198,12 @@ __global__ void __launch_bounds__(kCertThreads, 4) router_cert_kernel(const Rout
             wv[u] = *reinterpret_cast<const uint4*>(a.w_int4 + (size_t)e * (D / 2) + 16 * b);
             sz[u] = *reinterpret_cast<const float2*>(a.w_sz + 2 * ((size_t)e * nb + b));
           }
-          b_n += 32u;
-          while (b_n >= nb) { b_n -= nb; c_n++; }
+          b_n += step_b;
+          c_n += step_c;
+          if (b_n >= nb) { b_n -= nb; c_n++; }
         }
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < kPairBatch; u++) {
           if (p0 + (uint32_t)lane + 32u * u >= npairs) break;
           pb[cc[u] * (nb + 1) + bb[u]] =
               __fmul_rn(block_dot_ref(xs + bb[u] * 36u, wv[u], f2pack(sz[u].y, sz[u].y), tile_path), sz[u].x);

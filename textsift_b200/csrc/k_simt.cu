@@ -8,7 +8,7 @@
 //   rmsnorm           wasm_exports.zig:229-277
 //   add_rmsnorm       wasm_exports.zig:288-350
 //   matmul_w4_exact   wasm_exports.zig:560-708    f32 int4 GEMM, tile/tail order
-//   router_topk       wasm_exports.zig:367-426 + 919-958, block.ts:201-206
+//   router_topk       wasm_exports.zig:367-426 + 919-958, block.ts:98-102
 //   moe permute       expert.ts:127-145 (ascending token order per expert)
 //   moe combine       wasm_exports.zig:1027-1055 + 1153-1164 + 969-990
 //   swiglu_exact      wasm_exports.zig:855-903
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
 }
 
 // ---------------------------------------------------------------------------
-// Router top-k (wasm_exports.zig:367-426 + 919-958, block.ts:201-206): the
+// Router top-k (wasm_exports.zig:367-426 + 919-958, block.ts:98-102): the
 // k largest logits by (value descending, index ascending) -- exactly the set
 // and order the reference's strict-'>' insertion sort produces -- then softmax
 // over the k values in that order and x (1/k) in double like the JS caller.
@@ -663,7 +663,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
                                                            const uint16_t* __restrict__ gamma,
                                                            uint16_t* __restrict__ sum_out,
                                                            uint16_t* __restrict__ out16, uint32_t T, uint32_t D,
-                                                           float eps, float* __restrict__ absum) {
+                                                           float eps, float* __restrict__ absum,
+                                                           float* __restrict__ inv_out, float* __restrict__ out32) {
   pdl_trigger();
   pdl_wait();
   const int lane = threadIdx.x & 31;
@@ -707,6 +708,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float inv_rms = rsqrtf(ss / (float)D + eps);
+  if (inv_out && lane == 0) inv_out[row] = inv_rms;  // the router's exact pass rebuilds its input from it
   float as = 0.0f;  // sum of |normalised value| (the router's error bound, k_router.cu)
 #pragma unroll
   for (int r = 0; r < 4; r++) {
@@ -722,6 +724,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fast_kernel(const uint16_t* __res
       const float n0 = x.x * inv_rms * g.x, n1 = x.y * inv_rms * g.y;
       as += fabsf(n0) + fabsf(n1);
       ow[j] = f32x2_to_h2(n0, n1);
+      if (out32) *reinterpret_cast<float2*>(out32 + base + 8 * c + 2 * j) = make_float2(n0, n1);
     }
     *reinterpret_cast<uint4*>(out16 + base + 8 * c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
@@ -1085,15 +1088,16 @@ cudaError_t launch_split_rope(const uint16_t* qkv, uint16_t* q, uint16_t* k, uin
 }
 
 cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
-                                uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st, float* absum) {
+                                uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st, float* absum,
+                                float* inv_out, float* out32) {
   if (T == 0) return cudaSuccess;
   if (D % 8 || D > 1024 || !out16 || (b && !sum_out)) return cudaErrorInvalidValue;
   const uint32_t blocks = (T + 7) / 8;
   if (b)
     return launch_pdl(rmsnorm_fast_kernel<true>, dim3(blocks), dim3(256), 0, st, a, b, gamma, sum_out, out16, T, D, eps,
-                      absum);
+                      absum, inv_out, out32);
   return launch_pdl(rmsnorm_fast_kernel<false>, dim3(blocks), dim3(256), 0, st, a, (const uint16_t*)nullptr, gamma,
-                    (uint16_t*)nullptr, out16, T, D, eps, absum);
+                    (uint16_t*)nullptr, out16, T, D, eps, absum, inv_out, out32);
 }
 
 cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,

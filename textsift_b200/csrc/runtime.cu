@@ -2,7 +2,7 @@
 // the extern "C" ABI declared in include/textsift_cuda.h.
 //
 // Forward composition follows packages/textsift/src/browser/inference/
-// model.ts:50-105, block.ts:213-302, attention.ts:347-517 and
+// model.ts:50-105, block.ts:108-197, attention.ts:45-215 and
 // expert.ts:104-212; tensor names follow loadOnnxWeights
 // (browser/backends/wasm.ts:358-446).  All weights and activations stay in
 // HBM; a forward over many packed sequences is one pass of ~15 launches per
@@ -213,6 +213,7 @@ struct Workspace {
   DevArr<int4> tiles, tiles_tc;  // 128-row tiles (exact path), gemm_tm_rows()-row tiles (tensor cores)
   DevArr<int4> rcand;            // router candidates, 32 bytes per token (kEpiRouterCert)
   DevArr<float> absum;           // sum |x| of each token's router input
+  DevArr<float> rinv;            // the add+norm's 1 / rms of each token (fast mode)
   DevArr<int2> atiles;
   DevArr<uint16_t> aperm16, glu16;
   DevArr<float> aperm32, gu32, glu32, down32;
@@ -375,6 +376,7 @@ int ensure_workspace(ts_cuda* h, bool exact) {
     TS_CUDA_TRY(w.ridx.alloc(R));
     TS_CUDA_TRY(w.rcand.alloc(2 * T));
     TS_CUDA_TRY(w.absum.alloc(T));
+    TS_CUDA_TRY(w.rinv.alloc(T));
     TS_CUDA_TRY(w.rw.alloc(R));
     TS_CUDA_TRY(w.counts.alloc(E));
     TS_CUDA_TRY(w.hist.alloc((size_t)ts::route_chunks((uint32_t)T) * E));
@@ -452,12 +454,14 @@ struct Phase {
 // next_gamma (fast mode) fuses the next RMSNorm into the combine: xn16 then
 // holds RMSNorm(out) * next_gamma on return.
 // Where the fast router's exact candidate pass reads its f32 input: given
-// (x32) or rebuilt from the block's residual a, attention output b and norm
-// weight gamma; absum = each token's sum |x| from the kernel that made xn16.
+// (x32) or rebuilt from the add+norm's fp16 sum a (residual + attention
+// output), its 1 / rms per token inv and the norm weight gamma; absum = each
+// token's sum |x| from the kernel that made xn16.
 struct RouterIn {
   int src = ts::kRouterSrcF32;
   const float* x32 = nullptr;
-  const uint16_t *a = nullptr, *b = nullptr, *gamma = nullptr;
+  const uint16_t *a = nullptr, *gamma = nullptr;
+  const float* inv = nullptr;
   const float* absum = nullptr;
 };
 
@@ -533,7 +537,7 @@ ts::RouterCertArgs router_cert_args(ts_cuda* h, const LayerDev& L, const RouterI
   const ts_cuda_cfg& c = h->cfg;
   ts::RouterCertArgs a;
   a.cand = reinterpret_cast<const uint8_t*>(h->ws.rcand.p);
-  a.x32 = rin.x32; a.a = rin.a; a.b = rin.b; a.gamma = rin.gamma; a.eps = c.eps;
+  a.x32 = rin.x32; a.a = rin.a; a.inv = rin.inv; a.gamma = rin.gamma; a.eps = c.eps;
   a.w_int4 = L.router.int4.p; a.w_sz = L.rsz.p;
   a.bias = L.router.bias.p;
   a.rloc = rloc; a.rlen = rlen; a.idx = idx; a.w = wt; a.hist = hist;
@@ -747,7 +751,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
       }
       {
         Phase p(h, st, TS_PHASE_OTHER, 0, 1);
-        TS_K(ts::launch_rmsnorm_fast(src, w.o16.p, L.ln2.p, w.res2.p, w.xn16.p, T, D, c.eps, st, w.absum.p));
+        TS_K(ts::launch_rmsnorm_fast(src, w.o16.p, L.ln2.p, w.res2.p, w.xn16.p, T, D, c.eps, st, w.absum.p, w.rinv.p));
       }
     } else {
       Phase p(h, st, TS_PHASE_OTHER, fl_qkv + fl_o + fl_attn, 6);
@@ -766,7 +770,7 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
     }
     const uint16_t* next_gamma = exact ? nullptr : li + 1 < c.n_layers ? h->layers[li + 1]->ln1.p : h->final_norm.p;
     RouterIn rin;  // fast mode: the router input rebuilt from the block's add + RMSNorm
-    rin.src = ts::kRouterSrcAddNorm; rin.a = src; rin.b = w.o16.p; rin.gamma = L.ln2.p; rin.absum = w.absum.p;
+    rin.src = ts::kRouterSrcAddNorm; rin.a = w.res2.p; rin.inv = w.rinv.p; rin.gamma = L.ln2.p; rin.absum = w.absum.p;
     rc = moe_half(h, L, w.n32.p, w.xn16.p, w.res2.p, dst, T, w.pos.p, w.slen.p, exact, st, (int)li, rin, next_gamma);
     if (rc) return rc;
     std::swap(src, dst);
@@ -1360,6 +1364,39 @@ int ts_cuda_op_router_topk(ts_cuda_t* h, uint32_t layer, const float* d_x, int32
   ra.x = d_x; ra.ldx = c.d_model; ra.M = T; ra.out = h->ws.rlogits.p; ra.ldo = c.n_experts;
   TS_CUDA_TRY(ts::launch_matmul_exact(ra, true, ts::kOutF32, (T + 127) / 128, st));
   TS_CUDA_TRY(ts::launch_router_topk(h->ws.rlogits.p, d_idx, d_w, nullptr, T, c.n_experts, c.top_k, st));
+  return TS_OK;
+}
+
+int ts_cuda_op_router_addnorm(ts_cuda_t* h, uint32_t layer, const uint16_t* d_res, const uint16_t* d_attn,
+                              float* d_x32, int32_t* d_idx, float* d_w, uint32_t T, void* stream) {
+  if (!h || !d_res || !d_attn || !d_idx || !d_w) return fail(TS_ERR_ARG, "ts_cuda_op_router_addnorm: null argument");
+  if (!h->finalized || layer >= h->cfg.n_layers) return fail(TS_ERR_STATE, "handle not finalized or bad layer");
+  const ts_cuda_cfg& c = h->cfg;
+  if (c.mode == TS_MODE_EXACT || c.top_k != 4 || c.n_experts > ts::kMaxRouterExperts)
+    return fail(TS_ERR_UNSUPPORTED, "ts_cuda_op_router_addnorm: the fast mode's router (top_k 4, <= 128 experts)");
+  if (T > c.max_tokens) return fail(TS_ERR_UNSUPPORTED, "T > max_tokens");
+  if (T == 0) return TS_OK;
+  DevGuard g(c.device);
+  cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+  int rc = ensure_workspace(h, false);
+  if (rc) return rc;
+  Workspace& w = h->ws;
+  const LayerDev& L = *h->layers[layer];
+  // the forward's steps: add + RMSNorm (sum, 1 / rms, sum |x| and fp16 x
+  // kept), candidates from the tensor-core logits, the exact candidate pass
+  // on the f32 input rebuilt from the stored sum and 1 / rms
+  TS_CUDA_TRY(ts::launch_rmsnorm_fast(d_res, d_attn, L.ln2.p, w.res2.p, w.xn16.p, T, c.d_model, c.eps, st, w.absum.p,
+                                      w.rinv.p, d_x32));
+  CUtensorMap tx;
+  if (!ts::make_act_tmap(&tx, w.xn16.p, T, c.d_model)) return fail(TS_ERR_CUDA, "cuTensorMapEncodeTiled failed (router)");
+  ts::GemmArgs gr;
+  gr.M = T; gr.err = h->err.p; gr.out0 = w.rcand.p; gr.absum = w.absum.p; gr.rbound = L.rbound.p;
+  TS_CUDA_TRY(ts::launch_gemm_w4_tc(L.router.tiles(), tx, gr, ts::kEpiRouterCert, (T + 127) / 128, st));
+  RouterIn rin;
+  rin.src = ts::kRouterSrcAddNorm; rin.a = w.res2.p; rin.inv = w.rinv.p; rin.gamma = L.ln2.p; rin.absum = w.absum.p;
+  TS_CUDA_TRY(ts::launch_router_cert(router_cert_args(h, L, rin, nullptr, nullptr, d_idx, d_w, nullptr, T),
+                                     ts::kRouterSrcAddNorm, st));
+  h->n_launch += 3;
   return TS_OK;
 }
 

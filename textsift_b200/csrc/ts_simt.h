@@ -77,7 +77,7 @@ cudaError_t launch_viterbi(const float* logits, const int* offs_dev, uint32_t n_
 // to fp16, any summation order; MoE combine from fp16 expert outputs.
 cudaError_t launch_rmsnorm_fast(const uint16_t* a, const uint16_t* b, const uint16_t* gamma, uint16_t* sum_out,
                                 uint16_t* out16, uint32_t T, uint32_t D, float eps, cudaStream_t st,
-                                float* absum = nullptr);
+                                float* absum = nullptr, float* inv_out = nullptr, float* out32 = nullptr);
 // With norm_gamma set it also writes norm_out = RMSNorm(out) * norm_gamma, the
 // same bits as launch_rmsnorm_fast on out (D <= 1024).
 cudaError_t launch_moe_combine_fast(const uint16_t* down, const int32_t* idx, const float* w, const int* route_pos,
@@ -135,8 +135,8 @@ enum RouterSrc : int {
 struct RouterCertArgs {
   const uint8_t* cand = nullptr;   // uint4 per token from the kEpiRouterCert epilogue
   const float* x32 = nullptr;      // kRouterSrcF32: [T, D]
-  const uint16_t* a = nullptr;     // kRouterSrcAddNorm: residual fp16 [T, D]
-  const uint16_t* b = nullptr;     //   attention output fp16 [T, D]
+  const uint16_t* a = nullptr;     // kRouterSrcAddNorm: residual + attention output as fp16 [T, D]
+  const float* inv = nullptr;      //   the add+norm's 1 / rms of each token [T]
   const uint16_t* gamma = nullptr; //   norm weight fp16 [D]
   float eps = 0.0f;
   // the router weight: int4 [E][D/2] in reference layout, the table of
