@@ -485,6 +485,206 @@ __global__ void __launch_bounds__(640, 1)
 }
 
 // ---------------------------------------------------------------------------
+// The router's logits with the candidate epilogue (kEpiRouterCert).  The
+// router weight is one small matrix (n_experts <= 128 rows x K <= 640), the
+// same for every token tile, so each CTA dequantises it once into shared
+// memory, where it stays resident as the MMA's B operand (BN = 128 rows x
+// 64 K per chunk, the 128-byte swizzle of gemm_w4_tc_kernel's B tiles); only
+// the activations stream, one TMA box of 128 token rows x 64 K per chunk.
+// Persistent, 20 warps:
+//   warp 0       producer of the activation boxes (SA-stage ring across tiles)
+//   warp 1       MMA issuer: 4 x tcgen05.mma (M = 128 tokens, N = 128) per
+//                chunk into one of four TMEM accumulators
+//   warp 2       TMEM allocator (4 x 128 columns)
+//   warps 4..11  dequantise the weight once, chunk by chunk, from global
+//                memory into the resident tiles (warps 12..19 stage the bias
+//                and the bound table meanwhile)
+//   warps 4..19  then four epilogue groups of four warps (one per TMEM lane
+//                quarter); group g takes the CTA's tiles g, g + 4, ... from
+//                accumulator g, one token row per thread: router_cert_epilogue
+//                (the epilogue is latency-bound per thread, so four tiles'
+//                epilogues run side by side)
+// ---------------------------------------------------------------------------
+namespace rg {
+constexpr uint32_t BM = 128, BN = 128;
+constexpr uint32_t KC_MAX = 10;                // K <= 640
+constexpr uint32_t SA = 3;                     // activation stages
+constexpr uint32_t A_BYTES = BM * 128;         // 128 rows x 64 fp16
+constexpr uint32_t B_BYTES = BN * 128;         // one resident chunk of the weight
+constexpr uint32_t RAW_BYTES = BN * 37;        // packed blob of a chunk (w4_blob_bytes(128))
+constexpr uint32_t OFF_B = SA * A_BYTES;
+constexpr uint32_t OFF_BAR = OFF_B + KC_MAX * B_BYTES;
+constexpr uint32_t NACC = 4;                    // TMEM accumulators = epilogue groups
+constexpr uint32_t NUM_BARS = 2 * SA + 1 + 2 * NACC + 1;  // full/empty per stage, weight ready, acc full/empty, drain
+constexpr uint32_t OFF_BIAS = (OFF_BAR + NUM_BARS * 8 + 15u) & ~15u;  // f32 [BN]
+constexpr uint32_t OFF_RB = OFF_BIAS + BN * 4;                          // f32 [2 kMaxRouterExperts + 2]
+constexpr uint32_t OFF_MISC = (OFF_RB + (2 * kMaxRouterExperts + 2) * 4 + 15u) & ~15u;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+constexpr uint32_t TMEM_COLS = NACC * BN;
+static_assert(OFF_B % 1024 == 0 && B_BYTES % 1024 == 0, "SW128 tiles");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+}  // namespace rg
+
+__global__ void __launch_bounds__(640, 1)
+    router_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs args) {
+  using namespace rg;
+  extern __shared__ uint8_t smem_dyn[];
+  pdl_trigger();
+  pdl_wait();
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + OFF_B;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* full = bars;                   // [SA] activation box landed
+  uint64_t* empty = bars + SA;             // [SA] its MMAs completed
+  uint64_t* w_ready = bars + 2 * SA;       // the resident weight is in place
+  uint64_t* acc_full = bars + 2 * SA + 1;         // [NACC]
+  uint64_t* acc_empty = bars + 2 * SA + 1 + NACC; // [NACC]
+  uint64_t* drain = bars + 2 * SA + 1 + 2 * NACC; // every MMA issued has completed (teardown)
+  float* sbias = reinterpret_cast<float*>(smem + OFF_BIAS);
+  float* srb = reinterpret_cast<float*>(smem + OFF_RB);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+
+  const uint32_t m_tiles = (args.M + BM - 1u) / BM;
+  if (blockIdx.x >= m_tiles) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t n_kc = args.n_kc;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < SA; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(w_ready, 256);
+    for (uint32_t b = 0; b < NACC; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t m = blockIdx.x; m < m_tiles && ok; m += gridDim.x) {
+        for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+          const uint32_t s = it % SA, u = it / SA;
+          if (!wait_or_abort(&empty[s], (u & 1u) ^ 1u, args.err, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], A_BYTES);
+          tma_load_2d(sA + s * A_BYTES, &tmap_a, (int32_t)(kc * kChunkK), (int32_t)(m * BM), &full[s]);
+        }
+      }
+      if (!ok)
+        for (uint32_t j = it > SA ? it - SA : 0u; j < it; j++) mbar_wait(&full[j % SA], (j / SA) & 1u, args.err);
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc = umma_idesc_f16_f32(BM, BN);
+    const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA)), bdesc0 = umma_desc_sw128(smem_u32(sB));
+    bool ok = __all_sync(0xffffffffu, wait_or_abort(w_ready, 0, args.err, abort_flag));
+    uint32_t it = 0, lt = 0;
+    for (uint32_t m = blockIdx.x; m < m_tiles && ok; m += gridDim.x, lt++) {
+      const uint32_t b = lt % NACC, bph = (lt / NACC) & 1u;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&acc_empty[b], bph ^ 1u, args.err, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + b * BN;
+      for (uint32_t kc = 0; kc < n_kc; kc++, it++) {
+        const uint32_t s = it % SA;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&full[s], (it / SA) & 1u, args.err, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        if (elect_one()) {
+          // descriptor address fields step by bytes / 16
+          const uint64_t ad = adesc0 + (uint64_t)(s * (A_BYTES >> 4));
+          const uint64_t bd = bdesc0 + (uint64_t)(kc * (B_BYTES >> 4));
+#pragma unroll
+          for (uint32_t k = 0; k < 4; k++) tc_mma_f16(d_tmem, ad + 2u * k, bd + 2u * k, idesc, (kc | k) != 0u);
+          tc_commit(&empty[s]);
+        }
+        __syncwarp();
+      }
+      if (ok && elect_one()) tc_commit(&acc_full[b]);
+      __syncwarp();
+    }
+    // every MMA issued above has completed before TMEM is freed
+    if (elect_one()) tc_commit(drain);
+    __syncwarp();
+    if (lane == 0) mbar_wait(drain, 0, args.err);
+  } else if (warp >= 4) {
+    if (warp < 12) {
+      // ---- the resident weight: unit t = (row t % 128, K half t / 128) of
+      // every chunk, read from the packed blobs in global memory ----
+      const uint32_t t = threadIdx.x - 128u;  // 0..255
+      const uint32_t r = t % BN, hf = t / BN;
+      for (uint32_t kc = 0; kc < n_kc; kc++) {
+        const uint8_t* raw = args.wblob + (size_t)kc * RAW_BYTES;
+        const uint4 hw = *reinterpret_cast<const uint4*>(raw + hf * BN * 16 + r * 16);
+        const uint32_t sc = *reinterpret_cast<const uint16_t*>(raw + BN * 32 + r * 4 + hf * 2);
+        const uint32_t z = (raw[BN * 36 + r] >> (4 * hf)) & 15u;
+        const uint32_t sz = sc * 0x00010001u, zz = (0x6400u | z) * 0x00010001u;
+        const uint32_t wds[4] = {hw.x, hw.y, hw.z, hw.w};
+        uint8_t* bdst = sB + kc * B_BYTES;
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+          const uint32_t w = wds[cc];
+          const uint32_t c = 4u * hf + (uint32_t)cc;
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const uint32_t bits = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+            __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&bits), *reinterpret_cast<const __half2*>(&zz));
+            __half2 d = __hmul2(q, *reinterpret_cast<const __half2*>(&sz));
+            o[j] = *reinterpret_cast<uint32_t*>(&d);
+          }
+          *reinterpret_cast<uint4*>(bdst + r * 128 + ((c ^ (r & 7u)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(w_ready);
+    } else {
+      // the decoded bias and the router bound table, once for every tile
+      const uint32_t et = threadIdx.x - 384u;  // 0..255
+      if (et < BN) sbias[et] = et < args.N ? f16_ref_to_f32(args.bias[et]) : 0.0f;
+      srb[et] = args.rbound[et];
+      if (et < 2) srb[2 * kMaxRouterExperts + et] = args.rbound[2 * kMaxRouterExperts + et];
+    }
+    asm volatile("bar.sync 1, 512;" ::: "memory");  // warps 4..19: the tables are staged
+    // ---- epilogue: NACC groups of four warps (one per TMEM lane quarter);
+    // group g takes the CTA's tiles g, g + NACC, ... from accumulator g ----
+    const uint32_t quarter = (uint32_t)(warp & 3), g = (uint32_t)(warp - 4) >> 2;
+    uint32_t lt = 0;
+    for (uint32_t m = blockIdx.x; m < m_tiles; m += gridDim.x, lt++) {
+      if (lt % NACC != g) continue;
+      const uint32_t b = g, bph = (lt / NACC) & 1u;
+      if (!wait_or_abort(&acc_full[b], bph, args.err, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t grow = m * BM + quarter * 32u + (uint32_t)lane;
+      const uint32_t acc = tmem_base + b * BN + ((quarter * 32u) << 16);
+      router_cert_epilogue(args, acc, grow, grow < args.M, sbias, srb, &acc_empty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 // One thread per tile row: gathers the row's 64 K elements of one chunk from
@@ -656,6 +856,16 @@ cudaError_t launch_gemm_w4_tc(const W4Tiles& w, const CUtensorMap& tmap_a, GemmA
       case kEpiF16Widen: return launch_one<128, 256, kEpiF16Widen>(tmap_a, args, w.n_tiles, grid_m, st);
       case kEpiRouterCert:
         if (w.N > kMaxRouterExperts || w.n_tiles != 1 || !args.absum || !args.rbound) return cudaErrorInvalidValue;
+        if (!args.tiles && w.n_kc <= rg::KC_MAX) {
+          // the whole router weight resident in shared memory
+          static std::atomic<uint64_t> attr_done{0};
+          if (cudaError_t e = smem_attr_per_device(router_gemm_kernel, (int)rg::SMEM_BYTES, attr_done); e != cudaSuccess)
+            return e;
+          const uint32_t m_tiles = (args.M + rg::BM - 1u) / rg::BM;
+          if (m_tiles == 0) return cudaSuccess;
+          const uint32_t grid = std::min<uint32_t>(m_tiles, (uint32_t)num_sms());
+          return launch_pdl(router_gemm_kernel, dim3(grid), dim3(640), rg::SMEM_BYTES, st, tmap_a, args);
+        }
         return launch_one<128, 256, kEpiRouterCert>(tmap_a, args, w.n_tiles, grid_m, st);
     }
   }
