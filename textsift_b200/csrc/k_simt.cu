@@ -590,11 +590,29 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __r
   pdl_trigger();
   pdl_wait();
   const uint32_t rows = n_rows_dev ? (uint32_t)*n_rows_dev : n_rows;
-  const uint32_t per_row = row_bytes / 16;
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < rows * per_row; i += gridDim.x * blockDim.x) {
-    const uint32_t p = i / per_row, c = i % per_row;
-    reinterpret_cast<uint4*>(dst + (size_t)p * row_bytes)[c] =
-        reinterpret_cast<const uint4*>(src + (size_t)perm_tok[p] * row_bytes)[c];
+  const uint32_t per_row = row_bytes / 16, total = rows * per_row;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  // four independent 16-byte pieces per thread and pass: every load out
+  // before the first store; the stores stream past L2 (evict-first) so the
+  // source rows, read once per route, stay resident
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += 4u * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (uint32_t k = 0; k < 4; k++) {
+      const uint32_t j = i + k * stride;
+      if (j < total) {
+        const uint32_t p = j / per_row, c = j - p * per_row;
+        v[k] = __ldg(reinterpret_cast<const uint4*>(src + (size_t)perm_tok[p] * row_bytes) + c);
+      }
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < 4; k++) {
+      const uint32_t j = i + k * stride;
+      if (j < total) {
+        const uint32_t p = j / per_row, c = j - p * per_row;
+        __stcs(reinterpret_cast<uint4*>(dst + (size_t)p * row_bytes) + c, v[k]);
+      }
+    }
   }
 }
 
