@@ -115,6 +115,23 @@ int ts_cuda_forward(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, uint3
 int ts_cuda_forward_packed(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
                            uint32_t n_seqs, float* logits);
 
+/* ts_cuda_forward_packed in two halves, for a host loop that keeps the GPU
+ * busy: _begin copies ids/mask into pinned slot `slot` (0 or 1), enqueues
+ * their upload, the forward and the logits' download into that slot on the
+ * handle's stream (the download on a second stream, from the slot's own
+ * device buffer), and returns without waiting; _end waits for the slot,
+ * reports a device error flag raised by that forward (or by one begun after
+ * it) as TS_ERR_DEVICE and copies the logits (f32 [T, n_classes]) to
+ * `logits`.  Calling _begin(batch i + 1) before _end(batch i) overlaps batch
+ * i's download and host copy with batch i + 1's forward; results are those
+ * of ts_cuda_forward_packed.
+ * A slot takes one _begin, then one _end (TS_ERR_STATE otherwise).  No
+ * counterpart in the reference, whose forward() is one blocking call per
+ * chunk (browser/backends/abstract.ts:29-56). */
+int ts_cuda_forward_packed_begin(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
+                                 uint32_t n_seqs, uint32_t slot);
+int ts_cuda_forward_packed_end(ts_cuda_t* h, uint32_t slot, float* logits);
+
 /* As ts_cuda_forward_packed with ids/mask/logits in device memory, enqueued on
  * `stream` without synchronizing (seq_offsets stays a host array). */
 int ts_cuda_forward_packed_device(ts_cuda_t* h, const int32_t* d_ids, const uint8_t* d_mask,

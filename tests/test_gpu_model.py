@@ -240,6 +240,44 @@ def test_forward_packed_equals_separate(small_backend):
         assert np.array_equal(single.data, p.data)
 
 
+def test_forward_packed_begin_end(small_backend, cuda_lib):
+    """The two-slot pipelined entry (ts_cuda_forward_packed_begin/_end): three
+    batches with the next one begun before the previous one is collected give
+    the logits of ts_cuda_forward_packed bit for bit; misuse is refused."""
+    from textsift_b200 import PF_CONFIG
+    L, h, C = cuda_lib, small_backend._h, PF_CONFIG["n_classes"]
+    r = rng(12)
+    batches = []
+    for lens in ((5, 300, 64), (1,), (129, 2000, 17, 33)):
+        ids = r.integers(0, 4096, size=sum(lens)).astype(np.int32)
+        offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+        batches.append((ids, offs))
+    refs = []
+    for ids, offs in batches:
+        out = np.empty((ids.size, C), np.float32)
+        assert L.ts_cuda_forward_packed(h, ids.ctypes.data, None, offs.ctypes.data, len(offs) - 1,
+                                        out.ctypes.data) == 0, L.ts_cuda_last_error()
+        refs.append(out)
+    outs = [np.full((ids.size, C), np.nan, np.float32) for ids, _ in batches]
+    for k, (ids, offs) in enumerate(batches):
+        assert L.ts_cuda_forward_packed_begin(h, ids.ctypes.data, None, offs.ctypes.data, len(offs) - 1,
+                                              k % 2) == 0, L.ts_cuda_last_error()
+        if k > 0:
+            assert L.ts_cuda_forward_packed_end(h, (k - 1) % 2, outs[k - 1].ctypes.data) == 0
+    assert L.ts_cuda_forward_packed_end(h, (len(batches) - 1) % 2, outs[-1].ctypes.data) == 0
+    for out, ref in zip(outs, refs):
+        assert np.array_equal(out, ref)
+    TS_ERR_ARG, TS_ERR_STATE = -1, -2
+    ids, offs = batches[1]
+    sink = np.empty((ids.size, C), np.float32)
+    assert L.ts_cuda_forward_packed_end(h, 0, sink.ctypes.data) == TS_ERR_STATE  # nothing begun
+    assert L.ts_cuda_forward_packed_begin(h, ids.ctypes.data, None, offs.ctypes.data, 1, 2) == TS_ERR_ARG
+    assert L.ts_cuda_forward_packed_begin(h, ids.ctypes.data, None, offs.ctypes.data, 1, 1) == 0
+    assert L.ts_cuda_forward_packed_begin(h, ids.ctypes.data, None, offs.ctypes.data, 1, 1) == TS_ERR_STATE
+    assert L.ts_cuda_forward_packed_end(h, 1, sink.ctypes.data) == 0
+    assert np.array_equal(sink, refs[1])
+
+
 def test_forward_rejects_bad_input(small_backend):
     from textsift_b200 import TextsiftCudaError
     with pytest.raises(ValueError):

@@ -61,6 +61,8 @@ SIGNATURES = [
     ("ts_cuda_set_mode", ctypes.c_int, [P, I32]),
     ("ts_cuda_forward", ctypes.c_int, [P, P, P, U32, P]),
     ("ts_cuda_forward_packed", ctypes.c_int, [P, P, P, P, U32, P]),
+    ("ts_cuda_forward_packed_begin", ctypes.c_int, [P, P, P, P, U32, U32]),
+    ("ts_cuda_forward_packed_end", ctypes.c_int, [P, U32, P]),
     ("ts_cuda_forward_packed_device", ctypes.c_int, [P, P, P, P, U32, P, P]),
     ("ts_cuda_forward_packed_tags", ctypes.c_int, [P, P, P, P, U32, P, P]),
     ("ts_cuda_forward_trace", ctypes.c_int, [P, P, P, P, U32, P, P]),

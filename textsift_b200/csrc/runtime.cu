@@ -248,6 +248,19 @@ struct ts_cuda {
   struct Stage { uint8_t* p = nullptr; size_t cap = 0; cudaEvent_t done = nullptr; };
   Stage stage[4];
   uint32_t stage_next = 0;
+  // ts_cuda_forward_packed_begin/_end: two slots, each with its own device
+  // logits and a pinned block (logits, ids, the device error flag, mask); a
+  // slot's logits come down on copy_st (after the event `fwd` that ends its
+  // forward), so the download overlaps the next forward on `stream`
+  struct Slot {
+    uint8_t* p = nullptr;
+    DevArr<float> dlog;
+    cudaEvent_t fwd = nullptr, done = nullptr;
+    uint32_t T = 0;
+    bool busy = false;
+  };
+  Slot slot[2];
+  cudaStream_t copy_st = nullptr;
   // when set, each layer's top-k experts are copied here ([n_layers][T][top_k])
   int32_t* trace_topk = nullptr;
   // expert parallelism (ts_cuda_ep_init): this rank holds experts
@@ -1075,6 +1088,79 @@ int ts_cuda_forward_packed(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask
   return TS_OK;
 }
 
+int ts_cuda_forward_packed_begin(ts_cuda_t* h, const int32_t* ids, const uint8_t* mask, const uint32_t* seq_offsets,
+                                 uint32_t n_seqs, uint32_t slot) {
+  if (!h || !ids || !seq_offsets || n_seqs == 0) return fail(TS_ERR_ARG, "ts_cuda_forward_packed_begin: null argument");
+  if (slot > 1) return fail(TS_ERR_ARG, "slot must be 0 or 1");
+  if (!h->finalized) return fail(TS_ERR_STATE, "ts_cuda_finalize has not succeeded");
+  ts_cuda::Slot& sl = h->slot[slot];
+  if (sl.busy) return fail(TS_ERR_STATE, "slot %u holds a forward that ts_cuda_forward_packed_end has not collected", slot);
+  const uint32_t T = seq_offsets[n_seqs];
+  if (T > h->cfg.max_tokens) return fail(TS_ERR_UNSUPPORTED, "%u tokens > max_tokens %u", T, h->cfg.max_tokens);
+  DevGuard g(h->cfg.device);
+  cudaStream_t st = h->stream;
+  Workspace& w = h->ws;
+  const size_t C = h->cfg.n_classes, mt = h->cfg.max_tokens;
+  // slot layout: logits [mt][C] f32, ids [mt] i32, flag, mask [mt]
+  if (!sl.p) {
+    if (!h->copy_st) TS_CUDA_TRY(cudaStreamCreateWithFlags(&h->copy_st, cudaStreamNonBlocking));
+    if (!sl.fwd) TS_CUDA_TRY(cudaEventCreateWithFlags(&sl.fwd, cudaEventDisableTiming));
+    if (!sl.done) TS_CUDA_TRY(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+    TS_CUDA_TRY(sl.dlog.alloc(mt * C));
+    TS_CUDA_TRY(cudaMallocHost(&sl.p, mt * (4 * C + 4 + 1) + 16));
+  }
+  float* pin_log = reinterpret_cast<float*>(sl.p);
+  int32_t* pin_ids = reinterpret_cast<int32_t*>(sl.p + mt * C * 4);
+  int* pin_flag = reinterpret_cast<int*>(sl.p + mt * (C + 1) * 4);
+  uint8_t* pin_mask = sl.p + mt * (C + 1) * 4 + 16;
+  // the slot's previous forward was collected by _end, so its copies have run
+  memcpy(pin_ids, ids, (size_t)T * 4);
+  TS_CUDA_TRY(cudaMemcpyAsync(w.ids.p, pin_ids, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+  const uint8_t* dmask = nullptr;
+  if (mask) {
+    memcpy(pin_mask, mask, T);
+    TS_CUDA_TRY(cudaMemcpyAsync(w.mask.p, pin_mask, T, cudaMemcpyHostToDevice, st));
+    dmask = w.mask.p;
+  }
+  int rc = forward_device(h, w.ids.p, dmask, seq_offsets, n_seqs, sl.dlog.p, st);
+  if (rc) {
+    cudaStreamSynchronize(st);
+    return rc;
+  }
+  TS_CUDA_TRY(cudaEventRecord(sl.fwd, st));
+  TS_CUDA_TRY(cudaStreamWaitEvent(h->copy_st, sl.fwd, 0));
+  TS_CUDA_TRY(cudaMemcpyAsync(pin_log, sl.dlog.p, (size_t)T * C * 4, cudaMemcpyDeviceToHost, h->copy_st));
+  TS_CUDA_TRY(cudaMemcpyAsync(pin_flag, h->err.p, 4, cudaMemcpyDeviceToHost, h->copy_st));
+  TS_CUDA_TRY(cudaEventRecord(sl.done, h->copy_st));
+  sl.T = T;
+  sl.busy = true;
+  return TS_OK;
+}
+
+int ts_cuda_forward_packed_end(ts_cuda_t* h, uint32_t slot, float* logits) {
+  if (!h || !logits) return fail(TS_ERR_ARG, "ts_cuda_forward_packed_end: null argument");
+  if (slot > 1) return fail(TS_ERR_ARG, "slot must be 0 or 1");
+  ts_cuda::Slot& sl = h->slot[slot];
+  if (!sl.busy) return fail(TS_ERR_STATE, "slot %u holds no forward (ts_cuda_forward_packed_begin first)", slot);
+  DevGuard g(h->cfg.device);
+  sl.busy = false;
+  TS_CUDA_TRY(cudaEventSynchronize(sl.done));
+  const size_t C = h->cfg.n_classes, mt = h->cfg.max_tokens;
+  const int flag = *reinterpret_cast<const int*>(sl.p + mt * (C + 1) * 4);
+  if (flag != 0) {
+    // everything queued so far completes before the flag is cleared; a later
+    // slot whose download already ran reports the same flag
+    cudaStreamSynchronize(h->stream);
+    cudaStreamSynchronize(h->copy_st);
+    cudaMemsetAsync(h->err.p, 0, 4, h->stream);
+    cudaStreamSynchronize(h->stream);
+    return fail(TS_ERR_DEVICE, "device error flag %d (%s)", flag,
+                flag == ts::kDevErrWaitTimeout ? "bounded wait timed out" : "bad index");
+  }
+  memcpy(logits, sl.p, (size_t)sl.T * C * 4);
+  return TS_OK;
+}
+
 // Viterbi arguments: calibration values finite and below 1e20 in magnitude
 // (the range in which the kernel's restricted candidate scan equals the
 // reference's full one), sequences non-empty and short enough for the
@@ -1210,6 +1296,15 @@ void ts_cuda_destroy(ts_cuda_t* h) {
       if (sg.p) cudaFreeHost(sg.p);
       if (sg.done) cudaEventDestroy(sg.done);
     }
+    if (h->copy_st) cudaStreamSynchronize(h->copy_st);
+    for (auto& sl : h->slot) {
+      if (sl.p) cudaFreeHost(sl.p);
+      if (sl.fwd) cudaEventDestroy(sl.fwd);
+      if (sl.done) cudaEventDestroy(sl.done);
+      sl.dlog.release();
+    }
+    if (h->copy_st) cudaStreamDestroy(h->copy_st);
+    h->copy_st = nullptr;
     for (auto& m : h->marks) { cudaEventDestroy(m.a); cudaEventDestroy(m.b); }
     for (auto e : h->ev_pool) cudaEventDestroy(e);
     if (h->ep_hcounts) cudaFreeHost(h->ep_hcounts);
