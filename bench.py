@@ -919,11 +919,24 @@ def run_config3(args):
                                "tensor": {"achieved": fl / (ms * 1e-3) / 1e12, "peak": pk["tflops"],
                                           "frac": fl / (ms * 1e-3) / 1e12 / pk["tflops"]},
                                "exponentials_per_launch": n_exp,
+                               "sfu": sfu_floor(n_exp, ms, clk.summary()),
                                "peak_source": f"{pk['source']} (HBM copy; bf16 burst for the tensor share)"},
                      l2="inputs 1.2 GB > L2, no flush", clocks=clk.summary(), cpu_baseline=cpu,
                      gpu_launches=2 * reps)
     emit(line)
     be.dispose()
+
+
+def sfu_floor(n_exp: float, ms: float, clocks: dict) -> dict:
+    """The special-function unit's floor for the attention kernel: two of every
+    three exponential pairs go to ex2.approx.f16x2, which runs at the f32 rate
+    per element, nominally 16 exponentials per clock per SM (the third pair is
+    evaluated on the FMA pipe)."""
+    mhz = clocks.get("sm_mhz") or 1965.0
+    per_s = 16.0 * 148 * mhz * 1e6
+    floor_ms = n_exp * (2.0 / 3.0) / per_s * 1e3
+    return {"sfu_exponentials_per_launch": n_exp * 2.0 / 3.0, "floor_ms": floor_ms, "frac": floor_ms / ms,
+            "rate": "16 per clock per SM (nominal) at the sampled SM clock"}
 
 
 def main():
