@@ -278,6 +278,25 @@ def test_forward_packed_begin_end(small_backend, cuda_lib):
     assert np.array_equal(sink, refs[1])
 
 
+def test_forward_packed_stream(small_backend):
+    """CudaBackend.forward_packed_stream (the two-slot entry under a Python
+    generator) yields forward_packed's logits for each batch, and a stream the
+    caller abandons early leaves both slots free."""
+    r = rng(13)
+    batches = [[r.integers(0, 4096, size=n).astype(np.int32) for n in lens]
+               for lens in ((3, 250), (1000,), (7, 7, 7), (64, 1, 900))]
+    got = list(small_backend.forward_packed_stream(batches))
+    assert len(got) == len(batches)
+    for chunks, res in zip(batches, got):
+        for c, g, ref in zip(chunks, res, small_backend.forward_packed(chunks)):
+            assert g.sequence_length == c.size and np.array_equal(g.data, ref.data)
+    it = small_backend.forward_packed_stream(batches)
+    next(it)
+    it.close()  # one batch still in flight: collected and discarded
+    again = list(small_backend.forward_packed_stream(batches[:2]))
+    assert np.array_equal(again[1][0].data, got[1][0].data)
+
+
 def test_forward_rejects_bad_input(small_backend):
     from textsift_b200 import TextsiftCudaError
     with pytest.raises(ValueError):

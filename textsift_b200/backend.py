@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass
-from typing import Mapping, Sequence
+from typing import Iterable, Iterator, Mapping, Sequence
 
 import numpy as np
 
@@ -211,6 +211,40 @@ class CudaBackend:
             o = int(offs[s]) * self.num_classes
             res.append(Logits(out[o:o + n * self.num_classes].copy(), n, self.num_classes))
         return res
+
+    def forward_packed_stream(self, batches: Iterable[Sequence[np.ndarray]]) -> Iterator[list[Logits]]:
+        """forward_packed over a stream of batches (each a list of chunks),
+        yielding each batch's Logits in order while the next batch runs: batch
+        i + 1 is begun in the other pinned slot before batch i is collected
+        (ts_cuda_forward_packed_begin/_end).  Results equal forward_packed's."""
+        if not self._ready:
+            raise RuntimeError("CudaBackend: call warmup() before forward_packed_stream()")
+        L = abi.lib()
+        pending = None  # (slot, lens, offsets) of the batch in flight
+        slot = 0
+        try:
+            for chunks in batches:
+                lens = [int(np.asarray(c).size) for c in chunks]
+                offs = np.zeros(len(lens) + 1, dtype=np.uint32)
+                offs[1:] = np.cumsum(lens)
+                ids = np.ascontiguousarray(np.concatenate([np.asarray(c, dtype=np.int32) for c in chunks]))
+                abi.check(L.ts_cuda_forward_packed_begin(self._h, _ptr(ids), None, _ptr(offs), len(lens), slot))
+                done, pending = pending, (slot, lens, offs)
+                slot ^= 1
+                if done is not None:
+                    yield self._collect(*done)
+            if pending is not None:
+                done, pending = pending, None
+                yield self._collect(*done)
+        finally:
+            if pending is not None:  # the caller stopped early: free the slot
+                self._collect(*pending)
+
+    def _collect(self, slot: int, lens: list[int], offs: np.ndarray) -> list[Logits]:
+        out = np.empty((int(offs[-1]) * self.num_classes,), dtype=np.float32)
+        abi.check(abi.lib().ts_cuda_forward_packed_end(self._h, slot, _ptr(out)))
+        return [Logits(out[int(offs[s]) * self.num_classes:(int(offs[s]) + n) * self.num_classes].copy(), n,
+                       self.num_classes) for s, n in enumerate(lens)]
 
     def forward_packed_tags(self, chunks: Sequence[np.ndarray], calibration: Sequence[float],
                             masks: Sequence[np.ndarray] | None = None) -> list[np.ndarray]:
