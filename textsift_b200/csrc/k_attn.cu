@@ -102,6 +102,134 @@ __global__ void attn_exact_kernel(const AttnArgs a) {
   }
 }
 
+// dot_ref on operands already decoded with f16_ref_to_f32: the same products,
+// chains and additions, so the same bits.
+__device__ __forceinline__ float dot_ref_f32(const float* a, const float* b, uint32_t n) {
+  float acc[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; u++)
+#pragma unroll
+    for (int l = 0; l < 4; l++) acc[u][l] = 0.0f;
+  uint32_t i = 0;
+  for (; i + 16 <= n; i += 16)
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int l = 0; l < 4; l++) acc[u][l] = __fmaf_rn(a[i + 4 * u + l], b[i + 4 * u + l], acc[u][l]);
+  for (; i + 4 <= n; i += 4)
+#pragma unroll
+    for (int l = 0; l < 4; l++) acc[0][l] = __fmaf_rn(a[i + l], b[i + l], acc[0][l]);
+  float c[4];
+#pragma unroll
+  for (int l = 0; l < 4; l++) c[l] = __fadd_rn(__fadd_rn(acc[0][l], acc[1][l]), __fadd_rn(acc[2][l], acc[3][l]));
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[1]), c[2]), c[3]);
+  for (; i < n; i++) s = __fadd_rn(s, __fmul_rn(a[i], b[i]));
+  return s;
+}
+
+// attn_exact_kernel's result (the reference's order, bit for bit) for a tile
+// of the tensor-core path's list: one block per (16-query tile, KV head)
+// stages the keys and values any query of the tile can see, decoded once
+// with the reference's fp16 decode, and its 32 warps take the tile's (query,
+// head of the group) pairs one at a time.  Per pair: scores with dot_ref's
+// chains (lanes over keys), the maximum, every exponential with the
+// reference's choice of routine per index (lanes over indices), the sum in
+// the reference's four lane chains and tail, then each output column's
+// P.V chain over the keys in order (lanes over columns).
+constexpr uint32_t kExQ = 16;          // queries per tile of the list
+constexpr uint32_t kExMaxRows = 272;   // staged key rows: 16 + 2 W at W = 128
+constexpr uint32_t kExHd = 64;         // head_dim handled
+constexpr uint32_t kExKStride = 65;    // floats per staged K row: lanes reading one column of
+                                       // different rows hit different banks
+constexpr uint32_t kExThreads = 1024;
+constexpr size_t kExSmem = ((size_t)kExMaxRows * kExKStride + (size_t)kExMaxRows * kExHd + 32 * kExHd +
+                            32 * (kExMaxRows + 1)) * sizeof(float);
+static_assert(kExSmem <= 227u * 1024u, "shared memory budget");
+
+__global__ void __launch_bounds__(kExThreads, 1) attn_exact_tile_kernel(const AttnArgs a) {
+  extern __shared__ float ex_smem[];
+  float* sK = ex_smem;                        // [rows][kExKStride]
+  float* sV = sK + kExMaxRows * kExKStride;   // [rows][kExHd]
+  float* sQ = sV + kExMaxRows * kExHd;        // [warp][kExHd]
+  float* sE = sQ + 32 * kExHd;                // [warp][kExMaxRows + 1] scores, then exponentials
+  const int2 tile = a.tiles[blockIdx.x];
+  const uint32_t hk = blockIdx.y, hd = a.hd, W = a.window, group = a.Hq / a.Hkv;
+  const uint32_t q0 = (uint32_t)tile.x, nq = min(kExQ, (uint32_t)tile.y - q0);
+  const uint32_t s0 = a.sstart ? (uint32_t)a.sstart[q0] : 0u;
+  const uint32_t L = a.slen ? (uint32_t)a.slen[q0] : a.T;
+  // keys [kb, ke) of the sequence that some query of the tile attends
+  const uint32_t tl0 = q0 - s0, tl1 = tl0 + nq - 1u;
+  const uint32_t kb = s0 + (tl0 > W ? tl0 - W : 0u);
+  const uint32_t ke = s0 + min(tl1 + W + 1u, L);
+  const size_t kstr = (size_t)a.Hkv * hd;
+  for (uint32_t idx = threadIdx.x; idx < (ke - kb) * hd; idx += blockDim.x) {
+    const uint32_t r = idx / hd, c = idx % hd;
+    const size_t g = (size_t)(kb + r) * kstr + (size_t)hk * hd + c;
+    sK[r * kExKStride + c] = f16_ref_to_f32(a.k[g]);
+    sV[r * kExHd + c] = f16_ref_to_f32(a.v[g]);
+  }
+  __syncthreads();
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* qw = sQ + warp * kExHd;
+  float* ew = sE + warp * (kExMaxRows + 1);
+  for (uint32_t p = warp; p < nq * group; p += kExThreads / 32) {
+    const uint32_t t = q0 + p % nq, h = hk * group + p / nq;
+    const uint32_t tl = t - s0;
+    const uint32_t ws = tl > W ? tl - W : 0u, we = min(tl + W + 1u, L), nk = we - ws;
+    const uint16_t* qr = a.q + (size_t)t * a.Hq * hd + (size_t)h * hd;
+    for (uint32_t i = lane; i < hd; i += 32) qw[i] = f16_ref_to_f32(qr[i]);
+    __syncwarp();
+    const float sink = a.sinks[h];
+    // scores, and the maximum over them and the sink (attn_exact_kernel's
+    // running maximum: a value replaces it only when larger)
+    float mx = sink;
+    for (uint32_t j = lane; j < nk; j += 32) {
+      const uint32_t key = s0 + ws + j;
+      const bool valid = a.mask ? a.mask[key] != 0 : true;
+      const float sc = valid ? dot_ref_f32(qw, sK + (key - kb) * kExKStride, hd) : -INFINITY;
+      ew[j] = sc;
+      if (sc > mx) mx = sc;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float other = __shfl_xor_sync(0xffffffffu, mx, o);
+      if (other > mx) mx = other;
+    }
+    __syncwarp();
+    // exponentials: the polynomial for the first 4 floor(total / 4) entries,
+    // exp for the rest (the sink is entry nk)
+    const uint32_t total = nk + 1u, nfull = total & ~3u;
+    for (uint32_t i = lane; i < total; i += 32) {
+      const float x = __fsub_rn(i < nk ? ew[i] : sink, mx);
+      ew[i] = i < nfull ? exp_approx_ref(x) : expf_ref(x);
+    }
+    __syncwarp();
+    float part = 0.0f;
+    if (lane < 4)
+      for (uint32_t i = lane; i < nfull; i += 4) part = __fadd_rn(part, ew[i]);
+    const float p0 = __shfl_sync(0xffffffffu, part, 0), p1 = __shfl_sync(0xffffffffu, part, 1);
+    const float p2 = __shfl_sync(0xffffffffu, part, 2), p3 = __shfl_sync(0xffffffffu, part, 3);
+    float sum = __fadd_rn(__fadd_rn(__fadd_rn(p0, p1), p2), p3);
+    for (uint32_t i = nfull; i < total; i++) sum = __fadd_rn(sum, ew[i]);
+    const float inv = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 0.0f;
+    // P.V: output column d's chain over the keys in order
+    const float* vrow = sV + (s0 + ws - kb) * kExHd;
+    for (uint32_t d = lane; d < hd; d += 64) {
+      const bool two = d + 32u < hd;
+      float acc0 = 0.0f, acc1 = 0.0f;
+      for (uint32_t j = 0; j < nk; j++) {
+        const float pj = __fmul_rn(ew[j], inv);
+        acc0 = __fmaf_rn(pj, vrow[j * kExHd + d], acc0);
+        if (two) acc1 = __fmaf_rn(pj, vrow[j * kExHd + d + 32u], acc1);
+      }
+      uint16_t* o = a.out + (size_t)t * a.Hq * hd + (size_t)h * hd + d;
+      o[0] = f32_to_f16_ref(acc0);
+      if (two) o[32] = f32_to_f16_ref(acc1);
+    }
+    __syncwarp();  // before the next pair overwrites qw and ew
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Tensor-core path (mma.sync.m16n8k16, fp16 x fp16 -> f32)
 // ---------------------------------------------------------------------------
@@ -354,6 +482,14 @@ __global__ void __launch_bounds__(7 * 32) attn_tc_kernel(const AttnArgs a) {
 
 cudaError_t launch_attention_exact(const AttnArgs& a, cudaStream_t st) {
   if (a.T == 0) return cudaSuccess;
+  if (a.tiles && a.n_tiles && a.hd <= kExHd && a.window <= (kExMaxRows - kExQ) / 2 && a.Hkv &&
+      a.Hq % a.Hkv == 0) {
+    static std::atomic<uint64_t> attr_done{0};
+    if (cudaError_t e = smem_attr_per_device(attn_exact_tile_kernel, (int)kExSmem, attr_done); e != cudaSuccess)
+      return e;
+    attn_exact_tile_kernel<<<dim3(a.n_tiles, a.Hkv), kExThreads, kExSmem, st>>>(a);
+    return cudaGetLastError();
+  }
   dim3 grid(a.T, a.Hq);
   const size_t sm = (size_t)(2 * a.window + 4) * sizeof(float);
   attn_exact_kernel<<<grid, 64, sm, st>>>(a);

@@ -46,18 +46,16 @@ struct SeqOffsets {
   uint32_t v[kNoAllocMaxSeqs + 1];
 };
 
-// One block of 1024 threads: copies the offsets into the scratch array and,
-// for the tensor-core path, writes the tile list that attention_tiles() builds
-// on the host for the allocating entry point -- sequence s contributes
+// One block of 1024 threads: copies the offsets into the scratch array and
+// writes the tile list that attention_tiles() builds on the host for the
+// allocating entry point (both attention kernels work on it) -- sequence s contributes
 // ceil(len_s / rows) tiles {first query, sequence end} in order, placed after
 // the tiles of sequences 0..s-1 (an exclusive scan over one count per thread).
 __global__ void __launch_bounds__(1024) noalloc_prep_kernel(const SeqOffsets offs, uint32_t ns, uint32_t rows,
-                                                            int build_tiles, uint32_t* __restrict__ d_offs,
-                                                            int2* __restrict__ d_tiles) {
+                                                            uint32_t* __restrict__ d_offs, int2* __restrict__ d_tiles) {
   __shared__ uint32_t warp_total[32];
   const uint32_t s = threadIdx.x, lane = s & 31u, warp = s >> 5;
   for (uint32_t i = s; i <= ns; i += blockDim.x) d_offs[i] = offs.v[i];
-  if (!build_tiles) return;
   const uint32_t lo = s < ns ? offs.v[s] : 0u, hi = s < ns ? offs.v[s + 1] : 0u;
   const uint32_t cnt = (hi - lo + rows - 1) / rows;
   uint32_t incl = cnt;  // inclusive scan within the warp
@@ -125,20 +123,16 @@ extern "C" int ts_cuda_op_banded_attention_noalloc(const uint16_t* d_q, const ui
   SeqOffsets po;
   for (uint32_t s = 0; s <= ns; s++) po.v[s] = ho[s];
   const bool fast = mode == TS_MODE_FAST;
-  noalloc_prep_kernel<<<1, 1024, 0, st>>>(po, ns, rows, fast ? 1 : 0, d_offs, d_tiles);
+  noalloc_prep_kernel<<<1, 1024, 0, st>>>(po, ns, rows, d_offs, d_tiles);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = ts::launch_seq_info(d_offs, ns, T, d_pos, d_start, d_len, st);
   if (e != cudaSuccess) return noalloc_fail(TS_ERR_CUDA, cudaGetErrorString(e));
   ts::AttnArgs a;
   a.q = d_q; a.k = d_k; a.v = d_v; a.sinks = d_sinks; a.mask = d_mask; a.out = d_out;
   a.sstart = d_start; a.slen = d_len; a.T = T; a.Hq = Hq; a.Hkv = Hkv; a.hd = head_dim; a.window = window;
-  if (fast) {
-    a.tiles = d_tiles;
-    a.n_tiles = ntl;
-    e = ts::launch_attention_tc(a, st);
-  } else {
-    e = ts::launch_attention_exact(a, st);
-  }
+  a.tiles = d_tiles;  // both kernels work on the tile list
+  a.n_tiles = ntl;
+  e = fast ? ts::launch_attention_tc(a, st) : ts::launch_attention_exact(a, st);
   if (e != cudaSuccess) return noalloc_fail(TS_ERR_CUDA, cudaGetErrorString(e));
   return TS_OK;
 }

@@ -720,7 +720,8 @@ int forward_device(ts_cuda* h, const int32_t* d_ids, const uint8_t* d_mask, cons
   aa.q = w.q.p; aa.k = w.k.p; aa.v = w.v.p; aa.mask = d_mask; aa.out = w.attn.p;
   aa.sstart = w.sstart.p; aa.slen = w.slen.p; aa.T = T; aa.Hq = c.n_heads; aa.Hkv = c.n_kv_heads;
   aa.hd = c.head_dim; aa.window = c.window; aa.err = h->err.p;
-  if (!exact) {
+  {
+    // 16-query tiles (both modes: the exact kernel works on them too)
     uint32_t nt = 0;
     int2* th = reinterpret_cast<int2*>(sg->p + offs_bytes);
     ts::attention_tiles(offs, n_seqs, th, &nt);
@@ -1547,21 +1548,19 @@ int ts_cuda_op_banded_attention(const uint16_t* d_q, const uint16_t* d_k, const 
   ts::AttnArgs a;
   a.q = d_q; a.k = d_k; a.v = d_v; a.sinks = d_sinks; a.mask = d_mask; a.out = d_out;
   a.sstart = ss.p; a.slen = sl.p; a.T = T; a.Hq = Hq; a.Hkv = Hkv; a.hd = head_dim; a.window = window;
-  if (mode == TS_MODE_FAST) {
-    if (head_dim != 64 || Hq / Hkv > 7) return fail(TS_ERR_UNSUPPORTED, "tensor-core attention needs head_dim 64, group <= 7");
-    std::vector<int2> th(ts::attention_max_tiles(T, ns));
-    uint32_t ntl = 0;
-    ts::attention_tiles(ho, ns, th.data(), &ntl);
-    DevArr<int2> td;
-    TS_CUDA_TRY(td.alloc(ntl));
-    TS_CUDA_TRY(cudaMemcpyAsync(td.p, th.data(), (size_t)ntl * sizeof(int2), cudaMemcpyHostToDevice, st));
-    a.tiles = td.p;
-    a.n_tiles = ntl;
-    TS_CUDA_TRY(ts::launch_attention_tc(a, st));
-    TS_CUDA_TRY(cudaStreamSynchronize(st));
-  } else {
-    TS_CUDA_TRY(ts::launch_attention_exact(a, st));
-  }
+  if (mode == TS_MODE_FAST && (head_dim != 64 || Hq / Hkv > 7))
+    return fail(TS_ERR_UNSUPPORTED, "tensor-core attention needs head_dim 64, group <= 7");
+  // 16-query tiles (both modes: the exact kernel works on them too)
+  std::vector<int2> th(ts::attention_max_tiles(T, ns));
+  uint32_t ntl = 0;
+  ts::attention_tiles(ho, ns, th.data(), &ntl);
+  DevArr<int2> td;
+  TS_CUDA_TRY(td.alloc(ntl));
+  TS_CUDA_TRY(cudaMemcpyAsync(td.p, th.data(), (size_t)ntl * sizeof(int2), cudaMemcpyHostToDevice, st));
+  a.tiles = td.p;
+  a.n_tiles = ntl;
+  if (mode == TS_MODE_FAST) TS_CUDA_TRY(ts::launch_attention_tc(a, st));
+  else TS_CUDA_TRY(ts::launch_attention_exact(a, st));
   TS_CUDA_TRY(cudaStreamSynchronize(st));  // scratch above is freed on return
   return TS_OK;
 }
@@ -1657,7 +1656,7 @@ int ts_cuda_op_attention(ts_cuda_t* h, const uint16_t* d_q, const uint16_t* d_k,
   aa.q = d_q; aa.k = d_k; aa.v = d_v; aa.sinks = d_sinks; aa.mask = d_mask; aa.out = d_out;
   aa.sstart = w.sstart.p; aa.slen = w.slen.p; aa.T = T; aa.Hq = c.n_heads; aa.Hkv = c.n_kv_heads;
   aa.hd = c.head_dim; aa.window = c.window; aa.err = h->err.p;
-  if (!exact) {
+  {
     uint32_t nt = 0;
     int2* th = reinterpret_cast<int2*>(sg->p + offs_bytes);
     ts::attention_tiles(seq_offsets, n_seqs, th, &nt);
