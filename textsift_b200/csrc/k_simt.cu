@@ -298,45 +298,47 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
       if (has_zp) { uint8_t zb = zr[b >> 1]; zp = (b & 1) ? (zb >> 4) & 15 : zb & 15; }
       const uint4 pk = *reinterpret_cast<const uint4*>(wr + b * 16);
       const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
-      float q[32];
+      // byte i holds elements 2i (low nibble) and 2i + 1: one f32 pair each.
+      // The chains below run two at a time as packed f32x2 fused multiply-adds
+      // and adds (each half an IEEE operation: the same bits as scalar chains).
+      uint64_t q2[16];
 #pragma unroll
       for (int i = 0; i < 16; i++) {
-        uint32_t byte = (wd[i >> 2] >> (8 * (i & 3))) & 0xffu;
-        q[2 * i] = (float)((int)(byte & 15u) - zp);
-        q[2 * i + 1] = (float)((int)(byte >> 4) - zp);
+        const uint32_t byte = (wd[i >> 2] >> (8 * (i & 3))) & 0xffu;
+        q2[i] = f2pack((float)((int)(byte & 15u) - zp), (float)((int)(byte >> 4) - zp));
       }
 #pragma unroll
       for (int r = 0; r < 8; r++) {
         if ((uint32_t)r >= gr) break;
-        const float4* x4 = reinterpret_cast<const float4*>(myx + r * K + b * 32);
+        const ulonglong2* x4 = reinterpret_cast<const ulonglong2*>(myx + r * K + b * 32);
         float bs;
         if (tile_path[r]) {
-          float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
+          // v0..v3 over elements 4c + l: (v0, v1) and (v2, v3) as pairs
+          uint64_t v01 = 0u, v23 = 0u;
 #pragma unroll
           for (int c = 0; c < 8; c++) {
-            const float4 xv = x4[c];
-            v0 = __fmaf_rn(xv.x, q[4 * c + 0], v0);
-            v1 = __fmaf_rn(xv.y, q[4 * c + 1], v1);
-            v2 = __fmaf_rn(xv.z, q[4 * c + 2], v2);
-            v3 = __fmaf_rn(xv.w, q[4 * c + 3], v3);
+            const ulonglong2 xv = x4[c];
+            v01 = fma_f32x2(xv.x, q2[2 * c], v01);
+            v23 = fma_f32x2(xv.y, q2[2 * c + 1], v23);
           }
+          float v0, v1, v2, v3;
+          f2unpack(v01, v0, v1);
+          f2unpack(v23, v2, v3);
           bs = __fadd_rn(__fadd_rn(v0, v1), __fadd_rn(v2, v3));
         } else {
-          float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+          // a0[l] over elements 8k + l, a1[l] over 8k + 4 + l, as pairs
+          uint64_t a001 = 0u, a023 = 0u, a101 = 0u, a123 = 0u;
 #pragma unroll
           for (int k = 0; k < 4; k++) {
-            const float4 x0 = x4[2 * k], x1 = x4[2 * k + 1];
-            a0[0] = __fmaf_rn(x0.x, q[8 * k + 0], a0[0]);
-            a0[1] = __fmaf_rn(x0.y, q[8 * k + 1], a0[1]);
-            a0[2] = __fmaf_rn(x0.z, q[8 * k + 2], a0[2]);
-            a0[3] = __fmaf_rn(x0.w, q[8 * k + 3], a0[3]);
-            a1[0] = __fmaf_rn(x1.x, q[8 * k + 4], a1[0]);
-            a1[1] = __fmaf_rn(x1.y, q[8 * k + 5], a1[1]);
-            a1[2] = __fmaf_rn(x1.z, q[8 * k + 6], a1[2]);
-            a1[3] = __fmaf_rn(x1.w, q[8 * k + 7], a1[3]);
+            const ulonglong2 x0 = x4[2 * k], x1 = x4[2 * k + 1];
+            a001 = fma_f32x2(x0.x, q2[4 * k], a001);
+            a023 = fma_f32x2(x0.y, q2[4 * k + 1], a023);
+            a101 = fma_f32x2(x1.x, q2[4 * k + 2], a101);
+            a123 = fma_f32x2(x1.y, q2[4 * k + 3], a123);
           }
-          float c0 = __fadd_rn(a0[0], a1[0]), c1 = __fadd_rn(a0[1], a1[1]);
-          float c2 = __fadd_rn(a0[2], a1[2]), c3 = __fadd_rn(a0[3], a1[3]);
+          float c0, c1, c2, c3;
+          f2unpack(add_f32x2(a001, a101), c0, c1);
+          f2unpack(add_f32x2(a023, a123), c2, c3);
           bs = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
         }
         sum[r] = __fadd_rn(sum[r], __fmul_rn(bs, scale));
