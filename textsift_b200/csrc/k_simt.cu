@@ -265,15 +265,59 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
   const bool has_zp = a.w_zp != nullptr;
   const float bias = n_ok ? f16_ref_to_f32(a.bias[(size_t)expert * a.bias_estride + n]) : 0.0f;
   float* myx = xs + (size_t)half * 8 * K;
+  // rows of x start on 16-byte boundaries: stage them 16 bytes at a time
+  const bool vec_x = (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0 && (a.ldx * (X_F32 ? 4u : 2u)) % 16u == 0;
 
   for (uint32_t gp = row0; gp < row_end; gp += 16) {
     __syncthreads();
     const uint32_t rows_pair = min(16u, row_end - gp);
-    for (uint32_t i = threadIdx.x; i < rows_pair * K; i += blockDim.x) {
-      const uint32_t r = i / K, k = i % K;
-      const size_t src = (size_t)(gp + r) * a.ldx + k;
-      xs[r * K + k] = X_F32 ? reinterpret_cast<const float*>(a.x)[src]
-                            : f16_ref_to_f32(reinterpret_cast<const uint16_t*>(a.x)[src]);
+    if (vec_x) {
+      // 8-element pieces, 64 bytes per thread in flight before any is stored
+      constexpr uint32_t kDepth = X_F32 ? 2u : 4u;
+      const uint32_t ppr = K / 8u, n_pieces = rows_pair * ppr;
+#pragma unroll 1
+      for (uint32_t i0 = threadIdx.x; i0 < n_pieces; i0 += kDepth * blockDim.x) {
+        uint4 raw[kDepth][X_F32 ? 2 : 1];
+#pragma unroll
+        for (uint32_t u = 0; u < kDepth; u++) {
+          const uint32_t i = i0 + u * blockDim.x;
+          if (i < n_pieces) {
+            const uint32_t r = i / ppr, k = (i - r * ppr) * 8u;
+            const size_t src = (size_t)(gp + r) * a.ldx + k;
+            if constexpr (X_F32) {
+              raw[u][0] = *reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(a.x) + src);
+              raw[u][1] = *reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(a.x) + src + 4);
+            } else {
+              raw[u][0] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + src);
+            }
+          }
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kDepth; u++) {
+          const uint32_t i = i0 + u * blockDim.x;
+          if (i < n_pieces) {
+            const uint32_t r = i / ppr, k = (i - r * ppr) * 8u;
+            float4* dst = reinterpret_cast<float4*>(xs + r * K + k);
+            if constexpr (X_F32) {
+              dst[0] = *reinterpret_cast<const float4*>(&raw[u][0]);
+              dst[1] = *reinterpret_cast<const float4*>(&raw[u][1]);
+            } else {
+              const uint32_t w[4] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w};
+              dst[0] = make_float4(f16_ref_to_f32((uint16_t)(w[0] & 0xffffu)), f16_ref_to_f32((uint16_t)(w[0] >> 16)),
+                                   f16_ref_to_f32((uint16_t)(w[1] & 0xffffu)), f16_ref_to_f32((uint16_t)(w[1] >> 16)));
+              dst[1] = make_float4(f16_ref_to_f32((uint16_t)(w[2] & 0xffffu)), f16_ref_to_f32((uint16_t)(w[2] >> 16)),
+                                   f16_ref_to_f32((uint16_t)(w[3] & 0xffffu)), f16_ref_to_f32((uint16_t)(w[3] >> 16)));
+            }
+          }
+        }
+      }
+    } else {
+      for (uint32_t i = threadIdx.x; i < rows_pair * K; i += blockDim.x) {
+        const uint32_t r = i / K, k = i % K;
+        const size_t src = (size_t)(gp + r) * a.ldx + k;
+        xs[r * K + k] = X_F32 ? reinterpret_cast<const float*>(a.x)[src]
+                              : f16_ref_to_f32(reinterpret_cast<const uint16_t*>(a.x)[src]);
+      }
     }
     __syncthreads();
     const uint32_t g0 = gp + half * 8;
