@@ -242,17 +242,42 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
   const uint32_t n_base = blockIdx.x * 128u;
   const uint32_t ncols = min(128u, a.N - n_base);
   {
+    // every load of a thread's share is issued before its stores
     const uint8_t* w0 = a.w_int4 + (size_t)expert * a.w_int4_estride + (size_t)n_base * (K / 2);
     const uint32_t rowb = K / 2;  // a multiple of 16
-    for (uint32_t i = threadIdx.x; i < ncols * (rowb / 16); i += blockDim.x) {
-      const uint32_t r = i / (rowb / 16), c = i % (rowb / 16);
-      *reinterpret_cast<uint4*>(sw + r * wst + c * 16) = *reinterpret_cast<const uint4*>(w0 + (size_t)r * rowb + c * 16);
+    const uint32_t n16 = ncols * (rowb / 16);
+#pragma unroll 1
+    for (uint32_t i0 = threadIdx.x; i0 < n16; i0 += 4u * blockDim.x) {
+      uint4 v[4];
+#pragma unroll
+      for (uint32_t u = 0; u < 4; u++) {
+        const uint32_t i = i0 + u * blockDim.x, r = i / (rowb / 16), c = i % (rowb / 16);
+        if (i < n16) v[u] = *reinterpret_cast<const uint4*>(w0 + (size_t)r * rowb + c * 16);
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < 4; u++) {
+        const uint32_t i = i0 + u * blockDim.x, r = i / (rowb / 16), c = i % (rowb / 16);
+        if (i < n16) *reinterpret_cast<uint4*>(sw + r * wst + c * 16) = v[u];
+      }
     }
+    // the tile's scales and zero points are contiguous in global memory
     const uint16_t* s0 = a.w_scales + (size_t)expert * a.w_scales_estride + (size_t)n_base * nb;
-    for (uint32_t i = threadIdx.x; i < ncols * nb; i += blockDim.x) ssc[i] = s0[i];
-    if (a.w_zp) {
-      const uint8_t* z0 = a.w_zp + (size_t)expert * a.w_zp_estride + (size_t)n_base * zs;
-      for (uint32_t i = threadIdx.x; i < ncols * zs; i += blockDim.x) szp[i] = z0[i];
+    const uint8_t* z0 = a.w_zp ? a.w_zp + (size_t)expert * a.w_zp_estride + (size_t)n_base * zs : nullptr;
+    const uint32_t sbytes = ncols * nb * 2u, zbytes = z0 ? ncols * zs : 0u;
+    if ((reinterpret_cast<uintptr_t>(s0) & 15u) == 0 && sbytes % 16u == 0) {
+      for (uint32_t i = threadIdx.x; i < sbytes / 16u; i += blockDim.x)
+        reinterpret_cast<uint4*>(ssc)[i] = reinterpret_cast<const uint4*>(s0)[i];
+    } else {
+      for (uint32_t i = threadIdx.x; i < ncols * nb; i += blockDim.x) ssc[i] = s0[i];
+    }
+    if (z0) {
+      if ((reinterpret_cast<uintptr_t>(z0) & 15u) == 0 && zbytes % 16u == 0 &&
+          (reinterpret_cast<uintptr_t>(szp) & 15u) == 0) {
+        for (uint32_t i = threadIdx.x; i < zbytes / 16u; i += blockDim.x)
+          reinterpret_cast<uint4*>(szp)[i] = reinterpret_cast<const uint4*>(z0)[i];
+      } else {
+        for (uint32_t i = threadIdx.x; i < zbytes; i += blockDim.x) szp[i] = z0[i];
+      }
     }
   }
   const uint32_t half = threadIdx.x >> 7;  // which 8-row group of a pair this thread works on
