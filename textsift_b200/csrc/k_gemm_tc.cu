@@ -629,11 +629,27 @@ __global__ void __launch_bounds__(640, 1)
       // every chunk, read from the packed blobs in global memory ----
       const uint32_t t = threadIdx.x - 128u;  // 0..255
       const uint32_t r = t % BN, hf = t / BN;
-      for (uint32_t kc = 0; kc < n_kc; kc++) {
-        const uint8_t* raw = args.wblob + (size_t)kc * RAW_BYTES;
-        const uint4 hw = *reinterpret_cast<const uint4*>(raw + hf * BN * 16 + r * 16);
-        const uint32_t sc = *reinterpret_cast<const uint16_t*>(raw + BN * 32 + r * 4 + hf * 2);
-        const uint32_t z = (raw[BN * 36 + r] >> (4 * hf)) & 15u;
+      // five chunks' loads in flight at a time, then their arithmetic
+      constexpr uint32_t kBatch = 5;
+      for (uint32_t kc0 = 0; kc0 < n_kc; kc0 += kBatch) {
+        uint4 hwb[kBatch];
+        uint32_t scb[kBatch], zbb[kBatch];
+#pragma unroll
+        for (uint32_t u = 0; u < kBatch; u++) {
+          if (kc0 + u < n_kc) {
+            const uint8_t* raw = args.wblob + (size_t)(kc0 + u) * RAW_BYTES;
+            hwb[u] = *reinterpret_cast<const uint4*>(raw + hf * BN * 16 + r * 16);
+            scb[u] = *reinterpret_cast<const uint16_t*>(raw + BN * 32 + r * 4 + hf * 2);
+            zbb[u] = raw[BN * 36 + r];
+          }
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kBatch; u++) {
+        const uint32_t kc = kc0 + u;
+        if (kc >= n_kc) break;
+        const uint4 hw = hwb[u];
+        const uint32_t sc = scb[u];
+        const uint32_t z = (zbb[u] >> (4 * hf)) & 15u;
         const uint32_t sz = sc * 0x00010001u, zz = (0x6400u | z) * 0x00010001u;
         const uint32_t wds[4] = {hw.x, hw.y, hw.z, hw.w};
         uint8_t* bdst = sB + kc * B_BYTES;
@@ -650,6 +666,7 @@ __global__ void __launch_bounds__(640, 1)
             o[j] = *reinterpret_cast<uint32_t*>(&d);
           }
           *reinterpret_cast<uint4*>(bdst + r * 128 + ((c ^ (r & 7u)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
         }
       }
       fence_proxy_async_smem();

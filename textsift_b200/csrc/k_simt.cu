@@ -567,9 +567,16 @@ __global__ void __launch_bounds__(1024) moe_scan_segments_kernel(int* __restrict
   const bool act = g < G;
   const uint32_t L = (n_chunks + G - 1) / G;
   const uint32_t c0 = min(n_chunks, g * L), c1 = min(n_chunks, c0 + L);
+  // the chunk counts eight at a time: loads in flight together, then summed
   int s = 0;
   if (act)
-    for (uint32_t c = c0; c < c1; c++) s += hist[(size_t)c * E + e];
+    for (uint32_t c = c0; c < c1; c += 8) {
+      int v[8];
+#pragma unroll
+      for (uint32_t u = 0; u < 8; u++) v[u] = c + u < c1 ? hist[(size_t)(c + u) * E + e] : 0;
+#pragma unroll
+      for (uint32_t u = 0; u < 8; u++) s += v[u];
+    }
   part[tid] = s;
   __syncthreads();
   int run = 0, total = 0;
@@ -579,10 +586,15 @@ __global__ void __launch_bounds__(1024) moe_scan_segments_kernel(int* __restrict
       if (gg < g) run += v;
       total += v;
     }
-    for (uint32_t c = c0; c < c1; c++) {
-      const int v = hist[(size_t)c * E + e];
-      hist[(size_t)c * E + e] = run;
-      run += v;
+    for (uint32_t c = c0; c < c1; c += 8) {
+      int v[8];
+#pragma unroll
+      for (uint32_t u = 0; u < 8; u++) v[u] = c + u < c1 ? hist[(size_t)(c + u) * E + e] : 0;
+#pragma unroll
+      for (uint32_t u = 0; u < 8; u++) {
+        if (c + u < c1) hist[(size_t)(c + u) * E + e] = run;
+        run += v[u];
+      }
     }
   }
   // expert e's total sits with thread e (g == 0)
