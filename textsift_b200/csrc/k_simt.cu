@@ -699,6 +699,40 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __r
   }
 }
 
+// The same gather for rows of 80 or 160 16-byte pieces (1280 / 2560 bytes:
+// the forward's fp16 and f32 expert operands): a warp moves 160 pieces per
+// pass -- two rows of 80 or one of 160 -- lane l the pieces l, l + 32, ...,
+// with the rows' source indices loaded once and all five loads of a lane
+// issued before its stores (no per-piece division or index load).
+template <uint32_t P>
+__global__ void gather_rows_warp_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                        const int* __restrict__ perm_tok, const int* __restrict__ n_rows_dev,
+                                        uint32_t n_rows) {
+  static_assert(P == 80 || P == 160, "two rows of 80 pieces or one of 160 per warp pass");
+  constexpr uint32_t RW = 160 / P;
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t rows = n_rows_dev ? (uint32_t)*n_rows_dev : n_rows;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+  for (uint32_t r0 = gw * RW; r0 < rows; r0 += nw * RW) {
+    const int s0 = perm_tok[r0];
+    const int s1 = RW > 1 && r0 + 1 < rows ? perm_tok[r0 + 1] : 0;
+    uint4 v[5];
+#pragma unroll
+    for (uint32_t u = 0; u < 5; u++) {
+      const uint32_t q = lane + 32u * u, k = q / P, c = q - k * P;
+      if (r0 + k < rows)
+        v[u] = __ldg(reinterpret_cast<const uint4*>(src + (size_t)(k ? s1 : s0) * (P * 16u)) + c);
+    }
+#pragma unroll
+    for (uint32_t u = 0; u < 5; u++) {
+      const uint32_t q = lane + 32u * u, k = q / P, c = q - k * P;
+      if (r0 + k < rows) __stcs(reinterpret_cast<uint4*>(dst + (size_t)(r0 + k) * (P * 16u)) + c, v[u]);
+    }
+  }
+}
+
 // Deterministic MoE combine per token: acc = 0; for its experts in ascending
 // id: acc = fma(w, v, acc); moe = f16(acc * K); out = f16(res + moe) (or moe).
 __global__ void moe_combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ idx,
@@ -1159,6 +1193,15 @@ cudaError_t launch_moe_permute(const int32_t* idx, int* hist, uint32_t T, uint32
 cudaError_t launch_gather_rows(const void* src, void* dst, const int* perm_tok, const int* n_rows_dev,
                                uint32_t max_rows, uint32_t row_bytes, cudaStream_t st) {
   if (max_rows == 0) return cudaSuccess;
+  if (row_bytes == 1280u || row_bytes == 2560u) {
+    const uint32_t rw = row_bytes == 1280u ? 2u : 1u;  // rows per warp pass
+    const unsigned blocks = gs_blocks(((size_t)max_rows + rw - 1) / rw * 32u, 256);
+    if (row_bytes == 1280u)
+      return launch_pdl(gather_rows_warp_kernel<80>, dim3(blocks), dim3(256), 0, st, (const uint8_t*)src,
+                        (uint8_t*)dst, perm_tok, n_rows_dev, max_rows);
+    return launch_pdl(gather_rows_warp_kernel<160>, dim3(blocks), dim3(256), 0, st, (const uint8_t*)src,
+                      (uint8_t*)dst, perm_tok, n_rows_dev, max_rows);
+  }
   return launch_pdl(gather_rows_kernel, dim3(gs_blocks((size_t)max_rows * row_bytes / 16, 256)), dim3(256), 0, st,
                     (const uint8_t*)src, (uint8_t*)dst, perm_tok, n_rows_dev, max_rows, row_bytes);
 }
