@@ -201,9 +201,9 @@ def cpu_forward_rate(model, ids, n_threads: int, repeats: int = 1) -> float:
 
 
 def cpu_modes(model, ids, unique: int, budget: dict | None = None) -> dict:
-    """tokens/s of one chunk in the three modes BASELINE.md plans: single
-    thread (the canonical order), the reference's default worker count, and
-    every host core.  `budget` = forwards per mode."""
+    """tokens/s of one chunk in three thread modes: single thread (the
+    canonical order), the reference's default worker count, and every host
+    core.  `budget` = forwards per mode."""
     cores = host_cores()
     budget = budget or {}
     out = {}
