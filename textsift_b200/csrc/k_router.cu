@@ -34,12 +34,6 @@ constexpr uint32_t kCertTokens = 32;    // tokens per block, inside one permutat
 constexpr int kPairBatch = 2;           // (candidate, block) pairs per lane whose loads go out together
 static_assert(kPermChunk % kCertTokens == 0, "a block's tokens share one permutation chunk");
 
-// Nibble j (0..3 = byte j) of lohi (lo = w & 0x0F0F0F0F or hi = (w >> 4) &
-// 0x0F0F0F0F) placed in the mantissa of 2^23: the float 2^23 + nibble.
-__device__ __forceinline__ float nib_raw(uint32_t lohi, uint32_t j) {
-  return __uint_as_float(__byte_perm(lohi, 0x4B000000u, 0x7650u | j));
-}
-
 // The reference's value of one 32-block of int4 weights (16 bytes pk, low
 // nibble = even element) against 32 f32 inputs xb (16-byte aligned, in
 // shared memory): the tile path's four lane chains of eight fused

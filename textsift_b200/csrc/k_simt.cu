@@ -367,14 +367,18 @@ __global__ void __launch_bounds__(256) matmul_w4_exact_kernel(const ExactArgs a)
       if (has_zp) { uint8_t zb = zr[b >> 1]; zp = (b & 1) ? (zb >> 4) & 15 : zb & 15; }
       const uint4 pk = *reinterpret_cast<const uint4*>(wr + b * 16);
       const uint32_t wd[4] = {pk.x, pk.y, pk.z, pk.w};
-      // byte i holds elements 2i (low nibble) and 2i + 1: one f32 pair each.
+      // byte i holds elements 2i (low nibble) and 2i + 1: one f32 pair each,
+      // q - zp exactly as (2^23 + q) - (2^23 + zp) in one packed add.
       // The chains below run two at a time as packed f32x2 fused multiply-adds
       // and adds (each half an IEEE operation: the same bits as scalar chains).
+      const float nz = -(8388608.0f + (float)zp);
+      const uint64_t nzz = f2pack(nz, nz);
       uint64_t q2[16];
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const uint32_t byte = (wd[i >> 2] >> (8 * (i & 3))) & 0xffu;
-        q2[i] = f2pack((float)((int)(byte & 15u) - zp), (float)((int)(byte >> 4) - zp));
+      for (int w = 0; w < 4; w++) {
+        const uint32_t lo = wd[w] & 0x0F0F0F0Fu, hi = (wd[w] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (uint32_t j = 0; j < 4; j++) q2[4 * w + j] = add_f32x2(f2pack(nib_raw(lo, j), nib_raw(hi, j)), nzz);
       }
 #pragma unroll
       for (int r = 0; r < 8; r++) {

@@ -212,6 +212,12 @@ __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
+// Nibble j (0..3 = byte j) of lohi (lo = w & 0x0F0F0F0F or hi = (w >> 4) &
+// 0x0F0F0F0F) placed in the mantissa of 2^23: the float 2^23 + nibble.  A
+// packed add of -(2^23 + zp) then gives two weights q - zp exactly.
+__device__ __forceinline__ float nib_raw(uint32_t lohi, uint32_t j) {
+  return __uint_as_float(__byte_perm(lohi, 0x4B000000u, 0x7650u | j));
+}
 // max(a, b, c) in one instruction (sm_100)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
