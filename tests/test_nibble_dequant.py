@@ -3,11 +3,11 @@ matmul_w4_exact_kernel) and the router candidate pass (k_router.cu):
 nib_raw (ts_common.cuh) puts a nibble q in the mantissa of 2^23 (bits
 0x4B000000 | q) and one packed add of -(2^23 + zp) gives q - zp.  The
 embedding gather (k_simt.cu embed_block_ref) uses the same byte permute and
-subtracts 2^23 + zp, the same value.  Replayed in numpy for every nibble and zero point: the result
-must be the f32 value of the integer q - zp, bit for bit (+0.0 where equal,
-as the integer conversion gives), which is what the reference's
-(q - zp) * scale starts from.  The byte-permute selector is checked against
-the byte it must pick.  CPU only.
+subtracts 2^23 + zp, the same value.  Replayed in numpy for every nibble
+and zero point: the result must be the f32 value of the integer q - zp, bit
+for bit (+0.0 where equal, as the integer conversion gives), which is what
+the reference's (q - zp) * scale starts from.  The byte-permute selector is
+checked against the byte it must pick.  CPU only.
 """
 import os
 import re
